@@ -1,0 +1,241 @@
+"""Public TPR entry points: module-spec install, CE request entry, PPO mini-batch entry.
+
+* :func:`run_tpr_forward_backward_batch` -- PPO mini-batch -> token-trie forest
+  -> batched level execution (or per-tree Push/Pop under CP) -> one gradient
+  finalisation; returns ``{"model_output", "loss", "metrics"}`` like verl.
+* :func:`run_tpr_forward_backward` -- CE request (a :class:`SegmentPlan` with
+  loss terms, optional fixed event order) through one SegmentExecutor.
+
+Parity: verl/models/mcore/tpr/megatron_adapter.py:37-529 and
+verl/models/mcore/tpr/engine_adapter.py:24-39 (TPR_REQUEST_KEY,
+TPRForwardBackwardRequest), verl/models/mcore/tpr/module_spec.py:34-131.
+"""
+
+from __future__ import annotations
+
+import os
+import time
+from collections.abc import Callable, Sequence
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+from torch import Tensor, nn
+
+from ..models.layers import TPRGatedDeltaNet, TPRSelfAttention
+from ..rl.objective import SegmentPPOObjectiveAdapter, batch_meta
+from ..tpr.forest_executor import ForestExecutor
+from ..tpr.scheduler import FixedTopologyScheduler, TPRBatchRunner
+from ..tpr.segment_executor import SegmentExecutor
+from ..tpr.segment_plan import SegmentEvent, SegmentPlan
+from ..tpr.tree_plan_builder import build_tree_execution_plans
+
+TPR_REQUEST_KEY = "tpr_forward_backward_request"
+
+
+@dataclass(frozen=True, slots=True)
+class TPRForwardBackwardRequest:
+    plan: SegmentPlan
+    events: tuple[SegmentEvent, ...] | None = None
+
+    def __post_init__(self) -> None:
+        if not isinstance(self.plan, SegmentPlan):
+            raise TypeError("plan must be a SegmentPlan")
+        if self.plan.topology_only:
+            raise ValueError("a CE request needs a plan with loss terms (not topology_only)")
+        if self.events is not None:
+            object.__setattr__(self, "events", self.plan.validate_events(self.events))
+
+
+# --------------------------------------------------------------------------- module spec
+def replace_self_attention_with_tpr(model: nn.Module) -> nn.Module:
+    """Validate that every token-mixing layer is TPR-capable (this framework builds them natively).
+
+    A foreign attention module (anything that is neither ``TPRSelfAttention``
+    nor ``TPRGatedDeltaNet``) cannot take external prefix state and is rejected.
+    """
+    layers = getattr(model, "layers", None)
+    if layers is None:
+        raise TypeError("model has no decoder layers")
+    for layer in layers:
+        mixer = getattr(layer, "self_attention", None)
+        if not isinstance(mixer, (TPRSelfAttention, TPRGatedDeltaNet)):
+            raise TypeError(f"layer {getattr(layer, 'layer_number', '?')} uses {type(mixer).__name__}, "
+                            "which cannot consume TPR prefix state")
+    return model
+
+
+def make_tpr_module_spec_provider(provider: Callable[[], nn.Module]) -> Callable[[], nn.Module]:
+    def build() -> nn.Module:
+        return replace_self_attention_with_tpr(provider())
+
+    build.tpr_installed = True  # type: ignore[attr-defined]
+    return build
+
+
+def install_tpr_module_spec(provider: Callable[[], nn.Module]) -> Callable[[], nn.Module]:
+    if getattr(provider, "tpr_installed", False):
+        return provider
+    return make_tpr_module_spec_provider(provider)
+
+
+# --------------------------------------------------------------------------- helpers
+def validate_tpr_parallel_sizes(sizes: dict[str, int], *, ppo: bool) -> int:
+    if sizes.get("PP", 1) != 1:
+        raise NotImplementedError("TPR does not support pipeline parallelism")
+    for k, v in sizes.items():
+        if not isinstance(v, int) or v < 1:
+            raise ValueError(f"{k} size must be a positive integer, got {v!r}")
+    return sizes.get("TP", 1)
+
+
+def trajectory_keys_from_minibatch(data: Any) -> tuple[str, ...]:
+    keys = batch_meta(data, "tpr_trajectory_keys", None)
+    if keys is not None:
+        keys = tuple(str(k) for k in keys)
+        if len(set(keys)) != len(keys):
+            raise ValueError("tpr_trajectory_keys must be unique")
+        return keys
+    uids = batch_meta(data, "uid", None)
+    if uids is None:
+        raise ValueError("TPR PPO needs tpr_trajectory_keys or uid to group trajectories")
+    out = []
+    for row, u in enumerate(uids):
+        if hasattr(u, "item"):
+            u = u.item()
+        if isinstance(u, bytes):
+            u = u.decode("utf-8")
+        if not isinstance(u, (str, int)) or not str(u):
+            raise ValueError(f"uid row {row} must be a nonempty string or integer")
+        out.append(f"{u}_tpr_{row}")
+    return tuple(out)
+
+
+def _rows(data, key):
+    v = data[key]
+    return list(v) if isinstance(v, (list, tuple)) else list(v.unbind())
+
+
+# --------------------------------------------------------------------------- CE entry
+def run_tpr_forward_backward(engine, request: TPRForwardBackwardRequest) -> dict:
+    if not isinstance(request, TPRForwardBackwardRequest):
+        raise TypeError("request must be a TPRForwardBackwardRequest")
+    from ..parallel.engine_runtime import aggregate_cp_loss, resolve_engine_cp_runtime
+
+    model = engine.model
+    rt = resolve_engine_cp_runtime(engine)
+    ex = SegmentExecutor(model, request.plan, cp_group=rt.group, cp_backend=rt.backend,
+                         loss_chunk_size=engine.engine_config.log_prob_chunk_tokens or None)
+    sched = FixedTopologyScheduler(request.plan, ex, events=request.events)
+    result = sched.run()
+    engine.finalize_model_grads()
+    loss_sum, loss = aggregate_cp_loss(result.loss_sum, result.normalized_loss, rt)
+    return {
+        "tpr_loss": float(loss.item()),
+        "tpr_loss_sum": float(loss_sum.item()),
+        "tpr_cp_size": rt.size,
+        "tpr_cp_backend": None if rt.backend is None else rt.backend.backend_name,
+        "tpr_peak_path_tokens": result.peak_path_tokens,
+        "tpr_segment_count": result.executed_segment_count,
+        "tpr_direct_leaf_count": result.direct_leaf_count,
+    }
+
+
+# --------------------------------------------------------------------------- PPO entry
+def run_tpr_forward_backward_batch(engine, data: Any, loss_function: Any = None, *, forward_only: bool = False,
+                                   sync_loss: bool = True) -> dict:
+    """PPO mini-batch -> TPR forest schedule -> one gradient finalisation."""
+    if forward_only:
+        raise NotImplementedError("the TPR PPO schedule is training-only; use compute_tree_log_probs for scoring")
+    ec = engine.engine_config
+    if not ec.tpr_enabled:
+        raise RuntimeError("TPR PPO requires engine_config.tpr_enabled=True at model creation")
+    model = engine.model
+    if not model.training:
+        raise RuntimeError("TPR PPO requires model.train()")
+    ps = engine.parallel
+    validate_tpr_parallel_sizes({"TP": ps.tp, "CP": ps.cp, "DP": ps.dp, "EP": ps.ep, "PP": 1}, ppo=True)
+    token_count = batch_meta(data, "batch_num_tokens", None)
+    dp_size = batch_meta(data, "dp_size", None)
+    if token_count is None or int(token_count) <= 0 or int(dp_size or 0) != ps.dp:
+        raise ValueError(f"engine must attach positive GLOBAL batch_num_tokens and the actual dp_size={ps.dp}")
+    prof = ec.exec_profile
+    t0 = time.perf_counter()
+    stage: dict[str, float] = {}
+    keys = trajectory_keys_from_minibatch(data)
+    forest = build_tree_execution_plans(keys, data, tree_policy=ec.tree_policy,
+                                        turn_min_segment_tokens=ec.turn_min_segment_tokens)
+    if not forest.trees or not forest.logical_loss_tokens:
+        raise ValueError("TPR PPO mini-batch has no supervised response tokens")
+    if prof:
+        stage["tree_build_cpu_ms"] = (time.perf_counter() - t0) * 1e3
+    if ps.tp > 1:
+        from ..tpr.tp_validation import assert_tp_plan_agreement, digest_forest_plan
+
+        assert_tp_plan_agreement(digest_forest_plan(forest), tp_size=ps.tp, group=ps.tp_group)
+    from ..parallel.engine_runtime import aggregate_cp_loss, resolve_engine_cp_runtime
+
+    rt = resolve_engine_cp_runtime(engine)
+    objective = SegmentPPOObjectiveAdapter(data, loss_function, dp_group=ps.dp_group,
+                                           log_prob_chunk_size=ec.log_prob_chunk_tokens or None)
+    t_run = time.perf_counter()
+    metrics: dict[str, Any] = {}
+    if rt.group is None and ec.executor == "forest":
+        fx = ForestExecutor(model, objective, mode=ec.forest_mode, token_budget=ec.token_budget)
+        res = fx.run(forest)
+        if sync_loss and not bool(torch.isfinite(res.normalized_loss).item()):
+            raise FloatingPointError("non-finite TPR PPO loss; gradients will not be finalized")
+        engine.finalize_model_grads()
+        total_loss = res.normalized_loss
+        stats = res.stats
+        metrics["tpr/forward_tokens"] = [res.forward_tokens]
+        metrics["tpr/backward_tokens"] = [res.backward_tokens]
+        metrics["tpr/chunks"] = [res.chunks]
+        if objective.calculate_entropy and "entropy_sum" in res.metrics:
+            metrics["actor/entropy"] = [res.metrics["entropy_sum"] / forest.logical_loss_tokens]
+    else:
+        shard_for = None if rt.backend is None else (lambda seg: rt.backend.make_sequence_shard(seg.length))
+        seg_stats = []
+
+        def run_tree(tree_plan):
+            fn, counts = objective.bind_tree(tree_plan, shard_for_segment=shard_for, model=model)
+            ex = SegmentExecutor(model, tree_plan.segment_plan, segment_loss_fn=fn, segment_loss_term_counts=counts,
+                                 cp_group=rt.group, cp_backend=rt.backend)
+            out = FixedTopologyScheduler(tree_plan.segment_plan, ex).run()
+            for _, m in ex.segment_loss_metrics:
+                seg_stats.append(m)
+            return out
+
+        runner = TPRBatchRunner(run_tree=run_tree, finalize_gradients=engine.finalize_model_grads)
+        res = runner.run(forest)
+        total_loss = res.normalized_loss
+        rows = [m["stats"] * m["n"] for m in seg_stats]
+        stats = torch.stack(rows).sum(0) / max(sum(m["n"] for m in seg_stats), 1) if rows else None
+    if prof:
+        stage["tree_run_and_finalize_host_ms"] = (time.perf_counter() - t_run) * 1e3
+    _, global_loss = aggregate_cp_loss(total_loss, total_loss, rt)
+    logical_inputs = sum(int(r.numel()) for r in _rows(data, "input_ids"))
+    unique = forest.unique_tokens
+    metrics.update({
+        "tpr/forest_trees": [len(forest.trees)],
+        "tpr/physical_segments": [forest.segment_count],
+        "tpr/logical_loss_tokens": [forest.logical_loss_tokens],
+        "tpr/logical_input_tokens": [logical_inputs],
+        "tpr/unique_tree_tokens": [unique],
+        "tpr/topology_token_reuse_ratio": [logical_inputs / unique],
+    })
+    if stats is not None:
+        names = ("actor/pg_clipfrac", "actor/pg_clipfrac_lower", "actor/ppo_kl", "actor/ratio_mean")
+        metrics.update({n: [stats[i]] for i, n in enumerate(names)})
+    if sync_loss:
+        loss_val: Any = float(global_loss.item())
+        if not torch.isfinite(torch.tensor(loss_val)):
+            raise FloatingPointError("non-finite TPR PPO mini-batch loss")
+        for k, v in metrics.items():
+            metrics[k] = [float(x.item()) if isinstance(x, Tensor) else float(x) for x in v]
+    else:
+        loss_val = global_loss
+    if prof:
+        stage["whole_entry_host_ms"] = (time.perf_counter() - t0) * 1e3
+        engine._tpr_stage_profile = stage
+    return {"model_output": {}, "loss": [loss_val], "metrics": metrics}

@@ -1,0 +1,115 @@
+"""Decoder-only policy model (Qwen3 dense / hybrid GDN / hybrid MoE).
+
+``forward(input_ids [T], position_ids [T]) -> hidden [T, hidden]`` runs the
+embedding, every decoder layer (attention layers read the active TPR context)
+and the final RMSNorm on a packed token stream.  The LM head is applied only
+to the rows that carry a loss term, through
+:func:`~bridge_b200.ops.logprob.fused_lm_head_logprob` (PPO) or
+:meth:`logits` (CE / debugging) -- the full ``[T, vocab]`` logits of prompt
+rows are never computed.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+from ..parallel.tp import VocabParallelEmbedding, copy_to_tp, gather_from_sp, tp_rank, tp_size
+from .config import ModelConfig
+from .layers import DecoderLayer, RMSNorm, RotaryEmbedding
+
+
+class DecoderModel(nn.Module):
+    def __init__(self, cfg: ModelConfig, *, tp_group=None, sequence_parallel: bool = False, ep_group=None,
+                 device=None) -> None:
+        super().__init__()
+        self.config = cfg
+        self.tp_group = tp_group
+        self.sequence_parallel = sequence_parallel and tp_size(tp_group) > 1
+        self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, group=tp_group,
+                                                   std=cfg.init_std, device=device)
+        self.layers = nn.ModuleList(
+            DecoderLayer(cfg, i + 1, tp_group=tp_group, sequence_parallel=self.sequence_parallel,
+                         ep_group=ep_group, device=device)
+            for i in range(cfg.num_layers)
+        )
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_eps, device=device)
+        self.rotary_pos_emb = RotaryEmbedding(cfg.head_dim, cfg.rope_theta)
+        if cfg.tie_word_embeddings:
+            self.lm_head = None
+        else:
+            n = tp_size(tp_group)
+            self.lm_head = nn.Parameter(torch.randn(cfg.vocab_size // n, cfg.hidden_size, device=device,
+                                                    dtype=torch.bfloat16) * cfg.init_std)
+            self.lm_head.tp_split_dim = 0  # type: ignore[attr-defined]
+        self.vocab_size = cfg.vocab_size
+
+    # ------------------------------------------------------------------ metadata
+    @property
+    def attention_layer_numbers(self) -> tuple[int, ...]:
+        return self.config.attention_layer_numbers
+
+    @property
+    def gdn_layer_numbers(self) -> tuple[int, ...]:
+        return self.config.gdn_layer_numbers
+
+    @property
+    def head_weight(self) -> Tensor:
+        return self.embed_tokens.weight if self.lm_head is None else self.lm_head
+
+    @property
+    def vocab_start(self) -> int:
+        return tp_rank(self.tp_group) * (self.vocab_size // tp_size(self.tp_group))
+
+    # ------------------------------------------------------------------ compute
+    def forward(self, input_ids: Tensor, position_ids: Tensor, max_position: int | None = None) -> Tensor:
+        if input_ids.ndim == 2:  # [1, T] accepted for single-sequence callers
+            input_ids, position_ids = input_ids[0], position_ids[0]
+        x = self.embed_tokens(input_ids)
+        rope = self.rotary_pos_emb(position_ids, max_position)
+        if self.sequence_parallel:
+            n, r = tp_size(self.tp_group), tp_rank(self.tp_group)
+            if x.shape[0] % n:
+                raise ValueError("sequence-parallel segments must be divisible by the TP size")
+            x = x.chunk(n)[r]
+        for layer in self.layers:
+            x = layer(x, rope)
+        x = self.norm(x)
+        if self.sequence_parallel:
+            x = gather_from_sp(x, self.tp_group)
+        return x
+
+    def head_input(self, hidden_rows: Tensor) -> Tensor:
+        """Prepare selected hidden rows for the (vocab-parallel) LM head."""
+        return copy_to_tp(hidden_rows, self.tp_group)
+
+    def logits(self, hidden_rows: Tensor) -> Tensor:
+        """Local-vocab logits ``[U, V/TP]`` of selected rows."""
+        from ..ops.gemm import linear
+
+        return linear(self.head_input(hidden_rows), self.head_weight)
+
+
+def build_model(cfg: ModelConfig, *, device=None, seed: int = 0, tp_group=None, sequence_parallel=False,
+                ep_group=None, dtype: torch.dtype | None = None) -> DecoderModel:
+    """Random-init model; every rank of a TP group uses a rank-dependent stream for its shard.
+
+    Parameters are created on the host (deterministic across devices) and then
+    moved; ``dtype`` (e.g. FP32 for CPU oracles) converts every parameter.
+    """
+    g_state = torch.random.get_rng_state()
+    dev = torch.device(device) if device is not None else torch.device("cpu")
+    cuda_state = torch.cuda.get_rng_state(dev) if dev.type == "cuda" else None
+    torch.manual_seed(seed * 7919 + 104729 * tp_rank(tp_group))
+    try:
+        # Large models initialise directly on the GPU; host init is used for CPU runs.
+        model = DecoderModel(cfg, tp_group=tp_group, sequence_parallel=sequence_parallel, ep_group=ep_group,
+                             device=dev)
+    finally:
+        torch.random.set_rng_state(g_state)
+        if cuda_state is not None:
+            torch.cuda.set_rng_state(cuda_state, dev)
+    if dtype is not None:
+        model = model.to(dtype)
+    return model

@@ -1,0 +1,136 @@
+"""Mixture-of-experts FFN: softmax top-k router, SwiGLU experts, gated shared expert.
+
+Routing follows the Qwen3-Next form: ``p = softmax(x W_r^T)`` over all experts,
+keep the top-k, renormalise them to sum to one; the shared expert output is
+scaled by ``sigmoid(x w_g)``.  Under expert parallelism (``ep_group``) every
+rank owns ``E / ep`` experts; token rows are exchanged with an all-to-all
+(dispatch), run through the local experts as one grouped GEMM over
+expert-sorted rows, and exchanged back (combine).
+
+The reference MoE is absent from the TPR extension (it rejects MoE); this is a
+new capability of this framework.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+from torch import Tensor
+
+from ..ops.activation import swiglu
+from ..ops.gemm import linear
+from .config import ModelConfig
+
+
+def _ep_size(group) -> int:
+    return 1 if group is None else dist.get_world_size(group)
+
+
+class _AllToAll(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, send_counts, recv_counts, group):
+        ctx.group, ctx.send, ctx.recv = group, send_counts, recv_counts
+        out = x.new_empty((sum(recv_counts), *x.shape[1:]))
+        dist.all_to_all_single(out, x.contiguous(), recv_counts, send_counts, group=group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        out = g.new_empty((sum(ctx.send), *g.shape[1:]))
+        dist.all_to_all_single(out, g.contiguous(), ctx.send, ctx.recv, group=ctx.group)
+        return out, None, None, None
+
+
+def grouped_swiglu_experts(x: Tensor, counts: list[int], w1: Tensor, w2: Tensor) -> Tensor:
+    """Rows of ``x`` sorted by expert (``counts[e]`` rows each) through expert ``e``'s SwiGLU."""
+    outs = []
+    s = 0
+    for e, n in enumerate(counts):
+        if n:
+            h = x[s:s + n]
+            outs.append(linear(swiglu(linear(h, w1[e])), w2[e]))
+        s += n
+    if not outs:
+        return x.new_zeros((0, w2.shape[1]))
+    return torch.cat(outs)
+
+
+class MoELayer(nn.Module):
+    def __init__(self, cfg: ModelConfig, *, ep_group=None, device=None) -> None:
+        super().__init__()
+        ep = _ep_size(ep_group)
+        if cfg.num_experts % ep:
+            raise ValueError("num_experts must divide evenly over the EP group")
+        self.ep_group = ep_group
+        self.num_experts, self.top_k = cfg.num_experts, cfg.moe_top_k
+        self.local_experts = cfg.num_experts // ep
+        self.ep_rank = 0 if ep_group is None else dist.get_rank(ep_group)
+        h, f = cfg.hidden_size, cfg.moe_intermediate_size
+        std = cfg.init_std
+        self.router = nn.Parameter(torch.randn(cfg.num_experts, h, device=device, dtype=torch.bfloat16) * std)
+        self.w1 = nn.Parameter(torch.randn(self.local_experts, 2 * f, h, device=device, dtype=torch.bfloat16) * std)
+        self.w2 = nn.Parameter(torch.randn(self.local_experts, h, f, device=device, dtype=torch.bfloat16) * std)
+        self.shared = None
+        if cfg.shared_expert_intermediate_size:
+            fs = cfg.shared_expert_intermediate_size
+            self.shared_w1 = nn.Parameter(torch.randn(2 * fs, h, device=device, dtype=torch.bfloat16) * std)
+            self.shared_w2 = nn.Parameter(torch.randn(h, fs, device=device, dtype=torch.bfloat16) * std)
+            self.shared_gate = nn.Parameter(torch.randn(1, h, device=device, dtype=torch.bfloat16) * std)
+            self.shared = True
+        self.last_load = None
+
+    def route(self, x: Tensor) -> tuple[Tensor, Tensor]:
+        logits = linear(x, self.router).float()
+        probs = torch.softmax(logits, dim=-1)
+        w, idx = torch.topk(probs, self.top_k, dim=-1)
+        w = w / w.sum(-1, keepdim=True)
+        return w, idx
+
+    def forward(self, x: Tensor) -> Tensor:
+        t, h = x.shape
+        w, idx = self.route(x)
+        flat_e = idx.reshape(-1)                                   # [T*k]
+        order = torch.argsort(flat_e, stable=True)
+        rows = order // self.top_k
+        xs = x.index_select(0, rows)
+        counts_all = torch.bincount(flat_e, minlength=self.num_experts)
+        self.last_load = counts_all.detach()
+        ep = _ep_size(self.ep_group)
+        if ep == 1:
+            y_sorted = grouped_swiglu_experts(xs, counts_all.tolist(), self.w1, self.w2)
+        else:
+            per_rank = counts_all.view(ep, self.local_experts)
+            send = per_rank.sum(1)
+            recv_matrix = torch.empty_like(per_rank)
+            dist.all_to_all_single(recv_matrix, per_rank.contiguous(), group=self.ep_group)
+            send_l, recv_l = send.tolist(), recv_matrix.sum(1).tolist()
+            xr = _AllToAll.apply(xs, send_l, recv_l, self.ep_group)
+            # Received rows are grouped by source rank then by local expert: re-sort by expert.
+            rm = recv_matrix.tolist()
+            src_starts, s = [], 0
+            for r in range(ep):
+                src_starts.append(s)
+                s += sum(rm[r])
+            perm = []
+            counts_local = []
+            for e in range(self.local_experts):
+                n_e = 0
+                for r in range(ep):
+                    start = src_starts[r] + sum(rm[r][:e])
+                    perm.extend(range(start, start + rm[r][e]))
+                    n_e += rm[r][e]
+                counts_local.append(n_e)
+            perm_t = torch.tensor(perm, device=x.device, dtype=torch.long)
+            ye = grouped_swiglu_experts(xr.index_select(0, perm_t), counts_local, self.w1, self.w2)
+            inv = torch.empty_like(perm_t)
+            inv[perm_t] = torch.arange(perm_t.numel(), device=x.device)
+            y_sorted = _AllToAll.apply(ye.index_select(0, inv), recv_l, send_l, self.ep_group)
+        gate = w.reshape(-1).index_select(0, order).to(y_sorted.dtype)[:, None]
+        y = torch.zeros((t, h), device=x.device, dtype=torch.float32)
+        y.index_add_(0, rows, (y_sorted * gate).float())
+        y = y.to(x.dtype)
+        if self.shared:
+            sh = linear(swiglu(linear(x, self.shared_w1)), self.shared_w2)
+            y = y + sh * torch.sigmoid(linear(x, self.shared_gate).float()).to(sh.dtype)
+        return y

@@ -1,0 +1,196 @@
+"""Gated DeltaNet ops: stateful causal depthwise conv1d and the chunked gated delta rule.
+
+Both take packed varlen inputs (``cu_seqlens`` host list, one continuation
+state per sequence) so a batch of sibling segments runs in one call.
+
+causal_conv1d
+    ``x [T, C]``, depthwise weight ``[C, W]``, optional bias, SiLU.  The state
+    ``[B, C, W]`` holds the last ``W-1`` inputs in slots ``1..W-1`` (slot 0 is
+    unused and always zero); output row ``t`` of a sequence convolves
+    ``cat(h0[:, 1:], x)`` over a window of ``W``, so only rows ``t < W-1`` read
+    the initial state and ``dh0[:, :, 0] == 0``.
+
+gated delta rule (FLA convention)
+    ``S_t = e^{g_t} S_{t-1};  u_t = beta_t (v_t - S_t^T k_t);  S_t += k_t u_t^T;
+    o_t = scale * S_t^T q_t`` with FP32 state ``[B, H, K, V]``.  The chunked
+    form (chunk C) uses, per chunk with cumulative decay ``Gamma_t``,
+    ``A_ts = (Gamma_t/Gamma_s) k_t.k_s`` (s<t), ``T = (I + diag(beta) A)^-1``,
+    ``U = T diag(beta) V - T diag(beta Gamma) K S0``,
+    ``O = scale (diag(Gamma) Q S0 + (Mask ∘ Gamma_t/Gamma_s ∘ Q K^T) U)``,
+    ``S_C = Gamma_C S0 + K^T diag(Gamma_C/Gamma) U`` -- i.e. the chunk end state is
+    affine in ``S0`` (the basis of the sequence-sharded CP state chain).
+
+Parity: MindSpeed-Ops causal_conv1d / chunk_gated_delta_rule as called from
+verl/models/mcore/tpr/gated_delta_net.py:214-263; oracle restated from
+tests/unit_tests/triton/test_chunk_gated_delta_rule_stateful_experiment.py:96-215
+and tests/models/mcore/tpr/parallel/test_conv_dh0_bounds_npu.py:80-98.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor
+
+from ._ext import kernels, on_gpu
+
+
+# --------------------------------------------------------------------------- causal conv1d
+def causal_conv1d_reference(x: Tensor, weight: Tensor, bias: Tensor | None, cu_seqlens: list[int],
+                            initial_state: Tensor | None, *, activation: bool = True):
+    """Returns ``y [T, C]`` and final state ``[B, C, W]`` (slot 0 zero)."""
+    c, w = weight.shape
+    ys, finals = [], []
+    for i in range(len(cu_seqlens) - 1):
+        xs = x[cu_seqlens[i]:cu_seqlens[i + 1]]                      # [L, C]
+        if initial_state is not None:
+            hist = initial_state[i, :, 1:].transpose(0, 1).to(xs.dtype)   # [W-1, C]
+        else:
+            hist = xs.new_zeros((w - 1, c))
+        full = torch.cat((hist, xs), dim=0).float()                  # [L+W-1, C]
+        win = full.unfold(0, w, 1)                                   # [L, C, W]
+        y = (win * weight.float()[None]).sum(-1)
+        if bias is not None:
+            y = y + bias.float()
+        if activation:
+            y = F.silu(y)
+        ys.append(y.to(x.dtype))
+        tail = full[-(w - 1):].transpose(0, 1)                       # [C, W-1]
+        finals.append(torch.cat((tail.new_zeros((c, 1)), tail), dim=1).to(x.dtype))
+    return torch.cat(ys), torch.stack(finals)
+
+
+class _ConvFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, h0, cu_dev, cu_host, activation):
+        m = kernels()
+        x = x.contiguous()
+        y, hT = m.causal_conv1d_fwd(x, weight.contiguous(), bias, h0, cu_dev, bool(activation))
+        ctx.save_for_backward(x, weight, bias, h0, cu_dev)
+        ctx.activation = activation
+        return y, hT
+
+    @staticmethod
+    def backward(ctx, dy, dhT):
+        m = kernels()
+        x, weight, bias, h0, cu = ctx.saved_tensors
+        dx, dw, db, dh0 = m.causal_conv1d_bwd(dy.contiguous(), x, weight.contiguous(), bias, h0,
+                                              dhT.contiguous() if dhT is not None else None, cu,
+                                              bool(ctx.activation))
+        return dx, dw.to(weight.dtype), (db.to(bias.dtype) if bias is not None else None), \
+            (dh0 if h0 is not None else None), None, None, None
+
+
+def causal_conv1d(x: Tensor, weight: Tensor, bias: Tensor | None, cu_seqlens: list[int], cu_dev: Tensor | None,
+                  initial_state: Tensor | None, *, activation: bool = True):
+    if on_gpu(x):
+        if cu_dev is None:
+            cu_dev = torch.tensor(cu_seqlens, dtype=torch.int32, device=x.device)
+        return _ConvFn.apply(x, weight, bias, initial_state, cu_dev, tuple(cu_seqlens), activation)
+    return causal_conv1d_reference(x, weight, bias, cu_seqlens, initial_state, activation=activation)
+
+
+# --------------------------------------------------------------------------- gated delta rule
+def gated_delta_rule_recurrent(q, k, v, g, beta, initial_state, *, scale: float):
+    """Naive per-token recurrence for ONE sequence (oracle). ``q,k [L,H,K]``, ``v [L,H,V]``, ``g,beta [L,H]``."""
+    L, H, K = q.shape
+    V = v.shape[-1]
+    S = initial_state.float().clone() if initial_state is not None else q.new_zeros((H, K, V), dtype=torch.float32)
+    outs = []
+    for t in range(L):
+        S = S * torch.exp(g[t].float())[:, None, None]
+        kt, vt, qt = k[t].float(), v[t].float(), q[t].float()
+        pred = torch.einsum("hk,hkv->hv", kt, S)
+        u = beta[t].float()[:, None] * (vt - pred)
+        S = S + kt[:, :, None] * u[:, None, :]
+        outs.append(torch.einsum("hk,hkv->hv", qt, S) * scale)
+    return torch.stack(outs).to(q.dtype), S
+
+
+def _chunk_one(q, k, v, g, beta, S0, scale: float, chunk: int):
+    """Chunked form for one sequence; differentiable torch (FP32). Returns o [L,H,V], S [H,K,V]."""
+    L, H, K = q.shape
+    V = v.shape[-1]
+    S = S0
+    outs = []
+    for s in range(0, L, chunk):
+        e = min(L, s + chunk)
+        n = e - s
+        qc = q[s:e].float().transpose(0, 1)        # [H, n, K]
+        kc = k[s:e].float().transpose(0, 1)
+        vc = v[s:e].float().transpose(0, 1)        # [H, n, V]
+        bc = beta[s:e].float().transpose(0, 1)     # [H, n]
+        G = torch.cumsum(g[s:e].float().transpose(0, 1), dim=-1)   # [H, n]
+        decay = torch.exp(G[:, :, None] - G[:, None, :])           # Gamma_t / Gamma_s
+        tri_strict = torch.ones(n, n, dtype=torch.bool, device=q.device).tril(-1)
+        tri = torch.ones(n, n, dtype=torch.bool, device=q.device).tril()
+        kk = torch.matmul(kc, kc.transpose(1, 2))
+        A = torch.where(tri_strict, decay * kk, torch.zeros_like(kk))
+        eye = torch.eye(n, device=q.device, dtype=torch.float32).expand(H, n, n)
+        Tm = torch.linalg.solve_triangular(eye + bc[:, :, None] * A, eye, upper=False)
+        gam = torch.exp(G)
+        Wv = torch.matmul(Tm, bc[:, :, None] * vc)
+        Wk = torch.matmul(Tm, (bc * gam)[:, :, None] * kc)
+        U = Wv - torch.matmul(Wk, S)                                # [H, n, V]
+        qk = torch.where(tri, decay * torch.matmul(qc, kc.transpose(1, 2)), torch.zeros_like(kk))
+        o = (gam[:, :, None] * torch.matmul(qc, S) + torch.matmul(qk, U)) * scale
+        outs.append(o.transpose(0, 1))
+        gl = gam[:, -1]
+        S = gl[:, None, None] * S + torch.matmul((kc * torch.exp(G[:, -1:] - G)[:, :, None]).transpose(1, 2), U)
+    return torch.cat(outs).to(q.dtype), S
+
+
+def chunk_gated_delta_rule_reference(q, k, v, g, beta, cu_seqlens: list[int], initial_state: Tensor | None, *,
+                                     scale: float, chunk_size: int = 64):
+    """Packed varlen chunked GDR (torch). ``initial_state [B,H,K,V]`` FP32 or None."""
+    H, K, V = q.shape[1], q.shape[2], v.shape[2]
+    outs, finals = [], []
+    for i in range(len(cu_seqlens) - 1):
+        a, b = cu_seqlens[i], cu_seqlens[i + 1]
+        S0 = initial_state[i].float() if initial_state is not None else q.new_zeros((H, K, V), dtype=torch.float32)
+        o, S = _chunk_one(q[a:b], k[a:b], v[a:b], g[a:b], beta[a:b], S0, scale, chunk_size)
+        outs.append(o)
+        finals.append(S)
+    return torch.cat(outs), torch.stack(finals)
+
+
+class _GDRFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, h0, cu_dev, scale, chunk):
+        m = kernels()
+        q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
+        o, hT = m.gdr_fwd(q, k, v, g.float(), beta.float(), h0, cu_dev, float(scale), int(chunk))
+        ctx.save_for_backward(q, k, v, g, beta, h0, cu_dev)
+        ctx.scale, ctx.chunk = scale, chunk
+        return o, hT
+
+    @staticmethod
+    def backward(ctx, do, dhT):
+        m = kernels()
+        q, k, v, g, beta, h0, cu = ctx.saved_tensors
+        dq, dk, dv, dg, db, dh0 = m.gdr_bwd(do.contiguous(), dhT.contiguous() if dhT is not None else None,
+                                            q, k, v, g.float(), beta.float(), h0, cu, float(ctx.scale),
+                                            int(ctx.chunk))
+        return dq, dk, dv, dg.to(g.dtype), db.to(beta.dtype), (dh0 if h0 is not None else None), None, None, None
+
+
+def chunk_gated_delta_rule(q, k, v, g, beta, cu_seqlens: list[int], cu_dev: Tensor | None,
+                           initial_state: Tensor | None, *, scale: float, chunk_size: int = 64):
+    if on_gpu(q) and hasattr(kernels(), "gdr_fwd"):
+        if cu_dev is None:
+            cu_dev = torch.tensor(cu_seqlens, dtype=torch.int32, device=q.device)
+        return _GDRFn.apply(q, k, v, g, beta, initial_state, cu_dev, scale, chunk_size)
+    return chunk_gated_delta_rule_reference(q, k, v, g, beta, cu_seqlens, initial_state, scale=scale,
+                                            chunk_size=chunk_size)
+
+
+def l2norm(x: Tensor, eps: float = 1e-6) -> Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt((xf * xf).sum(-1, keepdim=True) + eps)).to(x.dtype)
+
+
+def gated_rmsnorm(o: Tensor, z: Tensor, weight: Tensor, eps: float) -> Tensor:
+    """``RMSNorm(o) * weight * silu(z)`` per head (last dim)."""
+    of = o.float()
+    y = of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps) * weight.float()
+    return (y * F.silu(z.float())).to(o.dtype)

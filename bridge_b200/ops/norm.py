@@ -1,0 +1,98 @@
+"""RMSNorm (row-wise over the last dim) and fused per-head qk-RMSNorm + RoPE.
+
+CUDA kernels (``csrc/elementwise.cu``): one warp per row, FP32 accumulation,
+vectorised 16-byte loads; backward recomputes ``rstd`` from the saved input
+and reduces the weight gradient per CTA before a final column sum.
+
+RoPE follows the Qwen/HF "rotate-half" convention: with
+``inv_freq[i] = theta^(-2i/d)`` and angle ``a = pos * inv_freq``,
+``x' = x*cos(a) + rotate_half(x)*sin(a)`` where ``rotate_half([x1, x2]) = [-x2, x1]``.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from ._ext import kernels, on_gpu
+
+
+def rmsnorm_reference(x: Tensor, weight: Tensor, eps: float) -> Tensor:
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (y * weight.float()).to(x.dtype)
+
+
+class _RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        m = kernels()
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        y, rstd = m.rmsnorm_fwd(x2, weight.contiguous(), float(eps))
+        ctx.save_for_backward(x2, weight, rstd)
+        ctx.shape = shape
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        m = kernels()
+        x2, weight, rstd = ctx.saved_tensors
+        dx, dw = m.rmsnorm_bwd(dy.reshape(x2.shape).contiguous(), x2, weight.contiguous(), rstd)
+        return dx.view(ctx.shape), dw.to(weight.dtype), None
+
+
+def rmsnorm(x: Tensor, weight: Tensor, eps: float = 1e-6) -> Tensor:
+    if on_gpu(x):
+        return _RMSNormFn.apply(x, weight, eps)
+    return rmsnorm_reference(x, weight, eps)
+
+
+# --------------------------------------------------------------------------- RoPE
+def rope_cos_sin(positions: Tensor, head_dim: int, theta: float) -> tuple[Tensor, Tensor]:
+    """FP32 ``cos, sin [T, head_dim/2]`` for integer positions."""
+    inv = theta ** (-torch.arange(0, head_dim, 2, device=positions.device, dtype=torch.float64) / head_dim)
+    ang = positions.to(torch.float64)[:, None] * inv[None, :]
+    return torch.cos(ang).float(), torch.sin(ang).float()
+
+
+def apply_rope_reference(x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
+    """``x [T, H, D]``; cos/sin ``[T, D/2]``."""
+    d2 = x.shape[-1] // 2
+    xf = x.float()
+    x1, x2 = xf[..., :d2], xf[..., d2:]
+    c, s = cos[:, None, :], sin[:, None, :]
+    return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1).to(x.dtype)
+
+
+def qk_norm_rope_reference(q, k, q_weight, k_weight, cos, sin, eps):
+    if q_weight is not None:
+        q = rmsnorm_reference(q, q_weight, eps)
+        k = rmsnorm_reference(k, k_weight, eps)
+    return apply_rope_reference(q, cos, sin), apply_rope_reference(k, cos, sin)
+
+
+class _QKNormRopeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, qw, kw, cos, sin, eps):
+        m = kernels()
+        q_, k_ = q.contiguous(), k.contiguous()
+        qo, ko, rq, rk = m.qk_norm_rope_fwd(q_, k_, qw, kw, cos, sin, float(eps))
+        ctx.save_for_backward(q_, k_, qw, kw, cos, sin, rq, rk)
+        ctx.eps = eps
+        return qo, ko
+
+    @staticmethod
+    def backward(ctx, dqo, dko):
+        m = kernels()
+        q, k, qw, kw, cos, sin, rq, rk = ctx.saved_tensors
+        dq, dk, dqw, dkw = m.qk_norm_rope_bwd(dqo.contiguous(), dko.contiguous(), q, k, qw, kw, cos, sin, rq, rk)
+        return dq, dk, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None
+
+
+def qk_norm_rope(q: Tensor, k: Tensor, q_weight: Tensor | None, k_weight: Tensor | None, cos: Tensor, sin: Tensor,
+                 eps: float = 1e-6) -> tuple[Tensor, Tensor]:
+    """Per-head RMSNorm of q and k (when weights are given) then RoPE; ``q [T,Hq,D]``, ``k [T,Hkv,D]``."""
+    if on_gpu(q) and q_weight is not None:
+        return _QKNormRopeFn.apply(q, k, q_weight, k_weight, cos.contiguous(), sin.contiguous(), eps)
+    return qk_norm_rope_reference(q, k, q_weight, k_weight, cos, sin, eps)

@@ -1,0 +1,221 @@
+"""Activation offload to pinned host memory, scoped to one Pop / VisitLeaf.
+
+While the scope is active, every tensor autograd saves (above ``min_bytes``)
+is copied device->host on a side stream right after it is produced; the
+device copy is released as soon as the D2H completes.  When the backward of
+decoder layer ``L`` starts, the saved tensors of layer ``L-1`` are copied back
+host->device on a second stream (prefetch), so the H2D of one layer overlaps
+the backward math of the next.  The prefix-KV anchors of the segment (and the
+new K/V a Pop hands to autograd as roots) are never offloaded: they are read
+by every descendant and must stay resident.
+
+Pinned host buffers come from a size-bucketed pool so steady-state steps do
+no ``cudaHostAlloc``.
+
+Parity: verl/models/mcore/tpr/activation_offload.py:61-328 (scope, limits,
+protected external storages, forced same-layer restore).  Built on
+``torch.autograd.graph.saved_tensors_hooks`` + ``cudaMemcpyAsync`` on
+dedicated streams instead of MindSpeed SwapPrefetch.
+"""
+
+from __future__ import annotations
+
+import functools
+import os
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor, nn
+
+
+@dataclass(frozen=True)
+class OffloadConfig:
+    enabled: bool = False
+    min_bytes: int = 1 << 20
+    prefetch: bool = True
+    force_restore_sync: bool = os.environ.get("TPR_OFFLOAD_B_FORCE_RESTORE_SYNC", "0") == "1"
+
+
+def validate_activation_offload(model: nn.Module, cp_size: int, cp_backend, cfg: OffloadConfig | None) -> None:
+    """Offload supports CP1 and the ring backend (any CP size); other backends are rejected."""
+    if cfg is None or not cfg.enabled:
+        return
+    name = getattr(cp_backend, "backend_name", None)
+    if cp_size > 1 and name != "ring":
+        raise NotImplementedError(f"activation offload requires CP=1 or the ring backend, got {name!r}")
+
+
+class _PinnedPool:
+    def __init__(self) -> None:
+        self.free: dict[tuple, list[Tensor]] = {}
+
+    def get(self, numel: int, dtype) -> Tensor:
+        key = (numel, dtype)
+        lst = self.free.get(key)
+        if lst:
+            return lst.pop()
+        return torch.empty(numel, dtype=dtype, pin_memory=torch.cuda.is_available())
+
+    def put(self, t: Tensor) -> None:
+        self.free.setdefault((t.numel(), t.dtype), []).append(t)
+
+
+_POOL = _PinnedPool()
+
+
+class _Saved:
+    __slots__ = ("host", "shape", "dtype", "device", "d2h_done", "layer", "restored", "h2d_done")
+
+    def __init__(self, host, shape, dtype, device, d2h_done, layer):
+        self.host, self.shape, self.dtype, self.device = host, shape, dtype, device
+        self.d2h_done, self.layer = d2h_done, layer
+        self.restored: Tensor | None = None
+        self.h2d_done = None
+
+
+class ActivationOffloader:
+    """saved_tensors_hooks pair plus per-layer prefetch bookkeeping."""
+
+    def __init__(self, cfg: OffloadConfig, protected: list[Tensor] | tuple = ()) -> None:
+        self.cfg = cfg
+        self.protected = {t.untyped_storage().data_ptr() for t in protected if isinstance(t, Tensor)}
+        self.layer = -1
+        self.by_layer: dict[int, list[_Saved]] = {}
+        self.cuda = torch.cuda.is_available()
+        self.d2h = torch.cuda.Stream() if self.cuda else None
+        self.h2d = torch.cuda.Stream() if self.cuda else None
+        self.offloaded_bytes = 0
+
+    def protect(self, tensors) -> None:
+        for t in tensors:
+            if isinstance(t, Tensor):
+                self.protected.add(t.untyped_storage().data_ptr())
+
+    # -- hooks
+    def pack(self, t: Tensor):
+        nbytes = t.numel() * t.element_size()
+        if (nbytes < self.cfg.min_bytes or isinstance(t, nn.Parameter) or t.untyped_storage().data_ptr()
+                in self.protected or not t.is_contiguous()):
+            return t
+        host = _POOL.get(t.numel(), t.dtype)
+        if t.is_cuda:
+            ev = torch.cuda.Event()
+            ev.record()
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(ev)
+                host.copy_(t.reshape(-1), non_blocking=True)
+                t.record_stream(self.d2h)
+                done = torch.cuda.Event()
+                done.record()
+        else:
+            host.copy_(t.reshape(-1))
+            done = None
+        s = _Saved(host, t.shape, t.dtype, t.device, done, self.layer)
+        self.by_layer.setdefault(self.layer, []).append(s)
+        self.offloaded_bytes += nbytes
+        return s
+
+    def _restore(self, s: _Saved, stream=None) -> None:
+        if s.restored is not None:
+            return
+        if s.device.type == "cuda":
+            ctx = torch.cuda.stream(stream) if stream is not None else torch.cuda.stream(torch.cuda.current_stream())
+            with ctx:
+                cur = torch.cuda.current_stream()
+                cur.wait_event(s.d2h_done)
+                dev = torch.empty(s.shape, dtype=s.dtype, device=s.device)
+                dev.view(-1).copy_(s.host, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record()
+            s.restored, s.h2d_done = dev, ev
+        else:
+            s.restored = s.host.view(s.shape).clone()
+
+    def unpack(self, s):
+        if isinstance(s, Tensor):
+            return s
+        if s.restored is None:
+            self._restore(s)
+        if s.h2d_done is not None:
+            torch.cuda.current_stream().wait_event(s.h2d_done)
+            if self.cfg.force_restore_sync:
+                s.h2d_done.synchronize()
+            s.restored.record_stream(torch.cuda.current_stream())
+        out = s.restored
+        return out
+
+    def prefetch_layer(self, layer: int) -> None:
+        if not self.cfg.prefetch:
+            return
+        for s in self.by_layer.get(layer, ()):
+            self._restore(s, self.h2d)
+
+    def release(self) -> None:
+        if self.cuda:
+            torch.cuda.current_stream().wait_stream(self.d2h)
+            self.d2h.synchronize()
+        for lst in self.by_layer.values():
+            for s in lst:
+                _POOL.put(s.host)
+        self.by_layer.clear()
+
+
+class _LayerTracker:
+    """Forward pre-hooks record the current layer; backward pre-hooks prefetch the layer below."""
+
+    def __init__(self, model: nn.Module, off: ActivationOffloader) -> None:
+        self.handles = []
+        layers = getattr(model, "layers", None)
+        if layers is None:
+            return
+        for i, layer in enumerate(layers):
+            self.handles.append(layer.register_forward_pre_hook(functools.partial(self._enter, off, i)))
+            self.handles.append(layer.register_full_backward_pre_hook(functools.partial(self._bwd, off, i)))
+
+    @staticmethod
+    def _enter(off, i, module, args):
+        off.layer = i
+
+    @staticmethod
+    def _bwd(off, i, module, grad_output):
+        off.prefetch_layer(i - 1)
+
+    def remove(self) -> None:
+        for h in self.handles:
+            h.remove()
+
+
+def offload_scope(model: nn.Module, cfg: OffloadConfig, protected=()):
+    """Context manager installing the offload hooks for one segment execution."""
+    import contextlib
+
+    @contextlib.contextmanager
+    def scope():
+        off = ActivationOffloader(cfg, protected)
+        tracker = _LayerTracker(model, off)
+        try:
+            with torch.autograd.graph.saved_tensors_hooks(off.pack, off.unpack):
+                yield off
+        finally:
+            tracker.remove()
+            off.release()
+
+    return scope()
+
+
+def with_activation_offload(method):
+    """Decorator for executor methods: runs them inside an offload scope when enabled."""
+
+    @functools.wraps(method)
+    def wrapper(self, *args, **kwargs):
+        cfg = getattr(self, "activation_offload", None)
+        if cfg is None or not cfg.enabled:
+            return method(self, *args, **kwargs)
+        protected = []
+        for e in getattr(self, "kv_stack", ()).entries() if hasattr(getattr(self, "kv_stack", None), "entries") else ():
+            for k, v in e.state.key_values.values():
+                protected += [k, v]
+        with offload_scope(self.model, cfg, protected):
+            return method(self, *args, **kwargs)
+
+    return wrapper

@@ -1,0 +1,369 @@
+"""Batched TPR execution of a whole forest (the training engine's hot loop).
+
+The per-segment executor runs one segment per model forward; on a B200 that
+leaves the tensor cores idle (a 512-token segment is a thin GEMM) and pays
+the prefix twice (graph-free push + recomputing pop).  This engine keeps the
+same relay semantics but schedules *levels of the forest*:
+
+1. **Push, top-down** -- the internal segments of every tree at depth ``d`` run
+   as packed varlen forwards of up to ``token_budget`` tokens.  Each chunk's
+   post-RoPE K / raw V become per-layer *anchor* leaves (one
+   ``[T_chunk, Hkv, D]`` tensor per layer, detached, ``requires_grad``).
+   In ``retain`` mode (default) the chunk keeps its autograd graph and its
+   owned loss; in ``recompute`` mode (the reference's memory profile) it runs
+   without grad and is recomputed at pop time.
+2. **Leaves** -- all leaf segments, siblings adjacent, run in packed chunks
+   that attend to their parents through ``(offset, length)`` spans into the
+   anchor bank (no per-sibling copies); loss + backward immediately.  The
+   attention backward reduces the prefix dK/dV of all siblings into the
+   anchor ``.grad`` inside the kernel.
+3. **Pop, bottom-up** -- each internal chunk back-propagates
+   ``[loss, K, V (, GDN states)]`` with ``[1, anchor.grad ...]``; its own prefix
+   gradients land in its ancestors' anchors.
+
+Internal segments therefore cost one forward and one backward (retain) instead
+of two forwards and one backward, and every GEMM sees thousands of rows.
+
+Parity: the event semantics of verl/models/mcore/tpr/segment_executor.py:208-444
+(Push/Pop/VisitLeaf, relay of dKV and GDN dState) applied level-wise;
+batching and graph retention are this framework's own design.
+"""
+
+from __future__ import annotations
+
+from collections import defaultdict
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+from torch import Tensor, nn
+
+from .context import SegmentBatchLayout, TPRAttentionContext, use_tpr_attention_context
+from .prefix_state import GDNLayerState
+from .segment_executor import model_device
+from .tree_plan_builder import ForestExecutionPlan
+
+
+@dataclass(eq=False)
+class _Node:
+    tree: int
+    seg_id: int
+    tokens: Tensor
+    start: int
+    depth: int
+    parent: "_Node | None"
+    children: list = field(default_factory=list)
+    # refs owned by this node (host arrays)
+    ref_rows: Tensor | None = None
+    ref_targets: Tensor | None = None
+    ref_samples: Tensor | None = None
+    ref_flat: Tensor | None = None
+    # placement after push
+    chunk: "_Chunk | None" = None
+    row0: int = 0
+    batch_index: int = 0
+
+    @property
+    def length(self) -> int:
+        return int(self.tokens.numel())
+
+    @property
+    def n_refs(self) -> int:
+        return 0 if self.ref_rows is None else int(self.ref_rows.numel())
+
+
+@dataclass(eq=False)
+class _Chunk:
+    nodes: list
+    kv_anchor: dict = field(default_factory=dict)     # layer -> (A_K, A_V) leaves
+    kv_graph: dict = field(default_factory=dict)      # layer -> (K, V) graph tensors (retain)
+    gdn_anchor: dict = field(default_factory=dict)    # layer -> (A_conv, A_rec)
+    gdn_graph: dict = field(default_factory=dict)
+    loss: Tensor | None = None
+    metrics: list = field(default_factory=list)
+
+
+@dataclass
+class ForestRunResult:
+    normalized_loss: Tensor
+    tree_count: int
+    segment_count: int
+    logical_loss_tokens: int
+    forward_tokens: int
+    backward_tokens: int
+    chunks: int
+    stats: Tensor | None
+    metrics: dict
+
+
+def _chunked(items: list, budget: int) -> list[list]:
+    out, cur, n = [], [], 0
+    for it in items:
+        if cur and n + it.length > budget:
+            out.append(cur)
+            cur, n = [], 0
+        cur.append(it)
+        n += it.length
+    if cur:
+        out.append(cur)
+    return out
+
+
+class ForestExecutor:
+    """Runs a :class:`ForestExecutionPlan` (PPO objective) level-wise in packed chunks."""
+
+    def __init__(self, model: nn.Module, objective, *, mode: str = "retain", token_budget: int = 8192,
+                 loss_scale: float = 1.0) -> None:
+        if mode not in ("retain", "recompute"):
+            raise ValueError(f"mode must be 'retain' or 'recompute', got {mode!r}")
+        self.model, self.objective, self.mode = model, objective, mode
+        self.token_budget = int(token_budget)
+        self.loss_scale = loss_scale
+        self.attn_layers = tuple(getattr(model, "attention_layer_numbers", ()))
+        self.gdn_layers = tuple(getattr(model, "gdn_layer_numbers", ()))
+        self.device = model_device(model)
+
+    # ------------------------------------------------------------------ planning
+    def _nodes(self, forest: ForestExecutionPlan) -> list[_Node]:
+        nodes: list[_Node] = []
+        for t, tree in enumerate(forest.trees):
+            plan = tree.segment_plan
+            by_id: dict[int, _Node] = {}
+            order = [plan.root_id]
+            i = 0
+            while i < len(order):
+                sid = order[i]
+                spec = plan.get(sid)
+                parent = by_id.get(spec.parent_id) if spec.parent_id is not None else None
+                node = _Node(t, sid, spec.token_ids, spec.position_start, 0 if parent is None else parent.depth + 1,
+                             parent)
+                if parent is not None:
+                    parent.children.append(node)
+                by_id[sid] = node
+                nodes.append(node)
+                order.extend(plan.child_ids(sid))
+                i += 1
+            refs: dict[int, list] = defaultdict(list)
+            for r in tree.objective_refs:
+                refs[r.segment_id].append(r)
+            for sid, lst in refs.items():
+                tab = self.objective.ref_table(lst)
+                n = by_id[sid]
+                n.ref_rows, n.ref_targets, n.ref_samples, n.ref_flat = (tab.query_offsets, tab.targets,
+                                                                        tab.sample_rows, tab.flat_index)
+        return nodes
+
+    # ------------------------------------------------------------------ one packed forward
+    def _prefix_bank(self, nodes: list[_Node]):
+        """Per-layer prefix bank + spans for ``nodes`` (each attends to its full ancestor path)."""
+        spans: list[tuple[int, int]] = []
+        parents = [n.parent for n in nodes]
+        if all(p is None for p in parents):
+            return {}, [(0, 0)] * len(nodes), None
+        # Fast path: every node's ancestor path is exactly one anchored chunk range (depth-1 nodes whose
+        # parents are roots) and all parents live in the same pushed chunk -> the bank IS that chunk's anchors.
+        chunks = {id(p.chunk): p.chunk for p in parents if p is not None}
+        simple = all(p is None or p.parent is None for p in parents) and len(chunks) == 1
+        if simple:
+            (ch,) = chunks.values()
+            for p in parents:
+                spans.append((0, 0) if p is None else (p.row0, p.length))
+            return {layer: ch.kv_anchor[layer] for layer in self.attn_layers}, spans, ch
+        # General path: concatenate each distinct ancestor path once.
+        paths: dict[int, tuple[int, int]] = {}
+        pieces: list[tuple[_Chunk, int, int]] = []
+        off = 0
+        for p in parents:
+            if p is None:
+                spans.append((0, 0))
+                continue
+            key = id(p)
+            if key not in paths:
+                chain = []
+                a = p
+                while a is not None:
+                    chain.append(a)
+                    a = a.parent
+                chain.reverse()
+                begin = off
+                for a in chain:
+                    pieces.append((a.chunk, a.row0, a.length))
+                    off += a.length
+                paths[key] = (begin, off - begin)
+            spans.append(paths[key])
+        bank = {}
+        for layer in self.attn_layers:
+            ks = [c.kv_anchor[layer][0][r:r + n] for c, r, n in pieces]
+            vs = [c.kv_anchor[layer][1][r:r + n] for c, r, n in pieces]
+            bank[layer] = (torch.cat(ks), torch.cat(vs))
+        return bank, spans, None
+
+    def _gdn_init(self, nodes: list[_Node]):
+        if not self.gdn_layers:
+            return {}
+        if all(n.parent is None for n in nodes):
+            return {}
+        out = {}
+        for layer in self.gdn_layers:
+            convs, recs = [], []
+            for n in nodes:
+                p = n.parent
+                if p is None:
+                    c0, r0 = None, None
+                    ref = next(x.parent for x in nodes if x.parent is not None)
+                    ac, ar = ref.chunk.gdn_anchor[layer]
+                    convs.append(torch.zeros_like(ac[:1]))
+                    recs.append(torch.zeros_like(ar[:1]))
+                else:
+                    ac, ar = p.chunk.gdn_anchor[layer]
+                    convs.append(ac[p.batch_index:p.batch_index + 1])
+                    recs.append(ar[p.batch_index:p.batch_index + 1])
+            out[layer] = GDNLayerState(torch.cat(convs), torch.cat(recs))
+        return out
+
+    def _forward(self, nodes: list[_Node], *, grad: bool, record: bool):
+        dev = self.device
+        seq_lens = [n.length for n in nodes]
+        ids = torch.cat([n.tokens for n in nodes])
+        pos = torch.cat([torch.arange(n.start, n.start + n.length) for n in nodes])
+        host = torch.stack([ids, pos])
+        if dev.type == "cuda":
+            host = host.pin_memory()
+        dev_ip = host.to(dev, non_blocking=True)
+        bank, spans, _ = self._prefix_bank(nodes)
+        layout = SegmentBatchLayout.build(seq_lens, spans, device=dev)
+        ctx = TPRAttentionContext(prefix_length=0, suffix_length=sum(seq_lens), past_key_values=bank,
+                                  layout=layout, initial_gdn_states=self._gdn_init(nodes),
+                                  capture_gdn_final_state=record, record_new_kv=record)
+        max_pos = max(n.start + n.length for n in nodes)
+        with (torch.enable_grad() if grad else torch.no_grad()), use_tpr_attention_context(ctx):
+            hidden = self.model(dev_ip[0], dev_ip[1], max_pos)
+        return ctx, hidden
+
+    def _loss(self, nodes: list[_Node], hidden: Tensor):
+        rows, tg, sm, fl = [], [], [], []
+        base = 0
+        for n in nodes:
+            if n.n_refs:
+                rows.append(n.ref_rows + base)
+                tg.append(n.ref_targets)
+                sm.append(n.ref_samples)
+                fl.append(n.ref_flat)
+            base += n.length
+        if not rows:
+            return None, None
+        loss, metrics = self.objective.rows_loss(self.model, hidden, torch.cat(rows), torch.cat(tg), torch.cat(sm),
+                                                 torch.cat(fl))
+        return loss, metrics
+
+    # ------------------------------------------------------------------ phases
+    def _push_chunk(self, nodes: list[_Node], stats: dict) -> _Chunk:
+        ch = _Chunk(nodes)
+        grad = self.mode == "retain"
+        ctx, hidden = self._forward(nodes, grad=grad, record=True)
+        stats["fwd"] += sum(n.length for n in nodes)
+        row = 0
+        for b, n in enumerate(nodes):
+            n.chunk, n.row0, n.batch_index = ch, row, b
+            row += n.length
+        for layer, (k, v) in ctx.new_key_values.items():
+            ch.kv_anchor[layer] = (k.detach().requires_grad_(True), v.detach().requires_grad_(True))
+            if grad:
+                ch.kv_graph[layer] = (k, v)
+        for layer, st in ctx.new_gdn_states.items():
+            ch.gdn_anchor[layer] = (st.conv_state.detach().requires_grad_(True),
+                                    st.recurrent_state.detach().requires_grad_(True))
+            if grad:
+                ch.gdn_graph[layer] = (st.conv_state, st.recurrent_state)
+        if grad:
+            loss, metrics = self._loss(nodes, hidden)
+            ch.loss = loss
+            if metrics is not None:
+                ch.metrics.append(metrics)
+        return ch
+
+    def _visit_leaves(self, nodes: list[_Node], stats: dict, acc: dict) -> None:
+        ctx, hidden = self._forward(nodes, grad=True, record=False)
+        stats["fwd"] += sum(n.length for n in nodes)
+        stats["bwd"] += sum(n.length for n in nodes)
+        loss, metrics = self._loss(nodes, hidden)
+        if loss is None:
+            loss = hidden.float().sum() * 0.0
+        else:
+            acc["metrics"].append(metrics)
+        acc["loss"] = loss.detach() if acc["loss"] is None else acc["loss"] + loss.detach()
+        (loss * self.loss_scale).backward()
+
+    def _pop_chunk(self, ch: _Chunk, stats: dict, acc: dict) -> None:
+        if self.mode == "recompute":
+            # Re-run the chunk with grad over the (still anchored) ancestors, then relay.
+            ctx, hidden = self._forward(ch.nodes, grad=True, record=True)
+            stats["fwd"] += sum(n.length for n in ch.nodes)
+            kv_graph = dict(ctx.new_key_values)
+            gdn_graph = {k: (s.conv_state, s.recurrent_state) for k, s in ctx.new_gdn_states.items()}
+            loss, metrics = self._loss(ch.nodes, hidden)
+            if metrics is not None:
+                ch.metrics.append(metrics)
+        else:
+            kv_graph, gdn_graph, loss = ch.kv_graph, ch.gdn_graph, ch.loss
+        roots, grads = [], []
+        if loss is not None:
+            roots.append(loss * self.loss_scale)
+            grads.append(None)
+            acc["loss"] = loss.detach() if acc["loss"] is None else acc["loss"] + loss.detach()
+        acc["metrics"].extend(ch.metrics)
+        for layer, (k, v) in kv_graph.items():
+            ak, av = ch.kv_anchor[layer]
+            if ak.grad is not None:
+                roots += [k, v]
+                grads += [ak.grad, av.grad]
+        for layer, (c, r) in gdn_graph.items():
+            ac, ar = ch.gdn_anchor[layer]
+            if ac.grad is not None or ar.grad is not None:
+                roots += [c, r]
+                grads += [ac.grad if ac.grad is not None else torch.zeros_like(ac),
+                          ar.grad if ar.grad is not None else torch.zeros_like(ar)]
+        if roots:
+            torch.autograd.backward(roots, grad_tensors=grads)
+        stats["bwd"] += sum(n.length for n in ch.nodes)
+        ch.kv_anchor.clear()
+        ch.kv_graph.clear()
+        ch.gdn_anchor.clear()
+        ch.gdn_graph.clear()
+        ch.loss = None
+
+    # ------------------------------------------------------------------ entry
+    def run(self, forest: ForestExecutionPlan) -> ForestRunResult:
+        nodes = self._nodes(forest)
+        internal: dict[int, list[_Node]] = defaultdict(list)
+        leaves: list[_Node] = []
+        for n in nodes:
+            (internal[n.depth] if n.children else leaves).append(n)
+        stats = {"fwd": 0, "bwd": 0, "chunks": 0}
+        acc: dict[str, Any] = {"loss": None, "metrics": []}
+        pushed: dict[int, list[_Chunk]] = {}
+        for d in sorted(internal):
+            pushed[d] = []
+            # Keep siblings of one parent adjacent so their children batch together later.
+            for grp in _chunked(internal[d], self.token_budget):
+                pushed[d].append(self._push_chunk(grp, stats))
+                stats["chunks"] += 1
+        # Leaves ordered by (parent chunk, parent row) so a chunk's spans hit few parents.
+        leaves.sort(key=lambda n: (n.depth == 0, id(n.parent.chunk) if n.parent else 0,
+                                   n.parent.row0 if n.parent else 0))
+        for grp in _chunked(leaves, self.token_budget):
+            self._visit_leaves(grp, stats, acc)
+            stats["chunks"] += 1
+        for d in sorted(pushed, reverse=True):
+            for ch in reversed(pushed[d]):
+                self._pop_chunk(ch, stats, acc)
+        loss = acc["loss"] if acc["loss"] is not None else torch.zeros((), device=self.device)
+        stat_rows = [m["stats"] * m["n"] for m in acc["metrics"] if m is not None]
+        total_n = sum(m["n"] for m in acc["metrics"] if m is not None)
+        stats_t = (torch.stack(stat_rows).sum(0) / max(total_n, 1)) if stat_rows else None
+        metrics = {"entropy_sum": sum((m["entropy_sum"] for m in acc["metrics"] if m and "entropy_sum" in m),
+                                      torch.zeros((), device=self.device))} if self.objective.calculate_entropy else {}
+        if self.objective.capture_log_probs:
+            metrics["log_probs"] = [m.get("log_probs") for m in acc["metrics"]]
+        return ForestRunResult(loss, len(forest.trees), forest.segment_count, forest.logical_loss_tokens,
+                               stats["fwd"], stats["bwd"], stats["chunks"], stats_t, metrics)
