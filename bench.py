@@ -1,0 +1,261 @@
+#!/usr/bin/env python
+"""PPO actor-update throughput with tree-prefix reuse on B200.
+
+Config (BASELINE config #2 shape): Qwen3-4B (36 layers, hidden 2560, 32q/8kv heads of 128,
+FFN 9728, vocab 151936, qk-RMSNorm, RoPE 1e6), bf16 weights with FP32 master weights and Adam
+state; every tree is a 512-token prompt with 8 sibling responses of 512 tokens; ids uniform from a
+seed, advantages ~ N(0,1), response mask all ones; random-init weights (no checkpoint access).
+Weak scaling: ``--trees-per-gpu`` trees per GPU (8 -> 64 trees on 8 GPUs, the named config).
+
+One step = plan the token-trie forest, forward + backward of every segment (prefix KV relayed),
+PPO loss over all supervised tokens, DP gradient finalisation, fused AdamW update.
+
+``value``: device time of K steps (CUDA events on the launching stream, barrier + synchronize on
+both sides, max over ranks), with planned inputs already staged.  ``e2e``: the same K steps through
+the public API (``TPREngine.train_step`` on a pinned-host batch: planning, H2D of the inputs, D2H
+of the loss each step), wall clock, max over ranks.
+
+``--impl reference`` runs the reference implementation; it cannot run on this machine (see the
+JSON line it prints).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+PUBLISHED_TPR_TOKENS_PER_S = 2456.0  # 36 933 PPO tokens / 15.035786 s, TPR TP2xCP4 on 8x Ascend 910B
+METRIC = "PPO actor-update tokens/s (whole box, max over ranks) w/ TPR at 1/2/4/8 B200"
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="bridge", choices=["bridge", "reference"])
+    p.add_argument("--model", default="qwen3_4b")
+    p.add_argument("--trees-per-gpu", type=int, default=8)
+    p.add_argument("--prefix", type=int, default=512)
+    p.add_argument("--siblings", type=int, default=8)
+    p.add_argument("--resp", type=int, default=512)
+    p.add_argument("--token-budget", type=int, default=int(os.environ.get("TPR_TOKEN_BUDGET", "8192")))
+    p.add_argument("--mode", default=os.environ.get("TPR_FOREST_MODE", "retain"))
+    p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--cp", type=int, default=1)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+def reference_unavailable(args) -> None:
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({
+            "impl": "reference",
+            "unavailable": "the reference is a verl/Megatron extension with no setup.py/pyproject (pip: 'not "
+                           "installable') whose kernels are Ascend-only (torch_npu, MindSpeed, MindSpeed-Ops); none "
+                           "of them exists on this CUDA image",
+            "metric": METRIC, "n_gpus": args.gpus,
+        }), flush=True)
+
+
+def synthetic_batch(args, rank: int, dp: int, vocab: int, device_pin: bool) -> dict:
+    g = torch.Generator().manual_seed(args.seed * 1000003 + rank)
+    ids, masks, old, adv, uids = [], [], [], [], []
+    for t in range(args.trees_per_gpu):
+        prompt = torch.randint(0, vocab, (args.prefix,), generator=g)
+        for s in range(args.siblings):
+            resp = torch.randint(0, vocab, (args.resp,), generator=g)
+            ids.append(torch.cat([prompt, resp]))
+            masks.append(torch.ones(args.resp, dtype=torch.bool))
+            adv.append(torch.randn(args.resp, generator=g))
+            old.append(torch.full((args.resp,), -11.93) - torch.rand(args.resp, generator=g) * 0.01)
+            uids.append(f"r{rank}t{t}")
+    if device_pin and torch.cuda.is_available():
+        ids = [x.pin_memory() for x in ids]
+        masks = [x.pin_memory() for x in masks]
+        old = [x.pin_memory() for x in old]
+        adv = [x.pin_memory() for x in adv]
+    per_rank = args.trees_per_gpu * args.siblings * args.resp
+    return {"input_ids": ids, "response_mask": masks, "old_log_probs": old, "advantages": adv, "uid": uids,
+            "temperature": 1.0, "batch_num_tokens": per_rank * dp, "dp_size": dp}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: str | None) -> None:
+        self.proc = None
+        self.lines: list[str] = []
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if gpus:
+            cmd[1:1] = ["-i", gpus]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        clocks, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                clocks.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(clocks) if clocks else None,
+                "sm_max_mhz": max(maxes) if maxes else None, "reasons": sorted(reasons), "samples": len(clocks)}
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        reference_unavailable(args)
+        return
+    from bridge_b200.engine import EngineConfig, TPREngine
+    from bridge_b200.engine.api import execute_prepared_tpr_batch, prepare_tpr_batch
+    from bridge_b200.engine.optim import AdamWConfig
+    from bridge_b200.models import get_config
+    from bridge_b200.ops._ext import ext
+    from bridge_b200.parallel.groups import collective_probe, init_distributed
+
+    rank, world = init_distributed(timeout_s=900)
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if world > 1:
+        collective_probe(device=dev)
+    cfg = get_config(args.model)
+    ec = EngineConfig(tensor_model_parallel_size=args.tp, context_parallel_size=args.cp,
+                      token_budget=args.token_budget, forest_mode=args.mode,
+                      tpr_cp_backend="ring" if args.cp > 1 else None)
+    eng = TPREngine(cfg, ec, AdamWConfig(lr=1e-6), device=dev, seed=args.seed)
+    dp = eng.parallel.dp
+    batch = synthetic_batch(args, eng.parallel.dp_rank, dp, cfg.vocab_size, device_pin=True)
+    prepared = prepare_tpr_batch(eng, batch)
+    ppo_tokens_global = args.trees_per_gpu * args.siblings * args.resp * dp
+    m = ext()
+
+    def device_step():
+        out = execute_prepared_tpr_batch(eng, prepared, sync_loss=False)
+        eng.optimizer_step()
+        return out
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES")) if rank == 0 else None
+    launches0 = m.launch_count()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        out = device_step()
+    end.record()
+    torch.cuda.synchronize()
+    launches = m.launch_count() - launches0
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    loss = float(out["loss"][0].item()) if isinstance(out["loss"][0], torch.Tensor) else out["loss"][0]
+
+    e2e = None
+    if not args.no_e2e:
+        h2d = sum(x.numel() * x.element_size() for k in ("input_ids", "response_mask", "old_log_probs", "advantages")
+                  for x in batch[k])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            r = eng.train_step(batch)      # public API: plan + H2D + F/B + finalize + AdamW + D2H(loss)
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) / args.steps
+        w = torch.tensor([wall], device=dev)
+        if world > 1:
+            dist.all_reduce(w, op=dist.ReduceOp.MAX)
+        wall = float(w.item())
+        e2e = {"value": ppo_tokens_global / wall, "unit": "tokens/s", "ms_per_step": wall * 1e3,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4 * (1 + len(r["metrics"])),
+               "timing": "wall clock around K public-API train_step calls, max over ranks"}
+
+    if rank == 0:
+        value = ppo_tokens_global / (ms / 1e3)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": value / PUBLISHED_TPR_TOKENS_PER_S,
+            "dtype": "bf16",
+            "data": "synthetic (uniform token ids from seed, advantages N(0,1), random-init weights)",
+            "config": {
+                "model": args.model, "global_batch": args.trees_per_gpu * args.siblings * dp, "seq_len":
+                args.prefix + args.resp, "parallelism": f"dp{dp}" + (f"tp{args.tp}" if args.tp > 1 else "") +
+                (f"cp{args.cp}" if args.cp > 1 else ""),
+                "trees": args.trees_per_gpu * dp, "prefix": args.prefix, "siblings": args.siblings,
+                "response": args.resp, "ppo_tokens_per_step": ppo_tokens_global, "forest_mode": args.mode,
+                "token_budget": args.token_budget,
+                "l2": "no flush: every step streams 8 GB of bf16 weights and GB-scale activations (>> 126 MB L2)",
+            },
+            "clocks": clocks,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "loss": loss,
+            "impl": "bridge_b200",
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

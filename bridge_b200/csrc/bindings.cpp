@@ -1,0 +1,50 @@
+// Python bindings of the bridge_b200 sm_100a kernels (module bridge_b200._C).
+#include <torch/extension.h>
+
+int64_t bb_launch_count();
+
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
+std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd);
+std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor qw, torch::Tensor kw,
+                                            torch::Tensor cosb, torch::Tensor sinb, double eps);
+std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
+                                            torch::Tensor qw, torch::Tensor kw, torch::Tensor cosb,
+                                            torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk);
+torch::Tensor swiglu_fwd(torch::Tensor gu);
+torch::Tensor swiglu_bwd(torch::Tensor dy, torch::Tensor gu);
+void logprob_stats(torch::Tensor logits, torch::Tensor targets, torch::Tensor inv_temp, int64_t vocab_start,
+                   torch::Tensor stats);
+std::vector<torch::Tensor> logprob_finalize(torch::Tensor stats);
+void logprob_grad_inplace(torch::Tensor logits, torch::Tensor targets, torch::Tensor inv_temp, torch::Tensor lse,
+                          torch::Tensor ezn, torch::Tensor dlp, c10::optional<torch::Tensor> dent,
+                          int64_t vocab_start);
+std::vector<torch::Tensor> ppo_loss_fwd(torch::Tensor x, torch::Tensor old, torch::Tensor adv,
+                                        c10::optional<torch::Tensor> w, double denom, double lo, double hi, double c);
+void adamw_step(torch::Tensor master, torch::Tensor param, torch::Tensor grad, torch::Tensor m, torch::Tensor v,
+                torch::Tensor clip, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2);
+std::vector<torch::Tensor> tree_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor pk,
+                                         torch::Tensor pv, torch::Tensor cu, torch::Tensor poff, torch::Tensor plen,
+                                         int64_t max_seqlen, int64_t max_prefix, double scale);
+std::vector<torch::Tensor> tree_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                         torch::Tensor pk, torch::Tensor pv, torch::Tensor o, torch::Tensor lse,
+                                         torch::Tensor cu, torch::Tensor poff, torch::Tensor plen, int64_t max_seqlen,
+                                         int64_t max_prefix, double scale, torch::Tensor users_meta, int64_t nspans);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "bridge_b200 sm_100a kernels";
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("logprob_stats", &logprob_stats);
+  m.def("logprob_finalize", &logprob_finalize);
+  m.def("logprob_grad_inplace", &logprob_grad_inplace);
+  m.def("ppo_loss_fwd", &ppo_loss_fwd);
+  m.def("adamw_step", &adamw_step);
+  m.def("tree_attn_fwd", &tree_attn_fwd);
+  m.def("tree_attn_bwd", &tree_attn_bwd);
+  m.def("launch_count", &bb_launch_count,
+        "kernels launched by this extension so far");
+}

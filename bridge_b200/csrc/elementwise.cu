@@ -1,0 +1,779 @@
+// Memory-bound hot ops for sm_100a: RMSNorm, fused per-head qk-RMSNorm + RoPE, SwiGLU,
+// vocab log-prob statistics / in-place logit gradient, PPO clip loss, fused AdamW.
+//
+// Every kernel reads its inputs once with 16-byte vector accesses and keeps all reductions in
+// FP32.  Shapes are validated on the host; the kernels assume contiguous row-major tensors.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "common.cuh"
+
+using bb::bf16x8;
+
+namespace {
+
+// ----------------------------------------------------------------------------------------- RMSNorm
+// One warp per row; H % 8 == 0.
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd, int rows, int H,
+                                   float eps) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
+    const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + (size_t)row * H);
+    float ss = 0.f;
+    for (int i = lane; i < H / 8; i += 32) {
+      float f[8];
+      bb::unpack8(xr[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+    }
+    ss = bb::warp_sum(ss);
+    const float r = rsqrtf(ss / H + eps);
+    if (lane == 0) rstd[row] = r;
+    bf16x8* yr = reinterpret_cast<bf16x8*>(y + (size_t)row * H);
+    const bf16x8* wr = reinterpret_cast<const bf16x8*>(w);
+    for (int i = lane; i < H / 8; i += 32) {
+      float f[8], g[8];
+      bb::unpack8(xr[i], f);
+      bb::unpack8(wr[i], g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
+      yr[i] = bb::pack8(f);
+    }
+  }
+}
+
+// dx = r * (dy*w - xhat * mean(dy*w*xhat)); dw partials per block -> [gridDim.x, H] (FP32).
+template <int MAXV>
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int rows, int H) {
+  extern __shared__ float sdw[];  // [H]
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
+  __syncthreads();
+  const int nv = H / 8;
+  float acc[MAXV][8];
+#pragma unroll
+  for (int a = 0; a < MAXV; ++a)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[a][j] = 0.f;
+  const bf16x8* wr = reinterpret_cast<const bf16x8*>(w);
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
+    const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + (size_t)row * H);
+    const bf16x8* gr = reinterpret_cast<const bf16x8*>(dy + (size_t)row * H);
+    const float r = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int a = 0; a < MAXV; ++a) {
+      int i = lane + a * 32;
+      if (i < nv) {
+        float f[8], g[8], ww[8];
+        bb::unpack8(xr[i], f);
+        bb::unpack8(gr[i], g);
+        bb::unpack8(wr[i], ww);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float xh = f[j] * r;
+          dot += g[j] * ww[j] * xh;
+          acc[a][j] += g[j] * xh;
+        }
+      }
+    }
+    dot = bb::warp_sum(dot) / H;
+    bf16x8* dxr = reinterpret_cast<bf16x8*>(dx + (size_t)row * H);
+#pragma unroll
+    for (int a = 0; a < MAXV; ++a) {
+      int i = lane + a * 32;
+      if (i < nv) {
+        float f[8], g[8], ww[8], o[8];
+        bb::unpack8(xr[i], f);
+        bb::unpack8(gr[i], g);
+        bb::unpack8(wr[i], ww);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = r * (g[j] * ww[j] - f[j] * r * dot);
+        dxr[i] = bb::pack8(o);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < MAXV; ++a) {
+    int i = lane + a * 32;
+    if (i < nv)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(&sdw[i * 8 + j], acc[a][j]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < H; i += blockDim.x) dw_part[(size_t)blockIdx.x * H + i] = sdw[i];
+}
+
+__global__ void column_sum_kernel(const float* __restrict__ part, float* __restrict__ out, int nrows, int H) {
+  int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  float s = 0.f;
+  for (int r = 0; r < nrows; ++r) s += part[(size_t)r * H + c];
+  out[c] = s;
+}
+
+// ------------------------------------------------------------------------------- qk-RMSNorm + RoPE
+// One warp per (token, head); D == 128 (4 elems / lane). Rotate-half partner of lane l is lane l^16.
+template <int D>
+__device__ __forceinline__ void norm_rope_row(const __nv_bfloat16* __restrict__ in, const float* __restrict__ w,
+                                              __nv_bfloat16* __restrict__ out, float* __restrict__ rstd_out,
+                                              const float* __restrict__ cs, const float* __restrict__ sn, float eps,
+                                              int lane) {
+  constexpr int E = D / 32;
+  float f[E];
+  const __nv_bfloat16* p = in + lane * E;
+#pragma unroll
+  for (int j = 0; j < E; ++j) f[j] = __bfloat162float(p[j]);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < E; ++j) ss += f[j] * f[j];
+  ss = bb::warp_sum(ss);
+  const float r = rsqrtf(ss / D + eps);
+  if (lane == 0) *rstd_out = r;
+#pragma unroll
+  for (int j = 0; j < E; ++j) f[j] = f[j] * r * w[lane * E + j];
+  // rotate half: first half lanes (0..15) hold x1, partner lanes hold x2 at the same offset.
+  const bool lo = lane < 16;
+  const int fi = (lane & 15) * E;  // frequency index of element 0
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    float other = __shfl_xor_sync(0xffffffffu, f[j], 16);
+    float c = cs[fi + j], s = sn[fi + j];
+    float v = lo ? (f[j] * c - other * s) : (f[j] * c + other * s);
+    out[lane * E + j] = __float2bfloat16(v);
+  }
+}
+
+template <int D>
+__global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                                        const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
+                                        const float* __restrict__ cosb, const float* __restrict__ sinb,
+                                        __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko,
+                                        float* __restrict__ rq, float* __restrict__ rk, int T, int Hq, int Hk,
+                                        float eps) {
+  __shared__ float swq[D], swk[D];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    swq[i] = __bfloat162float(qw[i]);
+    swk[i] = __bfloat162float(kw[i]);
+  }
+  __syncthreads();
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const long total = (long)T * (Hq + Hk);
+  for (long item = (long)blockIdx.x * warps + (threadIdx.x >> 5); item < total; item += (long)gridDim.x * warps) {
+    const int t = (int)(item / (Hq + Hk));
+    const int h = (int)(item % (Hq + Hk));
+    const float* cs = cosb + (size_t)t * (D / 2);
+    const float* sn = sinb + (size_t)t * (D / 2);
+    if (h < Hq) {
+      size_t off = ((size_t)t * Hq + h) * D;
+      norm_rope_row<D>(q + off, swq, qo + off, rq + (size_t)t * Hq + h, cs, sn, eps, lane);
+    } else {
+      int hh = h - Hq;
+      size_t off = ((size_t)t * Hk + hh) * D;
+      norm_rope_row<D>(k + off, swk, ko + off, rk + (size_t)t * Hk + hh, cs, sn, eps, lane);
+    }
+  }
+}
+
+// Backward of y = rope(rmsnorm(x) * w): un-rotate dy, then RMSNorm backward; dw accumulated per block.
+template <int D>
+__device__ __forceinline__ void norm_rope_row_bwd(const __nv_bfloat16* __restrict__ dyp,
+                                                  const __nv_bfloat16* __restrict__ xp, const float* __restrict__ w,
+                                                  float r, const float* __restrict__ cs, const float* __restrict__ sn,
+                                                  __nv_bfloat16* __restrict__ dxp, float* dwacc, int lane) {
+  constexpr int E = D / 32;
+  const bool lo = lane < 16;
+  const int fi = (lane & 15) * E;
+  float g[E], x[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    float d = __bfloat162float(dyp[lane * E + j]);
+    float other = __shfl_xor_sync(0xffffffffu, d, 16);
+    float c = cs[fi + j], s = sn[fi + j];
+    // forward: lo: y = a c - b s ; hi: y = b c + a s  (a = x1, b = x2)
+    g[j] = lo ? (d * c + other * s) : (d * c - other * s);
+    x[j] = __bfloat162float(xp[lane * E + j]);
+  }
+  float dot = 0.f;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    float xh = x[j] * r;
+    dot += g[j] * w[lane * E + j] * xh;
+    dwacc[j] += g[j] * xh;
+  }
+  dot = bb::warp_sum(dot) / D;
+#pragma unroll
+  for (int j = 0; j < E; ++j) dxp[lane * E + j] = __float2bfloat16(r * (g[j] * w[lane * E + j] - x[j] * r * dot));
+}
+
+template <int D>
+__global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, const __nv_bfloat16* __restrict__ dko,
+                                        const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                                        const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
+                                        const float* __restrict__ cosb, const float* __restrict__ sinb,
+                                        const float* __restrict__ rq, const float* __restrict__ rk,
+                                        __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk,
+                                        float* __restrict__ dqw, float* __restrict__ dkw, int T, int Hq, int Hk) {
+  constexpr int E = D / 32;
+  __shared__ float swq[D], swk[D], sdq[D], sdk[D];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    swq[i] = __bfloat162float(qw[i]);
+    swk[i] = __bfloat162float(kw[i]);
+    sdq[i] = 0.f;
+    sdk[i] = 0.f;
+  }
+  __syncthreads();
+  float aq[E], ak[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) aq[j] = ak[j] = 0.f;
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const long total = (long)T * (Hq + Hk);
+  for (long item = (long)blockIdx.x * warps + (threadIdx.x >> 5); item < total; item += (long)gridDim.x * warps) {
+    const int t = (int)(item / (Hq + Hk));
+    const int h = (int)(item % (Hq + Hk));
+    const float* cs = cosb + (size_t)t * (D / 2);
+    const float* sn = sinb + (size_t)t * (D / 2);
+    if (h < Hq) {
+      size_t off = ((size_t)t * Hq + h) * D;
+      norm_rope_row_bwd<D>(dqo + off, q + off, swq, rq[(size_t)t * Hq + h], cs, sn, dq + off, aq, lane);
+    } else {
+      int hh = h - Hq;
+      size_t off = ((size_t)t * Hk + hh) * D;
+      norm_rope_row_bwd<D>(dko + off, k + off, swk, rk[(size_t)t * Hk + hh], cs, sn, dk + off, ak, lane);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    atomicAdd(&sdq[lane * E + j], aq[j]);
+    atomicAdd(&sdk[lane * E + j], ak[j]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    atomicAdd(&dqw[i], sdq[i]);
+    atomicAdd(&dkw[i], sdk[i]);
+  }
+}
+
+// ----------------------------------------------------------------------------------------- SwiGLU
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ y, long rows,
+                                  int F) {
+  const int nv = F / 8;
+  const long total = rows * nv;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    long r = i / nv;
+    int c = (int)(i % nv);
+    const bf16x8* g = reinterpret_cast<const bf16x8*>(gu + (size_t)r * 2 * F) + c;
+    const bf16x8* u = reinterpret_cast<const bf16x8*>(gu + (size_t)r * 2 * F + F) + c;
+    float a[8], b[8];
+    bb::unpack8(*g, a);
+    bb::unpack8(*u, b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = bb::silu(a[j]) * b[j];
+    reinterpret_cast<bf16x8*>(y + (size_t)r * F)[c] = bb::pack8(a);
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ gu,
+                                  __nv_bfloat16* __restrict__ dgu, long rows, int F) {
+  const int nv = F / 8;
+  const long total = rows * nv;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    long r = i / nv;
+    int c = (int)(i % nv);
+    float a[8], b[8], d[8], da[8], db[8];
+    bb::unpack8(reinterpret_cast<const bf16x8*>(gu + (size_t)r * 2 * F)[c], a);
+    bb::unpack8(reinterpret_cast<const bf16x8*>(gu + (size_t)r * 2 * F + F)[c], b);
+    bb::unpack8(reinterpret_cast<const bf16x8*>(dy + (size_t)r * F)[c], d);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float s = bb::sigmoidf_(a[j]);
+      float sl = a[j] * s;
+      db[j] = d[j] * sl;
+      da[j] = d[j] * b[j] * s * (1.f + a[j] * (1.f - s));
+    }
+    reinterpret_cast<bf16x8*>(dgu + (size_t)r * 2 * F)[c] = bb::pack8(da);
+    reinterpret_cast<bf16x8*>(dgu + (size_t)r * 2 * F + F)[c] = bb::pack8(db);
+  }
+}
+
+// -------------------------------------------------------------------------------- log-prob over vocab
+// One block per row: online (max, sum exp, sum exp*z) of z = logit * inv_temp; target logit if local.
+__global__ void logprob_stats_kernel(const __nv_bfloat16* __restrict__ logits, const int64_t* __restrict__ targets,
+                                     const float* __restrict__ inv_temp, float* __restrict__ stats, int V,
+                                     long vocab_start) {
+  const int row = blockIdx.x;
+  const float it = inv_temp[row];
+  const __nv_bfloat16* lr = logits + (size_t)row * V;
+  float m = -INFINITY, s = 0.f, ez = 0.f;
+  auto push = [&](float z) {
+    if (z > m) {
+      float c = __expf(m - z);
+      s *= c;
+      ez *= c;
+      m = z;
+    }
+    float e = __expf(z - m);
+    s += e;
+    ez += e * z;
+  };
+  if ((V & 7) == 0) {
+    const bf16x8* v8 = reinterpret_cast<const bf16x8*>(lr);
+    for (int i = threadIdx.x; i < V / 8; i += blockDim.x) {
+      float f[8];
+      bb::unpack8(v8[i], f);
+      float bm = f[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) bm = fmaxf(bm, f[j]);
+      bm *= it;
+      if (bm > m) {
+        float c = __expf(m - bm);
+        s *= c;
+        ez *= c;
+        m = bm;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float z = f[j] * it;
+        float e = __expf(z - m);
+        s += e;
+        ez += e * z;
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) push(__bfloat162float(lr[i]) * it);
+  }
+  // combine across the block
+  __shared__ float sm[32], ss[32], se[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    float e2 = __shfl_xor_sync(0xffffffffu, ez, o);
+    float mm = fmaxf(m, m2);
+    float a = (m == -INFINITY) ? 0.f : __expf(m - mm), b = (m2 == -INFINITY) ? 0.f : __expf(m2 - mm);
+    s = s * a + s2 * b;
+    ez = ez * a + e2 * b;
+    m = mm;
+  }
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+    se[warp] = ez;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? sm[lane] : -INFINITY;
+    s = lane < nw ? ss[lane] : 0.f;
+    ez = lane < nw ? se[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      float e2 = __shfl_xor_sync(0xffffffffu, ez, o);
+      float mm = fmaxf(m, m2);
+      float a = (m == -INFINITY) ? 0.f : __expf(m - mm), b = (m2 == -INFINITY) ? 0.f : __expf(m2 - mm);
+      s = s * a + s2 * b;
+      ez = ez * a + e2 * b;
+      m = mm;
+    }
+    if (lane == 0) {
+      long t = targets[row] - vocab_start;
+      float tz = (t >= 0 && t < V) ? __bfloat162float(lr[t]) * it : 0.f;
+      stats[row * 4 + 0] = m;
+      stats[row * 4 + 1] = s;
+      stats[row * 4 + 2] = tz;
+      stats[row * 4 + 3] = ez;
+    }
+  }
+}
+
+__global__ void logprob_finalize_kernel(const float* __restrict__ stats, float* __restrict__ lse,
+                                        float* __restrict__ lp, float* __restrict__ ent, float* __restrict__ ezn,
+                                        int U) {
+  int u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= U) return;
+  float m = stats[u * 4], s = stats[u * 4 + 1], tz = stats[u * 4 + 2], ez = stats[u * 4 + 3];
+  float l = m + __logf(s);
+  lse[u] = l;
+  lp[u] = tz - l;
+  ezn[u] = ez / s;
+  ent[u] = l - ez / s;
+}
+
+// In place: logits[u, v] <- d loss / d logits = it * (dlp*(1[v==t] - p) - dent*p*(z - Ez)),  p = exp(z - lse).
+__global__ void logprob_grad_kernel(__nv_bfloat16* __restrict__ logits, const int64_t* __restrict__ targets,
+                                    const float* __restrict__ inv_temp, const float* __restrict__ lse,
+                                    const float* __restrict__ ezn, const float* __restrict__ dlp,
+                                    const float* __restrict__ dent, int V, long vocab_start) {
+  const int row = blockIdx.x;
+  const float it = inv_temp[row], l = lse[row], g = dlp[row];
+  const float de = dent ? dent[row] : 0.f, e = ezn[row];
+  const long t = targets[row] - vocab_start;
+  __nv_bfloat16* lr = logits + (size_t)row * V;
+  if ((V & 7) == 0) {
+    bf16x8* v8 = reinterpret_cast<bf16x8*>(lr);
+    for (int i = threadIdx.x; i < V / 8; i += blockDim.x) {
+      float f[8];
+      bb::unpack8(v8[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float z = f[j] * it;
+        float p = __expf(z - l);
+        float d = -g * p - de * p * (z - e);
+        if ((long)(i * 8 + j) == t) d += g;
+        f[j] = d * it;
+      }
+      v8[i] = bb::pack8(f);
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      float z = __bfloat162float(lr[i]) * it;
+      float p = __expf(z - l);
+      float d = -g * p - de * p * (z - e);
+      if ((long)i == t) d += g;
+      lr[i] = __float2bfloat16(d * it);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------------------- PPO loss
+__global__ void ppo_loss_kernel(const float* __restrict__ x, const float* __restrict__ old,
+                                const float* __restrict__ adv, const float* __restrict__ wts, float* __restrict__ out,
+                                float* __restrict__ grad, float* __restrict__ stats, long n, float inv_denom,
+                                float lo, float hi, float cdual) {
+  __shared__ float scratch[32];
+  float ls = 0.f, cf = 0.f, dcf = 0.f, kl = 0.f, rs = 0.f;
+  for (long i = threadIdx.x; i < n; i += blockDim.x) {
+    const float a = adv[i];
+    const float d = x[i] - old[i];
+    const float dc = fminf(fmaxf(d, -20.f), 20.f);
+    const float r = __expf(dc);
+    const float dr = (d > -20.f && d < 20.f) ? r : 0.f;  // d r / d x
+    const float l1 = -a * r;
+    const float rc = fminf(fmaxf(r, 1.f - lo), 1.f + hi);
+    const float l2 = -a * rc;
+    const float d1 = -a * dr;
+    const float d2 = (r >= 1.f - lo && r <= 1.f + hi) ? -a * dr : 0.f;
+    float prim = l1, dprim = d1;
+    if (l2 > l1) {
+      prim = l2;
+      dprim = d2;
+    }
+    float loss = prim, dl = dprim;
+    const float dual = -a * cdual;
+    if (a < 0.f && prim > dual) {
+      loss = dual;
+      dl = 0.f;
+    }
+    const float w = wts ? wts[i] : 1.f;
+    ls += loss * w;
+    grad[i] = dl * w * inv_denom;
+    cf += (l2 > l1) ? 1.f : 0.f;
+    dcf += (a < 0.f && prim > dual) ? 1.f : 0.f;
+    kl += -d;
+    rs += r;
+  }
+  ls = bb::block_sum(ls, scratch);
+  cf = bb::block_sum(cf, scratch);
+  dcf = bb::block_sum(dcf, scratch);
+  kl = bb::block_sum(kl, scratch);
+  rs = bb::block_sum(rs, scratch);
+  if (threadIdx.x == 0) {
+    out[0] = ls * inv_denom;
+    const float inv_n = 1.f / (float)(n > 0 ? n : 1);
+    stats[0] = cf * inv_n;
+    stats[1] = dcf * inv_n;
+    stats[2] = kl * inv_n;
+    stats[3] = rs * inv_n;
+  }
+}
+
+// ----------------------------------------------------------------------------------------- AdamW
+template <typename P>
+__global__ void adamw_kernel(float* __restrict__ master, P* __restrict__ param, const float* __restrict__ grad,
+                             float* __restrict__ m, float* __restrict__ v, const float* __restrict__ clip, long n,
+                             float lr, float b1, float b2, float eps, float wd, float bc1, float bc2) {
+  const float c = clip[0];
+  const float inv_bc1 = 1.f / bc1, inv_sqrt_bc2 = rsqrtf(bc2);
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    float g = grad[i] * c;
+    float mi = b1 * m[i] + (1.f - b1) * g;
+    float vi = b2 * v[i] + (1.f - b2) * g * g;
+    m[i] = mi;
+    v[i] = vi;
+    float w = master[i];
+    w = w * (1.f - lr * wd) - lr * (mi * inv_bc1) / (sqrtf(vi) * inv_sqrt_bc2 + eps);
+    master[i] = w;
+    if constexpr (std::is_same<P, float>::value) {
+      param[i] = w;
+    } else {
+      param[i] = __float2bfloat16(w);
+    }
+  }
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+void check_bf16(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), name,
+              " must be a contiguous CUDA bf16 tensor");
+}
+
+}  // namespace
+
+// ============================================================================================ host
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "weight");
+  const int H = x.size(-1);
+  TORCH_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm: hidden must be a multiple of 8 and match weight");
+  const long rows = x.numel() / H;
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({rows}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {y, rstd};
+  const int threads = 256;
+  int blocks = (int)std::min<long>((rows + 7) / 8, (long)sm_count() * 8);
+  rmsnorm_fwd_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
+      rstd.data_ptr<float>(), rows, H, (float)eps);
+  BB_POST_LAUNCH();
+  return {y, rstd};
+}
+
+std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd) {
+  check_bf16(dy, "dy");
+  check_bf16(x, "x");
+  const int H = x.size(-1);
+  const long rows = x.numel() / H;
+  auto dx = torch::empty_like(x);
+  auto dw = torch::zeros({H}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {dx, dw};
+  const int threads = 256;
+  int blocks = (int)std::min<long>((rows + 7) / 8, (long)sm_count() * 2);
+  auto part = torch::empty({blocks, H}, x.options().dtype(at::kFloat));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int nv = H / 8;
+  size_t smem = H * sizeof(float);
+#define BB_RMS_BWD(MV)                                                                                        \
+  rmsnorm_bwd_kernel<MV><<<blocks, threads, smem, stream>>>(                                                  \
+      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), \
+      rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), rows, H)
+  if (nv <= 32) {
+    BB_RMS_BWD(1);
+  } else if (nv <= 64) {
+    BB_RMS_BWD(2);
+  } else if (nv <= 128) {
+    BB_RMS_BWD(4);
+  } else if (nv <= 256) {
+    BB_RMS_BWD(8);
+  } else {
+    TORCH_CHECK(nv <= 512, "rmsnorm_bwd: hidden size too large");
+    BB_RMS_BWD(16);
+  }
+#undef BB_RMS_BWD
+  BB_POST_LAUNCH();
+  column_sum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(part.data_ptr<float>(), dw.data_ptr<float>(), blocks, H);
+  BB_POST_LAUNCH();
+  return {dx, dw};
+}
+
+std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor qw, torch::Tensor kw,
+                                            torch::Tensor cosb, torch::Tensor sinb, double eps) {
+  check_bf16(q, "q");
+  check_bf16(k, "k");
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && q.size(2) == k.size(2) && q.size(0) == k.size(0), "qk shapes");
+  const int T = q.size(0), Hq = q.size(1), Hk = k.size(1), D = q.size(2);
+  TORCH_CHECK(cosb.size(0) == T && cosb.size(1) == D / 2 && cosb.scalar_type() == at::kFloat && cosb.is_contiguous(),
+              "cos table must be [T, D/2] fp32");
+  auto qo = torch::empty_like(q), ko = torch::empty_like(k);
+  auto rq = torch::empty({T, Hq}, q.options().dtype(at::kFloat));
+  auto rk = torch::empty({T, Hk}, q.options().dtype(at::kFloat));
+  if (T == 0) return {qo, ko, rq, rk};
+  const int threads = 256;
+  long items = (long)T * (Hq + Hk);
+  int blocks = (int)std::min<long>((items + 7) / 8, (long)sm_count() * 8);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto qwb = qw.contiguous(), kwb = kw.contiguous();
+#define BB_QKF(DD)                                                                                               \
+  qk_norm_rope_fwd_kernel<DD><<<blocks, threads, 0, stream>>>(                                                   \
+      (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)qwb.data_ptr(), \
+      (const __nv_bfloat16*)kwb.data_ptr(), cosb.data_ptr<float>(), sinb.data_ptr<float>(),                      \
+      (__nv_bfloat16*)qo.data_ptr(), (__nv_bfloat16*)ko.data_ptr(), rq.data_ptr<float>(), rk.data_ptr<float>(), T, \
+      Hq, Hk, (float)eps)
+  if (D == 128) {
+    BB_QKF(128);
+  } else if (D == 64) {
+    BB_QKF(64);
+  } else if (D == 256) {
+    BB_QKF(256);
+  } else {
+    TORCH_CHECK(false, "qk_norm_rope: head_dim must be 64, 128 or 256");
+  }
+#undef BB_QKF
+  BB_POST_LAUNCH();
+  return {qo, ko, rq, rk};
+}
+
+std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
+                                            torch::Tensor qw, torch::Tensor kw, torch::Tensor cosb,
+                                            torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk) {
+  check_bf16(dqo, "dq");
+  check_bf16(dko, "dk");
+  const int T = q.size(0), Hq = q.size(1), Hk = k.size(1), D = q.size(2);
+  auto dq = torch::empty_like(q), dk = torch::empty_like(k);
+  auto dqw = torch::zeros({D}, q.options().dtype(at::kFloat));
+  auto dkw = torch::zeros({D}, q.options().dtype(at::kFloat));
+  if (T == 0) return {dq, dk, dqw, dkw};
+  const int threads = 256;
+  long items = (long)T * (Hq + Hk);
+  int blocks = (int)std::min<long>((items + 7) / 8, (long)sm_count() * 4);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto qwb = qw.contiguous(), kwb = kw.contiguous();
+#define BB_QKB(DD)                                                                                               \
+  qk_norm_rope_bwd_kernel<DD><<<blocks, threads, 0, stream>>>(                                                   \
+      (const __nv_bfloat16*)dqo.data_ptr(), (const __nv_bfloat16*)dko.data_ptr(), (const __nv_bfloat16*)q.data_ptr(), \
+      (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)qwb.data_ptr(), (const __nv_bfloat16*)kwb.data_ptr(), \
+      cosb.data_ptr<float>(), sinb.data_ptr<float>(), rq.data_ptr<float>(), rk.data_ptr<float>(),                \
+      (__nv_bfloat16*)dq.data_ptr(), (__nv_bfloat16*)dk.data_ptr(), dqw.data_ptr<float>(), dkw.data_ptr<float>(), T, \
+      Hq, Hk)
+  if (D == 128) {
+    BB_QKB(128);
+  } else if (D == 64) {
+    BB_QKB(64);
+  } else if (D == 256) {
+    BB_QKB(256);
+  } else {
+    TORCH_CHECK(false, "qk_norm_rope: head_dim must be 64, 128 or 256");
+  }
+#undef BB_QKB
+  BB_POST_LAUNCH();
+  return {dq, dk, dqw, dkw};
+}
+
+torch::Tensor swiglu_fwd(torch::Tensor gu) {
+  check_bf16(gu, "gate_up");
+  const int F2 = gu.size(-1);
+  TORCH_CHECK(F2 % 16 == 0, "swiglu: 2F must be a multiple of 16");
+  const int F = F2 / 2;
+  const long rows = gu.numel() / F2;
+  auto sizes = gu.sizes().vec();
+  sizes.back() = F;
+  auto y = torch::empty(sizes, gu.options());
+  if (rows == 0) return y;
+  long total = rows * (F / 8);
+  int blocks = (int)std::min<long>((total + 255) / 256, (long)sm_count() * 16);
+  swiglu_fwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)y.data_ptr(), rows, F);
+  BB_POST_LAUNCH();
+  return y;
+}
+
+torch::Tensor swiglu_bwd(torch::Tensor dy, torch::Tensor gu) {
+  check_bf16(dy, "dy");
+  check_bf16(gu, "gate_up");
+  const int F2 = gu.size(-1), F = F2 / 2;
+  const long rows = gu.numel() / F2;
+  auto dgu = torch::empty_like(gu);
+  if (rows == 0) return dgu;
+  long total = rows * (F / 8);
+  int blocks = (int)std::min<long>((total + 255) / 256, (long)sm_count() * 16);
+  swiglu_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)dgu.data_ptr(), rows,
+      F);
+  BB_POST_LAUNCH();
+  return dgu;
+}
+
+void logprob_stats(torch::Tensor logits, torch::Tensor targets, torch::Tensor inv_temp, int64_t vocab_start,
+                   torch::Tensor stats) {
+  check_bf16(logits, "logits");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && inv_temp.scalar_type() == at::kFloat, "targets/inv_temp dtype");
+  const int U = logits.size(0), V = logits.size(1);
+  if (U == 0) return;
+  TORCH_CHECK(stats.is_contiguous() && stats.size(0) == U && stats.size(1) == 4, "stats must be [U, 4]");
+  logprob_stats_kernel<<<U, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)logits.data_ptr(), targets.data_ptr<int64_t>(), inv_temp.data_ptr<float>(),
+      stats.data_ptr<float>(), V, (long)vocab_start);
+  BB_POST_LAUNCH();
+}
+
+std::vector<torch::Tensor> logprob_finalize(torch::Tensor stats) {
+  const int U = stats.size(0);
+  auto o = stats.options();
+  auto lse = torch::empty({U}, o), lp = torch::empty({U}, o), ent = torch::empty({U}, o), ez = torch::empty({U}, o);
+  if (U) {
+    logprob_finalize_kernel<<<(U + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        stats.data_ptr<float>(), lse.data_ptr<float>(), lp.data_ptr<float>(), ent.data_ptr<float>(),
+        ez.data_ptr<float>(), U);
+    BB_POST_LAUNCH();
+  }
+  return {lse, lp, ent, ez};
+}
+
+void logprob_grad_inplace(torch::Tensor logits, torch::Tensor targets, torch::Tensor inv_temp, torch::Tensor lse,
+                          torch::Tensor ezn, torch::Tensor dlp, c10::optional<torch::Tensor> dent,
+                          int64_t vocab_start) {
+  check_bf16(logits, "logits");
+  const int U = logits.size(0), V = logits.size(1);
+  if (U == 0) return;
+  const float* dptr = dent.has_value() ? dent->data_ptr<float>() : nullptr;
+  logprob_grad_kernel<<<U, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (__nv_bfloat16*)logits.data_ptr(), targets.data_ptr<int64_t>(), inv_temp.data_ptr<float>(),
+      lse.data_ptr<float>(), ezn.data_ptr<float>(), dlp.data_ptr<float>(), dptr, V, (long)vocab_start);
+  BB_POST_LAUNCH();
+}
+
+std::vector<torch::Tensor> ppo_loss_fwd(torch::Tensor x, torch::Tensor old, torch::Tensor adv,
+                                        c10::optional<torch::Tensor> w, double denom, double lo, double hi,
+                                        double c) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous(), "ppo: x must be fp32 contiguous");
+  const long n = x.numel();
+  auto out = torch::empty({}, x.options());
+  auto grad = torch::empty_like(x);
+  auto stats = torch::empty({4}, x.options());
+  ppo_loss_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      x.data_ptr<float>(), old.data_ptr<float>(), adv.data_ptr<float>(),
+      w.has_value() ? w->data_ptr<float>() : nullptr, out.data_ptr<float>(), grad.data_ptr<float>(),
+      stats.data_ptr<float>(), n, (float)(1.0 / denom), (float)lo, (float)hi, (float)c);
+  BB_POST_LAUNCH();
+  return {out, grad, stats};
+}
+
+void adamw_step(torch::Tensor master, torch::Tensor param, torch::Tensor grad, torch::Tensor m, torch::Tensor v,
+                torch::Tensor clip, double lr, double b1, double b2, double eps, double wd, double bc1,
+                double bc2) {
+  const long n = master.numel();
+  if (!n) return;
+  auto clipf = clip.to(at::kFloat).contiguous();
+  int blocks = (int)std::min<long>((n + 255) / 256, (long)sm_count() * 16);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (param.scalar_type() == at::kBFloat16) {
+    adamw_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+        master.data_ptr<float>(), (__nv_bfloat16*)param.data_ptr(), grad.data_ptr<float>(), m.data_ptr<float>(),
+        v.data_ptr<float>(), clipf.data_ptr<float>(), n, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
+        (float)bc1, (float)bc2);
+  } else {
+    adamw_kernel<float><<<blocks, 256, 0, stream>>>(
+        master.data_ptr<float>(), param.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(),
+        v.data_ptr<float>(), clipf.data_ptr<float>(), n, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
+        (float)bc1, (float)bc2);
+  }
+  BB_POST_LAUNCH();
+}
+
+int64_t bb_launch_count() { return (int64_t)bb::launch_counter().load(); }

@@ -142,42 +142,56 @@ def run_tpr_forward_backward(engine, request: TPRForwardBackwardRequest) -> dict
 
 
 # --------------------------------------------------------------------------- PPO entry
-def run_tpr_forward_backward_batch(engine, data: Any, loss_function: Any = None, *, forward_only: bool = False,
-                                   sync_loss: bool = True) -> dict:
-    """PPO mini-batch -> TPR forest schedule -> one gradient finalisation."""
-    if forward_only:
-        raise NotImplementedError("the TPR PPO schedule is training-only; use compute_tree_log_probs for scoring")
+@dataclass
+class PreparedTPRBatch:
+    """Host-side product of planning one PPO mini-batch (reusable across identical steps)."""
+
+    data: Any
+    forest: Any
+    objective: SegmentPPOObjectiveAdapter
+    logical_input_tokens: int
+    stage_ms: dict
+
+
+def prepare_tpr_batch(engine, data: Any, loss_function: Any = None) -> PreparedTPRBatch:
+    """Validate the mini-batch, build the token-trie forest and the PPO ref tables (host work)."""
     ec = engine.engine_config
     if not ec.tpr_enabled:
         raise RuntimeError("TPR PPO requires engine_config.tpr_enabled=True at model creation")
-    model = engine.model
-    if not model.training:
-        raise RuntimeError("TPR PPO requires model.train()")
     ps = engine.parallel
     validate_tpr_parallel_sizes({"TP": ps.tp, "CP": ps.cp, "DP": ps.dp, "EP": ps.ep, "PP": 1}, ppo=True)
     token_count = batch_meta(data, "batch_num_tokens", None)
     dp_size = batch_meta(data, "dp_size", None)
     if token_count is None or int(token_count) <= 0 or int(dp_size or 0) != ps.dp:
         raise ValueError(f"engine must attach positive GLOBAL batch_num_tokens and the actual dp_size={ps.dp}")
-    prof = ec.exec_profile
     t0 = time.perf_counter()
-    stage: dict[str, float] = {}
     keys = trajectory_keys_from_minibatch(data)
     forest = build_tree_execution_plans(keys, data, tree_policy=ec.tree_policy,
                                         turn_min_segment_tokens=ec.turn_min_segment_tokens)
     if not forest.trees or not forest.logical_loss_tokens:
         raise ValueError("TPR PPO mini-batch has no supervised response tokens")
-    if prof:
-        stage["tree_build_cpu_ms"] = (time.perf_counter() - t0) * 1e3
+    stage = {"tree_build_cpu_ms": (time.perf_counter() - t0) * 1e3}
     if ps.tp > 1:
         from ..tpr.tp_validation import assert_tp_plan_agreement, digest_forest_plan
 
         assert_tp_plan_agreement(digest_forest_plan(forest), tp_size=ps.tp, group=ps.tp_group)
-    from ..parallel.engine_runtime import aggregate_cp_loss, resolve_engine_cp_runtime
-
-    rt = resolve_engine_cp_runtime(engine)
     objective = SegmentPPOObjectiveAdapter(data, loss_function, dp_group=ps.dp_group,
                                            log_prob_chunk_size=ec.log_prob_chunk_tokens or None)
+    logical_inputs = sum(int(r.numel()) for r in _rows(data, "input_ids"))
+    return PreparedTPRBatch(data, forest, objective, logical_inputs, stage)
+
+
+def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss: bool = True) -> dict:
+    """Run the forest schedule of a prepared mini-batch and finalise gradients once."""
+    from ..parallel.engine_runtime import aggregate_cp_loss, resolve_engine_cp_runtime
+
+    ec = engine.engine_config
+    model = engine.model
+    if not model.training:
+        raise RuntimeError("TPR PPO requires model.train()")
+    forest, objective = prepared.forest, prepared.objective
+    objective._device_flat = None  # re-stage the per-ref PPO inputs (one H2D copy per step)
+    rt = resolve_engine_cp_runtime(engine)
     t_run = time.perf_counter()
     metrics: dict[str, Any] = {}
     if rt.group is None and ec.executor == "forest":
@@ -186,8 +200,7 @@ def run_tpr_forward_backward_batch(engine, data: Any, loss_function: Any = None,
         if sync_loss and not bool(torch.isfinite(res.normalized_loss).item()):
             raise FloatingPointError("non-finite TPR PPO loss; gradients will not be finalized")
         engine.finalize_model_grads()
-        total_loss = res.normalized_loss
-        stats = res.stats
+        total_loss, stats = res.normalized_loss, res.stats
         metrics["tpr/forward_tokens"] = [res.forward_tokens]
         metrics["tpr/backward_tokens"] = [res.backward_tokens]
         metrics["tpr/chunks"] = [res.chunks]
@@ -202,40 +215,46 @@ def run_tpr_forward_backward_batch(engine, data: Any, loss_function: Any = None,
             ex = SegmentExecutor(model, tree_plan.segment_plan, segment_loss_fn=fn, segment_loss_term_counts=counts,
                                  cp_group=rt.group, cp_backend=rt.backend)
             out = FixedTopologyScheduler(tree_plan.segment_plan, ex).run()
-            for _, m in ex.segment_loss_metrics:
-                seg_stats.append(m)
+            if sync_loss and not bool(torch.isfinite(out.normalized_loss).item()):
+                raise FloatingPointError("non-finite TPR PPO tree loss; gradients will not be finalized")
+            seg_stats.extend(m for _, m in ex.segment_loss_metrics)
             return out
 
-        runner = TPRBatchRunner(run_tree=run_tree, finalize_gradients=engine.finalize_model_grads)
-        res = runner.run(forest)
+        res = TPRBatchRunner(run_tree=run_tree, finalize_gradients=engine.finalize_model_grads).run(forest)
         total_loss = res.normalized_loss
         rows = [m["stats"] * m["n"] for m in seg_stats]
         stats = torch.stack(rows).sum(0) / max(sum(m["n"] for m in seg_stats), 1) if rows else None
-    if prof:
-        stage["tree_run_and_finalize_host_ms"] = (time.perf_counter() - t_run) * 1e3
+    stage = dict(prepared.stage_ms)
+    stage["tree_run_and_finalize_host_ms"] = (time.perf_counter() - t_run) * 1e3
     _, global_loss = aggregate_cp_loss(total_loss, total_loss, rt)
-    logical_inputs = sum(int(r.numel()) for r in _rows(data, "input_ids"))
     unique = forest.unique_tokens
     metrics.update({
         "tpr/forest_trees": [len(forest.trees)],
         "tpr/physical_segments": [forest.segment_count],
         "tpr/logical_loss_tokens": [forest.logical_loss_tokens],
-        "tpr/logical_input_tokens": [logical_inputs],
+        "tpr/logical_input_tokens": [prepared.logical_input_tokens],
         "tpr/unique_tree_tokens": [unique],
-        "tpr/topology_token_reuse_ratio": [logical_inputs / unique],
+        "tpr/topology_token_reuse_ratio": [prepared.logical_input_tokens / unique],
     })
     if stats is not None:
         names = ("actor/pg_clipfrac", "actor/pg_clipfrac_lower", "actor/ppo_kl", "actor/ratio_mean")
         metrics.update({n: [stats[i]] for i, n in enumerate(names)})
     if sync_loss:
         loss_val: Any = float(global_loss.item())
-        if not torch.isfinite(torch.tensor(loss_val)):
+        if loss_val != loss_val or loss_val in (float("inf"), float("-inf")):
             raise FloatingPointError("non-finite TPR PPO mini-batch loss")
         for k, v in metrics.items():
             metrics[k] = [float(x.item()) if isinstance(x, Tensor) else float(x) for x in v]
     else:
         loss_val = global_loss
-    if prof:
-        stage["whole_entry_host_ms"] = (time.perf_counter() - t0) * 1e3
+    if ec.exec_profile:
         engine._tpr_stage_profile = stage
     return {"model_output": {}, "loss": [loss_val], "metrics": metrics}
+
+
+def run_tpr_forward_backward_batch(engine, data: Any, loss_function: Any = None, *, forward_only: bool = False,
+                                   sync_loss: bool = True) -> dict:
+    """PPO mini-batch -> TPR forest schedule -> one gradient finalisation."""
+    if forward_only:
+        raise NotImplementedError("the TPR PPO schedule is training-only")
+    return execute_prepared_tpr_batch(engine, prepare_tpr_batch(engine, data, loss_function), sync_loss=sync_loss)

@@ -157,9 +157,10 @@ class _TreeAttentionFn(torch.autograd.Function):
         m = kernels()
         q, k, v, pk, pv, o, lse = ctx.saved_tensors
         lay = ctx.layout
+        users, nspans = _prefix_users(lay)
         dq, dk, dv, dpk, dpv = m.tree_attn_bwd(do.contiguous(), q, k, v, pk, pv, o, lse, lay.cu_seqlens,
                                                lay.prefix_offsets, lay.prefix_lengths, lay.max_seqlen,
-                                               lay.max_prefix, float(ctx.scale), _prefix_users(lay))
+                                               lay.max_prefix, float(ctx.scale), users, nspans)
         if not ctx.has_p:
             dpk = dpv = None
         return dq, dk, dv, dpk, dpv, None, None
@@ -183,8 +184,8 @@ def _prefix_users(layout):
         span_len.append(sp[1])
     dev = layout.cu_seqlens.device
     t = torch.tensor(rowptr + users + span_off + span_len + [len(keys)], dtype=torch.int32).to(dev, non_blocking=True)
-    layout.cache["users"] = t
-    return t
+    layout.cache["users"] = (t, len(keys))
+    return t, len(keys)
 
 
 def tree_attention(q: Tensor, k: Tensor, v: Tensor, pk: Tensor | None, pv: Tensor | None, layout,

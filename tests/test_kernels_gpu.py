@@ -1,0 +1,188 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch FP32 reference of the same op."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _close(a, b, atol, rtol, name=""):
+    a, b = a.float(), b.float()
+    err = (a - b).abs().max().item()
+    tol = atol + rtol * b.abs().max().item()
+    assert err <= tol, f"{name}: max err {err:.3e} > {tol:.3e}"
+
+
+def test_extension_loaded():
+    from bridge_b200 import _C
+
+    assert hasattr(_C, "tree_attn_fwd") and hasattr(_C, "launch_count")
+
+
+@pytest.mark.parametrize("rows,H", [(257, 2560), (64, 512), (3, 4096)])
+def test_rmsnorm(rows, H):
+    from bridge_b200.ops.norm import rmsnorm, rmsnorm_reference
+
+    x = torch.randn(rows, H, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16).requires_grad_()
+    y = rmsnorm(x, w, 1e-6)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    yr = rmsnorm_reference(xr, wr, 1e-6)
+    _close(y, yr, 2e-2, 1e-2, "y")
+    g = torch.randn_like(yr)
+    y.backward(g.to(y.dtype))
+    yr.backward(g)
+    _close(x.grad, xr.grad, 3e-2, 2e-2, "dx")
+    _close(w.grad, wr.grad, 1e-1, 2e-2, "dw")
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_qk_norm_rope(D):
+    from bridge_b200.ops.norm import qk_norm_rope, qk_norm_rope_reference, rope_cos_sin
+
+    T, Hq, Hk = 77, 8, 2
+    q = torch.randn(T, Hq, D, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(T, Hk, D, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    qw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16).requires_grad_()
+    kw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16).requires_grad_()
+    cos, sin = rope_cos_sin(torch.arange(1000, 1000 + T, device=DEV), D, 1e6)
+    qo, ko = qk_norm_rope(q, k, qw, kw, cos, sin, 1e-6)
+    ref = [t.detach().float().requires_grad_() for t in (q, k, qw, kw)]
+    qr, kr = qk_norm_rope_reference(ref[0], ref[1], ref[2], ref[3], cos, sin, 1e-6)
+    _close(qo, qr, 2e-2, 1e-2, "q")
+    _close(ko, kr, 2e-2, 1e-2, "k")
+    gq, gk = torch.randn_like(qr), torch.randn_like(kr)
+    torch.autograd.backward([qo, ko], [gq.bfloat16(), gk.bfloat16()])
+    torch.autograd.backward([qr, kr], [gq, gk])
+    for a, b, n in zip((q, k, qw, kw), ref, ("dq", "dk", "dqw", "dkw")):
+        _close(a.grad, b.grad, 5e-2, 2e-2, n)
+
+
+def test_swiglu():
+    from bridge_b200.ops.activation import swiglu, swiglu_reference
+
+    gu = torch.randn(133, 2 * 9728, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    y = swiglu(gu)
+    gr = gu.detach().float().requires_grad_()
+    yr = swiglu_reference(gr)
+    _close(y, yr, 2e-2, 1e-2, "y")
+    g = torch.randn_like(yr)
+    y.backward(g.bfloat16())
+    yr.backward(g)
+    _close(gu.grad, gr.grad, 3e-2, 2e-2, "dgu")
+
+
+@pytest.mark.parametrize("entropy", [False, True])
+def test_fused_lm_head_logprob(entropy):
+    from bridge_b200.ops.logprob import fused_lm_head_logprob, logprob_entropy_reference
+
+    U, H, V = 300, 256, 5000
+    h = (torch.randn(U, H, device=DEV) * 0.5).to(torch.bfloat16).requires_grad_()
+    W = (torch.randn(V, H, device=DEV) * 0.05).to(torch.bfloat16).requires_grad_()
+    tg = torch.randint(0, V, (U,), device=DEV)
+    temp = torch.rand(U, device=DEV) + 0.5
+    lp, ent = fused_lm_head_logprob(h, W, tg, temp, with_entropy=entropy, chunk_rows=128)
+    hr, Wr = h.detach().float().requires_grad_(), W.detach().float().requires_grad_()
+    lpr, entr = logprob_entropy_reference(hr @ Wr.t(), tg, temp, with_entropy=entropy)
+    _close(lp, lpr, 5e-2, 1e-2, "lp")
+    g = torch.randn(U, device=DEV)
+    loss = (lp * g).sum() + ((ent * g).sum() if entropy else 0)
+    lossr = (lpr * g).sum() + ((entr * g).sum() if entropy else 0)
+    if entropy:
+        _close(ent, entr, 5e-2, 1e-2, "entropy")
+    loss.backward()
+    lossr.backward()
+    _close(h.grad, hr.grad, 5e-2, 3e-2, "dh")
+    _close(W.grad, Wr.grad, 5e-2, 3e-2, "dW")
+
+
+def test_ppo_loss():
+    from bridge_b200.ops.ppo import PPOLossConfig, ppo_loss, ppo_loss_reference
+
+    n = 5000
+    x = (torch.randn(n, device=DEV) * 0.3 - 5).requires_grad_()
+    old = x.detach() + torch.randn(n, device=DEV) * 0.3
+    adv = torch.randn(n, device=DEV)
+    w = torch.rand(n, device=DEV)
+    loss, stats = ppo_loss(x, old, adv, denom=1234.0, weights=w)
+    xr = x.detach().clone().requires_grad_()
+    lr, sr = ppo_loss_reference(xr, old, adv, 1234.0, PPOLossConfig(), w)
+    _close(loss, lr, 1e-5, 1e-4, "loss")
+    _close(stats, sr, 1e-5, 1e-4, "stats")
+    loss.backward()
+    lr.backward()
+    _close(x.grad, xr.grad, 1e-6, 1e-4, "dx")
+
+
+def test_adamw_kernel():
+    from bridge_b200.ops._ext import kernels
+
+    n = 10001
+    master = torch.randn(n, device=DEV)
+    param = master.to(torch.bfloat16)
+    grad = torch.randn(n, device=DEV)
+    m = torch.randn(n, device=DEV).abs() * 0.1
+    v = torch.rand(n, device=DEV) * 0.01
+    ref = [t.clone() for t in (master, m, v)]
+    clip = torch.tensor([0.5], device=DEV)
+    kernels().adamw_step(master, param, grad, m, v, clip, 1e-3, 0.9, 0.999, 1e-8, 0.01, 0.19, 0.002)
+    mr, m2, v2 = ref
+    g = grad * 0.5
+    m2 = 0.9 * m2 + 0.1 * g
+    v2 = 0.999 * v2 + 0.001 * g * g
+    mr = mr * (1 - 1e-3 * 0.01) - 1e-3 * (m2 / 0.19) / ((v2 / 0.002).sqrt() + 1e-8)
+    _close(master, mr, 1e-5, 1e-5, "master")
+    _close(param, mr, 1e-2, 1e-2, "param")
+
+
+def _tree_case(D, hq, hkv, lens, spans, P, seed=0):
+    from bridge_b200.tpr.context import SegmentBatchLayout
+
+    torch.manual_seed(seed)
+    T = sum(lens)
+    q = torch.randn(T, hq, D, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(T, hkv, D, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(T, hkv, D, device=DEV, dtype=torch.bfloat16)
+    pk = torch.randn(max(P, 1), hkv, D, device=DEV, dtype=torch.bfloat16)
+    pv = torch.randn(max(P, 1), hkv, D, device=DEV, dtype=torch.bfloat16)
+    lay = SegmentBatchLayout.build(lens, spans, device=DEV)
+    return q, k, v, pk, pv, lay
+
+
+@pytest.mark.parametrize("D,hq,hkv,lens,spans,P", [
+    (128, 8, 2, (512, 512, 300, 1), ((0, 512), (0, 512), (512, 77), (0, 0)), 589),   # siblings share span 0
+    (128, 4, 4, (70,), ((0, 0),), 0),                                                  # plain causal, odd length
+    (64, 4, 2, (129, 64, 200), ((5, 130), (5, 130), (0, 3)), 140),
+    (128, 32, 8, (512,) * 8, ((0, 512),) * 8, 512),                                    # Qwen3-4B-shaped siblings
+])
+def test_tree_attention_fwd_bwd(D, hq, hkv, lens, spans, P):
+    from bridge_b200.ops.attention import tree_attention, tree_attention_reference
+
+    q, k, v, pk, pv, lay = _tree_case(D, hq, hkv, lens, spans, P)
+    scale = 1 / math.sqrt(D)
+    leaves = [t.clone().requires_grad_() for t in (q, k, v, pk, pv)]
+    o = tree_attention(*leaves, lay, softmax_scale=scale)
+    ref = [t.detach().float().requires_grad_() for t in (q, k, v, pk, pv)]
+    orf = tree_attention_reference(ref[0], ref[1], ref[2], ref[3], ref[4], lay, softmax_scale=scale)
+    _close(o, orf, 8e-3, 2e-2, "o")
+    g = torch.randn_like(orf)
+    o.backward(g.bfloat16())
+    orf.backward(g)
+    for a, b, n in zip(leaves, ref, ("dq", "dk", "dv", "dpk", "dpv")):
+        _close(a.grad, b.grad, 1e-2, 3e-2, n)
+
+
+def test_tree_attention_d256_forward():
+    from bridge_b200.ops.attention import tree_attention_reference
+    from bridge_b200.ops._ext import kernels
+
+    q, k, v, pk, pv, lay = _tree_case(256, 4, 2, (100, 130), ((0, 64), (0, 64)), 64)
+    o, lse = kernels().tree_attn_fwd(q, k, v, pk, pv, lay.cu_seqlens, lay.prefix_offsets, lay.prefix_lengths,
+                                     lay.max_seqlen, lay.max_prefix, 1 / 16)
+    orf = tree_attention_reference(q.float(), k.float(), v.float(), pk.float(), pv.float(), lay, softmax_scale=1 / 16)
+    _close(o, orf, 8e-3, 2e-2, "o")

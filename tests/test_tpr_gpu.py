@@ -1,0 +1,54 @@
+"""On the GPU (bf16, sm_100a kernels): TPR log-probs / loss / grads vs the flattened non-TPR batch."""
+
+import pytest
+import torch
+
+from tests.helpers import flat_ppo_loss, set_old_log_probs, tree_batch
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg():
+    from bridge_b200.models import get_config
+
+    return get_config("tiny", hidden_size=512, num_heads=8, num_kv_heads=2, head_dim=128, intermediate_size=1024,
+                      num_layers=3)
+
+
+def _cos(a, b):
+    return float(torch.nn.functional.cosine_similarity(a.flatten().float(), b.flatten().float(), dim=0))
+
+
+@pytest.mark.parametrize("mode", ["retain", "recompute"])
+def test_tpr_vs_flat_bf16(mode):
+    from bridge_b200.engine import EngineConfig, TPREngine
+    from bridge_b200.models.decoder import build_model
+
+    dev = torch.device("cuda")
+    batch = tree_batch(n_trees=2, prefix=200, siblings=4, resp=96, seed=5)
+    ref = build_model(_cfg(), device=dev, seed=0)
+    set_old_log_probs(ref, batch)
+    loss_ref, _ = flat_ppo_loss(ref, batch)
+    loss_ref.backward()
+    eng = TPREngine(_cfg(), EngineConfig(forest_mode=mode, token_budget=1024), device=dev,
+                    model=build_model(_cfg(), device=dev, seed=0))
+    out = eng.forward_backward_batch(batch)
+    assert abs(out["loss"][0] - float(loss_ref)) <= 2e-3 * abs(float(loss_ref)) + 1e-4
+    gr = {n: p.grad for n, p in ref.named_parameters()}
+    for n, p in eng.model.named_parameters():
+        a, b = p.main_grad.float(), gr[n].float()
+        rel = float((a - b).norm() / (b.norm() + 1e-12))
+        assert rel < 3e-2 and _cos(a, b) > 0.999, (n, rel)
+
+
+def test_bench_cli_small():
+    import json
+    import subprocess
+    import sys
+
+    out = subprocess.run([sys.executable, "bench.py", "--model", "tiny", "--steps", "2", "--warmup", "1",
+                          "--trees-per-gpu", "2", "--prefix", "64", "--siblings", "3", "--resp", "32"],
+                         capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["value"] > 0 and line["gpu_launches"] > 0 and line["n_gpus"] == 1
