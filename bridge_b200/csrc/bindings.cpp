@@ -30,6 +30,10 @@ std::vector<torch::Tensor> tree_attn_bwd(torch::Tensor dout, torch::Tensor q, to
                                          torch::Tensor cu, torch::Tensor poff, torch::Tensor plen, int64_t max_seqlen,
                                          int64_t max_prefix, double scale, torch::Tensor users_meta, int64_t nspans);
 
+torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, c10::optional<torch::Tensor> out,
+                   bool accumulate);
+int64_t gemm_error_code();
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bridge_b200 sm_100a kernels";
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
@@ -45,6 +49,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &adamw_step);
   m.def("tree_attn_fwd", &tree_attn_fwd);
   m.def("tree_attn_bwd", &tree_attn_bwd);
+  m.def("gemm", &gemm, "tcgen05 GEMM: C (+)= op(A) op(B)^T");
+  m.def("gemm_error_code", &gemm_error_code);
   m.def("launch_count", &bb_launch_count,
         "kernels launched by this extension so far");
 }

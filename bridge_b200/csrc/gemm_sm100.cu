@@ -1,0 +1,348 @@
+// Persistent tcgen05 GEMM for sm_100a:  C[M,N] (+)= A[M,K] * B[N,K]^T, bf16 operands, FP32 accumulate.
+//
+// * A and B may each be K-major (row-major [rows, K]) or MN-major (the transposed operand stored
+//   row-major as [K, rows]) -- so a linear layer's forward (x W^T), data gradient (dy W) and
+//   weight gradient (dy^T x) all run without a transpose copy.
+// * Tiles 128 x 256 x 64, 4-stage TMA ring (128-byte swizzle), accumulators double-buffered in
+//   TMEM (2 x 256 columns) so the epilogue of tile i overlaps the main loop of tile i+1.
+// * Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma (one
+//   thread), warps 2-5 drain TMEM (tcgen05.ld) and write C -- bf16 store, or FP32
+//   read-add-write (used to accumulate weight gradients straight into the FP32 main-grad arena).
+// * One CTA per SM, tiles swizzled in groups of 8 M-tiles for L2 reuse.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "sm100_common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;   // 16 KB
+constexpr int B_BYTES = BN * BK * 2;   // 32 KB
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+
+struct SmemLayout {
+  // stage buffers come first (1024-byte aligned by construction)
+  static constexpr int A_OFF = 0;
+  static constexpr int B_OFF = STAGES * A_BYTES;
+  static constexpr int BAR_OFF = B_OFF + STAGES * B_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256;
+};
+
+template <bool A_MN, bool B_MN, bool ACCUM_F32>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, void* C,
+                int M, int N, int K, long ldc, int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // Align the dynamic buffer to 1024 B (128-byte swizzle atoms).
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem + SmemLayout::A_OFF;
+  unsigned char* sB = smem + SmemLayout::B_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int nk = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tfull[a], 1);
+      sm100::mbar_init(&tempty[a], 128);
+    }
+    sm100::fence_mbar_init();
+    sm100::prefetch_tmap(&tmap_a);
+    sm100::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, TMEM_COLS);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto tile_coords = [&](int t, int& m0, int& n0) {
+    // group-of-8 M raster for L2 reuse of B tiles
+    const int group = 8;
+    const int per_group = group * n_tiles;
+    const int g = t / per_group;
+    const int first_m = g * group;
+    const int gm = min(group, m_tiles - first_m);
+    const int r = t % per_group;
+    m0 = (first_m + r % gm) * BM;
+    n0 = (r / gm) * BN;
+  };
+
+  constexpr uint32_t IDESC = sm100::umma_idesc_bf16(BM, BN, A_MN, B_MN);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int m0, n0;
+        tile_coords(t, m0, n0);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait(&empty[stage], phase ^ 1, err, 1)) {
+            ok = false;
+            break;
+          }
+          sm100::mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          unsigned char* a_dst = sA + stage * A_BYTES;
+          unsigned char* b_dst = sB + stage * B_BYTES;
+          if (A_MN) {
+#pragma unroll
+            for (int i = 0; i < BM / 64; ++i)
+              sm100::tma_load_2d(a_dst + i * 8192, &tmap_a, &full[stage], m0 + 64 * i, kb * BK);
+          } else {
+            sm100::tma_load_2d(a_dst, &tmap_a, &full[stage], kb * BK, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i)
+              sm100::tma_load_2d(b_dst + i * 8192, &tmap_b, &full[stage], n0 + 64 * i, kb * BK);
+          } else {
+            sm100::tma_load_2d(b_dst, &tmap_b, &full[stage], kb * BK, n0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!sm100::mbar_wait(&tempty[acc], acc_phase ^ 1, err, 2)) break;
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait(&full[stage], phase, err, 3)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t a_base = sm100::smem_addr(sA + stage * A_BYTES);
+          const uint32_t b_base = sm100::smem_addr(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sm100::umma_desc_sw128(a_base + kk * 2048, 8192, 1024)
+                                     : sm100::umma_desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sm100::umma_desc_sw128(b_base + kk * 2048, 8192, 1024)
+                                     : sm100::umma_desc_sw128(b_base + kk * 32, 16, 1024);
+            sm100::umma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+          }
+          sm100::umma_commit(&empty[stage]);  // stage reusable once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        sm100::umma_commit(&tfull[acc]);      // accumulator complete
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int m0, n0;
+      tile_coords(t, m0, n0);
+      const bool got = sm100::mbar_wait(&tfull[acc], acc_phase, err, 4);
+      if (!__all_sync(0xffffffffu, got)) break;  // keep the warp converged for tcgen05.ld
+      sm100::tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(t_row + c * 32, r);
+        sm100::tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (row < M && col0 < N) {
+          if (ACCUM_F32) {
+            float* dst = reinterpret_cast<float*>(C) + (size_t)row * ldc + col0;
+            if (col0 + 32 <= N) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float4 v = reinterpret_cast<float4*>(dst)[j];
+                v.x += __uint_as_float(r[4 * j]);
+                v.y += __uint_as_float(r[4 * j + 1]);
+                v.z += __uint_as_float(r[4 * j + 2]);
+                v.w += __uint_as_float(r[4 * j + 3]);
+                reinterpret_cast<float4*>(dst)[j] = v;
+              }
+            } else {
+              for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] += __uint_as_float(r[j]);
+            }
+          } else {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
+            if (col0 + 32 <= N) {
+              uint32_t p[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                p[j] = *reinterpret_cast<uint32_t*>(&h);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(dst)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+            } else {
+              for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = __float2bfloat16(__uint_as_float(r[j]));
+            }
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    BB_CHECK_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [rows, cols] (cols contiguous), box {64, box_rows}.
+CUtensorMap make_map(const void* base, long rows, long cols, long ld, int box_rows) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int d;
+    cudaGetDevice(&d);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+  }
+  return n;
+}
+
+torch::Tensor& error_word() {
+  static torch::Tensor e;
+  if (!e.defined()) e = torch::zeros({1}, torch::dtype(torch::kInt).device(torch::kCUDA));
+  return e;
+}
+
+template <bool A_MN, bool B_MN, bool ACC>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, int M, int N, int K, long ldc) {
+  auto kern = gemm_kernel<A_MN, B_MN, ACC>;
+  const int smem = SmemLayout::TOTAL + 1024;
+  static bool attr = false;
+  if (!attr) {
+    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = std::max(1, std::min(tiles, num_sms()));
+  kern<<<grid, NUM_THREADS, smem, at::cuda::getCurrentCUDAStream()>>>(ta, tb, c, M, N, K, ldc,
+                                                                     error_word().data_ptr<int>());
+  BB_POST_LAUNCH();
+}
+
+}  // namespace
+
+// C = op(A) * op(B)^T where op(A) is [M, K] and op(B) is [N, K].
+//   a_mn=false: A given as [M, K] (K contiguous);  a_mn=true: A given as [K, M] (M contiguous).
+//   b_mn=false: B given as [N, K];                 b_mn=true: B given as [K, N].
+// out: bf16 [M, N] written, or fp32 [M, N] accumulated into when `accumulate`.
+torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, c10::optional<torch::Tensor> out,
+                   bool accumulate) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "gemm operands must be CUDA bf16");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm operands: 2-D row-major");
+  const long M = a_mn ? a.size(1) : a.size(0);
+  const long K = a_mn ? a.size(0) : a.size(1);
+  const long N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm: inner dimensions differ");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "gemm: operand row strides must be multiples of 8");
+  torch::Tensor c;
+  if (out.has_value()) {
+    c = *out;
+    TORCH_CHECK(c.size(0) == M && c.size(1) == N && c.stride(1) == 1 && c.stride(0) % 8 == 0, "gemm: bad out shape");
+    TORCH_CHECK(accumulate ? c.scalar_type() == at::kFloat : c.scalar_type() == at::kBFloat16, "gemm: out dtype");
+  } else {
+    TORCH_CHECK(!accumulate, "accumulate needs an out tensor");
+    c = torch::empty({M, N}, a.options());
+  }
+  if (M == 0 || N == 0) return c;
+  if (K == 0) {
+    if (!accumulate) c.zero_();
+    return c;
+  }
+  const CUtensorMap ta = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64) : make_map(a.data_ptr(), M, K, a.stride(0), BM);
+  const CUtensorMap tb = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64) : make_map(b.data_ptr(), N, K, b.stride(0), BN);
+  const long ldc = c.stride(0);
+#define BB_G(AM, BMN, ACC) launch<AM, BMN, ACC>(ta, tb, c.data_ptr(), (int)M, (int)N, (int)K, ldc)
+  if (accumulate) {
+    if (!a_mn && !b_mn) BB_G(false, false, true);
+    else if (!a_mn && b_mn) BB_G(false, true, true);
+    else if (a_mn && !b_mn) BB_G(true, false, true);
+    else BB_G(true, true, true);
+  } else {
+    if (!a_mn && !b_mn) BB_G(false, false, false);
+    else if (!a_mn && b_mn) BB_G(false, true, false);
+    else if (a_mn && !b_mn) BB_G(true, false, false);
+    else BB_G(true, true, false);
+  }
+#undef BB_G
+  return c;
+}
+
+int64_t gemm_error_code() { return error_word().item<int>(); }

@@ -151,6 +151,7 @@ class PreparedTPRBatch:
     objective: SegmentPPOObjectiveAdapter
     logical_input_tokens: int
     stage_ms: dict
+    nodes: Any = None
 
 
 def prepare_tpr_batch(engine, data: Any, loss_function: Any = None) -> PreparedTPRBatch:
@@ -196,7 +197,9 @@ def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss:
     metrics: dict[str, Any] = {}
     if rt.group is None and ec.executor == "forest":
         fx = ForestExecutor(model, objective, mode=ec.forest_mode, token_budget=ec.token_budget)
-        res = fx.run(forest)
+        if prepared.nodes is None:
+            prepared.nodes = fx.plan(forest)
+        res = fx.run(forest, prepared.nodes)
         if sync_loss and not bool(torch.isfinite(res.normalized_loss).item()):
             raise FloatingPointError("non-finite TPR PPO loss; gradients will not be finalized")
         engine.finalize_model_grads()

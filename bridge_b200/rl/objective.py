@@ -23,6 +23,7 @@ from collections.abc import Callable, Sequence
 from dataclasses import dataclass
 from typing import Any
 
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -144,6 +145,7 @@ class SegmentPPOObjectiveAdapter:
         if t.numel() != n or not bool(((t > 0) & torch.isfinite(t)).all()):
             raise ValueError("temperature must be finite and positive per row")
         self.row_offsets = offsets
+        self._row_offsets_np = np.asarray(offsets, dtype=np.int64)
         self.row_temperature = t
         return flat
 
@@ -154,14 +156,12 @@ class SegmentPPOObjectiveAdapter:
 
     def ref_table(self, refs: Sequence[SegmentObjectiveRef]) -> RefTable:
         n = len(refs)
-        a = torch.empty((6, n), dtype=torch.long)
-        for i, r in enumerate(refs):
-            a[0, i] = r.segment_id
-            a[1, i] = r.query_offset
-            a[2, i] = r.target_token_id
-            a[3, i] = r.sample_row
-            a[4, i] = r.response_offset
-            a[5, i] = self.row_offsets[r.sample_row] + r.response_offset
+        # One vectorised conversion (a per-element tensor write is a host op per ref).
+        cols = np.fromiter((x for r in refs for x in (r.segment_id, r.query_offset, r.target_token_id,
+                                                      r.sample_row, r.response_offset)),
+                           dtype=np.int64, count=5 * n).reshape(n, 5).T
+        flat = self._row_offsets_np[cols[3]] + cols[4]
+        a = torch.from_numpy(np.vstack([cols, flat[None]]))
         if n and not bool(self._flat["mask"][a[5]].all()):
             raise ValueError("objective ref points to a masked token")
         return RefTable(a[0], a[1], a[2], a[3], a[4], a[5])

@@ -333,8 +333,13 @@ class ForestExecutor:
         ch.loss = None
 
     # ------------------------------------------------------------------ entry
-    def run(self, forest: ForestExecutionPlan) -> ForestRunResult:
-        nodes = self._nodes(forest)
+    def plan(self, forest: ForestExecutionPlan) -> list[_Node]:
+        """Static node table of a forest (reusable across runs of the same prepared batch)."""
+        return self._nodes(forest)
+
+    def run(self, forest: ForestExecutionPlan, nodes: list[_Node] | None = None) -> ForestRunResult:
+        if nodes is None:
+            nodes = self._nodes(forest)
         internal: dict[int, list[_Node]] = defaultdict(list)
         leaves: list[_Node] = []
         for n in nodes:

@@ -174,6 +174,9 @@ def test_tree_attention_fwd_bwd(D, hq, hkv, lens, spans, P):
     o.backward(g.bfloat16())
     orf.backward(g)
     for a, b, n in zip(leaves, ref, ("dq", "dk", "dv", "dpk", "dpv")):
+        if P == 0 and n in ("dpk", "dpv"):
+            assert a.grad is None
+            continue
         _close(a.grad, b.grad, 1e-2, 3e-2, n)
 
 
