@@ -12,9 +12,21 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <cudaTypedefs.h>
+#include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
 #include "sm100_common.cuh"
+
+static bool gemm_trace() {
+  static int v = -1;
+  if (v < 0) v = getenv("BB_GEMM_TRACE") ? 1 : 0;
+  return v == 1;
+}
+#define GTRACE(msg) \
+  do {              \
+    if (gemm_trace()) { fprintf(stderr, "[gemm] %s\n", msg); fflush(stderr); } \
+  } while (0)
+
 
 namespace {
 
@@ -249,19 +261,33 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D bf16 tensor map over a row-major matrix [rows, cols] (cols contiguous), box {64, box_rows}.
-CUtensorMap make_map(const void* base, long rows, long cols, long ld, int box_rows) {
+// Written in place: CUtensorMap is a 64-byte-aligned type and is never copied through the stack.
+void make_map(CUtensorMap* m, const void* base, long rows, long cols, long ld, int box_rows) {
   TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
-  CUtensorMap m;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(m) & 63) == 0, "tensor map storage must be 64-byte aligned");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
-  return m;
+}
+
+// Per-thread, explicitly aligned storage for the two maps of one launch.
+struct alignas(64) MapPair {
+  CUtensorMap a, b;
+};
+MapPair* map_storage() {
+  thread_local MapPair* p = nullptr;
+  if (!p) {
+    void* raw = nullptr;
+    TORCH_CHECK(posix_memalign(&raw, 64, sizeof(MapPair)) == 0, "posix_memalign failed");
+    p = reinterpret_cast<MapPair*>(raw);
+  }
+  return p;
 }
 
 int num_sms() {
@@ -281,7 +307,7 @@ torch::Tensor& error_word() {
 }
 
 template <bool A_MN, bool B_MN, bool ACC>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, int M, int N, int K, long ldc) {
+void launch(const MapPair* maps, void* c, int M, int N, int K, long ldc) {
   auto kern = gemm_kernel<A_MN, B_MN, ACC>;
   const int smem = SmemLayout::TOTAL + 1024;
   static bool attr = false;
@@ -291,8 +317,14 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, int M, int N,
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, num_sms()));
-  kern<<<grid, NUM_THREADS, smem, at::cuda::getCurrentCUDAStream()>>>(ta, tb, c, M, N, K, ldc,
-                                                                     error_word().data_ptr<int>());
+  GTRACE("launch: attr ok");
+  int* err = error_word().data_ptr<int>();
+  GTRACE("launch: err word");
+  // Arguments are passed by address: the runtime copies each by its declared size.
+  void* args[] = {const_cast<CUtensorMap*>(&maps->a), const_cast<CUtensorMap*>(&maps->b), &c, &M, &N, &K, &ldc, &err};
+  BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NUM_THREADS), args, smem,
+                                 at::cuda::getCurrentCUDAStream()));
+  GTRACE("launched");
   BB_POST_LAUNCH();
 }
 
@@ -304,6 +336,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, int M, int N,
 // out: bf16 [M, N] written, or fp32 [M, N] accumulated into when `accumulate`.
 torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, c10::optional<torch::Tensor> out,
                    bool accumulate) {
+  GTRACE("enter");
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
               "gemm operands must be CUDA bf16");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm operands: 2-D row-major");
@@ -326,10 +359,23 @@ torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, c10::
     if (!accumulate) c.zero_();
     return c;
   }
-  const CUtensorMap ta = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64) : make_map(a.data_ptr(), M, K, a.stride(0), BM);
-  const CUtensorMap tb = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64) : make_map(b.data_ptr(), N, K, b.stride(0), BN);
+  GTRACE("out ready");
+  // The tensor-map encoder needs a current context in the calling thread; autograd worker threads
+  // and fresh Python threads may not have made any runtime call yet.
+  at::cuda::CUDAGuard device_guard(a.get_device());
+  {
+    CUcontext cur = nullptr;
+    if (cuCtxGetCurrent(&cur) != CUDA_SUCCESS || cur == nullptr) BB_CHECK_CUDA(cudaFree(nullptr));
+  }
+  MapPair* maps = map_storage();
+  GTRACE("storage");
+  if (a_mn) make_map(&maps->a, a.data_ptr(), K, M, a.stride(0), 64);
+  else make_map(&maps->a, a.data_ptr(), M, K, a.stride(0), BM);
+  if (b_mn) make_map(&maps->b, b.data_ptr(), K, N, b.stride(0), 64);
+  else make_map(&maps->b, b.data_ptr(), N, K, b.stride(0), BN);
+  GTRACE("maps encoded");
   const long ldc = c.stride(0);
-#define BB_G(AM, BMN, ACC) launch<AM, BMN, ACC>(ta, tb, c.data_ptr(), (int)M, (int)N, (int)K, ldc)
+#define BB_G(AM, BMN, ACC) launch<AM, BMN, ACC>(maps, c.data_ptr(), (int)M, (int)N, (int)K, ldc)
   if (accumulate) {
     if (!a_mn && !b_mn) BB_G(false, false, true);
     else if (!a_mn && b_mn) BB_G(false, true, true);
