@@ -34,6 +34,12 @@ torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, c10::
                    bool accumulate);
 int64_t gemm_error_code();
 
+std::vector<torch::Tensor> tree_attn_fwd_sm100(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor pk,
+                                               torch::Tensor pv, torch::Tensor cu, torch::Tensor poff,
+                                               torch::Tensor plen, int64_t max_seqlen, int64_t max_prefix,
+                                               double scale);
+int64_t attn_error_code();
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bridge_b200 sm_100a kernels";
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
@@ -49,6 +55,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &adamw_step);
   m.def("tree_attn_fwd", &tree_attn_fwd);
   m.def("tree_attn_bwd", &tree_attn_bwd);
+  m.def("tree_attn_fwd_sm100", &tree_attn_fwd_sm100, "tcgen05 tree attention forward (head_dim 128)");
+  m.def("attn_error_code", &attn_error_code);
   m.def("gemm", &gemm, "tcgen05 GEMM: C (+)= op(A) op(B)^T");
   m.def("gemm_error_code", &gemm_error_code);
   m.def("launch_count", &bb_launch_count,

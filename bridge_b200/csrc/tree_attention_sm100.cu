@@ -1,0 +1,385 @@
+// tcgen05 / TMEM flash-attention forward for the tree (prefix-reuse) layout, head_dim 128.
+//
+// One CTA = 128 query rows of one sequence x one q head.  Key tiles of 128: first the sequence's
+// prefix span in the bank (full visibility), then its own keys up to the tile's last query (causal).
+//
+//   warp 0      TMA producer: Q once (2 boxes), then K/V tiles into a 2-stage ring
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer:
+//                 S_j = Q K_j^T  -> TMEM S[j%2]     (issued before PV_{j-1}, so it overlaps softmax_{j-1})
+//                 O  += P_j V_j  -> TMEM O          (A = P from swizzled smem, B = V MN-major)
+//   warps 2-5   softmax (one thread per query row): tcgen05.ld S, mask, online softmax in the exp2
+//               domain with a lazily updated reference max (O is rescaled in TMEM only when the row max
+//               grows by more than 2^8), P -> smem (128-byte swizzle), epilogue O / l -> bf16, LSE.
+//
+// TMEM: S0 | S1 | O = 384 of 512 columns.  Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + P 32 KB.
+// All waits are bounded (sm100_common.cuh).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "sm100_common.cuh"
+
+namespace {
+
+constexpr int D = 128;
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int TILE_BYTES = BQ * D * 2;  // 32 KB (two 64-column swizzle blocks of 16 KB)
+constexpr int NUM_THREADS = 192;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+
+struct Smem {
+  static constexpr int Q = 0;
+  static constexpr int K0 = Q + TILE_BYTES;
+  static constexpr int V0 = K0 + 2 * TILE_BYTES;
+  static constexpr int P = V0 + 2 * TILE_BYTES;
+  static constexpr int BAR = P + TILE_BYTES;
+  static constexpr int TOTAL = BAR + 256;
+};
+
+struct alignas(64) AttnMaps {
+  CUtensorMap q, k, v, pk, pv;
+};
+
+__device__ __forceinline__ void load_tile128(unsigned char* dst, const CUtensorMap* map, uint64_t* bar, int col0,
+                                             int row0) {
+  sm100::tma_load_2d(dst, map, bar, col0, row0);
+  sm100::tma_load_2d(dst + 16384, map, bar, col0 + 64, row0);
+}
+
+// K-major SW128 descriptor for a [128 rows x 128] bf16 tile stored as two 64-column blocks, k-step kk (16 elems).
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
+  return sm100::umma_desc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+// MN-major SW128 descriptor for V [128 keys (K) x 128 d (N)] stored as two 64-d blocks of 128 rows.
+__device__ __forceinline__ uint64_t vmajor_desc(uint32_t base, int kk) {
+  return sm100::umma_desc_sw128(base + kk * 2048, 16384, 1024);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tree_attn_fwd_sm100_kernel(const __grid_constant__ AttnMaps maps, const int* __restrict__ cu,
+                               const int* __restrict__ poff, const int* __restrict__ plen,
+                               __nv_bfloat16* __restrict__ out, float* __restrict__ lse, int T, int Hq, int Hk,
+                               float scale_log2, int* err) {
+  const int seq = blockIdx.y, h = blockIdx.z, hk = h / (Hq / Hk);
+  const int q0 = cu[seq], n = cu[seq + 1] - q0;
+  const int m0 = blockIdx.x * BQ;
+  if (m0 >= n) return;  // before any TMEM/barrier work
+  const int po = poff[seq], pl = plen[seq];
+  const int n_pre = (pl + BKV - 1) / BKV;
+  const int n_self_keys = min(n, m0 + BQ);
+  const int n_self = (n_self_keys + BKV - 1) / BKV;
+  const int ntiles = n_pre + n_self;
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::BAR);
+  uint64_t* bar_q = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(bar_q, 1);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&kv_full[i], 1);
+      sm100::mbar_init(&kv_empty[i], 1);
+      sm100::mbar_init(&s_full[i], 1);
+      sm100::mbar_init(&s_free[i], 128);
+    }
+    sm100::mbar_init(p_full, 128);
+    sm100::mbar_init(o_done, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, 512);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_S0 = tmem, TM_O = tmem + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      sm100::mbar_expect_tx(bar_q, TILE_BYTES);
+      load_tile128(smem + Smem::Q, &maps.q, bar_q, h * D, q0 + m0);
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, err, 11)) break;
+        sm100::mbar_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        const bool pre = j < n_pre;
+        const int row = pre ? po + j * BKV : q0 + (j - n_pre) * BKV;
+        load_tile128(smem + Smem::K0 + st * TILE_BYTES, pre ? &maps.pk : &maps.k, &kv_full[st], hk * D, row);
+        load_tile128(smem + Smem::V0 + st * TILE_BYTES, pre ? &maps.pv : &maps.v, &kv_full[st], hk * D, row);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = sm100::umma_idesc_bf16(BQ, BKV, false, false);
+      constexpr uint32_t IDESC_O = sm100::umma_idesc_bf16(BQ, D, false, true);
+      const uint32_t q_base = sm100::smem_addr(smem + Smem::Q);
+      const uint32_t p_base = sm100::smem_addr(smem + Smem::P);
+      bool ok = sm100::mbar_wait(bar_q, 0, err, 12);
+      auto issue_pv = [&](int j) -> bool {
+        if (!sm100::mbar_wait(p_full, j & 1, err, 13)) return false;
+        sm100::tc_fence_after();
+        const uint32_t v_base = sm100::smem_addr(smem + Smem::V0 + (j & 1) * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          sm100::umma_bf16(TM_O, kmajor_desc(p_base, kk), vmajor_desc(v_base, kk), IDESC_O, (j > 0 || kk > 0));
+        sm100::umma_commit(o_done);
+        sm100::umma_commit(&kv_empty[j & 1]);
+        return true;
+      };
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(&kv_full[st], (j >> 1) & 1, err, 14)) {
+          ok = false;
+          break;
+        }
+        if (!sm100::mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, err, 15)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t k_base = sm100::smem_addr(smem + Smem::K0 + st * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          sm100::umma_bf16(TM_S0 + st * BKV, kmajor_desc(q_base, kk), kmajor_desc(k_base, kk), IDESC_S, kk > 0);
+        sm100::umma_commit(&s_full[st]);
+        if (j > 0 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) issue_pv(ntiles - 1);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue (warps 2..5)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;       // TMEM lane == query row within the tile
+    const int qi = m0 + row;                   // local query index
+    const bool row_ok = qi < n;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    unsigned char* sP = smem + Smem::P;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j & 1;
+      const bool got = sm100::mbar_wait(&s_full[st], (j >> 1) & 1, err, 16);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      float s[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(TM_S0 + st * BKV + lane_off + c * 32, r);
+        sm100::tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[e]);
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&s_free[st]);  // S buffer may be overwritten by S_{j+2}
+      // mask + scale
+      const bool pre = j < n_pre;
+      const int kb = pre ? j * BKV : (j - n_pre) * BKV;
+      const int klim = pre ? pl : min(n, qi + 1);  // keys [kb, klim) visible to this row
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BKV; ++e) {
+        const bool vis = row_ok && (kb + e) < klim;
+        const float x = vis ? s[e] * scale_log2 : -INFINITY;
+        s[e] = x;
+        mx = fmaxf(mx, x);
+      }
+      // lazily updated reference max
+      float alpha = 1.f;
+      if (mx > m_ref + RESCALE_THRESHOLD || (m_ref == -INFINITY && mx > -INFINITY)) {
+        const float m_new = mx;
+        alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - m_new);
+        m_ref = m_new;
+      }
+      // P_{j-1} V_{j-1} must be done before O is rescaled or P is overwritten
+      if (j > 0) {
+        const bool g2 = sm100::mbar_wait(o_done, (j - 1) & 1, err, 17);
+        if (!__all_sync(0xffffffffu, g2)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const bool need = __any_sync(0xffffffffu, alpha != 1.f);
+        if (need) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            sm100::tmem_ld32(TM_O + lane_off + c * 32, r);
+            sm100::tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            sm100::tmem_st32(TM_O + lane_off + c * 32, r);
+          }
+          sm100::tmem_st_wait();
+        }
+      }
+      float rs = 0.f;
+      const float msafe = (m_ref == -INFINITY) ? 0.f : m_ref;
+      // P -> smem, 128-byte swizzle: 16-byte chunk index XOR (row & 7) within each 64-key block
+#pragma unroll
+      for (int c = 0; c < BKV / 8; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = exp2f(s[c * 8 + 2 * e] - msafe);
+          const float p1 = exp2f(s[c * 8 + 2 * e + 1] - msafe);
+          rs += p0 + p1;
+          __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
+          pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+        }
+        const int blk = c >> 3, chunk = c & 7;
+        unsigned char* dst = sP + blk * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      l = l * alpha + rs;
+      sm100::fence_proxy_async_smem();
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(p_full);
+    }
+    // epilogue
+    const bool g3 = ok && sm100::mbar_wait(o_done, (ntiles - 1) & 1, err, 18);
+    if (__all_sync(0xffffffffu, g3)) {
+      sm100::tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const size_t qstride = (size_t)Hq * D;
+      __nv_bfloat16* orow = out + (size_t)(q0 + qi) * qstride + (size_t)h * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(TM_O + lane_off + c * 32, r);
+        sm100::tmem_ld_wait();
+        if (row_ok) {
+          uint32_t pkd[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
+            pkd[e] = *reinterpret_cast<uint32_t*>(&hv);
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            reinterpret_cast<uint4*>(orow + c * 32)[e] = make_uint4(pkd[4 * e], pkd[4 * e + 1], pkd[4 * e + 2], pkd[4 * e + 3]);
+        }
+      }
+      if (row_ok) lse[(size_t)h * T + q0 + qi] = l > 0.f ? (m_ref + log2f(l)) * 0.6931471805599453f : -INFINITY;
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    BB_CHECK_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Row-major [rows, cols] bf16 -> map with box {64 cols, 128 rows}, 128-byte swizzle.
+void encode_rows(CUtensorMap* m, const void* base, long rows, long cols) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0 && (cols * 2) % 16 == 0, "attention TMA alignment");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)std::max<long>(rows, 1)};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (attention) failed: ", (int)r);
+}
+
+AttnMaps* attn_map_storage() {
+  thread_local AttnMaps* p = nullptr;
+  if (!p) {
+    void* raw = nullptr;
+    TORCH_CHECK(posix_memalign(&raw, 64, sizeof(AttnMaps)) == 0, "posix_memalign failed");
+    p = reinterpret_cast<AttnMaps*>(raw);
+  }
+  return p;
+}
+
+torch::Tensor& attn_error_word() {
+  static torch::Tensor e;
+  if (!e.defined()) e = torch::zeros({1}, torch::dtype(torch::kInt).device(torch::kCUDA));
+  return e;
+}
+
+}  // namespace
+
+std::vector<torch::Tensor> tree_attn_fwd_sm100(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor pk,
+                                               torch::Tensor pv, torch::Tensor cu, torch::Tensor poff,
+                                               torch::Tensor plen, int64_t max_seqlen, int64_t max_prefix,
+                                               double scale) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.is_contiguous() && k.is_contiguous() &&
+                  v.is_contiguous(), "q/k/v must be contiguous CUDA bf16");
+  const int T = q.size(0), Hq = q.size(1), Hk = k.size(1);
+  TORCH_CHECK(q.size(2) == D && k.size(2) == D, "tcgen05 attention is built for head_dim 128");
+  TORCH_CHECK(Hq % Hk == 0, "GQA: Hq % Hkv");
+  const int B = cu.numel() - 1;
+  auto o = torch::empty_like(q);
+  auto lse = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
+  if (T == 0 || B == 0) return {o, lse};
+  at::cuda::CUDAGuard guard(q.get_device());
+  {
+    CUcontext cur = nullptr;
+    if (cuCtxGetCurrent(&cur) != CUDA_SUCCESS || cur == nullptr) BB_CHECK_CUDA(cudaFree(nullptr));
+  }
+  AttnMaps* maps = attn_map_storage();
+  encode_rows(&maps->q, q.data_ptr(), T, (long)Hq * D);
+  encode_rows(&maps->k, k.data_ptr(), T, (long)Hk * D);
+  encode_rows(&maps->v, v.data_ptr(), T, (long)Hk * D);
+  const bool has_p = pk.numel() > 0;
+  encode_rows(&maps->pk, has_p ? pk.data_ptr() : k.data_ptr(), has_p ? pk.size(0) : T, (long)Hk * D);
+  encode_rows(&maps->pv, has_p ? pv.data_ptr() : v.data_ptr(), has_p ? pv.size(0) : T, (long)Hk * D);
+  const int smem = Smem::TOTAL + 1024;
+  auto kern = tree_attn_fwd_sm100_kernel;
+  static bool attr = false;
+  if (!attr) {
+    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  dim3 grid((max_seqlen + BQ - 1) / BQ, B, Hq);
+  const int* cup = cu.data_ptr<int>();
+  const int* pop = poff.data_ptr<int>();
+  const int* plp = plen.data_ptr<int>();
+  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  float* lp = lse.data_ptr<float>();
+  float sl2 = (float)(scale * 1.4426950408889634);
+  int* err = attn_error_word().data_ptr<int>();
+  int Ti = T, Hqi = Hq, Hki = Hk;
+  void* args[] = {maps, &cup, &pop, &plp, &op, &lp, &Ti, &Hqi, &Hki, &sl2, &err};
+  BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(NUM_THREADS), args, smem,
+                                 at::cuda::getCurrentCUDAStream()));
+  BB_POST_LAUNCH();
+  return {o, lse};
+}
+
+int64_t attn_error_code() { return attn_error_word().item<int>(); }

@@ -29,6 +29,11 @@ from torch import Tensor
 
 from ._ext import kernels, on_gpu
 
+import os
+
+# head_dim 128 runs the tcgen05/TMEM forward; BRIDGE_B200_ATTN=mma selects the mma.sync kernel.
+_ATTN_IMPL = os.environ.get("BRIDGE_B200_ATTN", "tcgen05")
+
 
 # --------------------------------------------------------------------------- reference math
 def masked_attention(q: Tensor, k: Tensor, v: Tensor, q_pos: Tensor, k_pos: Tensor, *,
@@ -146,8 +151,9 @@ class _TreeAttentionFn(torch.autograd.Function):
         q_, k_, v_ = q.contiguous(), k.contiguous(), v.contiguous()
         pk_ = pk.contiguous() if has_p else q_.new_empty((0, k.shape[1], k.shape[2]))
         pv_ = pv.contiguous() if has_p else q_.new_empty((0, v.shape[1], v.shape[2]))
-        o, lse = m.tree_attn_fwd(q_, k_, v_, pk_, pv_, layout.cu_seqlens, layout.prefix_offsets,
-                                 layout.prefix_lengths, layout.max_seqlen, layout.max_prefix, float(scale))
+        fwd = m.tree_attn_fwd_sm100 if (q.shape[-1] == 128 and _ATTN_IMPL == "tcgen05") else m.tree_attn_fwd
+        o, lse = fwd(q_, k_, v_, pk_, pv_, layout.cu_seqlens, layout.prefix_offsets, layout.prefix_lengths,
+                     layout.max_seqlen, layout.max_prefix, float(scale))
         ctx.save_for_backward(q_, k_, v_, pk_, pv_, o, lse)
         ctx.layout, ctx.scale, ctx.has_p = layout, scale, has_p
         return o

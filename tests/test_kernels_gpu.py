@@ -189,3 +189,28 @@ def test_tree_attention_d256_forward():
                                      lay.max_seqlen, lay.max_prefix, 1 / 16)
     orf = tree_attention_reference(q.float(), k.float(), v.float(), pk.float(), pv.float(), lay, softmax_scale=1 / 16)
     _close(o, orf, 8e-3, 2e-2, "o")
+
+
+@pytest.mark.parametrize("lens,spans,P,hq,hkv", [
+    ((512,) * 4, ((0, 512),) * 4, 512, 32, 8),
+    ((300, 77, 129), ((0, 200), (200, 13), (0, 0)), 213, 8, 2),
+    ((1,), ((0, 1000),), 1000, 4, 4),
+    ((640, 640), ((0, 0), (0, 0)), 0, 16, 4),
+])
+def test_tree_attention_sm100_forward(lens, spans, P, hq, hkv):
+    from bridge_b200.ops._ext import kernels
+    from bridge_b200.ops.attention import tree_attention_reference
+
+    q, k, v, pk, pv, lay = _tree_case(128, hq, hkv, lens, spans, P, seed=3)
+    if P == 0:
+        pk = pv = q.new_empty((0, hkv, 128))
+    o, lse = kernels().tree_attn_fwd_sm100(q, k, v, pk, pv, lay.cu_seqlens, lay.prefix_offsets, lay.prefix_lengths,
+                                           lay.max_seqlen, lay.max_prefix, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert kernels().attn_error_code() == 0
+    orf = tree_attention_reference(q.float(), k.float(), v.float(), pk.float() if P else None,
+                                   pv.float() if P else None, lay, softmax_scale=1 / math.sqrt(128))
+    _close(o, orf, 8e-3, 2e-2, "o")
+    o2, lse2 = kernels().tree_attn_fwd(q, k, v, pk, pv, lay.cu_seqlens, lay.prefix_offsets, lay.prefix_lengths,
+                                       lay.max_seqlen, lay.max_prefix, 1 / math.sqrt(128))
+    _close(lse, lse2, 1e-3, 1e-3, "lse")
