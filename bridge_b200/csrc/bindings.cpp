@@ -39,6 +39,10 @@ std::vector<torch::Tensor> tree_attn_fwd_sm100(torch::Tensor q, torch::Tensor k,
                                                torch::Tensor plen, int64_t max_seqlen, int64_t max_prefix,
                                                double scale);
 int64_t attn_error_code();
+std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                               torch::Tensor pk, torch::Tensor pv, torch::Tensor o, torch::Tensor lse,
+                                               torch::Tensor cu, torch::Tensor poff, torch::Tensor plen,
+                                               int64_t max_seqlen, int64_t max_prefix, double scale);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bridge_b200 sm_100a kernels";
@@ -57,6 +61,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tree_attn_bwd", &tree_attn_bwd);
   m.def("tree_attn_fwd_sm100", &tree_attn_fwd_sm100, "tcgen05 tree attention forward (head_dim 128)");
   m.def("attn_error_code", &attn_error_code);
+  m.def("tree_attn_bwd_sm100", &tree_attn_bwd_sm100, "tcgen05 tree attention backward (head_dim 128)");
   m.def("gemm", &gemm, "tcgen05 GEMM: C (+)= op(A) op(B)^T");
   m.def("gemm_error_code", &gemm_error_code);
   m.def("launch_count", &bb_launch_count,

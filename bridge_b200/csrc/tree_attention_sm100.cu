@@ -291,6 +291,448 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// =================================================================================== backward
+// Backward = two tcgen05 kernels (no per-tile dQ atomics):
+//   dkdv : one CTA = 128 keys x 1 kv head; loops over every (q head of the GQA group, 128-row q tile)
+//          that sees them.  S^T = K Q^T and dP^T = V dO^T land in TMEM; the softmax warps (one thread per
+//          key) form P^T and dS^T = P^T (dP^T - delta) in swizzled smem; dV += P^T dO, dK += dS^T Q
+//          accumulate in TMEM across the loop.  Own keys: written once (bf16).  Prefix keys: the work is
+//          split per reading sequence and merged with one vectorised FP32 atomic pass per CTA.
+//   dq   : one CTA = 128 queries x 1 q head (forward-like loop over key tiles): S, dP in TMEM, dS -> smem,
+//          dQ += dS K accumulated in TMEM, written once.
+struct alignas(64) BwdMaps {
+  CUtensorMap q, k, v, pk, pv, dout;
+};
+
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier over the 4 softmax warps that also ANDs a predicate: every warp takes the same branch afterwards,
+// so a bounded-wait failure in one warp can never leave the others waiting at a named barrier.
+__device__ __forceinline__ bool named_and_softmax(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+// Write 32 consecutive bf16-converted columns [c*32, c*32+32) of row `row` into a K-major SW128 tile.
+__device__ __forceinline__ void store_row32_sw128(unsigned char* tile, int row, int c, const float* v) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+  }
+  const int blk = c >> 1;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int chunk = (c & 1) * 4 + e;
+    unsigned char* dst = tile + blk * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+  }
+}
+
+struct SmemDKDV {
+  static constexpr int K = 0;
+  static constexpr int V = K + TILE_BYTES;
+  static constexpr int Q = V + TILE_BYTES;
+  static constexpr int DO = Q + TILE_BYTES;
+  static constexpr int PT = DO + TILE_BYTES;
+  static constexpr int DST = PT + TILE_BYTES;
+  static constexpr int LSE = DST + TILE_BYTES;  // 128 floats
+  static constexpr int DEL = LSE + 512;         // 128 floats
+  static constexpr int BAR = DEL + 512;
+  static constexpr int TOTAL = BAR + 256;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tree_attn_dkdv_sm100_kernel(const __grid_constant__ BwdMaps maps, const int* __restrict__ cu,
+                                const int* __restrict__ poff, const int* __restrict__ plen,
+                                const float* __restrict__ lse, const float* __restrict__ delta,
+                                __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
+                                float* __restrict__ dpk_acc, float* __restrict__ dpv_acc, int B, int T, int Hq,
+                                int Hk, float scale_log2, float scale, int* err) {
+  const int mode = blockIdx.y / B, b = blockIdx.y % B, hk = blockIdx.z, rep = Hq / Hk;
+  const int q0 = cu[b], n = cu[b + 1] - q0;
+  const int key_len = mode == 0 ? n : plen[b];
+  const int key_row0 = mode == 0 ? q0 : poff[b];
+  const int kb = blockIdx.x * BKV;
+  if (kb >= key_len || n <= 0) return;
+  const int it0 = mode == 0 ? kb / BQ : 0;
+  const int nq = (n + BQ - 1) / BQ - it0;
+  const int niter = rep * nq;
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* lse_s = reinterpret_cast<float*>(smem + SmemDKDV::LSE);
+  float* del_s = reinterpret_cast<float*>(smem + SmemDKDV::DEL);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemDKDV::BAR);
+  uint64_t* kv_bar = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* st_free = bars + 4;
+  uint64_t* p_full = bars + 5;
+  uint64_t* dkv_done = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(kv_bar, 1);
+    sm100::mbar_init(qdo_full, 1);
+    sm100::mbar_init(qdo_empty, 1);
+    sm100::mbar_init(s_full, 1);
+    sm100::mbar_init(st_free, 128);
+    sm100::mbar_init(p_full, 128);
+    sm100::mbar_init(dkv_done, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, 512);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_S = tmem, TM_DP = tmem + 128, TM_DV = tmem + 256, TM_DK = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const CUtensorMap* km = mode == 0 ? &maps.k : &maps.pk;
+      const CUtensorMap* vm = mode == 0 ? &maps.v : &maps.pv;
+      sm100::mbar_expect_tx(kv_bar, 2 * TILE_BYTES);
+      load_tile128(smem + SmemDKDV::K, km, kv_bar, hk * D, key_row0 + kb);
+      load_tile128(smem + SmemDKDV::V, vm, kv_bar, hk * D, key_row0 + kb);
+      for (int it = 0; it < niter; ++it) {
+        const int h = hk * rep + it / nq, qt = it0 + it % nq;
+        if (!sm100::mbar_wait(qdo_empty, (it & 1) ^ 1, err, 21)) break;
+        sm100::mbar_expect_tx(qdo_full, 2 * TILE_BYTES);
+        load_tile128(smem + SmemDKDV::Q, &maps.q, qdo_full, h * D, q0 + qt * BQ);
+        load_tile128(smem + SmemDKDV::DO, &maps.dout, qdo_full, h * D, q0 + qt * BQ);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_SS = sm100::umma_idesc_bf16(BKV, BQ, false, false);  // S^T, dP^T
+      constexpr uint32_t ID_ACC = sm100::umma_idesc_bf16(BKV, D, false, true);   // dV, dK (B MN-major)
+      const uint32_t k_b = sm100::smem_addr(smem + SmemDKDV::K), v_b = sm100::smem_addr(smem + SmemDKDV::V);
+      const uint32_t q_b = sm100::smem_addr(smem + SmemDKDV::Q), o_b = sm100::smem_addr(smem + SmemDKDV::DO);
+      const uint32_t pt_b = sm100::smem_addr(smem + SmemDKDV::PT), ds_b = sm100::smem_addr(smem + SmemDKDV::DST);
+      bool ok = sm100::mbar_wait(kv_bar, 0, err, 22);
+      for (int it = 0; it < niter && ok; ++it) {
+        if (!sm100::mbar_wait(qdo_full, it & 1, err, 23) || !sm100::mbar_wait(st_free, (it & 1) ^ 1, err, 24)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          sm100::umma_bf16(TM_S, kmajor_desc(k_b, kk), kmajor_desc(q_b, kk), ID_SS, kk > 0);
+          sm100::umma_bf16(TM_DP, kmajor_desc(v_b, kk), kmajor_desc(o_b, kk), ID_SS, kk > 0);
+        }
+        sm100::umma_commit(s_full);
+        if (!sm100::mbar_wait(p_full, it & 1, err, 25)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          sm100::umma_bf16(TM_DV, kmajor_desc(pt_b, kk), vmajor_desc(o_b, kk), ID_ACC, it > 0 || kk > 0);
+          sm100::umma_bf16(TM_DK, kmajor_desc(ds_b, kk), vmajor_desc(q_b, kk), ID_ACC, it > 0 || kk > 0);
+        }
+        sm100::umma_commit(qdo_empty);
+      }
+      if (ok) sm100::umma_commit(dkv_done);
+    }
+  } else {
+    const int quarter = warp & 3, row = quarter * 32 + lane, key = kb + row;
+    const bool key_ok = key < key_len;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int t = threadIdx.x - 64;  // 0..127 among the softmax threads
+    const float LOG2E = 1.4426950408889634f;
+    bool ok = true;
+    for (int it = 0; it < niter && ok; ++it) {
+      const int h = hk * rep + it / nq, qbase = (it0 + it % nq) * BQ;
+      {
+        const int q = qbase + t;
+        const bool v = q < n;
+        lse_s[t] = v ? lse[(size_t)h * T + q0 + q] * LOG2E : INFINITY;
+        del_s[t] = v ? delta[(size_t)h * T + q0 + q] : 0.f;
+      }
+      named_sync_softmax();
+      bool g = sm100::mbar_wait(s_full, it & 1, err, 26);
+      if (g && it > 0) g = sm100::mbar_wait(qdo_empty, (it - 1) & 1, err, 27);  // P^T / dS^T smem free
+      if (!named_and_softmax(g)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < BQ / 32; ++c) {
+        uint32_t rs[32], rd[32];
+        sm100::tmem_ld32(TM_S + lane_off + c * 32, rs);
+        sm100::tmem_ld32(TM_DP + lane_off + c * 32, rd);
+        sm100::tmem_ld_wait();
+        float p[32], ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int qq = qbase + c * 32 + e;
+          const bool vis = key_ok && (mode == 1 || key <= qq);  // invalid q rows carry lse=+inf -> p=0
+          const float pe = vis ? exp2f(__uint_as_float(rs[e]) * scale_log2 - lse_s[c * 32 + e]) : 0.f;
+          p[e] = pe;
+          ds[e] = pe * (__uint_as_float(rd[e]) - del_s[c * 32 + e]);
+        }
+        store_row32_sw128(smem + SmemDKDV::PT, row, c, p);
+        store_row32_sw128(smem + SmemDKDV::DST, row, c, ds);
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(st_free);
+      sm100::fence_proxy_async_smem();
+      sm100::mbar_arrive(p_full);
+      named_sync_softmax();  // lse_s / del_s are rewritten by the next iteration
+    }
+    const bool g = ok && sm100::mbar_wait(dkv_done, 0, err, 28);
+    if (__all_sync(0xffffffffu, g)) {
+      sm100::tc_fence_after();
+      const size_t kstride = (size_t)Hk * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t rk[32], rv[32];
+        sm100::tmem_ld32(TM_DK + lane_off + c * 32, rk);
+        sm100::tmem_ld32(TM_DV + lane_off + c * 32, rv);
+        sm100::tmem_ld_wait();
+        if (!key_ok) continue;
+        if (mode == 0) {
+          __nv_bfloat16* kd = dk + (size_t)(key_row0 + key) * kstride + (size_t)hk * D + c * 32;
+          __nv_bfloat16* vd = dv + (size_t)(key_row0 + key) * kstride + (size_t)hk * D + c * 32;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            reinterpret_cast<__nv_bfloat162*>(kd)[e] =
+                __floats2bfloat162_rn(__uint_as_float(rk[2 * e]) * scale, __uint_as_float(rk[2 * e + 1]) * scale);
+            reinterpret_cast<__nv_bfloat162*>(vd)[e] =
+                __floats2bfloat162_rn(__uint_as_float(rv[2 * e]), __uint_as_float(rv[2 * e + 1]));
+          }
+        } else {
+          float4* kd = reinterpret_cast<float4*>(dpk_acc + (size_t)(key_row0 + key) * kstride + (size_t)hk * D + c * 32);
+          float4* vd = reinterpret_cast<float4*>(dpv_acc + (size_t)(key_row0 + key) * kstride + (size_t)hk * D + c * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            atomicAdd(kd + e, make_float4(__uint_as_float(rk[4 * e]) * scale, __uint_as_float(rk[4 * e + 1]) * scale,
+                                          __uint_as_float(rk[4 * e + 2]) * scale, __uint_as_float(rk[4 * e + 3]) * scale));
+            atomicAdd(vd + e, make_float4(__uint_as_float(rv[4 * e]), __uint_as_float(rv[4 * e + 1]),
+                                          __uint_as_float(rv[4 * e + 2]), __uint_as_float(rv[4 * e + 3])));
+          }
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+struct SmemDQ {
+  static constexpr int Q = 0;
+  static constexpr int DO = Q + TILE_BYTES;
+  static constexpr int K0 = DO + TILE_BYTES;              // 2 stages of K
+  static constexpr int V0 = K0 + 2 * TILE_BYTES;          // 2 stages of V
+  static constexpr int DS = V0 + 2 * TILE_BYTES;
+  static constexpr int BAR = DS + TILE_BYTES;
+  static constexpr int TOTAL = BAR + 256;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tree_attn_dq_sm100_kernel(const __grid_constant__ BwdMaps maps, const int* __restrict__ cu,
+                              const int* __restrict__ poff, const int* __restrict__ plen,
+                              const float* __restrict__ lse, const float* __restrict__ delta,
+                              __nv_bfloat16* __restrict__ dq, int T, int Hq, int Hk, float scale_log2, float scale,
+                              int* err) {
+  const int seq = blockIdx.y, h = blockIdx.z, hk = h / (Hq / Hk);
+  const int q0 = cu[seq], n = cu[seq + 1] - q0;
+  const int m0 = blockIdx.x * BQ;
+  if (m0 >= n) return;
+  const int po = poff[seq], pl = plen[seq];
+  const int n_pre = (pl + BKV - 1) / BKV;
+  const int n_self = (min(n, m0 + BQ) + BKV - 1) / BKV;
+  const int ntiles = n_pre + n_self;
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemDQ::BAR);
+  uint64_t* qdo_bar = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* sd_free = bars + 6;
+  uint64_t* ds_full = bars + 7;
+  uint64_t* ds_done = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(qdo_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&kv_full[i], 1);
+      sm100::mbar_init(&kv_empty[i], 1);
+    }
+    sm100::mbar_init(s_full, 1);
+    sm100::mbar_init(sd_free, 128);
+    sm100::mbar_init(ds_full, 128);
+    sm100::mbar_init(ds_done, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, 512);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_S = tmem, TM_DP = tmem + 128, TM_DQ = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::mbar_expect_tx(qdo_bar, 2 * TILE_BYTES);
+      load_tile128(smem + SmemDQ::Q, &maps.q, qdo_bar, h * D, q0 + m0);
+      load_tile128(smem + SmemDQ::DO, &maps.dout, qdo_bar, h * D, q0 + m0);
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, err, 31)) break;
+        sm100::mbar_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        const bool pre = j < n_pre;
+        const int r0 = pre ? po + j * BKV : q0 + (j - n_pre) * BKV;
+        load_tile128(smem + SmemDQ::K0 + st * TILE_BYTES, pre ? &maps.pk : &maps.k, &kv_full[st], hk * D, r0);
+        load_tile128(smem + SmemDQ::V0 + st * TILE_BYTES, pre ? &maps.pv : &maps.v, &kv_full[st], hk * D, r0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_SS = sm100::umma_idesc_bf16(BQ, BKV, false, false);
+      constexpr uint32_t ID_DQ = sm100::umma_idesc_bf16(BQ, D, false, true);
+      const uint32_t q_b = sm100::smem_addr(smem + SmemDQ::Q), o_b = sm100::smem_addr(smem + SmemDQ::DO);
+      const uint32_t ds_b = sm100::smem_addr(smem + SmemDQ::DS);
+      bool ok = sm100::mbar_wait(qdo_bar, 0, err, 32);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(&kv_full[st], (j >> 1) & 1, err, 33) || !sm100::mbar_wait(sd_free, (j & 1) ^ 1, err, 34)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t k_b = sm100::smem_addr(smem + SmemDQ::K0 + st * TILE_BYTES);
+        const uint32_t v_b = sm100::smem_addr(smem + SmemDQ::V0 + st * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          sm100::umma_bf16(TM_S, kmajor_desc(q_b, kk), kmajor_desc(k_b, kk), ID_SS, kk > 0);
+          sm100::umma_bf16(TM_DP, kmajor_desc(o_b, kk), kmajor_desc(v_b, kk), ID_SS, kk > 0);
+        }
+        sm100::umma_commit(s_full);
+        if (!sm100::mbar_wait(ds_full, j & 1, err, 35)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          sm100::umma_bf16(TM_DQ, kmajor_desc(ds_b, kk), vmajor_desc(k_b, kk), ID_DQ, j > 0 || kk > 0);
+        sm100::umma_commit(&kv_empty[st]);
+        sm100::umma_commit(ds_done);
+      }
+    }
+  } else {
+    const int quarter = warp & 3, row = quarter * 32 + lane, qi = m0 + row;
+    const bool row_ok = qi < n;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float LOG2E = 1.4426950408889634f;
+    const float lse_r = row_ok ? lse[(size_t)h * T + q0 + qi] * LOG2E : 0.f;
+    const float del_r = row_ok ? delta[(size_t)h * T + q0 + qi] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      bool g = sm100::mbar_wait(s_full, j & 1, err, 36);
+      if (g && j > 0) g = sm100::mbar_wait(ds_done, (j - 1) & 1, err, 37);
+      if (!__all_sync(0xffffffffu, g)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const bool pre = j < n_pre;
+      const int kbase = pre ? j * BKV : (j - n_pre) * BKV;
+      const int klim = pre ? pl : min(n, qi + 1);
+#pragma unroll 1
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t rs[32], rd[32];
+        sm100::tmem_ld32(TM_S + lane_off + c * 32, rs);
+        sm100::tmem_ld32(TM_DP + lane_off + c * 32, rd);
+        sm100::tmem_ld_wait();
+        float ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const bool vis = row_ok && (kbase + c * 32 + e) < klim;
+          const float pe = vis ? exp2f(__uint_as_float(rs[e]) * scale_log2 - lse_r) : 0.f;
+          ds[e] = pe * (__uint_as_float(rd[e]) - del_r);
+        }
+        store_row32_sw128(smem + SmemDQ::DS, row, c, ds);
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(sd_free);
+      sm100::fence_proxy_async_smem();
+      sm100::mbar_arrive(ds_full);
+    }
+    const bool g = ok && sm100::mbar_wait(ds_done, (ntiles - 1) & 1, err, 38);
+    if (__all_sync(0xffffffffu, g)) {
+      sm100::tc_fence_after();
+      __nv_bfloat16* dst = dq + (size_t)(q0 + qi) * Hq * D + (size_t)h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(TM_DQ + lane_off + c * 32, r);
+        sm100::tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            reinterpret_cast<__nv_bfloat162*>(dst + c * 32)[e] =
+                __floats2bfloat162_rn(__uint_as_float(r[2 * e]) * scale, __uint_as_float(r[2 * e + 1]) * scale);
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+__global__ void delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
+                             float* __restrict__ delta, int T, int Hq) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const long total = (long)T * Hq;
+  for (long it = (long)blockIdx.x * warps + (threadIdx.x >> 5); it < total; it += (long)gridDim.x * warps) {
+    const int t = (int)(it / Hq), h = (int)(it % Hq);
+    const bb::bf16x8* a = reinterpret_cast<const bb::bf16x8*>(dout + ((size_t)t * Hq + h) * D);
+    const bb::bf16x8* o = reinterpret_cast<const bb::bf16x8*>(out + ((size_t)t * Hq + h) * D);
+    float fa[8], fo[8];
+    bb::unpack8(a[lane & 15], fa);
+    bb::unpack8(o[lane & 15], fo);
+    float s = 0.f;
+    if (lane < 16)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += fa[e] * fo[e];
+    s = bb::warp_sum(s);
+    if (lane == 0) delta[(size_t)h * T + t] = s;
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long n) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16(src[i]);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -383,3 +825,96 @@ std::vector<torch::Tensor> tree_attn_fwd_sm100(torch::Tensor q, torch::Tensor k,
 }
 
 int64_t attn_error_code() { return attn_error_word().item<int>(); }
+
+std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                               torch::Tensor pk, torch::Tensor pv, torch::Tensor o, torch::Tensor lse,
+                                               torch::Tensor cu, torch::Tensor poff, torch::Tensor plen,
+                                               int64_t max_seqlen, int64_t max_prefix, double scale) {
+  TORCH_CHECK(dout.is_contiguous() && q.size(2) == D, "tcgen05 attention backward: contiguous, head_dim 128");
+  const int T = q.size(0), Hq = q.size(1), Hk = k.size(1);
+  const int B = cu.numel() - 1;
+  auto dq = torch::empty_like(q);
+  auto dk = torch::empty_like(k), dv = torch::empty_like(v);
+  const bool has_p = pk.numel() > 0;
+  auto dpk = torch::zeros_like(pk), dpv = torch::zeros_like(pv);
+  if (T == 0 || B == 0) return {dq, dk, dv, dpk, dpv};
+  at::cuda::CUDAGuard guard(q.get_device());
+  {
+    CUcontext cur = nullptr;
+    if (cuCtxGetCurrent(&cur) != CUDA_SUCCESS || cur == nullptr) BB_CHECK_CUDA(cudaFree(nullptr));
+  }
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto delta = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
+  {
+    const int blocks = (int)std::min<long>(((long)T * Hq + 7) / 8, 148l * 16);
+    delta_kernel<<<blocks, 256, 0, stream>>>((const __nv_bfloat16*)dout.data_ptr(), (const __nv_bfloat16*)o.data_ptr(),
+                                             delta.data_ptr<float>(), T, Hq);
+    BB_POST_LAUNCH();
+  }
+  torch::Tensor dpk_acc, dpv_acc;
+  if (has_p) {
+    dpk_acc = torch::zeros(pk.sizes(), pk.options().dtype(at::kFloat));
+    dpv_acc = torch::zeros(pv.sizes(), pv.options().dtype(at::kFloat));
+  }
+  static thread_local BwdMaps* maps = nullptr;
+  if (!maps) {
+    void* raw = nullptr;
+    TORCH_CHECK(posix_memalign(&raw, 64, sizeof(BwdMaps)) == 0, "posix_memalign failed");
+    maps = reinterpret_cast<BwdMaps*>(raw);
+  }
+  encode_rows(&maps->q, q.data_ptr(), T, (long)Hq * D);
+  encode_rows(&maps->k, k.data_ptr(), T, (long)Hk * D);
+  encode_rows(&maps->v, v.data_ptr(), T, (long)Hk * D);
+  encode_rows(&maps->pk, has_p ? pk.data_ptr() : k.data_ptr(), has_p ? pk.size(0) : T, (long)Hk * D);
+  encode_rows(&maps->pv, has_p ? pv.data_ptr() : v.data_ptr(), has_p ? pv.size(0) : T, (long)Hk * D);
+  encode_rows(&maps->dout, dout.data_ptr(), T, (long)Hq * D);
+  const int* cup = cu.data_ptr<int>();
+  const int* pop = poff.data_ptr<int>();
+  const int* plp = plen.data_ptr<int>();
+  const float* lsep = lse.data_ptr<float>();
+  const float* delp = delta.data_ptr<float>();
+  float sl2 = (float)(scale * 1.4426950408889634), sc = (float)scale;
+  int* err = attn_error_word().data_ptr<int>();
+  int Bi = B, Ti = T, Hqi = Hq, Hki = Hk;
+  {
+    auto kern = tree_attn_dkdv_sm100_kernel;
+    const int smem = SmemDKDV::TOTAL + 1024;
+    static bool attr = false;
+    if (!attr) {
+      BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr = true;
+    }
+    const long xt = std::max<long>((max_seqlen + BKV - 1) / BKV, has_p ? (max_prefix + BKV - 1) / BKV : 0);
+    dim3 grid((unsigned)std::max<long>(xt, 1), (unsigned)(has_p ? 2 * B : B), (unsigned)Hk);
+    __nv_bfloat16* dkp = (__nv_bfloat16*)dk.data_ptr();
+    __nv_bfloat16* dvp = (__nv_bfloat16*)dv.data_ptr();
+    float* dpkp = has_p ? dpk_acc.data_ptr<float>() : nullptr;
+    float* dpvp = has_p ? dpv_acc.data_ptr<float>() : nullptr;
+    void* args[] = {maps, &cup, &pop, &plp, &lsep, &delp, &dkp, &dvp, &dpkp, &dpvp, &Bi, &Ti, &Hqi, &Hki, &sl2, &sc, &err};
+    BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(NUM_THREADS), args, smem, stream));
+    BB_POST_LAUNCH();
+  }
+  {
+    auto kern = tree_attn_dq_sm100_kernel;
+    const int smem = SmemDQ::TOTAL + 1024;
+    static bool attr = false;
+    if (!attr) {
+      BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr = true;
+    }
+    dim3 grid((unsigned)((max_seqlen + BQ - 1) / BQ), (unsigned)B, (unsigned)Hq);
+    __nv_bfloat16* dqp = (__nv_bfloat16*)dq.data_ptr();
+    void* args[] = {maps, &cup, &pop, &plp, &lsep, &delp, &dqp, &Ti, &Hqi, &Hki, &sl2, &sc, &err};
+    BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(NUM_THREADS), args, smem, stream));
+    BB_POST_LAUNCH();
+  }
+  if (has_p) {
+    const long nel = dpk.numel();
+    const int blocks = (int)std::min<long>((nel + 255) / 256, 148l * 16);
+    f32_to_bf16_kernel<<<blocks, 256, 0, stream>>>(dpk_acc.data_ptr<float>(), (__nv_bfloat16*)dpk.data_ptr(), nel);
+    BB_POST_LAUNCH();
+    f32_to_bf16_kernel<<<blocks, 256, 0, stream>>>(dpv_acc.data_ptr<float>(), (__nv_bfloat16*)dpv.data_ptr(), nel);
+    BB_POST_LAUNCH();
+  }
+  return {dq, dk, dv, dpk, dpv};
+}

@@ -163,6 +163,13 @@ class _TreeAttentionFn(torch.autograd.Function):
         m = kernels()
         q, k, v, pk, pv, o, lse = ctx.saved_tensors
         lay = ctx.layout
+        if q.shape[-1] == 128 and _ATTN_IMPL == "tcgen05":
+            dq, dk, dv, dpk, dpv = m.tree_attn_bwd_sm100(do.contiguous(), q, k, v, pk, pv, o, lse, lay.cu_seqlens,
+                                                         lay.prefix_offsets, lay.prefix_lengths, lay.max_seqlen,
+                                                         lay.max_prefix, float(ctx.scale))
+            if not ctx.has_p:
+                dpk = dpv = None
+            return dq, dk, dv, dpk, dpv, None, None
         users, nspans = _prefix_users(lay)
         dq, dk, dv, dpk, dpv = m.tree_attn_bwd(do.contiguous(), q, k, v, pk, pv, o, lse, lay.cu_seqlens,
                                                lay.prefix_offsets, lay.prefix_lengths, lay.max_seqlen,

@@ -214,3 +214,36 @@ def test_tree_attention_sm100_forward(lens, spans, P, hq, hkv):
     o2, lse2 = kernels().tree_attn_fwd(q, k, v, pk, pv, lay.cu_seqlens, lay.prefix_offsets, lay.prefix_lengths,
                                        lay.max_seqlen, lay.max_prefix, 1 / math.sqrt(128))
     _close(lse, lse2, 1e-3, 1e-3, "lse")
+
+
+@pytest.mark.parametrize("lens,spans,P,hq,hkv", [
+    ((512,) * 4, ((0, 512),) * 4, 512, 32, 8),
+    ((300, 77, 129), ((0, 200), (200, 13), (0, 0)), 213, 8, 2),
+    ((640, 640), ((0, 0), (0, 0)), 0, 16, 4),
+    ((5, 260), ((0, 700), (100, 300)), 700, 4, 2),
+])
+def test_tree_attention_sm100_backward(lens, spans, P, hq, hkv):
+    from bridge_b200.ops._ext import kernels
+    from bridge_b200.ops.attention import tree_attention_reference
+
+    q, k, v, pk, pv, lay = _tree_case(128, hq, hkv, lens, spans, P, seed=4)
+    if P == 0:
+        pk = pv = q.new_empty((0, hkv, 128))
+    sc = 1 / math.sqrt(128)
+    o, lse = kernels().tree_attn_fwd_sm100(q, k, v, pk, pv, lay.cu_seqlens, lay.prefix_offsets, lay.prefix_lengths,
+                                           lay.max_seqlen, lay.max_prefix, sc)
+    do = torch.randn_like(o)
+    dq, dk, dv, dpk, dpv = kernels().tree_attn_bwd_sm100(do, q, k, v, pk, pv, o, lse, lay.cu_seqlens,
+                                                         lay.prefix_offsets, lay.prefix_lengths, lay.max_seqlen,
+                                                         lay.max_prefix, sc)
+    torch.cuda.synchronize()
+    assert kernels().attn_error_code() == 0
+    ref = [t.detach().float().requires_grad_() for t in (q, k, v, pk, pv)]
+    orf = tree_attention_reference(ref[0], ref[1], ref[2], ref[3] if P else None, ref[4] if P else None, lay,
+                                   softmax_scale=sc)
+    orf.backward(do.float())
+    for a, b_, n in zip((dq, dk, dv), ref[:3], ("dq", "dk", "dv")):
+        _close(a, b_.grad, 1e-2, 3e-2, n)
+    if P:
+        _close(dpk, ref[3].grad, 1e-2, 3e-2, "dpk")
+        _close(dpv, ref[4].grad, 1e-2, 3e-2, "dpv")
