@@ -23,6 +23,7 @@ import torch.distributed as dist
 from torch import Tensor
 
 from ._ext import kernels, on_gpu
+from .gemm import gemm
 
 
 def logprob_entropy_reference(logits: Tensor, targets: Tensor, temperature: Tensor | float = 1.0,
@@ -85,7 +86,7 @@ class _FusedHeadLogProbFn(torch.autograd.Function):
         logits_chunks = []
         for s in range(0, u, chunk_rows):
             e = min(u, s + chunk_rows)
-            lg = torch.matmul(h[s:e], weight.t())                    # [c, V_local] bf16
+            lg = gemm(h[s:e], weight)                                 # [c, V_local] bf16 (tcgen05)
             m.logprob_stats(lg, targets[s:e], inv_temp[s:e], int(vocab_start), stats[s:e])
             logits_chunks.append(lg)
         if tp_group is not None and dist.get_world_size(tp_group) > 1:
@@ -104,14 +105,18 @@ class _FusedHeadLogProbFn(torch.autograd.Function):
         dent = dent.float().contiguous() if (dent is not None and ctx.with_entropy) else None
         dh = torch.empty_like(h)
         dw = None
+        main = getattr(weight, "main_grad", None)
         for i, lg in enumerate(ctx.logits):
             s = i * ctx.chunk_rows
             e = s + lg.shape[0]
             m.logprob_grad_inplace(lg, targets[s:e], inv_temp[s:e], lse[s:e], ez[s:e], dlp[s:e],
                                    dent[s:e] if dent is not None else None, int(ctx.vocab_start))
-            torch.matmul(lg, weight, out=dh[s:e])
-            part = torch.matmul(lg.t(), h[s:e])
-            dw = part if dw is None else dw.add_(part)
+            dh[s:e] = gemm(lg, weight, b_mn=True)                      # dlogits @ W
+            if main is not None:                                       # W.main_grad += dlogits^T h
+                gemm(lg, h[s:e].contiguous(), a_mn=True, b_mn=True, out=main, accumulate=True)
+            else:
+                part = gemm(lg, h[s:e].contiguous(), a_mn=True, b_mn=True)
+                dw = part if dw is None else dw.add_(part)
         ctx.logits = None
         return dh, dw, None, None, None, None, None, None
 

@@ -114,7 +114,7 @@ def _peer(group, offset: int) -> int:
 def ring_exchange(tensors: list[Tensor], group) -> list[Tensor]:
     """Send ``tensors`` to rank+1 and receive the same shapes from rank-1 (one hop)."""
     nxt, prv = _peer(group, 1), _peer(group, -1)
-    recv = [torch.empty_like(t) for t in tensors]
+    recv = [torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in tensors]
     ops = []
     for t in tensors:
         ops.append(dist.P2POp(dist.isend, t.contiguous(), nxt, group))

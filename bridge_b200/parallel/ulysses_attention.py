@@ -25,8 +25,9 @@ from .execution_context import CPAttentionBackendBase, LocalKVBlock, prefix_bloc
 
 
 def _a2a(x: Tensor, group) -> Tensor:
-    out = torch.empty_like(x)
-    dist.all_to_all_single(out, x.contiguous(), group=group)
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)  # contiguous, unlike empty_like of a view
+    dist.all_to_all_single(out, x, group=group)
     return out
 
 
