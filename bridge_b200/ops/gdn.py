@@ -121,9 +121,11 @@ def _chunk_one(q, k, v, g, beta, S0, scale: float, chunk: int):
         vc = v[s:e].float().transpose(0, 1)        # [H, n, V]
         bc = beta[s:e].float().transpose(0, 1)     # [H, n]
         G = torch.cumsum(g[s:e].float().transpose(0, 1), dim=-1)   # [H, n]
-        decay = torch.exp(G[:, :, None] - G[:, None, :])           # Gamma_t / Gamma_s
         tri_strict = torch.ones(n, n, dtype=torch.bool, device=q.device).tril(-1)
         tri = torch.ones(n, n, dtype=torch.bool, device=q.device).tril()
+        # Gamma_t / Gamma_s, masked in the exponent: the upper triangle would overflow (and 0*inf -> NaN grads)
+        diff = G[:, :, None] - G[:, None, :]
+        decay = torch.exp(torch.where(tri, diff, torch.full_like(diff, float("-inf"))))
         kk = torch.matmul(kc, kc.transpose(1, 2))
         A = torch.where(tri_strict, decay * kk, torch.zeros_like(kk))
         eye = torch.eye(n, device=q.device, dtype=torch.float32).expand(H, n, n)

@@ -103,8 +103,9 @@ def affine_chunk_state_map(k: Tensor, v: Tensor, g: Tensor, beta: Tensor, *, chu
         vc = v[s:e].float().transpose(0, 1)
         bc = beta[s:e].float().transpose(0, 1)
         G = torch.cumsum(g[s:e].float().transpose(0, 1), -1)
-        decay = torch.exp(G[:, :, None] - G[:, None, :])
         strict = torch.ones(n, n, dtype=torch.bool, device=k.device).tril(-1)
+        diff = G[:, :, None] - G[:, None, :]
+        decay = torch.exp(torch.where(strict, diff, torch.full_like(diff, float("-inf"))))
         A = torch.where(strict, decay * torch.matmul(kc, kc.transpose(1, 2)), torch.zeros(1, device=k.device))
         eye = torch.eye(n, device=k.device).expand(H, n, n)
         T = torch.linalg.solve_triangular(eye + bc[:, :, None] * A, eye, upper=False)

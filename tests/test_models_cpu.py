@@ -1,0 +1,103 @@
+"""Hybrid GDN/attention and hybrid MoE models through TPR (GDN state relay) vs the flattened batch;
+checkpoint round trip; activation offload scope (CPU, FP32)."""
+
+import os
+
+import pytest
+import torch
+
+from bridge_b200.engine import EngineConfig, TPREngine
+from bridge_b200.models import get_config
+from bridge_b200.models.decoder import build_model
+from tests.helpers import flat_ppo_loss, rel_err, set_old_log_probs, tree_batch
+
+
+@pytest.mark.parametrize("preset", ["tiny_hybrid", "tiny_moe"])
+@pytest.mark.parametrize("executor,mode", [("forest", "retain"), ("forest", "recompute"), ("segment", "retain")])
+def test_hybrid_models_tpr_match_flattened(preset, executor, mode):
+    cfg = get_config(preset)
+    batch = tree_batch(n_trees=2, prefix=48, siblings=3, resp=16, seed=7)
+    ref = build_model(cfg, dtype=torch.float32, seed=0)
+    set_old_log_probs(ref, batch)
+    loss_ref, _ = flat_ppo_loss(ref, batch)
+    loss_ref.backward()
+    eng = TPREngine(cfg, EngineConfig(executor=executor, forest_mode=mode, token_budget=80), device="cpu",
+                    model=build_model(cfg, dtype=torch.float32, seed=0))
+    out = eng.forward_backward_batch(batch)
+    assert abs(out["loss"][0] - float(loss_ref)) < 1e-5 * max(1, abs(float(loss_ref)))
+    for n, p in eng.model.named_parameters():
+        g = dict(ref.named_parameters())[n].grad
+        if g is None:
+            assert float(p.main_grad.abs().max()) == 0.0, n
+            continue
+        assert rel_err(p.main_grad, g) < 2e-4, n
+
+
+def test_deep_session_tree_relays_through_three_levels():
+    """A multi-turn session: prompt -> turn1 fork -> turn2 fork (depth 3), exact trie."""
+    g = torch.Generator().manual_seed(11)
+    p = torch.randint(0, 1024, (24,), generator=g)
+    t1 = [torch.randint(0, 1024, (12,), generator=g) for _ in range(2)]
+    rows, masks = [], []
+    for a in range(2):
+        for b in range(2):
+            tail = torch.randint(0, 1024, (10,), generator=g)
+            ids = torch.cat([p, t1[a], tail])
+            rows.append(ids)
+            m = torch.zeros(22, dtype=torch.bool)
+            m[-10:] = True
+            m[2:8] = True
+            masks.append(m)
+    batch = {"input_ids": rows, "response_mask": masks, "old_log_probs": [torch.zeros(22)] * 4,
+             "advantages": [torch.randn(22, generator=g) for _ in range(4)], "uid": ["s"] * 4, "temperature": 1.0,
+             "dp_size": 1}
+    batch["batch_num_tokens"] = int(sum(int(m.sum()) for m in masks))
+    for preset in ("tiny", "tiny_hybrid"):
+        cfg = get_config(preset)
+        ref = build_model(cfg, dtype=torch.float32, seed=0)
+        set_old_log_probs(ref, batch)
+        loss_ref, _ = flat_ppo_loss(ref, batch)
+        loss_ref.backward()
+        for budget in (1000, 30):
+            eng = TPREngine(cfg, EngineConfig(token_budget=budget), device="cpu",
+                            model=build_model(cfg, dtype=torch.float32, seed=0))
+            out = eng.forward_backward_batch(batch)
+            assert out["metrics"]["tpr/physical_segments"] == [7]
+            assert abs(out["loss"][0] - float(loss_ref)) < 1e-5
+            for n, prm in eng.model.named_parameters():
+                gref = dict(ref.named_parameters())[n].grad
+                assert rel_err(prm.main_grad, gref) < 2e-4, (preset, budget, n)
+
+
+def test_checkpoint_round_trip(tmp_path):
+    from bridge_b200.models.checkpoint import hf_state_dict, load_checkpoint, save_checkpoint
+
+    for preset in ("tiny", "tiny_moe"):
+        cfg = get_config(preset)
+        eng = TPREngine(cfg, EngineConfig(), device="cpu", model=build_model(cfg, dtype=torch.float32, seed=1))
+        d = os.path.join(tmp_path, preset)
+        eng.optimizer.step_count = 7
+        save_checkpoint(d, eng, step=7)
+        eng2 = TPREngine(cfg, EngineConfig(), device="cpu", model=build_model(cfg, dtype=torch.float32, seed=2))
+        assert load_checkpoint(d, eng2) == 7 and eng2.optimizer.step_count == 7
+        a, b = hf_state_dict(eng.model), hf_state_dict(eng2.model)
+        assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
+        if preset == "tiny":
+            assert "model.layers.0.self_attn.q_proj.weight" in a and "model.layers.1.mlp.down_proj.weight" in a
+
+
+def test_activation_offload_scope_preserves_gradients():
+    from bridge_b200.tpr.activation_offload import OffloadConfig, offload_scope
+
+    cfg = get_config("tiny")
+    model = build_model(cfg, dtype=torch.float32, seed=0)
+    ids = torch.randint(0, 1024, (40,))
+    pos = torch.arange(40)
+    model(ids, pos).pow(2).mean().backward()
+    ref = {n: p.grad.clone() for n, p in model.named_parameters()}
+    model.zero_grad()
+    with offload_scope(model, OffloadConfig(enabled=True, min_bytes=1)) as off:
+        model(ids, pos).pow(2).mean().backward()
+    assert off.offloaded_bytes > 0
+    for n, p in model.named_parameters():
+        assert torch.allclose(p.grad, ref[n], atol=1e-6), n
