@@ -44,6 +44,20 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
                                                torch::Tensor cu, torch::Tensor poff, torch::Tensor plen,
                                                int64_t max_seqlen, int64_t max_prefix, double scale);
 
+std::vector<torch::Tensor> causal_conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                                             c10::optional<torch::Tensor> h0, torch::Tensor cu, int64_t max_len,
+                                             bool silu_act);
+std::vector<torch::Tensor> causal_conv1d_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w,
+                                             c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> h0,
+                                             c10::optional<torch::Tensor> dhT, torch::Tensor cu, int64_t max_len,
+                                             bool silu_act);
+std::vector<torch::Tensor> gdr_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                                   torch::Tensor beta, c10::optional<torch::Tensor> h0, torch::Tensor cu,
+                                   int64_t max_len, double scale, int64_t chunk);
+std::vector<torch::Tensor> gdr_bwd(torch::Tensor dout, c10::optional<torch::Tensor> dhT, torch::Tensor q,
+                                   torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                                   torch::Tensor ckpt, torch::Tensor cu, int64_t max_len, bool has_h0, double scale);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bridge_b200 sm_100a kernels";
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
@@ -62,6 +76,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tree_attn_fwd_sm100", &tree_attn_fwd_sm100, "tcgen05 tree attention forward (head_dim 128)");
   m.def("attn_error_code", &attn_error_code);
   m.def("tree_attn_bwd_sm100", &tree_attn_bwd_sm100, "tcgen05 tree attention backward (head_dim 128)");
+  m.def("causal_conv1d_fwd", &causal_conv1d_fwd);
+  m.def("causal_conv1d_bwd", &causal_conv1d_bwd);
+  m.def("gdr_fwd", &gdr_fwd, "chunked gated delta rule forward (returns o, final state, chunk checkpoints)");
+  m.def("gdr_bwd", &gdr_bwd, "chunked gated delta rule backward");
   m.def("gemm", &gemm, "tcgen05 GEMM: C (+)= op(A) op(B)^T");
   m.def("gemm_error_code", &gemm_error_code);
   m.def("launch_count", &bb_launch_count,

@@ -65,20 +65,23 @@ class _ConvFn(torch.autograd.Function):
     def forward(ctx, x, weight, bias, h0, cu_dev, cu_host, activation):
         m = kernels()
         x = x.contiguous()
-        y, hT = m.causal_conv1d_fwd(x, weight.contiguous(), bias, h0, cu_dev, bool(activation))
-        ctx.save_for_backward(x, weight, bias, h0, cu_dev)
-        ctx.activation = activation
-        return y, hT
+        max_len = max(b - a for a, b in zip(cu_host[:-1], cu_host[1:]))
+        h0c = h0.contiguous() if h0 is not None else None
+        y, hT = m.causal_conv1d_fwd(x, weight.contiguous(), bias, h0c, cu_dev, max_len, bool(activation))
+        ctx.save_for_backward(x, weight, bias, h0c, cu_dev)
+        ctx.activation, ctx.max_len = activation, max_len
+        ctx.h0_dtype = None if h0 is None else h0.dtype
+        return y, hT.to(x.dtype)
 
     @staticmethod
     def backward(ctx, dy, dhT):
         m = kernels()
         x, weight, bias, h0, cu = ctx.saved_tensors
         dx, dw, db, dh0 = m.causal_conv1d_bwd(dy.contiguous(), x, weight.contiguous(), bias, h0,
-                                              dhT.contiguous() if dhT is not None else None, cu,
+                                              dhT.contiguous() if dhT is not None else None, cu, ctx.max_len,
                                               bool(ctx.activation))
         return dx, dw.to(weight.dtype), (db.to(bias.dtype) if bias is not None else None), \
-            (dh0 if h0 is not None else None), None, None, None
+            (dh0.to(ctx.h0_dtype) if h0 is not None else None), None, None, None
 
 
 def causal_conv1d(x: Tensor, weight: Tensor, bias: Tensor | None, cu_seqlens: list[int], cu_dev: Tensor | None,
@@ -158,30 +161,42 @@ def chunk_gated_delta_rule_reference(q, k, v, g, beta, cu_seqlens: list[int], in
 
 class _GDRFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, g, beta, h0, cu_dev, scale, chunk):
+    def forward(ctx, q, k, v, g, beta, h0, cu_dev, cu_host, scale, chunk):
         m = kernels()
-        q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
-        o, hT = m.gdr_fwd(q, k, v, g.float(), beta.float(), h0, cu_dev, float(scale), int(chunk))
-        ctx.save_for_backward(q, k, v, g, beta, h0, cu_dev)
-        ctx.scale, ctx.chunk = scale, chunk
+        q, k, v = (t.contiguous() for t in (q, k, v))
+        gf, bf = g.float().contiguous(), beta.float().contiguous()
+        max_len = max(b - a for a, b in zip(cu_host[:-1], cu_host[1:]))
+        o, hT, ckpt = m.gdr_fwd(q, k, v, gf, bf, h0, cu_dev, max_len, float(scale), int(chunk))
+        ctx.save_for_backward(q, k, v, gf, bf, ckpt, cu_dev)
+        ctx.scale, ctx.max_len, ctx.has_h0 = scale, max_len, h0 is not None
+        ctx.dtypes = (g.dtype, beta.dtype, None if h0 is None else h0.dtype)
         return o, hT
 
     @staticmethod
     def backward(ctx, do, dhT):
         m = kernels()
-        q, k, v, g, beta, h0, cu = ctx.saved_tensors
+        q, k, v, g, beta, ckpt, cu = ctx.saved_tensors
         dq, dk, dv, dg, db, dh0 = m.gdr_bwd(do.contiguous(), dhT.contiguous() if dhT is not None else None,
-                                            q, k, v, g.float(), beta.float(), h0, cu, float(ctx.scale),
-                                            int(ctx.chunk))
-        return dq, dk, dv, dg.to(g.dtype), db.to(beta.dtype), (dh0 if h0 is not None else None), None, None, None
+                                            q, k, v, g, beta, ckpt, cu, ctx.max_len, ctx.has_h0, float(ctx.scale))
+        gdt, bdt, hdt = ctx.dtypes
+        return (dq.to(q.dtype), dk.to(k.dtype), dv, dg.to(gdt), db.to(bdt),
+                (dh0.to(hdt) if ctx.has_h0 else None), None, None, None, None)
 
 
 def chunk_gated_delta_rule(q, k, v, g, beta, cu_seqlens: list[int], cu_dev: Tensor | None,
                            initial_state: Tensor | None, *, scale: float, chunk_size: int = 64):
-    if on_gpu(q) and hasattr(kernels(), "gdr_fwd"):
+    """Packed varlen chunked gated delta rule; ``o [T,H,V]`` (q dtype) and final state ``[B,H,K,V]`` FP32.
+
+    On CUDA this runs the chunked kernel (bf16; key dim 32/64/128; value dim a multiple of 32).  The
+    kernel always works in 64-token chunks: the chunking changes rounding only, not the result, so
+    ``chunk_size`` applies to the PyTorch path.
+    """
+    if on_gpu(q):
+        if q.shape[-1] not in (32, 64, 128) or v.shape[-1] % 32 or q.dtype != torch.bfloat16:
+            raise NotImplementedError("gated delta rule kernel: bf16, key dim 32/64/128, value dim %32")
         if cu_dev is None:
             cu_dev = torch.tensor(cu_seqlens, dtype=torch.int32, device=q.device)
-        return _GDRFn.apply(q, k, v, g, beta, initial_state, cu_dev, scale, chunk_size)
+        return _GDRFn.apply(q, k, v, g, beta, initial_state, cu_dev, tuple(cu_seqlens), scale, 64)
     return chunk_gated_delta_rule_reference(q, k, v, g, beta, cu_seqlens, initial_state, scale=scale,
                                             chunk_size=chunk_size)
 
