@@ -52,6 +52,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--mode", default=os.environ.get("TPR_FOREST_MODE", "retain"))
     p.add_argument("--tp", type=int, default=1)
     p.add_argument("--cp", type=int, default=1)
+    p.add_argument("--dp-comm", default="auto", choices=["auto", "nvlink", "nccl"],
+                   help="DP gradient path: fused NVLink P2P kernels + sharded optimizer, or NCCL all-reduce")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
@@ -161,7 +163,7 @@ def main() -> None:
     cfg = get_config(args.model)
     ec = EngineConfig(tensor_model_parallel_size=args.tp, context_parallel_size=args.cp,
                       token_budget=args.token_budget, forest_mode=args.mode,
-                      tpr_cp_backend="ring" if args.cp > 1 else None)
+                      tpr_cp_backend="ring" if args.cp > 1 else None, dp_comm=args.dp_comm)
     eng = TPREngine(cfg, ec, AdamWConfig(lr=1e-6), device=dev, seed=args.seed)
     dp = eng.parallel.dp
     batch = synthetic_batch(args, eng.parallel.dp_rank, dp, cfg.vocab_size, device_pin=True)
@@ -243,6 +245,7 @@ def main() -> None:
                 "trees": args.trees_per_gpu * dp, "prefix": args.prefix, "siblings": args.siblings,
                 "response": args.resp, "ppo_tokens_per_step": ppo_tokens_global, "forest_mode": args.mode,
                 "token_budget": args.token_budget,
+                "dp_comm": "nvlink-p2p-fused" if eng.symm_heap is not None else ("nccl" if world > 1 else "none"),
                 "l2": "no flush: every step streams 8 GB of bf16 weights and GB-scale activations (>> 126 MB L2)",
             },
             "clocks": clocks,
@@ -252,6 +255,9 @@ def main() -> None:
             "impl": "bridge_b200",
         }
         print(json.dumps(line), flush=True)
+    if eng.symm_heap is not None:
+        eng.symm_heap.check()
+        eng.symm_heap.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

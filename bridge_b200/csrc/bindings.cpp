@@ -57,6 +57,25 @@ std::vector<torch::Tensor> gdr_fwd(torch::Tensor q, torch::Tensor k, torch::Tens
 std::vector<torch::Tensor> gdr_bwd(torch::Tensor dout, c10::optional<torch::Tensor> dhT, torch::Tensor q,
                                    torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                                    torch::Tensor ckpt, torch::Tensor cu, int64_t max_len, bool has_h0, double scale);
+std::vector<torch::Tensor> symm_alloc(int64_t nbytes);
+int64_t symm_open(torch::Tensor handle);
+void symm_close(int64_t ptr);
+int64_t symm_pad_bytes();
+void symm_barrier(std::vector<int64_t> pads, int64_t rank, int64_t epoch, c10::optional<torch::Tensor> payload,
+                  double timeout_s);
+void dp_reduce_scatter(std::vector<int64_t> grads, int64_t rank, int64_t offset, int64_t count, double scale,
+                       torch::Tensor partials);
+void dp_adamw_allgather(torch::Tensor master, torch::Tensor m, torch::Tensor v, torch::Tensor grad_shard,
+                        std::vector<int64_t> data, int64_t offset, bool bf16_params, int64_t pad_ptr, double max_norm,
+                        double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
+                        torch::Tensor norm_out);
+int64_t symm_error_code();
+torch::Tensor tp_ag_gemm(torch::Tensor gather, torch::Tensor b, bool b_mn, std::vector<int64_t> peers, int64_t rank,
+                         int64_t ms, torch::Tensor counters, double timeout_s);
+void tp_gemm_rs(torch::Tensor a, torch::Tensor b, bool b_mn, std::vector<int64_t> peers, int64_t rank, int64_t ms,
+                double timeout_s);
+torch::Tensor tp_sum_slots(torch::Tensor recv, int64_t n, int64_t ms, int64_t N);
+void symm_clear_error();
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bridge_b200 sm_100a kernels";
@@ -80,6 +99,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("causal_conv1d_bwd", &causal_conv1d_bwd);
   m.def("gdr_fwd", &gdr_fwd, "chunked gated delta rule forward (returns o, final state, chunk checkpoints)");
   m.def("gdr_bwd", &gdr_bwd, "chunked gated delta rule backward");
+  m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle (symmetric peer memory)");
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_pad_bytes", &symm_pad_bytes);
+  m.def("symm_barrier", &symm_barrier, "cross-GPU barrier over peer signal pads (bounded wait)");
+  m.def("dp_reduce_scatter", &dp_reduce_scatter, "P2P-load reduce-scatter of FP32 gradients with scale");
+  m.def("dp_adamw_allgather", &dp_adamw_allgather, "AdamW on the local shard + P2P-store parameter all-gather");
+  m.def("symm_error_code", &symm_error_code);
+  m.def("symm_clear_error", &symm_clear_error);
+  m.def("tp_ag_gemm", &tp_ag_gemm, "all-gather (P2P pull inside the kernel) + tcgen05 GEMM");
+  m.def("tp_gemm_rs", &tp_gemm_rs, "tcgen05 GEMM + reduce-scatter (epilogue P2P stores to row owners)");
+  m.def("tp_sum_slots", &tp_sum_slots);
   m.def("gemm", &gemm, "tcgen05 GEMM: C (+)= op(A) op(B)^T");
   m.def("gemm_error_code", &gemm_error_code);
   m.def("launch_count", &bb_launch_count,

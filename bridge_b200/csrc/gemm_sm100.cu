@@ -392,3 +392,396 @@ torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, c10::
 }
 
 int64_t gemm_error_code() { return error_word().item<int>(); }
+
+// ================================================================================================
+// Tensor-parallel GEMMs fused with their collective over NVLink peer memory (sequence parallel).
+//
+//   AG mode  C[M, N] = A_full[M, K] B^T, where rank j holds rows [j*Ms, (j+1)*Ms) of A in its
+//            symmetric staging buffer.  At kernel start the four epilogue warps of every CTA pull
+//            the peers' rows into the local A_full buffer (16-byte P2P loads, each remote row crosses
+//            NVLink once) and bump a per-M-tile counter; the TMA producer issues A loads for a tile
+//            only when its counter shows all remote rows present.  Tiles run local-rows-first, so the
+//            pull overlaps the MMAs of the local tiles.
+//   RS mode  C_partial = A B^T; the epilogue stores every output row straight into the receive slot
+//            of the rank that owns it (bf16, 16-byte P2P stores), peer-owned tiles first, so the
+//            reduce-scatter traffic overlaps the remaining MMAs.  The owner sums its slots after a
+//            barrier (tp_sum_slots).
+//
+// Parity: Megatron sequence-parallel ColumnParallelLinear (all-gather -> GEMM) and
+// RowParallelLinear (GEMM -> reduce-scatter) used by the reference's TP2 path
+// (verl/models/mcore/tpr/attention.py:117-126, 195-221).
+// ================================================================================================
+namespace {
+
+struct TpArgs {
+  void* peer[8];          // AG: peers' staging [Ms, K]; RS: peers' receive buffers [n, Ms, N]
+  int n, rank, Ms;
+  int* counters;          // AG: rows copied per M-tile
+  __nv_bfloat16* gather;  // AG: local A_full [M, K]
+  long lda;               // AG: row stride (elements) of staging and A_full
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ uint64_t tp_now() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// remote rows of A that fall in M-tile mt (rows not owned by `rank`)
+__device__ __forceinline__ int tp_expected(int mt, int M, int Ms, int rank) {
+  const int lo = mt * BM, hi = min(M, lo + BM);
+  const int own_lo = max(lo, rank * Ms), own_hi = min(hi, (rank + 1) * Ms);
+  return (hi - lo) - max(0, own_hi - own_lo);
+}
+
+template <int MODE, bool B_MN>  // MODE 1: all-gather A then GEMM; MODE 2: GEMM then reduce-scatter rows
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tp_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, void* C,
+                   int M, int N, int K, long ldc, int* err, const __grid_constant__ TpArgs tp) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem + SmemLayout::A_OFF;
+  unsigned char* sB = smem + SmemLayout::B_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int nk = (K + BK - 1) / BK;
+  // first M-tile in the schedule: the local shard (AG) or the next rank's shard (RS)
+  const int first_row = MODE == 1 ? tp.rank * tp.Ms : ((tp.rank + 1) % tp.n) * tp.Ms;
+  const int shift = min(first_row / BM, m_tiles - 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tfull[a], 1);
+      sm100::mbar_init(&tempty[a], 128);
+    }
+    sm100::fence_mbar_init();
+    sm100::prefetch_tmap(&tmap_a);
+    sm100::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, TMEM_COLS);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto tile_coords = [&](int t, int& m0, int& n0, int& mt) {
+    const int group = 8;
+    const int per_group = group * n_tiles;
+    const int g = t / per_group;
+    const int first_m = g * group;
+    const int gm = min(group, m_tiles - first_m);
+    const int r = t % per_group;
+    mt = (first_m + r % gm + shift) % m_tiles;
+    m0 = mt * BM;
+    n0 = (r / gm) * BN;
+  };
+
+  constexpr uint32_t IDESC = sm100::umma_idesc_bf16(BM, BN, false, B_MN);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int ready_mt = -1;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int m0, n0, mt;
+        tile_coords(t, m0, n0, mt);
+        if (MODE == 1 && mt != ready_mt) {
+          const int want = tp_expected(mt, M, tp.Ms, tp.rank);
+          const uint64_t t0 = tp_now();
+          while (ld_acquire_gpu(tp.counters + mt) < want) {
+            if (tp_now() - t0 > tp.timeout_ns) {
+              atomicCAS(err, 0, 20);
+              ok = false;
+              break;
+            }
+            __nanosleep(128);
+          }
+          if (!ok) break;
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          ready_mt = mt;
+        }
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait(&empty[stage], phase ^ 1, err, 1)) {
+            ok = false;
+            break;
+          }
+          sm100::mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          unsigned char* a_dst = sA + stage * A_BYTES;
+          unsigned char* b_dst = sB + stage * B_BYTES;
+          sm100::tma_load_2d(a_dst, &tmap_a, &full[stage], kb * BK, m0);
+          if (B_MN) {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i)
+              sm100::tma_load_2d(b_dst + i * 8192, &tmap_b, &full[stage], n0 + 64 * i, kb * BK);
+          } else {
+            sm100::tma_load_2d(b_dst, &tmap_b, &full[stage], kb * BK, n0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!sm100::mbar_wait(&tempty[acc], acc_phase ^ 1, err, 2)) break;
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait(&full[stage], phase, err, 3)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t a_base = sm100::smem_addr(sA + stage * A_BYTES);
+          const uint32_t b_base = sm100::smem_addr(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sm100::umma_desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sm100::umma_desc_sw128(b_base + kk * 2048, 8192, 1024)
+                                     : sm100::umma_desc_sw128(b_base + kk * 32, 16, 1024);
+            sm100::umma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+          }
+          sm100::umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        sm100::umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    if (MODE == 1) {
+      // ---- pull the peers' rows of A into the local gather buffer, local-first tile order
+      const int gw = blockIdx.x * 4 + (warp - 2), nw = gridDim.x * 4;
+      const int vecs = K / 8;
+      for (int idx = gw; idx < M; idx += nw) {
+        const int row = (idx + tp.rank * tp.Ms) % M;
+        const int owner = min(row / tp.Ms, tp.n - 1);
+        if (owner == tp.rank) continue;
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(tp.peer[owner]) +
+                                                          (size_t)(row - owner * tp.Ms) * tp.lda);
+        uint4* dst = reinterpret_cast<uint4*>(tp.gather + (size_t)row * tp.lda);
+        for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(tp.counters + row / BM, 1);
+      }
+    }
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int m0, n0, mt;
+      tile_coords(t, m0, n0, mt);
+      const bool got = sm100::mbar_wait(&tfull[acc], acc_phase, err, 4);
+      if (!__all_sync(0xffffffffu, got)) break;
+      sm100::tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      __nv_bfloat16* dst_row = nullptr;
+      if (row < M) {
+        if (MODE == 2) {
+          const int owner = min(row / tp.Ms, tp.n - 1);
+          dst_row = static_cast<__nv_bfloat16*>(tp.peer[owner]) +
+                    ((size_t)tp.rank * tp.Ms + (row - owner * tp.Ms)) * (size_t)N;
+        } else {
+          dst_row = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc;
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(t_row + c * 32, r);
+        sm100::tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (dst_row && col0 < N) {
+          __nv_bfloat16* dst = dst_row + col0;
+          if (col0 + 32 <= N) {
+            uint32_t p[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+              p[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<uint4*>(dst)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = __float2bfloat16(__uint_as_float(r[j]));
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int MODE, bool B_MN>
+void tp_launch(const MapPair* maps, void* c, int M, int N, int K, long ldc, const TpArgs& tp) {
+  auto kern = tp_gemm_kernel<MODE, B_MN>;
+  const int smem = SmemLayout::TOTAL + 1024;
+  static bool attr = false;
+  if (!attr) {
+    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  // AG: every CTA must be resident (CTAs wait on rows copied by other CTAs): at most one per SM
+  const int grid = std::max(1, std::min(tiles, num_sms()));
+  int* err = error_word().data_ptr<int>();
+  void* args[] = {const_cast<CUtensorMap*>(&maps->a), const_cast<CUtensorMap*>(&maps->b), &c, &M, &N, &K, &ldc,
+                  &err, const_cast<TpArgs*>(&tp)};
+  BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NUM_THREADS), args, smem,
+                                 at::cuda::getCurrentCUDAStream()));
+  BB_POST_LAUNCH();
+}
+
+__global__ void tp_sum_slots_kernel(const uint4* __restrict__ recv, uint4* __restrict__ out, int n, size_t vecs) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < vecs; i += stride) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < n; ++s) {
+      bb::bf16x8 v = reinterpret_cast<const bb::bf16x8*>(recv)[(size_t)s * vecs + i];
+      float f[8];
+      bb::unpack8(v, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += f[e];
+    }
+    reinterpret_cast<bb::bf16x8*>(out)[i] = bb::pack8(acc);
+  }
+}
+
+TpArgs make_tp_args(const std::vector<int64_t>& peers, int64_t rank, int64_t ms, double timeout_s) {
+  TORCH_CHECK(!peers.empty() && peers.size() <= 8, "tp gemm: 1..8 ranks");
+  TORCH_CHECK(rank >= 0 && rank < (int64_t)peers.size() && ms > 0, "tp gemm: bad rank / rows per rank");
+  TpArgs tp{};
+  for (size_t i = 0; i < peers.size(); ++i) {
+    TORCH_CHECK(peers[i] % 16 == 0, "tp gemm: peer buffers must be 16-byte aligned");
+    tp.peer[i] = reinterpret_cast<void*>(peers[i]);
+  }
+  tp.n = (int)peers.size();
+  tp.rank = (int)rank;
+  tp.Ms = (int)ms;
+  tp.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  return tp;
+}
+
+void tp_context(int dev) {
+  at::cuda::CUDAGuard guard(dev);
+  CUcontext cur = nullptr;
+  if (cuCtxGetCurrent(&cur) != CUDA_SUCCESS || cur == nullptr) BB_CHECK_CUDA(cudaFree(nullptr));
+}
+
+}  // namespace
+
+// AG + GEMM: `gather` [M, K] bf16 holds this rank's rows already; the kernel pulls the others from the
+// peers' staging buffers (`peers[j]` = rank j's [Ms, K] staging) and returns C = gather @ op(B)^T.
+torch::Tensor tp_ag_gemm(torch::Tensor gather, torch::Tensor b, bool b_mn, std::vector<int64_t> peers, int64_t rank,
+                         int64_t ms, torch::Tensor counters, double timeout_s) {
+  TORCH_CHECK(gather.is_cuda() && gather.scalar_type() == at::kBFloat16 && gather.is_contiguous(), "tp_ag_gemm: A");
+  TORCH_CHECK(b.scalar_type() == at::kBFloat16 && b.stride(1) == 1, "tp_ag_gemm: B");
+  const long M = gather.size(0), K = gather.size(1);
+  const long N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K && K % 8 == 0 && b.stride(0) % 8 == 0, "tp_ag_gemm: shapes");
+  TORCH_CHECK(M <= (long)ms * (long)peers.size(), "tp_ag_gemm: M exceeds ranks x rows per rank");
+  const int m_tiles = (int)((M + BM - 1) / BM);
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= m_tiles,
+              "tp_ag_gemm: counters");
+  auto c = torch::empty({M, N}, gather.options());
+  tp_context(gather.get_device());
+  counters.zero_();
+  TpArgs tp = make_tp_args(peers, rank, ms, timeout_s);
+  tp.counters = counters.data_ptr<int>();
+  tp.gather = reinterpret_cast<__nv_bfloat16*>(gather.data_ptr());
+  tp.lda = K;
+  MapPair* maps = map_storage();
+  make_map(&maps->a, gather.data_ptr(), M, K, K, BM);
+  if (b_mn) make_map(&maps->b, b.data_ptr(), K, N, b.stride(0), 64);
+  else make_map(&maps->b, b.data_ptr(), N, K, b.stride(0), BN);
+  if (b_mn) tp_launch<1, true>(maps, c.data_ptr(), (int)M, (int)N, (int)K, N, tp);
+  else tp_launch<1, false>(maps, c.data_ptr(), (int)M, (int)N, (int)K, N, tp);
+  return c;
+}
+
+// GEMM + RS: C_partial = A @ op(B)^T with row r stored into the receive buffer of rank r / Ms,
+// slot `rank` (`peers[j]` = rank j's [n, Ms, N] bf16 receive buffer).
+void tp_gemm_rs(torch::Tensor a, torch::Tensor b, bool b_mn, std::vector<int64_t> peers, int64_t rank, int64_t ms,
+                double timeout_s) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.stride(1) == 1 && a.stride(0) % 8 == 0,
+              "tp_gemm_rs: A");
+  TORCH_CHECK(b.scalar_type() == at::kBFloat16 && b.stride(1) == 1 && b.stride(0) % 8 == 0, "tp_gemm_rs: B");
+  const long M = a.size(0), K = a.size(1);
+  const long N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K && N % 8 == 0, "tp_gemm_rs: shapes (N must be a multiple of 8)");
+  TORCH_CHECK(M <= (long)ms * (long)peers.size(), "tp_gemm_rs: M exceeds ranks x rows per rank");
+  if (M == 0 || N == 0) return;
+  tp_context(a.get_device());
+  TpArgs tp = make_tp_args(peers, rank, ms, timeout_s);
+  MapPair* maps = map_storage();
+  make_map(&maps->a, a.data_ptr(), M, K, a.stride(0), BM);
+  if (b_mn) make_map(&maps->b, b.data_ptr(), K, N, b.stride(0), 64);
+  else make_map(&maps->b, b.data_ptr(), N, K, b.stride(0), BN);
+  if (b_mn) tp_launch<2, true>(maps, nullptr, (int)M, (int)N, (int)K, N, tp);
+  else tp_launch<2, false>(maps, nullptr, (int)M, (int)N, (int)K, N, tp);
+}
+
+// out[Ms, N] = sum over the n slots of recv[n, Ms, N] (FP32 accumulation, bf16 out)
+torch::Tensor tp_sum_slots(torch::Tensor recv, int64_t n, int64_t ms, int64_t N) {
+  TORCH_CHECK(recv.is_cuda() && recv.scalar_type() == at::kBFloat16 && recv.numel() >= n * ms * N && N % 8 == 0,
+              "tp_sum_slots: recv");
+  auto out = torch::empty({ms, N}, recv.options());
+  const size_t vecs = (size_t)ms * N / 8;
+  const int blocks = (int)std::min<size_t>((vecs + 255) / 256, (size_t)num_sms() * 8);
+  tp_sum_slots_kernel<<<std::max(blocks, 1), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint4*>(recv.data_ptr()), reinterpret_cast<uint4*>(out.data_ptr()), (int)n, vecs);
+  BB_POST_LAUNCH();
+  return out;
+}

@@ -45,6 +45,12 @@ class EngineConfig:
     exec_profile: bool = False
     mem_trace: bool = False
     grad_comm_dtype: str = "bf16"
+    # data-parallel gradient path: "auto" (NVLink P2P kernels + sharded optimizer on a single-node
+    # CUDA group, NCCL otherwise), "nvlink" or "nccl"
+    dp_comm: str = "auto"
+    # sequence-parallel TP linears: "auto" (all-gather / reduce-scatter fused into the tcgen05 GEMM over
+    # NVLink on a single-node CUDA group, NCCL otherwise), "nvlink" or "nccl"
+    tp_comm: str = "auto"
     extra: dict = field(default_factory=dict)
 
     def with_env(self) -> "EngineConfig":
@@ -66,9 +72,17 @@ class EngineConfig:
             kw["token_budget"] = _env_int("TPR_TOKEN_BUDGET", self.token_budget)
         if "TPR_EXECUTOR" in os.environ:
             kw["executor"] = os.environ["TPR_EXECUTOR"]
+        if "TPR_TP_COMM" in os.environ:
+            kw["tp_comm"] = os.environ["TPR_TP_COMM"]
+        if "TPR_DP_COMM" in os.environ:
+            kw["dp_comm"] = os.environ["TPR_DP_COMM"]
         cfg = replace(self, **kw) if kw else self
         if cfg.tree_policy not in ("exact", "qwen_turn"):
             raise ValueError(f"unknown TPR tree_policy: {cfg.tree_policy!r}")
+        if cfg.tp_comm not in ("auto", "nvlink", "nccl"):
+            raise ValueError(f"unknown tp_comm: {cfg.tp_comm!r}")
+        if cfg.dp_comm not in ("auto", "nvlink", "nccl"):
+            raise ValueError(f"unknown dp_comm: {cfg.dp_comm!r}")
         if cfg.log_prob_chunk_tokens < 0:
             raise ValueError("TPR_PPO_LOGPROB_CHUNK_TOKENS must be nonnegative")
         if cfg.turn_min_segment_tokens < 1:

@@ -27,6 +27,22 @@ from .config import EngineConfig
 from .optim import AdamWConfig, MixedPrecisionAdamW
 
 
+def _use_nvlink_dp(mode: str, device: torch.device, group) -> bool:
+    """The fused NVLink data-parallel path needs CUDA, a single-node group of 2..8 ranks."""
+    import os
+
+    import torch.distributed as dist
+
+    if mode == "nccl" or device.type != "cuda" or group is None:
+        return False
+    n = dist.get_world_size(group)
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", dist.get_world_size()))
+    ok = 1 < n <= 8 and local >= dist.get_world_size()
+    if mode == "nvlink" and not ok:
+        raise ValueError("dp_comm='nvlink' needs a single-node data-parallel group of 2..8 GPUs")
+    return ok
+
+
 class TPREngine:
     def __init__(self, model_config: ModelConfig, engine_config: EngineConfig = EngineConfig(),
                  optim_config: AdamWConfig = AdamWConfig(), *, device=None, seed: int = 0,
@@ -39,6 +55,9 @@ class TPREngine:
         self.parallel = parallel_state or build_parallel_state(ec.tensor_model_parallel_size,
                                                                ec.context_parallel_size,
                                                                ec.expert_model_parallel_size)
+        from ..parallel.tp_fused import set_tp_comm_mode
+
+        set_tp_comm_mode(ec.tp_comm)
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
@@ -50,12 +69,21 @@ class TPREngine:
                 sequence_parallel=ec.sequence_parallel, ep_group=self.parallel.ep_group))
             model = provider()
         self.module = [model]
-        self.optimizer = MixedPrecisionAdamW(model, optim_config)
         grad_group = self.parallel.dp_cp_group if (self.parallel.dp * self.parallel.cp) > 1 else None
         if self.parallel.tp == 1 and grad_group is None and self.parallel.dp > 1:
             grad_group = self.parallel.dp_group
         comm = torch.bfloat16 if ec.grad_comm_dtype == "bf16" else torch.float32
-        self.grad_reducer = DataParallelGradReducer(grad_group, comm_dtype=comm)
+        self.symm_heap = None
+        if _use_nvlink_dp(ec.dp_comm, self.device, grad_group):
+            from ..parallel.symmetric import SymmetricHeap
+            from .optim import ShardedNVLinkAdamW
+
+            self.symm_heap = SymmetricHeap(grad_group, self.device)
+            self.optimizer = ShardedNVLinkAdamW(model, optim_config, self.symm_heap)
+            self.grad_reducer = DataParallelGradReducer(None)   # reduction happens inside optimizer.step()
+        else:
+            self.optimizer = MixedPrecisionAdamW(model, optim_config)
+            self.grad_reducer = DataParallelGradReducer(grad_group, comm_dtype=comm)
         self.enable_routing_replay = False
         self.last_metrics: dict[str, Any] = {}
 
@@ -93,4 +121,6 @@ class TPREngine:
     def train_step(self, data: Any, loss_function=None) -> dict:
         out = self.forward_backward_batch(data, loss_function)
         out["grad_norm"] = self.optimizer_step()
+        if self.symm_heap is not None:
+            self.symm_heap.check()
         return out

@@ -130,6 +130,12 @@ class ColumnParallelLinear(nn.Module):
         self.weight.tp_split_dim = 0  # type: ignore[attr-defined]
 
     def forward(self, x: Tensor) -> Tensor:
+        if self.sp and x.dim() == 2:
+            from .tp_fused import ag_linear, fused_comm
+
+            comm = fused_comm(self.group, x)
+            if comm is not None:
+                return ag_linear(x, self.weight, comm)      # all-gather fused into the GEMM
         x = gather_from_sp(x, self.group) if self.sp else copy_to_tp(x, self.group)
         return linear(x, self.weight)
 
@@ -149,6 +155,12 @@ class RowParallelLinear(nn.Module):
         self.weight.tp_split_dim = 1  # type: ignore[attr-defined]
 
     def forward(self, x: Tensor) -> Tensor:
+        if self.sp and x.dim() == 2:
+            from .tp_fused import fused_comm, linear_rs
+
+            comm = fused_comm(self.group, x)
+            if comm is not None:
+                return linear_rs(x, self.weight, comm)      # reduce-scatter fused into the GEMM epilogue
         y = linear(x, self.weight)
         return reduce_scatter_to_sp(y, self.group) if self.sp else reduce_from_tp(y, self.group)
 

@@ -1,0 +1,163 @@
+"""Sequence-parallel TP linears whose collective is fused into the tcgen05 GEMM over NVLink.
+
+* :func:`ag_linear` (column-parallel): ``y[M, N/tp] = all_gather(x[M/tp, K]) @ W^T`` in ONE kernel --
+  the GEMM pulls the peers' token rows into a local buffer itself (P2P loads) while its first
+  tiles run on the local rows.  Backward: ``dx`` = GEMM + reduce-scatter kernel, ``dW`` accumulates
+  ``dy^T x_full`` into the FP32 main gradient.
+* :func:`linear_rs` (row-parallel): ``y[M/tp, N] = reduce_scatter(x[M, K/tp] @ W^T)``: the GEMM epilogue
+  stores each output row into its owner's receive slot (P2P stores); the owner sums the slots.
+  Backward: ``dx`` = all-gather + GEMM kernel on ``dy``, ``dW`` from the gathered ``dy``.
+
+Each call uses one of two symmetric workspaces (alternating) and exactly one cross-GPU barrier:
+before the kernel for the all-gather (every rank's staging is written), after it for the
+reduce-scatter (every slot has landed).  With two alternating buffers that one barrier also
+guarantees no rank overwrites a buffer a peer is still reading from the call before.  Every TP
+rank must make the same sequence of calls (true for SPMD model code).
+
+Parity: Megatron sequence-parallel ColumnParallelLinear / RowParallelLinear as used by the
+reference's TP2 path (verl/models/mcore/tpr/attention.py:117-126, 195-221).
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from ..ops._ext import kernels
+from ..ops.gemm import gemm
+
+_MODE = os.environ.get("TPR_TP_COMM", "auto")  # auto | nvlink | nccl
+_COMMS: dict = {}
+
+
+def set_tp_comm_mode(mode: str) -> None:
+    global _MODE
+    if mode not in ("auto", "nvlink", "nccl"):
+        raise ValueError(f"unknown tp_comm mode {mode!r}")
+    _MODE = mode
+
+
+class TPFusedComm:
+    def __init__(self, group, device: torch.device, capacity_bytes: int = 64 << 20,
+                 timeout_s: float = 60.0) -> None:
+        from .symmetric import SymmetricHeap
+
+        self.group = group
+        self.heap = SymmetricHeap(group, device, timeout_s=timeout_s)
+        self.n, self.rank = self.heap.size, self.heap.rank
+        self.capacity = capacity_bytes
+        self.timeout_s = timeout_s
+        self.bufs = [self.heap.alloc(capacity_bytes), self.heap.alloc(capacity_bytes)]
+        self.calls = 0
+        self.counters = torch.zeros(8192, dtype=torch.int32, device=device)
+
+    def _next(self, nbytes: int):
+        if nbytes > self.capacity:      # same shapes on every TP rank -> every rank grows together
+            torch.cuda.synchronize()
+            self.heap.barrier()
+            self.capacity = max(nbytes, 2 * self.capacity)
+            self.bufs = [self.heap.alloc(self.capacity), self.heap.alloc(self.capacity)]
+        buf = self.bufs[self.calls % 2]
+        self.calls += 1
+        return buf
+
+    def ag_gemm(self, x_local: Tensor, w: Tensor, *, b_mn: bool) -> tuple[Tensor, Tensor]:
+        """``(all_gather(x_local) @ op(w)^T, all_gather(x_local))``."""
+        ms, k = x_local.shape
+        buf = self._next(ms * k * 2)
+        buf.view(torch.bfloat16, ms * k).view(ms, k).copy_(x_local)
+        gather = torch.empty((ms * self.n, k), dtype=x_local.dtype, device=x_local.device)
+        gather[self.rank * ms:(self.rank + 1) * ms].copy_(x_local)
+        self.heap.barrier()
+        y = kernels().tp_ag_gemm(gather, w, b_mn, buf.ptrs, self.rank, ms, self.counters, self.timeout_s)
+        return y, gather
+
+    def gemm_rs(self, a: Tensor, w: Tensor, *, b_mn: bool) -> Tensor:
+        """``reduce_scatter(a @ op(w)^T)`` over token rows: this rank's ``[M/n, N]``."""
+        m, _ = a.shape
+        if m % self.n:
+            raise ValueError("token count must divide by the TP size under sequence parallelism")
+        ms = m // self.n
+        nout = w.shape[1] if b_mn else w.shape[0]
+        buf = self._next(self.n * ms * nout * 2)
+        kernels().tp_gemm_rs(a, w, b_mn, buf.ptrs, self.rank, ms, self.timeout_s)
+        self.heap.barrier()
+        return kernels().tp_sum_slots(buf.view(torch.bfloat16), self.n, ms, nout)
+
+    def close(self) -> None:
+        self.heap.close()
+
+
+def fused_comm(group, x: Tensor) -> TPFusedComm | None:
+    """The fused comm object for ``group`` when the NVLink path applies to ``x``, else None."""
+    if _MODE == "nccl" or group is None or not x.is_cuda or x.dtype != torch.bfloat16:
+        return None
+    n = dist.get_world_size(group)
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", dist.get_world_size()))
+    if not (1 < n <= 8 and local >= dist.get_world_size()):
+        if _MODE == "nvlink":
+            raise ValueError("tp_comm='nvlink' needs a single-node TP group of 2..8 GPUs")
+        return None
+    key = id(group)
+    if key not in _COMMS:
+        _COMMS[key] = TPFusedComm(group, x.device)
+    return _COMMS[key]
+
+
+def close_all() -> None:
+    for c in _COMMS.values():
+        c.close()
+    _COMMS.clear()
+
+
+def _wgrad(w: Tensor, dy: Tensor, x: Tensor):
+    main = getattr(w, "main_grad", None)
+    if main is not None:
+        gemm(dy, x, a_mn=True, b_mn=True, out=main, accumulate=True)
+        return None
+    return gemm(dy, x, a_mn=True, b_mn=True)
+
+
+class _AGLinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, comm):
+        y, gather = comm.ag_gemm(x.contiguous(), w, b_mn=False)
+        ctx.save_for_backward(gather, w)
+        ctx.comm = comm
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        gather, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = ctx.comm.gemm_rs(dy, w, b_mn=True)           # reduce_scatter(dy @ W)
+        dw = _wgrad(w, dy, gather)
+        return dx, dw, None
+
+
+class _LinearRS(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, comm):
+        x = x.contiguous()
+        y = comm.gemm_rs(x, w, b_mn=False)
+        ctx.save_for_backward(x, w)
+        ctx.comm = comm
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dx, dy_full = ctx.comm.ag_gemm(dy.contiguous(), w, b_mn=True)   # all_gather(dy) @ W
+        dw = _wgrad(w, dy_full, x)
+        return dx, dw, None
+
+
+def ag_linear(x: Tensor, w: Tensor, comm: TPFusedComm) -> Tensor:
+    return _AGLinear.apply(x, w, comm)
+
+
+def linear_rs(x: Tensor, w: Tensor, comm: TPFusedComm) -> Tensor:
+    return _LinearRS.apply(x, w, comm)
