@@ -41,7 +41,9 @@ struct SmemLayout {
   static constexpr int A_OFF = 0;
   static constexpr int B_OFF = STAGES * A_BYTES;
   static constexpr int BAR_OFF = B_OFF + STAGES * B_BYTES;
+  static constexpr int EPI_OFF = BAR_OFF + 256;              // RS epilogue staging: 4 warps x 32 x 33 words
   static constexpr int TOTAL = BAR_OFF + 256;
+  static constexpr int TOTAL_EPI = EPI_OFF + 4 * 32 * 33 * 4;
 };
 
 template <bool A_MN, bool B_MN, bool ACCUM_F32>
@@ -596,7 +598,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(tp.peer[owner]) +
                                                           (size_t)(row - owner * tp.Ms) * tp.lda);
         uint4* dst = reinterpret_cast<uint4*>(tp.gather + (size_t)row * tp.lda);
-        for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
+        // 8 independent 16-byte NVLink loads in flight per lane, then the local stores
+        for (int v0 = 0; v0 < vecs; v0 += 32 * 8) {
+          uint4 buf[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int v = v0 + u * 32 + lane;
+            if (v < vecs) buf[u] = __ldg(src + v);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int v = v0 + u * 32 + lane;
+            if (v < vecs) dst[v] = buf[u];
+          }
+        }
         asm volatile("fence.proxy.async.global;" ::: "memory");
         __threadfence();
         __syncwarp();
@@ -614,36 +629,69 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       sm100::tc_fence_after();
       const int row = m0 + quarter * 32 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      __nv_bfloat16* dst_row = nullptr;
-      if (row < M) {
-        if (MODE == 2) {
-          const int owner = min(row / tp.Ms, tp.n - 1);
-          dst_row = static_cast<__nv_bfloat16*>(tp.peer[owner]) +
-                    ((size_t)tp.rank * tp.Ms + (row - owner * tp.Ms)) * (size_t)N;
-        } else {
-          dst_row = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc;
-        }
-      }
+      if (MODE == 2) {
+        // 32 rows x 64 columns per pass through a per-warp shared tile; lane groups of 8 then write
+        // 128 contiguous bytes of one row each (4 rows per store instruction) to the row's owner.
+        uint32_t* stile = reinterpret_cast<uint32_t*>(smem + SmemLayout::EPI_OFF) + (warp - 2) * (32 * 33);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        sm100::tmem_ld32(t_row + c * 32, r);
-        sm100::tmem_ld_wait();
-        const int col0 = n0 + c * 32;
-        if (dst_row && col0 < N) {
-          __nv_bfloat16* dst = dst_row + col0;
-          if (col0 + 32 <= N) {
-            uint32_t p[16];
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t r[32], r2[32];
+          sm100::tmem_ld32(t_row + c * 64, r);
+          sm100::tmem_ld32(t_row + c * 64 + 32, r2);
+          sm100::tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-              p[j] = *reinterpret_cast<uint32_t*>(&h);
+          for (int j = 0; j < 16; ++j) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(r2[2 * j]), __uint_as_float(r2[2 * j + 1]));
+            stile[lane * 33 + j] = *reinterpret_cast<uint32_t*>(&h);
+            stile[lane * 33 + 16 + j] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          __syncwarp();
+          const int col0 = n0 + c * 64;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);    // tile row handled by this lane group
+            const int part = lane & 7;              // 16-byte part of the 128-byte row segment
+            const int grow = m0 + quarter * 32 + rr;
+            const int col = col0 + part * 8;
+            if (grow < M && col < N) {
+              const int owner = min(grow / tp.Ms, tp.n - 1);
+              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(tp.peer[owner]) +
+                                   ((size_t)tp.rank * tp.Ms + (grow - owner * tp.Ms)) * (size_t)N + col;
+              const uint32_t* srow = stile + rr * 33 + part * 4;
+              if (col + 8 <= N) {
+                *reinterpret_cast<uint4*>(dst) = make_uint4(srow[0], srow[1], srow[2], srow[3]);
+              } else {
+                const __nv_bfloat16* hs = reinterpret_cast<const __nv_bfloat16*>(srow);
+                for (int e = 0; e < 8 && col + e < N; ++e) dst[e] = hs[e];
+              }
             }
+          }
+          __syncwarp();
+        }
+      } else {
+        __nv_bfloat16* dst_row = row < M ? reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(t_row + c * 32, r);
+          sm100::tmem_ld_wait();
+          const int col0 = n0 + c * 32;
+          if (dst_row && col0 < N) {
+            __nv_bfloat16* dst = dst_row + col0;
+            if (col0 + 32 <= N) {
+              uint32_t p[16];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              reinterpret_cast<uint4*>(dst)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
-          } else {
-            for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = __float2bfloat16(__uint_as_float(r[j]));
+              for (int j = 0; j < 16; ++j) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                p[j] = *reinterpret_cast<uint32_t*>(&h);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(dst)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+            } else {
+              for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = __float2bfloat16(__uint_as_float(r[j]));
+            }
           }
         }
       }
@@ -667,7 +715,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 template <int MODE, bool B_MN>
 void tp_launch(const MapPair* maps, void* c, int M, int N, int K, long ldc, const TpArgs& tp) {
   auto kern = tp_gemm_kernel<MODE, B_MN>;
-  const int smem = SmemLayout::TOTAL + 1024;
+  const int smem = (MODE == 2 ? SmemLayout::TOTAL_EPI : SmemLayout::TOTAL) + 1024;
   static bool attr = false;
   if (!attr) {
     BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
