@@ -262,9 +262,12 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, const 
   }
 }
 
-// One CTA: 64 keys of one KV head.  mode 0 = own (self) keys of sequence `blockIdx.y`;
-// mode 1 = keys of prefix span `blockIdx.y`, read by the sequences users[rowptr[sp]..rowptr[sp+1]).
-template <int D>
+// One CTA: 64 keys of one KV head and DH of the D output columns (blockIdx.z = kv head * D/DH + column
+// block).  S = QK^T and dP = dO V^T always contract over the full head dim; only the dK / dV / dQ
+// columns [c0, c0 + DH) are produced, which keeps the register accumulators of D = 256 at the size
+// of the D = 128 case.  mode 0 = own (self) keys of sequence `blockIdx.y`; mode 1 = keys of prefix
+// span `blockIdx.y`, read by the sequences users[rowptr[sp]..rowptr[sp+1]).
+template <int D, int DH>
 __global__ void __launch_bounds__(NWARP * 32, 1) tree_attn_bwd_kernel(
     int mode, const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
     const __nv_bfloat16* __restrict__ v, const __nv_bfloat16* __restrict__ pk, const __nv_bfloat16* __restrict__ pv,
@@ -283,7 +286,9 @@ __global__ void __launch_bounds__(NWARP * 32, 1) tree_attn_bwd_kernel(
   float* sL = reinterpret_cast<float*>(sdS + BN * LDS);       // lse*log2e per q row
   float* sDl = sL + BM;                                        // delta per q row
 
-  const int hk = blockIdx.z;
+  constexpr int NSPLIT = D / DH;
+  const int hk = blockIdx.z / NSPLIT;
+  const int c0 = (blockIdx.z % NSPLIT) * DH;
   const int rep = Hq / Hk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
@@ -317,9 +322,9 @@ __global__ void __launch_bounds__(NWARP * 32, 1) tree_attn_bwd_kernel(
   }, v);
   cp_async_commit();
 
-  float dK[D / 8][4], dV[D / 8][4];
+  float dK[DH / 8][4], dV[DH / 8][4];
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) {
+  for (int i = 0; i < DH / 8; ++i) {
     dK[i][0] = dK[i][1] = dK[i][2] = dK[i][3] = 0.f;
     dV[i][0] = dV[i][1] = dV[i][2] = dV[i][3] = 0.f;
   }
@@ -407,9 +412,9 @@ __global__ void __launch_bounds__(NWARP * 32, 1) tree_attn_bwd_kernel(
           ad[2] = pack_bf16(dpt[2 * kk + 1][0], dpt[2 * kk + 1][1]);
           ad[3] = pack_bf16(dpt[2 * kk + 1][2], dpt[2 * kk + 1][3]);
 #pragma unroll
-          for (int dp = 0; dp < D / 16; ++dp) {
+          for (int dp = 0; dp < DH / 16; ++dp) {
             uint32_t b0, b1, b2, b3;
-            const int off = (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + dp * 16 + (lane >> 4) * 8;
+            const int off = (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + c0 + dp * 16 + (lane >> 4) * 8;
             ldsm_x4_t(b0, b1, b2, b3, sdO + off);
             mma16816(dV[2 * dp], ap, b0, b1);
             mma16816(dV[2 * dp + 1], ap, b2, b3);
@@ -421,9 +426,9 @@ __global__ void __launch_bounds__(NWARP * 32, 1) tree_attn_bwd_kernel(
         __syncthreads();
         // dQ (this warp's 16 q rows x D) = dS K over the 64 keys
         {
-          float dq[D / 8][4];
+          float dq[DH / 8][4];
 #pragma unroll
-          for (int i = 0; i < D / 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
+          for (int i = 0; i < DH / 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             uint32_t a[4];
@@ -431,18 +436,18 @@ __global__ void __launch_bounds__(NWARP * 32, 1) tree_attn_bwd_kernel(
             ldsm_x4_t(a[0], a[1], a[2], a[3],
                       sdS + (kk * 16 + (lane & 7) + (lane >> 4) * 8) * LDS + warp * 16 + ((lane >> 3) & 1) * 8);
 #pragma unroll
-            for (int dp = 0; dp < D / 16; ++dp) {
+            for (int dp = 0; dp < DH / 16; ++dp) {
               uint32_t b0, b1, b2, b3;
               ldsm_x4_t(b0, b1, b2, b3,
-                        sK + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + dp * 16 + (lane >> 4) * 8);
+                        sK + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + c0 + dp * 16 + (lane >> 4) * 8);
               mma16816(dq[2 * dp], a, b0, b1);
               mma16816(dq[2 * dp + 1], a, b2, b3);
             }
           }
           const int r0 = m0 + warp * 16 + g, r1 = r0 + 8;
 #pragma unroll
-          for (int i = 0; i < D / 8; ++i) {
-            const int col = i * 8 + tig * 2;
+          for (int i = 0; i < DH / 8; ++i) {
+            const int col = c0 + i * 8 + tig * 2;
             if (r0 < n) {
               float* dst = dq_acc + (size_t)(q0 + r0) * qstride + (size_t)h * D + col;
               atomicAdd(dst, dq[i][0] * scale);
@@ -463,8 +468,8 @@ __global__ void __launch_bounds__(NWARP * 32, 1) tree_attn_bwd_kernel(
   __nv_bfloat16* dvb = (mode == 0) ? dv + (size_t)cu[own_seq] * kstride : dpv + (size_t)span_off * kstride;
   const int key0 = kb + warp * 16 + g, key1 = key0 + 8;
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) {
-    const int col = i * 8 + tig * 2;
+  for (int i = 0; i < DH / 8; ++i) {
+    const int col = c0 + i * 8 + tig * 2;
     if (key0 < key_len) {
       *reinterpret_cast<__nv_bfloat162*>(dkb + (size_t)key0 * kstride + (size_t)hk * D + col) =
           __floats2bfloat162_rn(dK[i][0] * scale, dK[i][1] * scale);
@@ -554,15 +559,15 @@ std::vector<torch::Tensor> tree_attn_bwd(torch::Tensor dout, torch::Tensor q, to
   const __nv_bfloat16* pvp = pv.numel() ? (const __nv_bfloat16*)pv.data_ptr() : (const __nv_bfloat16*)v.data_ptr();
   __nv_bfloat16* dpkp = dpk.numel() ? (__nv_bfloat16*)dpk.data_ptr() : nullptr;
   __nv_bfloat16* dpvp = dpv.numel() ? (__nv_bfloat16*)dpv.data_ptr() : nullptr;
-#define BB_BWD(DD)                                                                                                 \
+#define BB_BWD(DD, DHH)                                                                                            \
   {                                                                                                                \
     attn_delta_kernel<DD><<<std::max(1, std::min((T * Hq + 7) / 8, 148 * 8)), 256, 0, stream>>>(                  \
         (const __nv_bfloat16*)dout.data_ptr(), (const __nv_bfloat16*)o.data_ptr(), delta.data_ptr<float>(), T, Hq); \
     bb::launch_counter().fetch_add(nspans > 0 && max_prefix > 0 ? 3 : 2);                                          \
-    auto kern = tree_attn_bwd_kernel<DD>;                                                                          \
+    auto kern = tree_attn_bwd_kernel<DD, DHH>;                                                                     \
     size_t sm = bwd_smem<DD>();                                                                                    \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);                              \
-    dim3 g0((max_seqlen + BN - 1) / BN, B, Hk);                                                                    \
+    dim3 g0((max_seqlen + BN - 1) / BN, B, Hk * (DD / DHH));                                                       \
     kern<<<g0, NWARP * 32, sm, stream>>>(0, (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), \
                                          (const __nv_bfloat16*)v.data_ptr(), pkp, pvp,                             \
                                          (const __nv_bfloat16*)dout.data_ptr(), lse.data_ptr<float>(),             \
@@ -570,7 +575,7 @@ std::vector<torch::Tensor> tree_attn_bwd(torch::Tensor dout, torch::Tensor q, to
                                          nspans, dq_acc.data_ptr<float>(), (__nv_bfloat16*)dk.data_ptr(),          \
                                          (__nv_bfloat16*)dv.data_ptr(), dpkp, dpvp, T, Hq, Hk, (float)scale, sl2); \
     if (nspans > 0 && max_prefix > 0) {                                                                            \
-      dim3 g1((max_prefix + BN - 1) / BN, nspans, Hk);                                                             \
+      dim3 g1((max_prefix + BN - 1) / BN, nspans, Hk * (DD / DHH));                                                \
       kern<<<g1, NWARP * 32, sm, stream>>>(1, (const __nv_bfloat16*)q.data_ptr(),                                 \
                                            (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)v.data_ptr(), \
                                            pkp, pvp, (const __nv_bfloat16*)dout.data_ptr(), lse.data_ptr<float>(), \
@@ -581,11 +586,13 @@ std::vector<torch::Tensor> tree_attn_bwd(torch::Tensor dout, torch::Tensor q, to
     }                                                                                                              \
   }
   if (D == 128) {
-    BB_BWD(128)
+    BB_BWD(128, 128)
   } else if (D == 64) {
-    BB_BWD(64)
+    BB_BWD(64, 64)
+  } else if (D == 256) {
+    BB_BWD(256, 128)
   } else {
-    TORCH_CHECK(false, "tree attention backward: head_dim must be 64 or 128");
+    TORCH_CHECK(false, "tree attention backward: head_dim must be 64, 128 or 256");
   }
 #undef BB_BWD
   BB_CHECK_CUDA(cudaGetLastError());

@@ -159,6 +159,8 @@ def _tree_case(D, hq, hkv, lens, spans, P, seed=0):
     (128, 4, 4, (70,), ((0, 0),), 0),                                                  # plain causal, odd length
     (64, 4, 2, (129, 64, 200), ((5, 130), (5, 130), (0, 3)), 140),
     (128, 32, 8, (512,) * 8, ((0, 512),) * 8, 512),                                    # Qwen3-4B-shaped siblings
+    (256, 4, 2, (100, 130, 64), ((0, 64), (0, 64), (64, 10)), 74),                      # gated-attention head dim
+    (256, 16, 2, (256, 256), ((0, 256), (0, 256)), 256),
 ])
 def test_tree_attention_fwd_bwd(D, hq, hkv, lens, spans, P):
     from bridge_b200.ops.attention import tree_attention, tree_attention_reference

@@ -54,14 +54,14 @@ def test_bench_cli_small():
     assert line["value"] > 0 and line["gpu_launches"] > 0 and line["n_gpus"] == 1
 
 
-@pytest.mark.parametrize("preset", ["tiny_hybrid", "tiny_moe"])
-def test_hybrid_tpr_vs_flat_bf16(preset):
+@pytest.mark.parametrize("preset,head_dim", [("tiny_hybrid", 128), ("tiny_hybrid", 256), ("tiny_moe", 128)])
+def test_hybrid_tpr_vs_flat_bf16(preset, head_dim):
     """Hybrid GDN/attention (and hybrid MoE) on the GPU kernels: conv + gated delta rule state relay."""
     from bridge_b200.engine import EngineConfig, TPREngine
     from bridge_b200.models import get_config
     from bridge_b200.models.decoder import build_model
 
-    cfg = get_config(preset, hidden_size=512, num_heads=4, num_kv_heads=2, head_dim=128, gdn_num_qk_heads=2,
+    cfg = get_config(preset, hidden_size=512, num_heads=4, num_kv_heads=2, head_dim=head_dim, gdn_num_qk_heads=2,
                      gdn_num_v_heads=4, gdn_head_dim=64)
     dev = torch.device("cuda")
     batch = tree_batch(n_trees=2, prefix=150, siblings=3, resp=70, seed=9)
@@ -87,4 +87,7 @@ def test_hybrid_tpr_vs_flat_bf16(preset):
             continue
         a = p.main_grad.float()
         rel = float((a - b.float()).norm() / (b.float().norm() + 1e-12))
-        assert rel < 5e-2 and _cos(a, b) > 0.998, (n, rel)
+        # per-head scalars (A_log, dt_bias: a handful of values, each a long cancelling token sum) carry
+        # more bf16 noise than the matrices
+        small = p.numel() < 64
+        assert rel < (0.15 if small else 5e-2) and _cos(a, b) > (0.99 if small else 0.998), (n, rel)
