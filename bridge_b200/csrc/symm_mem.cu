@@ -298,3 +298,113 @@ void symm_clear_error() {
   const unsigned int z = 0;
   BB_CHECK_CUDA(cudaMemcpyToSymbol(g_symm_error, &z, sizeof(z)));
 }
+
+// ------------------------------------------------------------------------------------------------
+// Row-indexed P2P movement over symmetric buffers (context-parallel KV exchange, MoE dispatch):
+//   p2p_gather_rows  out[i, :] = peer[src_rank[i]][src_row[i], :]              (bf16 rows)
+//   p2p_reduce_rows  out[i, :] = sum_r peer[r][src_row[i], :]  (+ add[i, :])    (bf16 or fp32 rows,
+//                    fixed rank order, FP32 accumulation, bf16 out)
+// One warp per row, 16-byte vectors, several loads in flight per lane.
+namespace {
+
+__global__ void p2p_gather_rows_kernel(PeerPtrs peers, const int* __restrict__ src_rank,
+                                       const int* __restrict__ src_row, uint4* __restrict__ out, int rows,
+                                       int vecs /* 16-byte vectors per row */) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+  for (int i = gw; i < rows; i += nw) {
+    const int r = src_rank[i];
+    const uint4* src = reinterpret_cast<const uint4*>(peers.p[r]) + (size_t)src_row[i] * vecs;
+    uint4* dst = out + (size_t)i * vecs;
+    for (int v0 = 0; v0 < vecs; v0 += 32 * 4) {
+      uint4 buf[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (v < vecs) buf[u] = __ldg(src + v);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (v < vecs) dst[v] = buf[u];
+      }
+    }
+  }
+}
+
+template <bool SRC_F32>
+__global__ void p2p_reduce_rows_kernel(PeerPtrs peers, int n, const int* __restrict__ src_row,
+                                       const bb::bf16x8* __restrict__ add, bb::bf16x8* __restrict__ out, int rows,
+                                       int vecs /* 8-element vectors per row */) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+  for (int i = gw; i < rows; i += nw) {
+    const size_t srow = (size_t)src_row[i] * vecs;
+    for (int v = lane; v < vecs; v += 32) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (add) bb::unpack8(add[(size_t)i * vecs + v], acc);
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r) {
+        if (r >= n) break;
+        float f[8];
+        if (SRC_F32) {
+          const float4* s = reinterpret_cast<const float4*>(peers.p[r]) + 2 * (srow + v);
+          const float4 a = __ldg(s), b = __ldg(s + 1);
+          f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+        } else {
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(peers.p[r]) + srow + v);
+          bb::unpack8(*reinterpret_cast<const bb::bf16x8*>(&raw), f);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += f[e];
+      }
+      out[(size_t)i * vecs + v] = bb::pack8(acc);
+    }
+  }
+}
+
+}  // namespace
+
+void p2p_gather_rows(torch::Tensor out, std::vector<int64_t> peers, torch::Tensor src_rank, torch::Tensor src_row) {
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.dim() == 2, "p2p_gather_rows: out [rows, width]");
+  const int64_t row_bytes = out.size(1) * out.element_size();
+  TORCH_CHECK(row_bytes % 16 == 0, "p2p_gather_rows: row bytes must be a multiple of 16");
+  const int rows = (int)out.size(0);
+  TORCH_CHECK(src_rank.numel() == rows && src_row.numel() == rows && src_rank.scalar_type() == at::kInt &&
+                  src_row.scalar_type() == at::kInt && src_rank.is_cuda(),
+              "p2p_gather_rows: int32 index tensors of out.size(0) on the device");
+  if (rows == 0) return;
+  const int blocks = num_blocks((size_t)rows * 32, 256, 8);
+  p2p_gather_rows_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      make_ptrs(peers), src_rank.data_ptr<int>(), src_row.data_ptr<int>(), reinterpret_cast<uint4*>(out.data_ptr()),
+      rows, (int)(row_bytes / 16));
+  BB_POST_LAUNCH();
+}
+
+void p2p_reduce_rows(torch::Tensor out, std::vector<int64_t> peers, torch::Tensor src_row, bool src_f32,
+                     c10::optional<torch::Tensor> add) {
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.dim() == 2 && out.scalar_type() == at::kBFloat16,
+              "p2p_reduce_rows: bf16 out [rows, width]");
+  TORCH_CHECK(out.size(1) % 8 == 0, "p2p_reduce_rows: width must be a multiple of 8");
+  const int rows = (int)out.size(0);
+  TORCH_CHECK(src_row.numel() == rows && src_row.scalar_type() == at::kInt && src_row.is_cuda(),
+              "p2p_reduce_rows: int32 row index on the device");
+  const bb::bf16x8* addp = nullptr;
+  if (add.has_value()) {
+    TORCH_CHECK(add->is_contiguous() && add->scalar_type() == at::kBFloat16 && add->numel() == out.numel(),
+                "p2p_reduce_rows: add must match out");
+    addp = reinterpret_cast<const bb::bf16x8*>(add->data_ptr());
+  }
+  if (rows == 0) return;
+  const int blocks = num_blocks((size_t)rows * 32, 256, 8);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto* o = reinterpret_cast<bb::bf16x8*>(out.data_ptr());
+  const int vecs = (int)(out.size(1) / 8);
+  if (src_f32)
+    p2p_reduce_rows_kernel<true><<<blocks, 256, 0, stream>>>(make_ptrs(peers), (int)peers.size(),
+                                                             src_row.data_ptr<int>(), addp, o, rows, vecs);
+  else
+    p2p_reduce_rows_kernel<false><<<blocks, 256, 0, stream>>>(make_ptrs(peers), (int)peers.size(),
+                                                              src_row.data_ptr<int>(), addp, o, rows, vecs);
+  BB_POST_LAUNCH();
+}

@@ -195,8 +195,15 @@ def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss:
     rt = resolve_engine_cp_runtime(engine)
     t_run = time.perf_counter()
     metrics: dict[str, Any] = {}
+    profiler = None
+    if ec.exec_profile:
+        from ..utils.profiler import SegmentEventProfiler
+
+        profiler = SegmentEventProfiler()
+        engine._tpr_segment_event_profiler = profiler
     if rt.group is None and ec.executor == "forest":
         fx = ForestExecutor(model, objective, mode=ec.forest_mode, token_budget=ec.token_budget)
+        fx.profiler = profiler
         if prepared.nodes is None:
             prepared.nodes = fx.plan(forest)
         res = fx.run(forest, prepared.nodes)
@@ -217,7 +224,8 @@ def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss:
             fn, counts = objective.bind_tree(tree_plan, shard_for_segment=shard_for, model=model)
             ex = SegmentExecutor(model, tree_plan.segment_plan, segment_loss_fn=fn, segment_loss_term_counts=counts,
                                  cp_group=rt.group, cp_backend=rt.backend)
-            out = FixedTopologyScheduler(tree_plan.segment_plan, ex).run()
+            out = FixedTopologyScheduler(tree_plan.segment_plan, ex, event_profiler=profiler,
+                                         tree_index=len(seg_stats)).run()
             if sync_loss and not bool(torch.isfinite(out.normalized_loss).item()):
                 raise FloatingPointError("non-finite TPR PPO tree loss; gradients will not be finalized")
             seg_stats.extend(m for _, m in ex.segment_loss_metrics)
@@ -260,4 +268,12 @@ def run_tpr_forward_backward_batch(engine, data: Any, loss_function: Any = None,
     """PPO mini-batch -> TPR forest schedule -> one gradient finalisation."""
     if forward_only:
         raise NotImplementedError("the TPR PPO schedule is training-only")
+    import os
+
+    from ..utils.capture import ENV_DIR, capture_actor_update_minibatch
+
+    if os.environ.get(ENV_DIR) and isinstance(data, dict):
+        idx = getattr(engine, "_tpr_capture_count", 0)
+        capture_actor_update_minibatch(data, batch_idx=idx, capture_index=idx)
+        engine._tpr_capture_count = idx + 1
     return execute_prepared_tpr_batch(engine, prepare_tpr_batch(engine, data, loss_function), sync_loss=sync_loss)

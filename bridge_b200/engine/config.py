@@ -51,6 +51,9 @@ class EngineConfig:
     # sequence-parallel TP linears: "auto" (all-gather / reduce-scatter fused into the tcgen05 GEMM over
     # NVLink on a single-node CUDA group, NCCL otherwise), "nvlink" or "nccl"
     tp_comm: str = "auto"
+    # ring / all-gather CP attention transport: "auto" (NVLink P2P gather + owner reduction on a
+    # single-node CUDA group, NCCL otherwise), "nvlink" or "nccl"
+    cp_comm: str = "auto"
     extra: dict = field(default_factory=dict)
 
     def with_env(self) -> "EngineConfig":
@@ -72,6 +75,8 @@ class EngineConfig:
             kw["token_budget"] = _env_int("TPR_TOKEN_BUDGET", self.token_budget)
         if "TPR_EXECUTOR" in os.environ:
             kw["executor"] = os.environ["TPR_EXECUTOR"]
+        if "TPR_CP_COMM" in os.environ:
+            kw["cp_comm"] = os.environ["TPR_CP_COMM"]
         if "TPR_TP_COMM" in os.environ:
             kw["tp_comm"] = os.environ["TPR_TP_COMM"]
         if "TPR_DP_COMM" in os.environ:
@@ -79,6 +84,8 @@ class EngineConfig:
         cfg = replace(self, **kw) if kw else self
         if cfg.tree_policy not in ("exact", "qwen_turn"):
             raise ValueError(f"unknown TPR tree_policy: {cfg.tree_policy!r}")
+        if cfg.cp_comm not in ("auto", "nvlink", "nccl"):
+            raise ValueError(f"unknown cp_comm: {cfg.cp_comm!r}")
         if cfg.tp_comm not in ("auto", "nvlink", "nccl"):
             raise ValueError(f"unknown tp_comm: {cfg.tp_comm!r}")
         if cfg.dp_comm not in ("auto", "nvlink", "nccl"):

@@ -55,9 +55,11 @@ class TPREngine:
         self.parallel = parallel_state or build_parallel_state(ec.tensor_model_parallel_size,
                                                                ec.context_parallel_size,
                                                                ec.expert_model_parallel_size)
+        from ..parallel.cp_p2p import set_cp_comm_mode
         from ..parallel.tp_fused import set_tp_comm_mode
 
         set_tp_comm_mode(ec.tp_comm)
+        set_cp_comm_mode(ec.cp_comm)
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)

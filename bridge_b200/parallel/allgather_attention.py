@@ -100,6 +100,13 @@ def allgather_cp_rectangular_attention(query: Tensor, key: Tensor, value: Tensor
 class AllGatherCPAttentionBackend(CPAttentionBackendBase):
     def attention(self, layer_number: int, query: Tensor, key: Tensor, value: Tensor, *,
                   softmax_scale: float | None = None) -> Tensor:
+        from .cp_p2p import cp_comm, p2p_cp_attention
+
+        comm = cp_comm(self.cp_group, query)
+        if comm is not None:     # NVLink P2P gather + tcgen05 attention + P2P dK/dV owner reduction
+            scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(query.shape[-1])
+            return p2p_cp_attention(query, key, value, prefix_blocks=self.blocks(layer_number),
+                                    current_shard=self.current_shard, comm=comm, softmax_scale=scale)
         return allgather_cp_rectangular_attention(query, key, value, prefix_blocks=self.blocks(layer_number),
                                                   current_shard=self.current_shard, cp_group=self.cp_group,
                                                   softmax_scale=softmax_scale)

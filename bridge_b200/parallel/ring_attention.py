@@ -12,10 +12,10 @@ cast).  Backward replays the ring in the same direction with a packet
 the packet, and after ``cp`` hops the packet is home with the full gradient
 of the owner's block.  Constant buffers: 2 (forward), 4 (backward).
 
-On B200 the block math runs in the tree-attention kernel (prefix-only blocks
-for FULL, causal self blocks for the diagonal) and the transport is NCCL
-send/recv between NVLink peers; the fused in-kernel peer-memory variant lives
-in ``csrc/ring_p2p.cu``.
+On CUDA with a single-node CP group the backend uses the NVLink peer-memory
+transport of :mod:`bridge_b200.parallel.cp_p2p` (P2P row gathers into a
+global-order bank + the tcgen05 tree-attention kernel + P2P owner reduction of
+dK/dV); the NCCL ring below is the baseline and the CPU/gloo path.
 
 Parity: verl/models/mcore/tpr/parallel/ring_attention.py:57-1140
 (RingBlockKind, classify_ring_block, zigzag shard, streaming ring forward,
@@ -225,6 +225,13 @@ def ordinary_ring_cp_attention(query: Tensor, key: Tensor, value: Tensor, *, cp_
 class RingCPAttentionBackend(CPAttentionBackendBase):
     def attention(self, layer_number: int, query: Tensor, key: Tensor, value: Tensor, *,
                   softmax_scale: float | None = None) -> Tensor:
+        from .cp_p2p import cp_comm, p2p_cp_attention
+
+        comm = cp_comm(self.cp_group, query)
+        if comm is not None:
+            scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(query.shape[-1])
+            return p2p_cp_attention(query, key, value, prefix_blocks=self.blocks(layer_number),
+                                    current_shard=self.current_shard, comm=comm, softmax_scale=scale)
         return ring_cp_attention(query, key, value, prefix_blocks=self.blocks(layer_number),
                                  current_shard=self.current_shard, cp_group=self.cp_group,
                                  softmax_scale=softmax_scale)

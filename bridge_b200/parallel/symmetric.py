@@ -38,7 +38,12 @@ class SymmetricBuffer:
 
 
 class SymmetricHeap:
-    def __init__(self, group, device: torch.device | None = None, *, timeout_s: float = 60.0) -> None:
+    def __init__(self, group, device: torch.device | None = None, *, timeout_s: float | None = None) -> None:
+        import os
+
+        if timeout_s is None:
+            timeout_s = float(os.environ.get("BB_SYMM_TIMEOUT_S", "60"))
+        self._debug = os.environ.get("BB_SYMM_DEBUG") == "1"
         self.group = group
         self.rank = dist.get_rank(group)
         self.size = dist.get_world_size(group)
@@ -76,6 +81,13 @@ class SymmetricHeap:
     def barrier(self, payload: Tensor | None = None, *, timeout_s: float | None = None) -> None:
         """Stream-ordered cross-GPU barrier; ``payload`` (FP32 partials) is summed and published to every peer."""
         self.epoch += 1
+        if self._debug:
+            import sys
+            import traceback
+
+            where = traceback.extract_stack(limit=4)[0]
+            print(f"[symm r{self.rank}] barrier epoch {self.epoch} from {where.name}:{where.lineno}",
+                  file=sys.stderr, flush=True)
         kernels().symm_barrier(self.pad.ptrs, self.rank, self.epoch, payload,
                                float(self.timeout_s if timeout_s is None else timeout_s))
 

@@ -42,14 +42,14 @@ def set_tp_comm_mode(mode: str) -> None:
 
 class TPFusedComm:
     def __init__(self, group, device: torch.device, capacity_bytes: int = 64 << 20,
-                 timeout_s: float = 60.0) -> None:
+                 timeout_s: float | None = None) -> None:
         from .symmetric import SymmetricHeap
 
         self.group = group
         self.heap = SymmetricHeap(group, device, timeout_s=timeout_s)
         self.n, self.rank = self.heap.size, self.heap.rank
         self.capacity = capacity_bytes
-        self.timeout_s = timeout_s
+        self.timeout_s = self.heap.timeout_s
         self.bufs = [self.heap.alloc(capacity_bytes), self.heap.alloc(capacity_bytes)]
         self.calls = 0
         self.counters = torch.zeros(8192, dtype=torch.int32, device=device)

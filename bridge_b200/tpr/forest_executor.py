@@ -122,6 +122,7 @@ class ForestExecutor:
         self.attn_layers = tuple(getattr(model, "attention_layer_numbers", ()))
         self.gdn_layers = tuple(getattr(model, "gdn_layer_numbers", ()))
         self.device = model_device(model)
+        self.profiler = None
 
     # ------------------------------------------------------------------ planning
     def _nodes(self, forest: ForestExecutionPlan) -> list[_Node]:
@@ -333,6 +334,15 @@ class ForestExecutor:
         ch.loss = None
 
     # ------------------------------------------------------------------ entry
+    def _prof_begin(self, kind: str, nodes, depth: int):
+        if self.profiler is None:
+            return None
+        return self.profiler.begin(kind=kind, depth=depth, tokens=sum(n.length for n in nodes))
+
+    def _prof_end(self, rec) -> None:
+        if rec is not None:
+            self.profiler.end(rec)
+
     def plan(self, forest: ForestExecutionPlan) -> list[_Node]:
         """Static node table of a forest (reusable across runs of the same prepared batch)."""
         return self._nodes(forest)
@@ -351,17 +361,23 @@ class ForestExecutor:
             pushed[d] = []
             # Keep siblings of one parent adjacent so their children batch together later.
             for grp in _chunked(internal[d], self.token_budget):
+                rec = self._prof_begin("push_chunk", grp, d)
                 pushed[d].append(self._push_chunk(grp, stats))
+                self._prof_end(rec)
                 stats["chunks"] += 1
         # Leaves ordered by (parent chunk, parent row) so a chunk's spans hit few parents.
         leaves.sort(key=lambda n: (n.depth == 0, id(n.parent.chunk) if n.parent else 0,
                                    n.parent.row0 if n.parent else 0))
         for grp in _chunked(leaves, self.token_budget):
+            rec = self._prof_begin("visit_chunk", grp, grp[0].depth)
             self._visit_leaves(grp, stats, acc)
+            self._prof_end(rec)
             stats["chunks"] += 1
         for d in sorted(pushed, reverse=True):
             for ch in reversed(pushed[d]):
+                rec = self._prof_begin("pop_chunk", ch.nodes, d)
                 self._pop_chunk(ch, stats, acc)
+                self._prof_end(rec)
         loss = acc["loss"] if acc["loss"] is not None else torch.zeros((), device=self.device)
         stat_rows = [m["stats"] * m["n"] for m in acc["metrics"] if m is not None]
         total_n = sum(m["n"] for m in acc["metrics"] if m is not None)

@@ -117,8 +117,62 @@ def tp_fused() -> None:
     dist.destroy_process_group()
 
 
+def cp_p2p() -> None:
+    """TPR with CP over the NVLink P2P transport (ring zigzag and all-gather contiguous shards) vs the
+    flattened batch on one GPU and vs the NCCL transport."""
+    from bridge_b200.engine import EngineConfig, TPREngine
+    from bridge_b200.models import get_config
+    from bridge_b200.models.decoder import build_model
+    from bridge_b200.parallel import cp_p2p
+    from bridge_b200.parallel.groups import build_parallel_state, init_distributed
+    from tests.helpers import flat_ppo_loss, set_old_log_probs, tree_batch
+
+    rank, world = init_distributed(timeout_s=120)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = get_config("tiny", hidden_size=512, num_heads=8, num_kv_heads=2, head_dim=128, intermediate_size=1024,
+                     num_layers=2)
+    batch = tree_batch(n_trees=2, prefix=131, siblings=3, resp=77, seed=3)
+    ref = build_model(cfg, device=dev, seed=0)
+    set_old_log_probs(ref, batch)
+    loss_ref, _ = flat_ppo_loss(ref, batch)
+    loss_ref.backward()
+    gref = {n: p.grad.float() for n, p in ref.named_parameters()}
+    ps = build_parallel_state(tp=1, cp=world)
+    results = {}
+    import os
+
+    combos = [(b, m) for b in ("ring", "allgather") for m in ("nvlink", "nccl")]
+    if os.environ.get("CP_P2P_ONLY"):
+        combos = [tuple(os.environ["CP_P2P_ONLY"].split(","))]
+    for backend, mode in combos:
+        if True:
+            eng = TPREngine(cfg, EngineConfig(context_parallel_size=world, tpr_cp_backend=backend, cp_comm=mode,
+                                              dp_comm="nccl"),
+                            device=dev, model=build_model(cfg, device=dev, seed=0), parallel_state=ps)
+            print(f"[r{rank}] start {backend} {mode}", file=sys.stderr, flush=True)
+            out = eng.forward_backward_batch(batch)
+            loss = float(out["loss"][0])
+            print(f"[r{rank}] done {backend} {mode} loss={loss}", file=sys.stderr, flush=True)
+            worst = 0.0
+            for n, p in eng.model.named_parameters():
+                a = p.main_grad.float()
+                rel = float((a - gref[n]).norm() / (gref[n].norm() + 1e-12))
+                worst = max(worst, rel)
+            results[(backend, mode)] = (loss, worst)
+            assert abs(loss - float(loss_ref)) <= 5e-3 * abs(float(loss_ref)) + 1e-4, (backend, mode, loss,
+                                                                                        float(loss_ref))
+            assert worst < 5e-2, (backend, mode, worst)
+    if any(m == "nvlink" for _, m in combos):
+        assert cp_p2p._COMMS, "the P2P transport was not used"
+    cp_p2p.close_all()
+    dist.barrier()
+    if rank == 0:
+        print("CP_P2P_OK", results, float(loss_ref), flush=True)
+    dist.destroy_process_group()
+
+
 if __name__ == "__main__":
     import os
 
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
-    {"dp_nvlink": dp_nvlink, "tp_fused": tp_fused}[sys.argv[1]]()
+    {"dp_nvlink": dp_nvlink, "tp_fused": tp_fused, "cp_p2p": cp_p2p}[sys.argv[1]]()

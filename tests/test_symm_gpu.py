@@ -62,3 +62,8 @@ def test_nvlink_dp_matches_nccl_two_gpus():
 @pytest.mark.multigpu
 def test_tp_fused_linears_match_nccl_two_gpus():
     _run_worker("tp_fused", "TP_FUSED_OK")
+
+
+@pytest.mark.multigpu
+def test_cp_p2p_attention_matches_flattened_two_gpus():
+    _run_worker("cp_p2p", "CP_P2P_OK")
