@@ -78,8 +78,10 @@ def allgather_cp_rectangular_attention(query: Tensor, key: Tensor, value: Tensor
     if on_gpu(query):
         from ..tpr.context import SegmentBatchLayout
 
-        bank_k = torch.cat(pk + [ck[:start]]) if (pk or start) else None
-        bank_v = torch.cat(pv + [cv[:start]]) if (pv or start) else None
+        # Always route the gathered current K/V into the graph (an empty bank on rank 0 of a root
+        # segment): its backward is a reduce-scatter every CP rank must enter, or the peers hang.
+        bank_k = torch.cat(pk + [ck[:start]])
+        bank_v = torch.cat(pv + [cv[:start]])
         plen = P + start
         lay = SegmentBatchLayout.build((n_local,), ((0, plen),), device=query.device)
         o = tree_attention(query, key, value, bank_k, bank_v, lay, softmax_scale=scale)
