@@ -33,6 +33,8 @@ std::vector<torch::Tensor> tree_attn_bwd(torch::Tensor dout, torch::Tensor q, to
 torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, c10::optional<torch::Tensor> out,
                    bool accumulate);
 int64_t gemm_error_code();
+torch::Tensor grouped_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, bool trans_w);
+void grouped_gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor offsets, torch::Tensor acc);
 
 std::vector<torch::Tensor> tree_attn_fwd_sm100(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor pk,
                                                torch::Tensor pv, torch::Tensor cu, torch::Tensor poff,
@@ -118,6 +120,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_sum_slots", &tp_sum_slots);
   m.def("gemm", &gemm, "tcgen05 GEMM: C (+)= op(A) op(B)^T");
   m.def("gemm_error_code", &gemm_error_code);
+  m.def("grouped_gemm", &grouped_gemm, "MoE grouped tcgen05 GEMM (device expert offsets)");
+  m.def("grouped_gemm_wgrad", &grouped_gemm_wgrad, "MoE grouped weight gradient, FP32 accumulate");
   m.def("launch_count", &bb_launch_count,
         "kernels launched by this extension so far");
 }

@@ -833,3 +833,334 @@ torch::Tensor tp_sum_slots(torch::Tensor recv, int64_t n, int64_t ms, int64_t N)
   BB_POST_LAUNCH();
   return out;
 }
+
+// ================================================================================================
+// Grouped (mixture-of-experts) tcgen05 GEMMs with device-side expert offsets (no host sync):
+//
+//   MODE 0  out[off_e + i, :] = x[off_e + i, :] @ W[e]^T        W as [E*N, K]   (forward)
+//   MODE 1  out[off_e + i, :] = x[off_e + i, :] @ W[e]          W as [E*K', N]  (data gradient;
+//                                                                K' % 64 == 0, MN-major B)
+//   MODE 2  acc[e] += dy[rows_e, :]^T @ x[rows_e, :]           FP32 [E, M, N]  (weight gradient;
+//                                                                K = the expert's token rows)
+// Rows of one expert are contiguous (tokens sorted by expert); offsets int32 [E+1] live on the
+// device.  Each CTA scans the offsets into shared memory and walks the same persistent tile list
+// as the plain GEMM.  In MODE 2 the last K block of an expert also covers the next expert's rows:
+// the MMA warp zeroes those rows of the A stage in shared memory (generic stores, then a proxy
+// fence) before issuing the MMAs, so only the expert's own tokens contribute.
+// ================================================================================================
+namespace {
+
+constexpr int kMaxExperts = 1024;
+
+template <int MODE>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, void* C,
+                        const int* __restrict__ offsets, int E, int N, int K, long ldc, int* err) {
+  // MODE 0/1: N = output columns, K = reduction dim (per-expert weight rows for MODE 1).
+  // MODE 2  : N = output columns (x width), K unused (rows per expert from offsets); M = ldc rows per expert.
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem + SmemLayout::A_OFF;
+  unsigned char* sB = smem + SmemLayout::B_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  int* pre = reinterpret_cast<int*>(smem + SmemLayout::BAR_OFF + 256);   // [E+1] prefix of M tiles
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int Mrows = (int)ldc;  // MODE 2: rows of one expert's output (= out features)
+  const int m2_tiles = (Mrows + BM - 1) / BM;
+
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    pre[0] = 0;
+    for (int e = 0; e < E; ++e) {
+      const int rows = offsets[e + 1] - offsets[e];
+      acc += MODE == 2 ? (rows > 0 ? m2_tiles : 0) : (rows + BM - 1) / BM;
+      pre[e + 1] = acc;
+    }
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tfull[a], 1);
+      sm100::mbar_init(&tempty[a], 128);
+    }
+    sm100::fence_mbar_init();
+    sm100::prefetch_tmap(&tmap_a);
+    sm100::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, TMEM_COLS);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = pre[E] * n_tiles;
+
+  // tile t -> expert e, M tile mt (within the expert), N tile nt
+  auto tile_of = [&](int t, int& e, int& m0, int& n0) {
+    const int mt_global = t / n_tiles;
+    int lo = 0, hi = E - 1;
+    while (lo < hi) {  // last e with pre[e] <= mt_global
+      const int mid = (lo + hi + 1) >> 1;
+      if (pre[mid] <= mt_global) lo = mid;
+      else hi = mid - 1;
+    }
+    e = lo;
+    m0 = (mt_global - pre[e]) * BM;
+    n0 = (t % n_tiles) * BN;
+  };
+  auto kblocks = [&](int e) {
+    return MODE == 2 ? (offsets[e + 1] - offsets[e] + BK - 1) / BK : (K + BK - 1) / BK;
+  };
+
+  constexpr bool A_MN = MODE == 2;
+  constexpr bool B_MN = MODE != 0;
+  constexpr uint32_t IDESC = sm100::umma_idesc_bf16(BM, BN, A_MN, B_MN);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int e, m0, n0;
+        tile_of(t, e, m0, n0);
+        const int nk = kblocks(e);
+        const int row0 = offsets[e];
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait(&empty[stage], phase ^ 1, err, 1)) {
+            ok = false;
+            break;
+          }
+          sm100::mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          unsigned char* a_dst = sA + stage * A_BYTES;
+          unsigned char* b_dst = sB + stage * B_BYTES;
+          if (MODE == 2) {
+            // A = dy^T: MN-major tile of dy rows [row0 + kb*64, +64), columns [m0, m0+128)
+#pragma unroll
+            for (int i = 0; i < BM / 64; ++i)
+              sm100::tma_load_2d(a_dst + i * 8192, &tmap_a, &full[stage], m0 + 64 * i, row0 + kb * BK);
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i)
+              sm100::tma_load_2d(b_dst + i * 8192, &tmap_b, &full[stage], n0 + 64 * i, row0 + kb * BK);
+          } else {
+            sm100::tma_load_2d(a_dst, &tmap_a, &full[stage], kb * BK, row0 + m0);
+            if (MODE == 1) {
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i)
+                sm100::tma_load_2d(b_dst + i * 8192, &tmap_b, &full[stage], n0 + 64 * i, e * K + kb * BK);
+            } else {
+              sm100::tma_load_2d(b_dst, &tmap_b, &full[stage], kb * BK, e * N + n0);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int e, m0, n0;
+      tile_of(t, e, m0, n0);
+      const int nk = kblocks(e);
+      const int rows_e = offsets[e + 1] - offsets[e];
+      // every lane waits; decisions are warp-uniform so the whole warp leaves together
+      if (!__all_sync(0xffffffffu, sm100::mbar_wait(&tempty[acc], acc_phase ^ 1, err, 2))) break;
+      sm100::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < nk; ++kb) {
+        if (!__all_sync(0xffffffffu, sm100::mbar_wait(&full[stage], phase, err, 3))) {
+          ok = false;
+          break;
+        }
+        if (MODE == 2) {
+          const int valid = rows_e - kb * BK;  // token rows of this expert in the block
+          if (valid < BK) {
+            // zero K rows [valid, 64) of the A stage: each 8 KB chunk holds 64 rows of 128 bytes
+            unsigned char* a_st = sA + stage * A_BYTES;
+            const int nrows = BK - valid;
+            for (int i = lane; i < (BM / 64) * nrows * 8; i += 32) {
+              const int chunk = i / (nrows * 8), rem = i % (nrows * 8);
+              const int r = valid + rem / 8, part = rem % 8;
+              *reinterpret_cast<uint4*>(a_st + chunk * 8192 + r * 128 + part * 16) = make_uint4(0, 0, 0, 0);
+            }
+            sm100::fence_proxy_async_smem();
+            __syncwarp();
+          }
+        }
+        sm100::tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_base = sm100::smem_addr(sA + stage * A_BYTES);
+          const uint32_t b_base = sm100::smem_addr(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sm100::umma_desc_sw128(a_base + kk * 2048, 8192, 1024)
+                                     : sm100::umma_desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sm100::umma_desc_sw128(b_base + kk * 2048, 8192, 1024)
+                                     : sm100::umma_desc_sw128(b_base + kk * 32, 16, 1024);
+            sm100::umma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+          }
+          sm100::umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) sm100::umma_commit(&tfull[acc]);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int e, m0, n0;
+      tile_of(t, e, m0, n0);
+      const bool got = sm100::mbar_wait(&tfull[acc], acc_phase, err, 4);
+      if (!__all_sync(0xffffffffu, got)) break;
+      sm100::tc_fence_after();
+      const int r = m0 + quarter * 32 + lane;  // row within the expert's output block
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const int rows_lim = MODE == 2 ? Mrows : offsets[e + 1] - offsets[e];
+      const bool row_ok = r < rows_lim;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        sm100::tmem_ld32(t_row + c * 32, v);
+        sm100::tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (!row_ok || col0 >= N) continue;
+        if (MODE == 2) {
+          float* dst = reinterpret_cast<float*>(C) + ((size_t)e * Mrows + r) * (size_t)N + col0;
+          if (col0 + 32 <= N) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 a = reinterpret_cast<float4*>(dst)[j];
+              a.x += __uint_as_float(v[4 * j]);
+              a.y += __uint_as_float(v[4 * j + 1]);
+              a.z += __uint_as_float(v[4 * j + 2]);
+              a.w += __uint_as_float(v[4 * j + 3]);
+              reinterpret_cast<float4*>(dst)[j] = a;
+            }
+          } else {
+            for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] += __uint_as_float(v[j]);
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)(offsets[e] + r) * (size_t)N + col0;
+          if (col0 + 32 <= N) {
+            uint32_t p[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+              p[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<uint4*>(dst)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = __float2bfloat16(__uint_as_float(v[j]));
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int MODE>
+void grouped_launch(const MapPair* maps, void* c, const int* offsets, int E, int N, int K, long ldc, int grid) {
+  auto kern = grouped_gemm_kernel<MODE>;
+  const int smem = SmemLayout::TOTAL + 4 * (kMaxExperts + 1) + 1024;
+  static bool attr = false;
+  if (!attr) {
+    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  int* err = error_word().data_ptr<int>();
+  void* args[] = {const_cast<CUtensorMap*>(&maps->a), const_cast<CUtensorMap*>(&maps->b), &c,
+                  const_cast<int**>(&offsets), &E, &N, &K, &ldc, &err};
+  BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NUM_THREADS), args, smem,
+                                 at::cuda::getCurrentCUDAStream()));
+  BB_POST_LAUNCH();
+}
+
+}  // namespace
+
+// x [T, K] rows sorted by expert, offsets int32 [E+1] (device), w [E, N, K] (trans_w=false: out = x W_e^T)
+// or w [E, K, N] (trans_w=true: out = x W_e).  Returns bf16 [T, N].
+torch::Tensor grouped_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, bool trans_w) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "grouped: x");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "grouped: w [E, rows, cols]");
+  TORCH_CHECK(offsets.is_cuda() && offsets.scalar_type() == at::kInt && offsets.numel() == w.size(0) + 1,
+              "grouped: offsets int32 [E+1] on the device");
+  const int E = (int)w.size(0);
+  TORCH_CHECK(E <= kMaxExperts, "grouped: at most 1024 experts");
+  const long T = x.size(0), K = x.size(1);
+  const long N = trans_w ? w.size(2) : w.size(1);
+  TORCH_CHECK((trans_w ? w.size(1) : w.size(2)) == K, "grouped: inner dimensions differ");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0, "grouped: K and N must be multiples of 8");
+  if (trans_w) TORCH_CHECK(K % BK == 0, "grouped: the reduction dim of a transposed expert weight must be % 64");
+  auto out = torch::empty({T, N}, x.options());
+  if (T == 0 || N == 0) return out;
+  tp_context(x.get_device());
+  MapPair* maps = map_storage();
+  make_map(&maps->a, x.data_ptr(), T, K, K, BM);
+  if (trans_w) make_map(&maps->b, w.data_ptr(), (long)E * K, N, N, 64);
+  else make_map(&maps->b, w.data_ptr(), (long)E * N, K, K, BN);
+  const long n_tiles = (N + BN - 1) / BN;
+  const int grid = (int)std::max<long>(1, std::min<long>((T / BM + E) * n_tiles, num_sms()));
+  if (trans_w) grouped_launch<1>(maps, out.data_ptr(), offsets.data_ptr<int>(), E, (int)N, (int)K, N, grid);
+  else grouped_launch<0>(maps, out.data_ptr(), offsets.data_ptr<int>(), E, (int)N, (int)K, N, grid);
+  return out;
+}
+
+// acc [E, M, N] FP32 += per expert dy[rows_e]^T @ x[rows_e] with dy [T, M], x [T, N] (rows sorted by expert).
+void grouped_gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor offsets, torch::Tensor acc) {
+  TORCH_CHECK(dy.is_cuda() && dy.scalar_type() == at::kBFloat16 && dy.is_contiguous(), "grouped wgrad: dy");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.size(0) == dy.size(0), "grouped wgrad: x");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.dim() == 3, "grouped wgrad: acc");
+  const int E = (int)acc.size(0);
+  TORCH_CHECK(E <= kMaxExperts && offsets.numel() == E + 1 && offsets.scalar_type() == at::kInt, "grouped wgrad: E");
+  const long T = dy.size(0), M = dy.size(1), N = x.size(1);
+  TORCH_CHECK(acc.size(1) == M && acc.size(2) == N && M % 8 == 0 && N % 8 == 0, "grouped wgrad: shapes");
+  if (T == 0) return;
+  tp_context(dy.get_device());
+  MapPair* maps = map_storage();
+  make_map(&maps->a, dy.data_ptr(), T, M, M, 64);
+  make_map(&maps->b, x.data_ptr(), T, N, N, 64);
+  const long tiles = (long)E * ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = (int)std::max<long>(1, std::min<long>(tiles, num_sms()));
+  grouped_launch<2>(maps, acc.data_ptr(), offsets.data_ptr<int>(), E, (int)N, 0, M, grid);
+}

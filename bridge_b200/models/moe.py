@@ -19,6 +19,7 @@ import torch.nn as nn
 from torch import Tensor
 
 from ..ops.activation import swiglu
+from ..ops._ext import kernels, on_gpu
 from ..ops.gemm import linear
 from .config import ModelConfig
 
@@ -42,8 +43,58 @@ class _AllToAll(torch.autograd.Function):
         return out, None, None, None
 
 
-def grouped_swiglu_experts(x: Tensor, counts: list[int], w1: Tensor, w2: Tensor) -> Tensor:
-    """Rows of ``x`` sorted by expert (``counts[e]`` rows each) through expert ``e``'s SwiGLU."""
+class _GroupedSwiGLUExperts(torch.autograd.Function):
+    """All experts' SwiGLU FFNs as two grouped tcgen05 GEMMs over expert-sorted rows (device offsets)."""
+
+    @staticmethod
+    def forward(ctx, x, w1, w2, offsets):
+        m = kernels()
+        h1 = m.grouped_gemm(x, w1, offsets, False)          # [R, 2F] = x W1_e^T
+        a = m.swiglu_fwd(h1)                                 # [R, F]
+        y = m.grouped_gemm(a, w2, offsets, False)           # [R, H] = a W2_e^T
+        ctx.save_for_backward(x, h1, a, w1, w2, offsets)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        m = kernels()
+        x, h1, a, w1, w2, offsets = ctx.saved_tensors
+        dy = dy.contiguous()
+        da = m.grouped_gemm(dy, w2, offsets, True)          # dy W2_e
+        dh1 = m.swiglu_bwd(da, h1)
+        dx = m.grouped_gemm(dh1, w1, offsets, True)         # dh1 W1_e
+        grads = []
+        for w, g_out, g_in in ((w1, dh1, x), (w2, dy, a)):
+            main = getattr(w, "main_grad", None)
+            if main is not None:                           # accumulate straight into the FP32 main grad
+                m.grouped_gemm_wgrad(g_out, g_in, offsets, main)
+                grads.append(None)
+            else:
+                acc = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+                m.grouped_gemm_wgrad(g_out, g_in, offsets, acc)
+                grads.append(acc.to(w.dtype))
+        return dx, grads[0], grads[1], None
+
+
+def _grouped_ok(x: Tensor, w1: Tensor, w2: Tensor) -> bool:
+    h, f2, f = w1.shape[2], w1.shape[1], w2.shape[2]
+    return (on_gpu(x) and x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and h % 64 == 0
+            and f2 % 64 == 0 and f % 8 == 0 and w1.shape[0] <= 1024)
+
+
+def grouped_swiglu_experts(x: Tensor, counts, w1: Tensor, w2: Tensor) -> Tensor:
+    """Rows of ``x`` sorted by expert (``counts[e]`` rows each) through expert ``e``'s SwiGLU.
+
+    ``counts`` is a host list or a device tensor; on CUDA the experts run as grouped tcgen05 GEMMs
+    whose tile scheduler reads the expert offsets on the device (no host synchronisation).
+    """
+    if _grouped_ok(x, w1, w2):
+        c = counts if isinstance(counts, Tensor) else torch.tensor(counts, device=x.device)
+        offsets = torch.zeros(w1.shape[0] + 1, dtype=torch.int32, device=x.device)
+        offsets[1:] = torch.cumsum(c.to(x.device), 0).to(torch.int32)
+        return _GroupedSwiGLUExperts.apply(x.contiguous(), w1, w2, offsets)
+    if isinstance(counts, Tensor):
+        counts = counts.tolist()
     outs = []
     s = 0
     for e, n in enumerate(counts):
@@ -98,7 +149,7 @@ class MoELayer(nn.Module):
         self.last_load = counts_all.detach()
         ep = _ep_size(self.ep_group)
         if ep == 1:
-            y_sorted = grouped_swiglu_experts(xs, counts_all.tolist(), self.w1, self.w2)
+            y_sorted = grouped_swiglu_experts(xs, counts_all, self.w1, self.w2)
         else:
             per_rank = counts_all.view(ep, self.local_experts)
             send = per_rank.sum(1)
