@@ -54,6 +54,9 @@ class EngineConfig:
     # ring / all-gather CP attention transport: "auto" (NVLink P2P gather + owner reduction on a
     # single-node CUDA group, NCCL otherwise), "nvlink" or "nccl"
     cp_comm: str = "auto"
+    # MoE expert-parallel dispatch / combine: "auto" (NVLink P2P gathers on a single-node CUDA group,
+    # NCCL all-to-all otherwise), "nvlink" or "nccl"
+    ep_comm: str = "auto"
     extra: dict = field(default_factory=dict)
 
     def with_env(self) -> "EngineConfig":
@@ -75,6 +78,8 @@ class EngineConfig:
             kw["token_budget"] = _env_int("TPR_TOKEN_BUDGET", self.token_budget)
         if "TPR_EXECUTOR" in os.environ:
             kw["executor"] = os.environ["TPR_EXECUTOR"]
+        if "TPR_EP_COMM" in os.environ:
+            kw["ep_comm"] = os.environ["TPR_EP_COMM"]
         if "TPR_CP_COMM" in os.environ:
             kw["cp_comm"] = os.environ["TPR_CP_COMM"]
         if "TPR_TP_COMM" in os.environ:
@@ -84,6 +89,8 @@ class EngineConfig:
         cfg = replace(self, **kw) if kw else self
         if cfg.tree_policy not in ("exact", "qwen_turn"):
             raise ValueError(f"unknown TPR tree_policy: {cfg.tree_policy!r}")
+        if cfg.ep_comm not in ("auto", "nvlink", "nccl"):
+            raise ValueError(f"unknown ep_comm: {cfg.ep_comm!r}")
         if cfg.cp_comm not in ("auto", "nvlink", "nccl"):
             raise ValueError(f"unknown cp_comm: {cfg.cp_comm!r}")
         if cfg.tp_comm not in ("auto", "nvlink", "nccl"):

@@ -148,8 +148,16 @@ class MoELayer(nn.Module):
         counts_all = torch.bincount(flat_e, minlength=self.num_experts)
         self.last_load = counts_all.detach()
         ep = _ep_size(self.ep_group)
+        comm = None
+        if ep > 1:
+            from ..parallel.ep_p2p import ep_comm, ep_moe_experts
+
+            comm = ep_comm(self.ep_group, xs)
         if ep == 1:
             y_sorted = grouped_swiglu_experts(xs, counts_all, self.w1, self.w2)
+        elif comm is not None:                 # NVLink P2P dispatch / combine around the grouped GEMMs
+            y_sorted = ep_moe_experts(xs, counts_all, comm, self.local_experts,
+                                      lambda xr, cl: grouped_swiglu_experts(xr, cl, self.w1, self.w2))
         else:
             per_rank = counts_all.view(ep, self.local_experts)
             send = per_rank.sum(1)

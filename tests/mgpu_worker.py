@@ -171,8 +171,62 @@ def cp_p2p() -> None:
     dist.destroy_process_group()
 
 
+def ep_p2p() -> None:
+    """MoE layer with EP over the NVLink P2P dispatch/combine vs the NCCL all-to-all path and vs the
+    unsharded layer (all experts on every rank)."""
+    from bridge_b200.models import get_config
+    from bridge_b200.models.moe import MoELayer
+    from bridge_b200.parallel import ep_p2p
+    from bridge_b200.parallel.groups import init_distributed
+
+    rank, world = init_distributed(timeout_s=120)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    group = dist.group.WORLD
+    cfg = get_config("tiny_moe", hidden_size=256, moe_intermediate_size=128, num_experts=8, moe_top_k=3)
+    torch.manual_seed(0)
+    full = MoELayer(cfg, device=dev)
+    with torch.no_grad():
+        full.router.mul_(20.0)
+    el = cfg.num_experts // world
+    x = torch.randn(257 + 31 * rank, 256, device=dev, generator=torch.Generator(device=dev).manual_seed(rank)).bfloat16()
+    dy = torch.randn(x.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(50 + rank)).bfloat16()
+    xf = x.clone().requires_grad_()
+    yf = full(xf)
+    yf.backward(dy)
+    gfull = {n: p.grad.float() for n, p in full.named_parameters()}
+    for n in ("w1", "w2"):
+        dist.all_reduce(gfull[n], group=group)          # expert grads see every rank's tokens under EP
+    for mode in ("nvlink", "nccl"):
+        ep_p2p.set_ep_comm_mode(mode)
+        torch.manual_seed(0)
+        layer = MoELayer(cfg, ep_group=group, device=dev)
+        with torch.no_grad():
+            layer.router.copy_(full.router)
+            layer.w1.copy_(full.w1[rank * el:(rank + 1) * el])
+            layer.w2.copy_(full.w2[rank * el:(rank + 1) * el])
+            for n in ("shared_w1", "shared_w2", "shared_gate"):
+                getattr(layer, n).copy_(getattr(full, n))
+        xe = x.clone().requires_grad_()
+        ye = layer(xe)
+        ye.backward(dy)
+        def close(a, b, name):
+            err = (a.float() - b.float()).abs().max().item()
+            tol = 2e-2 * b.float().abs().max().item() + 1e-3
+            assert err <= tol, (mode, name, err, tol)
+        close(ye, yf, "y")
+        close(xe.grad, xf.grad, "dx")
+        close(layer.w1.grad, gfull["w1"][rank * el:(rank + 1) * el], "dw1")
+        close(layer.w2.grad, gfull["w2"][rank * el:(rank + 1) * el], "dw2")
+    assert ep_p2p._COMMS, "P2P dispatch was not used"
+    ep_p2p.close_all()
+    dist.barrier()
+    if rank == 0:
+        print("EP_P2P_OK", flush=True)
+    dist.destroy_process_group()
+
+
 if __name__ == "__main__":
     import os
 
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
-    {"dp_nvlink": dp_nvlink, "tp_fused": tp_fused, "cp_p2p": cp_p2p}[sys.argv[1]]()
+    {"dp_nvlink": dp_nvlink, "tp_fused": tp_fused, "cp_p2p": cp_p2p, "ep_p2p": ep_p2p}[sys.argv[1]]()

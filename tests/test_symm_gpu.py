@@ -67,3 +67,8 @@ def test_tp_fused_linears_match_nccl_two_gpus():
 @pytest.mark.multigpu
 def test_cp_p2p_attention_matches_flattened_two_gpus():
     _run_worker("cp_p2p", "CP_P2P_OK")
+
+
+@pytest.mark.multigpu
+def test_ep_p2p_moe_matches_unsharded_two_gpus():
+    _run_worker("ep_p2p", "EP_P2P_OK")
