@@ -54,11 +54,12 @@ std::vector<torch::Tensor> causal_conv1d_bwd(torch::Tensor dy, torch::Tensor x, 
                                              c10::optional<torch::Tensor> dhT, torch::Tensor cu, int64_t max_len,
                                              bool silu_act);
 std::vector<torch::Tensor> gdr_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
-                                   torch::Tensor beta, c10::optional<torch::Tensor> h0, torch::Tensor cu,
-                                   int64_t max_len, double scale, int64_t chunk);
+                                   torch::Tensor beta, c10::optional<torch::Tensor> h0, torch::Tensor chunks,
+                                   torch::Tensor seq0, int64_t max_chunks, double scale);
 std::vector<torch::Tensor> gdr_bwd(torch::Tensor dout, c10::optional<torch::Tensor> dhT, torch::Tensor q,
                                    torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
-                                   torch::Tensor ckpt, torch::Tensor cu, int64_t max_len, bool has_h0, double scale);
+                                   torch::Tensor ckpt, torch::Tensor wk, torch::Tensor u, torch::Tensor chunks,
+                                   torch::Tensor seq0, int64_t max_chunks, bool has_h0, double scale);
 std::vector<torch::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(torch::Tensor handle);
 void symm_close(int64_t ptr);

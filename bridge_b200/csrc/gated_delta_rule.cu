@@ -1,20 +1,25 @@
-// Chunked gated delta rule (Gated DeltaNet), forward and backward, with initial / final state.
+// Chunked gated delta rule (Gated DeltaNet) on bf16 tensor cores, forward and backward, varlen,
+// with initial / final state.
 //
 // Recurrence (per head, FLA convention): S_t = e^{g_t} S_{t-1};  u_t = beta_t (v_t - S_t^T k_t);
 // S_t += k_t u_t^T;  o_t = scale * S_t^T q_t.  State S is [K, V] FP32.
 //
-// The value columns of S evolve independently, so one CTA owns (sequence b, head h, value block of
-// VB=32 columns): its state block [K, VB] lives in shared memory for the whole sequence.  Chunks of
-// CS=64 tokens use the WY/UT form (G = cumsum g, D_ts = e^{G_t-G_s}):
+// Chunks of C = 64 tokens (G = cumsum g inside the chunk, Gam = e^G, D_ts = e^{G_t - G_s},
+// E_t = e^{G_last - G_t}):
 //   A = D o (K K^T) strictly lower,  T = (I + diag(beta) A)^-1,
-//   Wk = T diag(beta e^G) K,  U = T diag(beta) V - Wk S0,
-//   O = scale (diag(e^G) Q S0 + (D o Q K^T)_{s<=t} U),   S1 = e^{G_n} S0 + K^T diag(e^{G_n-G}) U.
-// Forward checkpoints S0 of every chunk (FP32) for the backward, which walks the chunks in reverse,
-// recomputes the chunk intermediates and applies the hand-derived adjoint of every line above.
-// dq / dk / dg / dbeta are sums over value blocks (FP32 atomics); dv and dh0 are written by their owner.
-//
-// Matrix products run on CUDA cores from padded shared memory (FP32 accumulation); q/k are kept as
-// bf16 in shared memory (exact copies of the inputs).
+//   Wk = T diag(beta Gam) K,  Wv = T diag(beta) V,  U = Wv - Wk S0,
+//   O = scale (diag(Gam) Q S0 + (D o Q K^T)_{s<=t} U),   S1 = Gam_last S0 + K^T diag(E) U.
+// Everything except the S0 -> S1 chain is independent per chunk, so the work is split into
+//   gdr_prep_kernel       per (chunk, head):          A, T (blocked 16x16 inverse), Wk, Wv
+//   gdr_scan_kernel       per (sequence, head, V blk): the state chain; U, O, S1; FP32 chunk states
+//   gdr_bwd_scan_kernel   per (sequence, head, V blk): reverse chain of dS; dU, dWk and the
+//                                                      state-dependent parts of dq / dk / dG
+//   gdr_bwd_chunk_kernel  per (chunk, head):          everything else (through dP, dT, dL = -T^T dT T^T)
+// and every matrix product runs on mma.sync bf16 tensor cores with FP32 accumulation; the chained
+// FP32 states (S0, dS1) enter the tensor cores as bf16 hi + lo pairs (two passes) so the chain keeps
+// ~16 significant bits instead of bf16's 8.  Gradients
+// shared by the V blocks of one head (dq, dk, dWk, dG) are summed with FP32 atomics in the scan
+// kernels and finished by the chunk kernel, which owns its rows.
 //
 // Parity: MindSpeed-Ops chunk_gated_delta_rule (chunk 64, head_first=False, initial_state /
 // output_final_state, dh0 / dht) as called from verl/models/mcore/tpr/gated_delta_net.py:239-263.
@@ -22,63 +27,57 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include "common.cuh"
+#include "warp_mma.cuh"
 
 namespace {
 
 constexpr int CS = 64;
-constexpr int VB = 32;
 constexpr int NT = 256;
+using bf = __nv_bfloat16;
 
-template <int K>
-struct Lay {
-  static constexpr int LQ = K + 2;   // bf16 row stride (odd word count -> conflict-free column walks)
-  static constexpr int LW = K + 1;   // fp32 [CS][K]
-  static constexpr int LS = VB + 1;  // fp32 [K][VB] and [CS][VB]
-  static constexpr int LN = CS + 1;  // fp32 [CS][CS]
+__device__ __forceinline__ float b2f(bf x) { return __bfloat162float(x); }
+__device__ __forceinline__ bf f2b(float x) { return __float2bfloat16(x); }
+
+struct Chunk {
+  int row0, n, b, c;
 };
 
-__device__ __forceinline__ float bf(const __nv_bfloat16 x) { return __bfloat162float(x); }
-
-template <int K>
-__device__ __forceinline__ float dotqk(const __nv_bfloat16* a, const __nv_bfloat16* b) {
-  float s = 0.f;
-#pragma unroll 8
-  for (int i = 0; i < K; ++i) s += bf(a[i]) * bf(b[i]);
-  return s;
+__device__ __forceinline__ Chunk load_chunk_desc(const int* chunks, int i) {
+  const int4 d = reinterpret_cast<const int4*>(chunks)[i];
+  return {d.x, d.y, d.z, d.w};
 }
 
-// Load one chunk of q, k (bf16 rows), v block, g, beta; rows >= n are zero.
-template <int K>
-__device__ void load_chunk(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                           const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
-                           const float* __restrict__ beta, int row0, int n, int H, int V, int h, int v0,
-                           __nv_bfloat16* sQ, __nv_bfloat16* sK, float* sV, float* sG, float* sB) {
-  using LY = Lay<K>;
-  for (int i = threadIdx.x; i < CS * K; i += NT) {
-    const int t = i / K, c = i % K;
-    const bool ok = t < n;
-    const size_t off = ((size_t)(row0 + t) * H + h) * K + c;
-    sQ[t * LY::LQ + c] = ok ? q[off] : __float2bfloat16(0.f);
-    sK[t * LY::LQ + c] = ok ? k[off] : __float2bfloat16(0.f);
-  }
-  for (int i = threadIdx.x; i < CS * VB; i += NT) {
-    const int t = i / VB, j = i % VB;
-    sV[t * LY::LS + j] = t < n ? bf(v[((size_t)(row0 + t) * H + h) * V + v0 + j]) : 0.f;
-  }
-  for (int t = threadIdx.x; t < CS; t += NT) {
-    sG[t] = t < n ? g[(size_t)(row0 + t) * H + h] : 0.f;
-    sB[t] = t < n ? beta[(size_t)(row0 + t) * H + h] : 0.f;
+// rows [row0, row0+n) of a [T, H, W] bf16 tensor (head h, columns [c0, c0+w)) -> smem [64][ld]; zero rows >= n
+template <int W>
+__device__ __forceinline__ void load_rows(bf* dst, int ld, const bf* __restrict__ src, int row0, int n, int H, int h,
+                                          int width, int c0) {
+  constexpr int VEC = W / 8;
+  for (int i = threadIdx.x; i < CS * VEC; i += NT) {
+    const int t = i / VEC, v = i % VEC;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (t < n) val = *reinterpret_cast<const uint4*>(src + ((size_t)(row0 + t) * H + h) * width + c0 + v * 8);
+    *reinterpret_cast<uint4*>(dst + t * ld + v * 8) = val;
   }
 }
 
-// G = cumsum(g) (in place), Gam = exp(G), E = exp(G_last - G).
-__device__ void chunk_scan(float* sG, float* sGam, float* sE, int n) {
-  if (threadIdx.x == 0) {
-    float acc = 0.f;
-    for (int t = 0; t < CS; ++t) {
-      acc += sG[t];
-      sG[t] = acc;
+// G = cumsum(g) over the chunk (rows >= n hold the last value), Gam = e^G, E = e^{G_last - G}.
+__device__ __forceinline__ void chunk_decay(const float* __restrict__ g, int row0, int n, int H, int h, float* sG,
+                                            float* sGam, float* sE) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float a = lane < n ? g[(size_t)(row0 + lane) * H + h] : 0.f;
+    float b = lane + 32 < n ? g[(size_t)(row0 + lane + 32) * H + h] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float ya = __shfl_up_sync(0xffffffffu, a, o), yb = __shfl_up_sync(0xffffffffu, b, o);
+      if (lane >= o) {
+        a += ya;
+        b += yb;
+      }
     }
+    b += __shfl_sync(0xffffffffu, a, 31);
+    sG[lane] = a;
+    sG[lane + 32] = b;
   }
   __syncthreads();
   const float gl = sG[max(n - 1, 0)];
@@ -89,496 +88,753 @@ __device__ void chunk_scan(float* sG, float* sGam, float* sE, int n) {
   __syncthreads();
 }
 
-// A (strictly lower, D o KK^T) and T = (I + diag(beta) A)^-1 (lower, unit diagonal).
-template <int K>
-__device__ void build_A_T(const __nv_bfloat16* sK, const float* sG, const float* sB, float* sA, float* sT, int n) {
-  using LY = Lay<K>;
-  for (int i = threadIdx.x; i < CS * CS; i += NT) {
-    const int t = i / CS, s = i % CS;
-    float a = 0.f;
-    if (s < t && t < n) a = __expf(sG[t] - sG[s]) * dotqk<K>(sK + t * LY::LQ, sK + s * LY::LQ);
-    sA[t * LY::LN + s] = a;
-    sT[t * LY::LN + s] = 0.f;
+// sA (fp32 [64][65]) = D o K K^T strictly lower (raw, without beta); sTf = (I + diag(beta) A)^-1 (fp32);
+// sTb = bf16(sTf) with rows >= n zeroed.  The inverse is blocked by 16: each of the first four warps
+// inverts one unit-lower diagonal block by warp-synchronous substitution, then the off-diagonal
+// blocks follow level by level, T_ij = -T_ii sum_{j<=k<i} L_ik T_kj (L_ik = diag(beta) A block).
+template <int KD>
+__device__ void build_T(const bf* sK, int ldk, const float* sG, const float* sB, float* sA, float* sTf, bf* sTb, int n) {
+  wm::block_gemm<false, true>(CS, CS, KD, sK, ldk, sK, ldk, [&](int t, int s, float v) {
+    sA[t * 65 + s] = (s < t && t < n) ? __expf(sG[t] - sG[s]) * v : 0.f;
+  });
+  for (int i = threadIdx.x; i < CS * 65; i += NT) sTf[i] = 0.f;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < 4) {  // diagonal block w: rows / cols [16w, 16w + 16)
+    const int o = warp * 16;
+    const int c = lane & 15;
+    if (lane < 16) sTf[(o + c) * 65 + o + c] = 1.f;
+    __syncwarp();
+    for (int r = 1; r < 16; ++r) {
+      if (lane < r) {
+        float acc = 0.f;
+        for (int s2 = c; s2 < r; ++s2) acc += sA[(o + r) * 65 + o + s2] * sTf[(o + s2) * 65 + o + c];
+        sTf[(o + r) * 65 + o + c] = -sB[o + r] * acc;
+      }
+      __syncwarp();
+    }
   }
   __syncthreads();
-  // forward substitution, row by row: T[t, j] = [t==j] - beta_t sum_{j<=s<t} A[t, s] T[s, j]
-  for (int t = 0; t < n; ++t) {
-    for (int j = threadIdx.x; j <= t; j += NT) {
-      float acc = 0.f;
-      for (int s = j; s < t; ++s) acc += sA[t * LY::LN + s] * sT[s * LY::LN + j];
-      sT[t * LY::LN + j] = (t == j ? 1.f : 0.f) - sB[t] * acc;
+  float* scratch = sTf + CS * 65;  // callers reserve 4 x 16 x 17 floats after sTf
+  for (int d = 1; d < 4; ++d) {
+    const int blk = warp;              // block (i, j) = (j + d, j), j = warp
+    if (blk + d < 4) {
+      const int i = blk + d, j = blk;
+      float* X = scratch + warp * 16 * 17;
+      // X = sum_{k=j}^{i-1} L_ik T_kj  (16 x 16), each lane 8 elements
+      for (int e = lane; e < 256; e += 32) {
+        const int r = e / 16, c = e % 16;
+        float acc = 0.f;
+        for (int kb = j; kb < i; ++kb)
+          for (int m = 0; m < 16; ++m)
+            acc += sB[i * 16 + r] * sA[(i * 16 + r) * 65 + kb * 16 + m] * sTf[(kb * 16 + m) * 65 + j * 16 + c];
+        X[r * 17 + c] = acc;
+      }
+      __syncwarp();
+      for (int e = lane; e < 256; e += 32) {
+        const int r = e / 16, c = e % 16;
+        float acc = 0.f;
+        for (int m = 0; m <= r; ++m) acc += sTf[(i * 16 + r) * 65 + i * 16 + m] * X[m * 17 + c];
+        sTf[(i * 16 + r) * 65 + j * 16 + c] = -acc;
+      }
     }
     __syncthreads();
   }
-}
-
-// Wk = T diag(beta Gam) K  [CS x K];  U = T diag(beta) V - Wk S0  [CS x VB]
-template <int K>
-__device__ void build_W_U(const __nv_bfloat16* sK, const float* sT, const float* sB, const float* sGam,
-                          const float* sV, const float* sS, float* sW, float* sU, int n) {
-  using LY = Lay<K>;
-  for (int i = threadIdx.x; i < CS * K; i += NT) {
-    const int t = i / K, c = i % K;
-    float acc = 0.f;
-    if (t < n)
-      for (int s = 0; s <= t; ++s) acc += sT[t * LY::LN + s] * sB[s] * sGam[s] * bf(sK[s * LY::LQ + c]);
-    sW[t * LY::LW + c] = acc;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < CS * VB; i += NT) {
-    const int t = i / VB, j = i % VB;
-    float acc = 0.f;
-    if (t < n) {
-      for (int s = 0; s <= t; ++s) acc += sT[t * LY::LN + s] * sB[s] * sV[s * LY::LS + j];
-      for (int c = 0; c < K; ++c) acc -= sW[t * LY::LW + c] * sS[c * LY::LS + j];
-    }
-    sU[t * LY::LS + j] = acc;
+  for (int i = threadIdx.x; i < CS * CS; i += NT) {
+    const int r = i / CS, c = i % CS;
+    sTb[r * 72 + c] = f2b(r < n ? sTf[r * 65 + c] : 0.f);
   }
   __syncthreads();
 }
 
-template <int K>
-struct FwdSmem {
-  using LY = Lay<K>;
-  static constexpr size_t Q = 0;
-  static constexpr size_t KK = Q + sizeof(__nv_bfloat16) * CS * LY::LQ;
-  static constexpr size_t W = KK + sizeof(__nv_bfloat16) * CS * LY::LQ;
-  static constexpr size_t S = W + sizeof(float) * CS * LY::LW;
-  static constexpr size_t V = S + sizeof(float) * K * LY::LS;
-  static constexpr size_t U = V + sizeof(float) * CS * LY::LS;
-  static constexpr size_t A = U + sizeof(float) * CS * LY::LS;
-  static constexpr size_t T = A + sizeof(float) * CS * LY::LN;
-  static constexpr size_t VEC = T + sizeof(float) * CS * LY::LN;  // G, B, Gam, E
+// ------------------------------------------------------------------------------------------------ forward
+template <int KD, int VD>
+struct PrepSmem {
+  static constexpr int LK = KD + 8, LV = VD + 8;
+  static constexpr size_t K = 0;
+  static constexpr size_t KB = K + sizeof(bf) * CS * LK;
+  static constexpr size_t VB = KB + sizeof(bf) * CS * LK;
+  static constexpr size_t A = VB + sizeof(bf) * CS * LV;
+  static constexpr size_t TF = A + sizeof(float) * CS * 65;
+  static constexpr size_t TB = TF + sizeof(float) * (CS * 65 + 4 * 16 * 17);   // T + blocked-inverse scratch
+  static constexpr size_t VEC = TB + sizeof(bf) * CS * 72;
   static constexpr size_t TOTAL = VEC + sizeof(float) * 4 * CS;
 };
 
-template <int K>
-__global__ void __launch_bounds__(NT) gdr_fwd_kernel(
-    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
-    const float* __restrict__ g, const float* __restrict__ beta, const float* __restrict__ h0,
-    const int* __restrict__ cu, __nv_bfloat16* __restrict__ o, float* __restrict__ hT, float* __restrict__ ckpt,
-    int H, int V, int nc_max, float scale) {
-  using LY = Lay<K>;
-  using SM = FwdSmem<K>;
+template <int KD, int VD>
+__global__ void __launch_bounds__(NT) gdr_prep_kernel(const bf* __restrict__ k, const bf* __restrict__ v,
+                                                      const float* __restrict__ g, const float* __restrict__ beta,
+                                                      const int* __restrict__ chunks, bf* __restrict__ wk,
+                                                      bf* __restrict__ wv, int H) {
+  using SM = PrepSmem<KD, VD>;
   extern __shared__ __align__(16) unsigned char smem[];
-  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem + SM::Q);
-  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(smem + SM::KK);
-  float* sW = reinterpret_cast<float*>(smem + SM::W);
-  float* sS = reinterpret_cast<float*>(smem + SM::S);
-  float* sV = reinterpret_cast<float*>(smem + SM::V);
-  float* sU = reinterpret_cast<float*>(smem + SM::U);
+  bf* sK = reinterpret_cast<bf*>(smem + SM::K);
+  bf* sKb = reinterpret_cast<bf*>(smem + SM::KB);
+  bf* sVb = reinterpret_cast<bf*>(smem + SM::VB);
   float* sA = reinterpret_cast<float*>(smem + SM::A);
-  float* sT = reinterpret_cast<float*>(smem + SM::T);
+  float* sTf = reinterpret_cast<float*>(smem + SM::TF);
+  bf* sTb = reinterpret_cast<bf*>(smem + SM::TB);
   float* sG = reinterpret_cast<float*>(smem + SM::VEC);
-  float* sB = sG + CS;
-  float* sGam = sB + CS;
+  float* sGam = sG + CS;
   float* sE = sGam + CS;
-
-  const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int v0 = vb * VB;
-  const int q0 = cu[b], L = cu[b + 1] - q0;
-  const int nch = (L + CS - 1) / CS;
-  for (int i = threadIdx.x; i < K * VB; i += NT) {
-    const int c = i / VB, j = i % VB;
-    sS[c * LY::LS + j] = h0 ? h0[(((size_t)b * H + h) * K + c) * V + v0 + j] : 0.f;
+  float* sB = sE + CS;
+  const Chunk ch = load_chunk_desc(chunks, blockIdx.x);
+  const int h = blockIdx.y;
+  load_rows<KD>(sK, SM::LK, k, ch.row0, ch.n, H, h, KD, 0);
+  for (int t = threadIdx.x; t < CS; t += NT) sB[t] = t < ch.n ? beta[(size_t)(ch.row0 + t) * H + h] : 0.f;
+  chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);
+  // scaled operands: Kb = beta Gam K, Vb = beta V
+  for (int i = threadIdx.x; i < CS * KD; i += NT) {
+    const int t = i / KD, c = i % KD;
+    sKb[t * SM::LK + c] = f2b(sB[t] * sGam[t] * b2f(sK[t * SM::LK + c]));
+  }
+  for (int i = threadIdx.x; i < CS * VD; i += NT) {
+    const int t = i / VD, c = i % VD;
+    sVb[t * SM::LV + c] = t < ch.n ? f2b(sB[t] * b2f(v[((size_t)(ch.row0 + t) * H + h) * VD + c])) : f2b(0.f);
   }
   __syncthreads();
-  for (int ch = 0; ch < nch; ++ch) {
-    const int t0 = ch * CS, n = min(CS, L - t0);
-    float* ck = ckpt + ((((size_t)b * H + h) * nc_max + ch) * K) * V;
-    for (int i = threadIdx.x; i < K * VB; i += NT) {
-      const int c = i / VB, j = i % VB;
-      ck[(size_t)c * V + v0 + j] = sS[c * LY::LS + j];
-    }
-    load_chunk<K>(q, k, v, g, beta, q0 + t0, n, H, V, h, v0, sQ, sK, sV, sG, sB);
-    __syncthreads();
-    chunk_scan(sG, sGam, sE, n);
-    build_A_T<K>(sK, sG, sB, sA, sT, n);
-    build_W_U<K>(sK, sT, sB, sGam, sV, sS, sW, sU, n);
-    // P = D o (Q K^T) for s <= t (into sA; A is no longer needed)
-    for (int i = threadIdx.x; i < CS * CS; i += NT) {
-      const int t = i / CS, s = i % CS;
-      float p = 0.f;
-      if (s <= t && t < n) p = __expf(sG[t] - sG[s]) * dotqk<K>(sQ + t * LY::LQ, sK + s * LY::LQ);
-      sA[t * LY::LN + s] = p;
-    }
-    __syncthreads();
-    // O = scale (Gam o (Q S0) + P U)
-    for (int i = threadIdx.x; i < CS * VB; i += NT) {
-      const int t = i / VB, j = i % VB;
-      if (t >= n) continue;
-      float qs = 0.f;
-      for (int c = 0; c < K; ++c) qs += bf(sQ[t * LY::LQ + c]) * sS[c * LY::LS + j];
-      float pu = 0.f;
-      for (int s = 0; s <= t; ++s) pu += sA[t * LY::LN + s] * sU[s * LY::LS + j];
-      o[((size_t)(q0 + t0 + t) * H + h) * V + v0 + j] = __float2bfloat16(scale * (sGam[t] * qs + pu));
-    }
-    __syncthreads();
-    // S1 = Gam_last S0 + K^T diag(E) U
-    const float gl = sGam[n - 1];
-    for (int i = threadIdx.x; i < K * VB; i += NT) {
-      const int c = i / VB, j = i % VB;
-      float acc = gl * sS[c * LY::LS + j];
-      for (int t = 0; t < n; ++t) acc += bf(sK[t * LY::LQ + c]) * sE[t] * sU[t * LY::LS + j];
-      sS[c * LY::LS + j] = acc;
-    }
-    __syncthreads();
-  }
-  for (int i = threadIdx.x; i < K * VB; i += NT) {
-    const int c = i / VB, j = i % VB;
-    hT[(((size_t)b * H + h) * K + c) * V + v0 + j] = sS[c * LY::LS + j];
-  }
+  build_T<KD>(sK, SM::LK, sG, sB, sA, sTf, sTb, ch.n);
+  wm::block_gemm<false, false>(CS, KD, CS, sTb, 72, sKb, SM::LK, [&](int t, int c, float val) {
+    if (t < ch.n) wk[((size_t)(ch.row0 + t) * H + h) * KD + c] = f2b(val);
+  });
+  wm::block_gemm<false, false>(CS, VD, CS, sTb, 72, sVb, SM::LV, [&](int t, int c, float val) {
+    if (t < ch.n) wv[((size_t)(ch.row0 + t) * H + h) * VD + c] = f2b(val);
+  });
 }
 
-template <int K>
-struct BwdSmem {
-  using LY = Lay<K>;
+template <int KD, int VB>
+struct ScanSmem {
+  static constexpr int LK = KD + 8, LV = VB + 8;
   static constexpr size_t Q = 0;
-  static constexpr size_t KK = Q + sizeof(__nv_bfloat16) * CS * LY::LQ;
-  static constexpr size_t W = KK + sizeof(__nv_bfloat16) * CS * LY::LQ;  // Wk, then dWk, then dKb
-  static constexpr size_t S0 = W + sizeof(float) * CS * LY::LW;
-  static constexpr size_t DS = S0 + sizeof(float) * K * LY::LS;
-  static constexpr size_t V = DS + sizeof(float) * K * LY::LS;
-  static constexpr size_t DO = V + sizeof(float) * CS * LY::LS;
-  static constexpr size_t U = DO + sizeof(float) * CS * LY::LS;
-  static constexpr size_t DU = U + sizeof(float) * CS * LY::LS;
-  static constexpr size_t A = DU + sizeof(float) * CS * LY::LS;
-  static constexpr size_t T = A + sizeof(float) * CS * LY::LN;
-  static constexpr size_t P = T + sizeof(float) * CS * LY::LN;
-  static constexpr size_t DP = P + sizeof(float) * CS * LY::LN;
-  static constexpr size_t VEC = DP + sizeof(float) * CS * LY::LN;  // G B Gam E dG dB dGam de
-  static constexpr size_t TOTAL = VEC + sizeof(float) * 8 * CS + 16;
+  static constexpr size_t K = Q + sizeof(bf) * CS * LK;
+  static constexpr size_t WK = K + sizeof(bf) * CS * LK;
+  static constexpr size_t S = WK + sizeof(bf) * CS * LK;       // state, bf16 hi then lo
+  static constexpr size_t U = S + 2 * sizeof(bf) * KD * LV;
+  static constexpr size_t EU = U + sizeof(bf) * CS * LV;
+  static constexpr size_t WV = EU + sizeof(bf) * CS * LV;
+  static constexpr size_t P = WV + sizeof(bf) * CS * LV;
+  static constexpr size_t VEC = P + sizeof(bf) * CS * 72;
+  static constexpr size_t TOTAL = VEC + sizeof(float) * 3 * CS;
 };
 
-template <int K>
-__global__ void __launch_bounds__(NT) gdr_bwd_kernel(
-    const __nv_bfloat16* __restrict__ dout, const float* __restrict__ dhT, const __nv_bfloat16* __restrict__ q,
-    const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
-    const float* __restrict__ beta, const float* __restrict__ ckpt, const int* __restrict__ cu,
-    float* __restrict__ dq, float* __restrict__ dk, __nv_bfloat16* __restrict__ dv, float* __restrict__ dg,
-    float* __restrict__ dbeta, float* __restrict__ dh0, int H, int V, int nc_max, float scale) {
-  using LY = Lay<K>;
-  using SM = BwdSmem<K>;
-  extern __shared__ __align__(16) unsigned char smem[];
-  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem + SM::Q);
-  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(smem + SM::KK);
-  float* sW = reinterpret_cast<float*>(smem + SM::W);
-  float* sS0 = reinterpret_cast<float*>(smem + SM::S0);
-  float* sdS = reinterpret_cast<float*>(smem + SM::DS);
-  float* sV = reinterpret_cast<float*>(smem + SM::V);
-  float* sdO = reinterpret_cast<float*>(smem + SM::DO);
-  float* sU = reinterpret_cast<float*>(smem + SM::U);
-  float* sdU = reinterpret_cast<float*>(smem + SM::DU);
-  float* sA = reinterpret_cast<float*>(smem + SM::A);
-  float* sT = reinterpret_cast<float*>(smem + SM::T);
-  float* sP = reinterpret_cast<float*>(smem + SM::P);
-  float* sdP = reinterpret_cast<float*>(smem + SM::DP);
-  float* sG = reinterpret_cast<float*>(smem + SM::VEC);
-  float* sB = sG + CS;
-  float* sGam = sB + CS;
-  float* sE = sGam + CS;
-  float* sdG = sE + CS;
-  float* sdB = sdG + CS;
-  float* sdGam = sdB + CS;
-  float* sde = sdGam + CS;
-  float* sRed = sde + CS;  // 1 float: <dS1, S0>
+// state tiles (16 x 16) of a [KD, VB] matrix owned by warp w: t = w, w + 8, ...
+template <int KD, int VB>
+struct StateTiles {
+  static constexpr int TILES = (KD / 16) * (VB / 16);
+  static constexpr int PER_WARP = (TILES + 7) / 8;
+  static constexpr int TN = VB / 16;
+};
 
+template <int KD, int VD, int VB>
+__global__ void __launch_bounds__(NT) gdr_scan_kernel(
+    const bf* __restrict__ q, const bf* __restrict__ k, const bf* __restrict__ wk, const bf* __restrict__ wv,
+    const float* __restrict__ g, const float* __restrict__ h0, const int* __restrict__ chunks,
+    const int* __restrict__ seq_chunk0, bf* __restrict__ o, bf* __restrict__ u, float* __restrict__ hT,
+    float* __restrict__ ckpt, int H, int nc_max, float scale) {
+  using SM = ScanSmem<KD, VB>;
+  using ST = StateTiles<KD, VB>;
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf* sQ = reinterpret_cast<bf*>(smem + SM::Q);
+  bf* sK = reinterpret_cast<bf*>(smem + SM::K);
+  bf* sWk = reinterpret_cast<bf*>(smem + SM::WK);
+  bf* sS = reinterpret_cast<bf*>(smem + SM::S);
+  bf* sSl = sS + KD * SM::LV;
+  bf* sU = reinterpret_cast<bf*>(smem + SM::U);
+  bf* sEU = reinterpret_cast<bf*>(smem + SM::EU);
+  bf* sWv = reinterpret_cast<bf*>(smem + SM::WV);
+  bf* sP = reinterpret_cast<bf*>(smem + SM::P);
+  float* sG = reinterpret_cast<float*>(smem + SM::VEC);
+  float* sGam = sG + CS;
+  float* sE = sGam + CS;
   const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int v0 = vb * VB;
-  const int q0 = cu[b], L = cu[b + 1] - q0;
-  const int nch = (L + CS - 1) / CS;
-  for (int i = threadIdx.x; i < K * VB; i += NT) {
-    const int c = i / VB, j = i % VB;
-    sdS[c * LY::LS + j] = dhT ? dhT[(((size_t)b * H + h) * K + c) * V + v0 + j] : 0.f;
-  }
-  __syncthreads();
-  for (int ch = nch - 1; ch >= 0; --ch) {
-    const int t0 = ch * CS, n = min(CS, L - t0);
-    const float* ck = ckpt + ((((size_t)b * H + h) * nc_max + ch) * K) * V;
-    for (int i = threadIdx.x; i < K * VB; i += NT) {
-      const int c = i / VB, j = i % VB;
-      sS0[c * LY::LS + j] = ck[(size_t)c * V + v0 + j];
-    }
-    load_chunk<K>(q, k, v, g, beta, q0 + t0, n, H, V, h, v0, sQ, sK, sV, sG, sB);
-    for (int i = threadIdx.x; i < CS * VB; i += NT) {
-      const int t = i / VB, j = i % VB;
-      sdO[t * LY::LS + j] = t < n ? bf(dout[((size_t)(q0 + t0 + t) * H + h) * V + v0 + j]) : 0.f;
-    }
-    for (int t = threadIdx.x; t < CS; t += NT) sdG[t] = sdB[t] = sdGam[t] = sde[t] = 0.f;
-    if (threadIdx.x == 0) sRed[0] = 0.f;
-    __syncthreads();
-    chunk_scan(sG, sGam, sE, n);
-    build_A_T<K>(sK, sG, sB, sA, sT, n);
-    build_W_U<K>(sK, sT, sB, sGam, sV, sS0, sW, sU, n);
-    // P = D o QK^T (s <= t)
-    for (int i = threadIdx.x; i < CS * CS; i += NT) {
-      const int t = i / CS, s = i % CS;
-      float p = 0.f;
-      if (s <= t && t < n) p = __expf(sG[t] - sG[s]) * dotqk<K>(sQ + t * LY::LQ, sK + s * LY::LQ);
-      sP[t * LY::LN + s] = p;
-    }
-    __syncthreads();
-    // dU = scale P^T dO + E o (K dS);  de_s = sum_j (K dS)[s,j] U[s,j]
-    for (int i = threadIdx.x; i < CS * VB; i += NT) {
-      const int s = i / VB, j = i % VB;
-      float a = 0.f, kds = 0.f;
-      if (s < n) {
-        for (int t = s; t < n; ++t) a += sP[t * LY::LN + s] * sdO[t * LY::LS + j];
-        for (int c = 0; c < K; ++c) kds += bf(sK[s * LY::LQ + c]) * sdS[c * LY::LS + j];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c_begin = seq_chunk0[b], c_end = seq_chunk0[b + 1];
+
+  float st[ST::PER_WARP][2][4];
+#pragma unroll
+  for (int i = 0; i < ST::PER_WARP; ++i) {
+    const int t = warp + 8 * i;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = (t / ST::TN) * 16 + (lane >> 2) + 8 * (e >> 1);
+        const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+        st[i][j][e] = (t < ST::TILES && h0) ? h0[(((size_t)b * H + h) * KD + r) * VD + v0 + c] : 0.f;
       }
-      sdU[s * LY::LS + j] = scale * a + sE[s] * kds;
-      if (s < n) atomicAdd(&sde[s], kds * sU[s * LY::LS + j]);
+  }
+  for (int ci = c_begin; ci < c_end; ++ci) {
+    const Chunk ch = load_chunk_desc(chunks, ci);
+    float* ck = ckpt + (((size_t)b * H + h) * nc_max + ch.c) * KD * VD;
+    // checkpoint S0 (FP32) and its bf16 copy for the tensor cores
+#pragma unroll
+    for (int i = 0; i < ST::PER_WARP; ++i) {
+      const int t = warp + 8 * i;
+      if (t >= ST::TILES) continue;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = (t / ST::TN) * 16 + (lane >> 2) + 8 * (e >> 1);
+          const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+          ck[(size_t)r * VD + v0 + c] = st[i][j][e];
+          wm::split_bf16(st[i][j][e], sS[r * SM::LV + c], sSl[r * SM::LV + c]);
+        }
     }
-    // dP = scale dO U^T (s <= t);  <dS1, S0>
-    for (int i = threadIdx.x; i < CS * CS; i += NT) {
-      const int t = i / CS, s = i % CS;
-      float a = 0.f;
-      if (s <= t && t < n)
-        for (int j = 0; j < VB; ++j) a += sdO[t * LY::LS + j] * sU[s * LY::LS + j];
-      sdP[t * LY::LN + s] = scale * a;
-    }
+    load_rows<KD>(sQ, SM::LK, q, ch.row0, ch.n, H, h, KD, 0);
+    load_rows<KD>(sK, SM::LK, k, ch.row0, ch.n, H, h, KD, 0);
+    load_rows<KD>(sWk, SM::LK, wk, ch.row0, ch.n, H, h, KD, 0);
+    load_rows<VB>(sWv, SM::LV, wv, ch.row0, ch.n, H, h, VD, v0);
+    chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);  // ends with __syncthreads
+    // P = D o Q K^T (s <= t)
+    wm::block_gemm<false, true>(CS, CS, KD, sQ, SM::LK, sK, SM::LK, [&](int t, int s, float val) {
+      sP[t * 72 + s] = f2b((s <= t && t < ch.n) ? __expf(sG[t] - sG[s]) * val : 0.f);
+    });
+    // U = Wv - Wk S0
+    wm::block_gemm2<false, false>(CS, VB, KD, sWk, SM::LK, sS, sSl, SM::LV, [&](int t, int c, float val) {
+      const float uu = t < ch.n ? b2f(sWv[t * SM::LV + c]) - val : 0.f;
+      sU[t * SM::LV + c] = f2b(uu);
+      sEU[t * SM::LV + c] = f2b(sE[t] * uu);
+      if (t < ch.n) u[((size_t)(ch.row0 + t) * H + h) * VD + v0 + c] = f2b(uu);
+    });
+    __syncthreads();
+    // O = scale (Gam o (Q S0) + P U)
     {
-      float part = 0.f;
-      for (int i = threadIdx.x; i < K * VB; i += NT) {
-        const int c = i / VB, j = i % VB;
-        part += sdS[c * LY::LS + j] * sS0[c * LY::LS + j];
+      const int tn = VB / 16, tiles = (CS / 16) * tn;
+      for (int t = warp; t < tiles; t += 8) {
+        const int m0 = (t / tn) * 16, n0 = (t % tn) * 16;
+        float c1[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        float c2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        wm::warp_tile<false, false>(c1, sQ, SM::LK, sS, SM::LV, m0, n0, KD);
+        wm::warp_tile<false, false>(c1, sQ, SM::LK, sSl, SM::LV, m0, n0, KD);
+        wm::warp_tile<false, false>(c2, sP, 72, sU, SM::LV, m0, n0, CS);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int r = m0 + (lane >> 2) + 8 * (e >> 1), c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+            if (r < ch.n)
+              o[((size_t)(ch.row0 + r) * H + h) * VD + v0 + c] = f2b(scale * (sGam[r] * c1[j][e] + c2[j][e]));
+          }
       }
-      part = bb::warp_sum(part);
-      if ((threadIdx.x & 31) == 0) atomicAdd(sRed, part);
     }
-    __syncthreads();
-    // dGam_t += scale <(Q S0)_t, dO_t>;  dG from P: (dD o D)_ts = dP_ts P_ts
-    for (int t = threadIdx.x; t < n; t += NT) {
-      float a = 0.f;
-      for (int j = 0; j < VB; ++j) {
-        float qs = 0.f;
-        for (int c = 0; c < K; ++c) qs += bf(sQ[t * LY::LQ + c]) * sS0[c * LY::LS + j];
-        a += qs * sdO[t * LY::LS + j];
-      }
-      float rs = 0.f, cs = 0.f;
-      for (int s = 0; s <= t; ++s) rs += sdP[t * LY::LN + s] * sP[t * LY::LN + s];
-      for (int u = t; u < n; ++u) cs += sdP[u * LY::LN + t] * sP[u * LY::LN + t];
-      sdGam[t] += scale * a;
-      sdG[t] += rs - cs;
-    }
-    // dQ (this value block's share): scale Gam_t dO_t S0^T + (dP o D) K ;  dK from P: (dP o D)^T Q
-    for (int i = threadIdx.x; i < CS * K; i += NT) {
-      const int t = i / K, c = i % K;
-      if (t >= n) continue;
-      float a = 0.f;
-      for (int j = 0; j < VB; ++j) a += sdO[t * LY::LS + j] * sS0[c * LY::LS + j];
-      a *= scale * sGam[t];
-      float bq = 0.f, bk = 0.f;
-      for (int s = 0; s <= t; ++s) bq += sdP[t * LY::LN + s] * __expf(sG[t] - sG[s]) * bf(sK[s * LY::LQ + c]);
-      for (int u = t; u < n; ++u) bk += sdP[u * LY::LN + t] * __expf(sG[u] - sG[t]) * bf(sQ[u * LY::LQ + c]);
-      // dK from S1 = ... K^T E U:  E_t (U_t . dS_c)
-      float ks = 0.f;
-      for (int j = 0; j < VB; ++j) ks += sU[t * LY::LS + j] * sdS[c * LY::LS + j];
-      const size_t off = ((size_t)(q0 + t0 + t) * H + h) * K + c;
-      atomicAdd(&dq[off], a + bq);
-      atomicAdd(&dk[off], bk + sE[t] * ks);
-    }
-    __syncthreads();
-    // dS0 = scale Q^T (Gam o dO) + Gam_last dS - Wk^T dU   (written into sdS after all uses of dS1)
-    const float gl = sGam[n - 1];
-    // dGam_last += <dS1, S0>; de-terms: dG_last += sum de E, dG_t -= de_t E_t
-    if (threadIdx.x == 0) {
-      float tot = 0.f;
-      for (int t = 0; t < n; ++t) tot += sde[t] * sE[t];
-      sdGam[n - 1] += sRed[0];
-      sdG[n - 1] += tot;
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < n; t += NT) sdG[t] -= sde[t] * sE[t];
-    for (int i = threadIdx.x; i < K * VB; i += NT) {
-      const int c = i / VB, j = i % VB;
-      float a = 0.f, w = 0.f;
-      for (int t = 0; t < n; ++t) {
-        a += bf(sQ[t * LY::LQ + c]) * sGam[t] * sdO[t * LY::LS + j];
-        w += sW[t * LY::LW + c] * sdU[t * LY::LS + j];
-      }
-      sdS[c * LY::LS + j] = scale * a + gl * sdS[c * LY::LS + j] - w;
-    }
-    __syncthreads();
-    // dT = dU (beta o V)^T + dWk (beta Gam o K)^T with dWk = -dU S0^T  (into sA's twin: reuse sP)
-    for (int i = threadIdx.x; i < CS * K; i += NT) {
-      const int t = i / K, c = i % K;
-      float a = 0.f;
-      if (t < n)
-        for (int j = 0; j < VB; ++j) a += sdU[t * LY::LS + j] * sS0[c * LY::LS + j];
-      sW[t * LY::LW + c] = -a;  // dWk
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < CS * CS; i += NT) {
-      const int t = i / CS, s = i % CS;
-      float a = 0.f;
-      if (t < n && s < n) {
-        for (int j = 0; j < VB; ++j) a += sdU[t * LY::LS + j] * sB[s] * sV[s * LY::LS + j];
-        for (int c = 0; c < K; ++c) a += sW[t * LY::LW + c] * sB[s] * sGam[s] * bf(sK[s * LY::LQ + c]);
-      }
-      sP[t * LY::LN + s] = a;  // dT
-    }
-    __syncthreads();
-    // dVb = T^T dU -> dv = beta o dVb, dbeta += <v, dVb>;  dKb = T^T dWk (into sU's role: compute per element)
-    for (int i = threadIdx.x; i < CS * VB; i += NT) {
-      const int s = i / VB, j = i % VB;
-      if (s >= n) continue;
-      float a = 0.f;
-      for (int t = s; t < n; ++t) a += sT[t * LY::LN + s] * sdU[t * LY::LS + j];
-      dv[((size_t)(q0 + t0 + s) * H + h) * V + v0 + j] = __float2bfloat16(sB[s] * a);
-      atomicAdd(&sdB[s], a * sV[s * LY::LS + j]);
-    }
-    for (int i = threadIdx.x; i < CS * K; i += NT) {
-      const int s = i / K, c = i % K;
-      if (s >= n) continue;
-      float a = 0.f;
-      for (int t = s; t < n; ++t) a += sT[t * LY::LN + s] * sW[t * LY::LW + c];
-      const float kv = bf(sK[s * LY::LQ + c]);
-      atomicAdd(&dk[((size_t)(q0 + t0 + s) * H + h) * K + c], sB[s] * sGam[s] * a);
-      const float r = kv * a;
-      atomicAdd(&sdB[s], sGam[s] * r);
-      atomicAdd(&sdGam[s], sB[s] * r);
-    }
-    __syncthreads();
-    // dL = -T^T dT T^T  (two triangular products; dT lives in sP, result into sdP)
-    for (int i = threadIdx.x; i < CS * CS; i += NT) {  // X = dT T^T  (into sdP temporarily)
-      const int t = i / CS, s = i % CS;
-      float a = 0.f;
-      if (t < n && s < n)
-        for (int u = 0; u <= s; ++u) a += sP[t * LY::LN + u] * sT[s * LY::LN + u];
-      sdP[t * LY::LN + s] = a;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < CS * CS; i += NT) {  // dL = -T^T X  (into sP)
-      const int t = i / CS, s = i % CS;
-      float a = 0.f;
-      if (t < n && s < n)
-        for (int u = t; u < n; ++u) a += sT[u * LY::LN + t] * sdP[u * LY::LN + s];
-      sP[t * LY::LN + s] = -a;
-    }
-    __syncthreads();
-    // dA_ts = beta_t dL_ts (s < t); dbeta_t += sum_s dL_ts A_ts; dG from A: (dA o A);  dKK = dA o D
-    for (int t = threadIdx.x; t < n; t += NT) {
-      float r = 0.f, rs = 0.f;
-      for (int s = 0; s < t; ++s) {
-        r += sP[t * LY::LN + s] * sA[t * LY::LN + s];
-        rs += sB[t] * sP[t * LY::LN + s] * sA[t * LY::LN + s];
-      }
-      float cs = 0.f;
-      for (int u = t + 1; u < n; ++u) cs += sB[u] * sP[u * LY::LN + t] * sA[u * LY::LN + t];
-      sdB[t] += r;
-      sdG[t] += rs - cs;
-    }
-    for (int i = threadIdx.x; i < CS * K; i += NT) {
-      const int t = i / K, c = i % K;
-      if (t >= n) continue;
-      float a = 0.f;
-      for (int s = 0; s < n; ++s) {
-        if (s == t) continue;
-        const int hi = max(t, s), lo = min(t, s);
-        const float dkk = sB[hi] * sP[hi * LY::LN + lo] * __expf(sG[hi] - sG[lo]);
-        a += dkk * bf(sK[s * LY::LQ + c]);
-      }
-      atomicAdd(&dk[((size_t)(q0 + t0 + t) * H + h) * K + c], a);
-    }
-    __syncthreads();
-    // dG_t += dGam_t Gam_t; dg = reverse cumsum(dG); flush dbeta
-    if (threadIdx.x == 0) {
-      float acc = 0.f;
-      for (int t = n - 1; t >= 0; --t) {
-        acc += sdG[t] + sdGam[t] * sGam[t];
-        atomicAdd(&dg[(size_t)(q0 + t0 + t) * H + h], acc);
-        atomicAdd(&dbeta[(size_t)(q0 + t0 + t) * H + h], sdB[t]);
-      }
+    // S1 = Gam_last S0 + K^T (E o U)
+    const float gl = sGam[ch.n - 1];
+#pragma unroll
+    for (int i = 0; i < ST::PER_WARP; ++i) {
+      const int t = warp + 8 * i;
+      if (t >= ST::TILES) continue;
+      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      wm::warp_tile<true, false>(c, sK, SM::LK, sEU, SM::LV, (t / ST::TN) * 16, (t % ST::TN) * 16, CS);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) st[i][j][e] = gl * st[i][j][e] + c[j][e];
     }
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < K * VB; i += NT) {
-    const int c = i / VB, j = i % VB;
-    if (dh0) dh0[(((size_t)b * H + h) * K + c) * V + v0 + j] = sdS[c * LY::LS + j];
+#pragma unroll
+  for (int i = 0; i < ST::PER_WARP; ++i) {
+    const int t = warp + 8 * i;
+    if (t >= ST::TILES) continue;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = (t / ST::TN) * 16 + (lane >> 2) + 8 * (e >> 1);
+        const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+        hT[(((size_t)b * H + h) * KD + r) * VD + v0 + c] = st[i][j][e];
+      }
   }
 }
 
-template <int K>
-void set_smem(const void* kern, size_t bytes) {
+// ------------------------------------------------------------------------------------------------ backward
+template <int KD, int VB>
+struct BScanSmem {
+  static constexpr int LK = KD + 8, LV = VB + 8;
+  static constexpr size_t Q = 0;
+  static constexpr size_t K = Q + sizeof(bf) * CS * LK;
+  static constexpr size_t WK = K + sizeof(bf) * CS * LK;
+  static constexpr size_t S = WK + sizeof(bf) * CS * LK;
+  static constexpr size_t DS = S + 2 * sizeof(bf) * KD * LV;   // S0 and dS1, each bf16 hi then lo
+  static constexpr size_t U = DS + 2 * sizeof(bf) * KD * LV;
+  static constexpr size_t DO = U + sizeof(bf) * CS * LV;
+  static constexpr size_t GDO = DO + sizeof(bf) * CS * LV;
+  static constexpr size_t NDU = GDO + sizeof(bf) * CS * LV;
+  static constexpr size_t P = NDU + sizeof(bf) * CS * LV;
+  static constexpr size_t VEC = P + sizeof(bf) * CS * 72;   // G Gam E dG de red
+  static constexpr size_t TOTAL = VEC + sizeof(float) * (5 * CS + 32);
+};
+
+template <int KD, int VD, int VB>
+__global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
+    const bf* __restrict__ dout, const float* __restrict__ dhT, const bf* __restrict__ q, const bf* __restrict__ k,
+    const bf* __restrict__ wk, const bf* __restrict__ u, const float* __restrict__ g, const float* __restrict__ ckpt,
+    const int* __restrict__ chunks, const int* __restrict__ seq_chunk0, float* __restrict__ du,
+    float* __restrict__ dwk, float* __restrict__ dq, float* __restrict__ dk, float* __restrict__ dG,
+    float* __restrict__ dh0, int H, int nc_max, float scale) {
+  using SM = BScanSmem<KD, VB>;
+  using ST = StateTiles<KD, VB>;
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf* sQ = reinterpret_cast<bf*>(smem + SM::Q);
+  bf* sK = reinterpret_cast<bf*>(smem + SM::K);
+  bf* sWk = reinterpret_cast<bf*>(smem + SM::WK);
+  bf* sS = reinterpret_cast<bf*>(smem + SM::S);
+  bf* sSl = sS + KD * SM::LV;
+  bf* sdS = reinterpret_cast<bf*>(smem + SM::DS);
+  bf* sdSl = sdS + KD * SM::LV;
+  bf* sU = reinterpret_cast<bf*>(smem + SM::U);
+  bf* sdO = reinterpret_cast<bf*>(smem + SM::DO);
+  bf* sGdO = reinterpret_cast<bf*>(smem + SM::GDO);
+  bf* snDU = reinterpret_cast<bf*>(smem + SM::NDU);
+  bf* sP = reinterpret_cast<bf*>(smem + SM::P);
+  float* sG = reinterpret_cast<float*>(smem + SM::VEC);
+  float* sGam = sG + CS;
+  float* sE = sGam + CS;
+  float* sdG = sE + CS;
+  float* sde = sdG + CS;
+  float* sred = sde + CS;
+  const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int v0 = vb * VB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c_begin = seq_chunk0[b], c_end = seq_chunk0[b + 1];
+
+  float ds[ST::PER_WARP][2][4];
+#pragma unroll
+  for (int i = 0; i < ST::PER_WARP; ++i) {
+    const int t = warp + 8 * i;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = (t / ST::TN) * 16 + (lane >> 2) + 8 * (e >> 1);
+        const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+        ds[i][j][e] = (t < ST::TILES && dhT) ? dhT[(((size_t)b * H + h) * KD + r) * VD + v0 + c] : 0.f;
+      }
+  }
+  for (int ci = c_end - 1; ci >= c_begin; --ci) {
+    const Chunk ch = load_chunk_desc(chunks, ci);
+    const float* ck = ckpt + (((size_t)b * H + h) * nc_max + ch.c) * KD * VD;
+    for (int i = threadIdx.x; i < KD * VB; i += NT) {
+      const int r = i / VB, c = i % VB;
+      wm::split_bf16(ck[(size_t)r * VD + v0 + c], sS[r * SM::LV + c], sSl[r * SM::LV + c]);
+    }
+    float dot = 0.f;  // <dS1, S0> partial
+#pragma unroll
+    for (int i = 0; i < ST::PER_WARP; ++i) {
+      const int t = warp + 8 * i;
+      if (t >= ST::TILES) continue;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = (t / ST::TN) * 16 + (lane >> 2) + 8 * (e >> 1);
+          const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+          wm::split_bf16(ds[i][j][e], sdS[r * SM::LV + c], sdSl[r * SM::LV + c]);
+          dot += ds[i][j][e] * ck[(size_t)r * VD + v0 + c];
+        }
+    }
+    dot = bb::warp_sum(dot);
+    if (lane == 0) sred[warp] = dot;
+    load_rows<KD>(sQ, SM::LK, q, ch.row0, ch.n, H, h, KD, 0);
+    load_rows<KD>(sK, SM::LK, k, ch.row0, ch.n, H, h, KD, 0);
+    load_rows<KD>(sWk, SM::LK, wk, ch.row0, ch.n, H, h, KD, 0);
+    load_rows<VB>(sU, SM::LV, u, ch.row0, ch.n, H, h, VD, v0);
+    load_rows<VB>(sdO, SM::LV, dout, ch.row0, ch.n, H, h, VD, v0);
+    for (int t = threadIdx.x; t < CS; t += NT) sdG[t] = sde[t] = 0.f;
+    chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);  // syncs
+    for (int i = threadIdx.x; i < CS * VB; i += NT) {
+      const int t = i / VB, c = i % VB;
+      sGdO[t * SM::LV + c] = f2b(scale * sGam[t] * b2f(sdO[t * SM::LV + c]));
+    }
+    wm::block_gemm<false, true>(CS, CS, KD, sQ, SM::LK, sK, SM::LK, [&](int t, int s, float val) {
+      sP[t * 72 + s] = f2b((s <= t && t < ch.n) ? __expf(sG[t] - sG[s]) * val : 0.f);
+    });
+    __syncthreads();
+    // dU = scale P^T dO + E o (K dS1);  de_s = sum_j (K dS1)_sj U_sj
+    {
+      const int tn = VB / 16, tiles = (CS / 16) * tn;
+      for (int t = warp; t < tiles; t += 8) {
+        const int m0 = (t / tn) * 16, n0 = (t % tn) * 16;
+        float c1[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        float c2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        wm::warp_tile<false, false>(c1, sK, SM::LK, sdS, SM::LV, m0, n0, KD);
+        wm::warp_tile<false, false>(c1, sK, SM::LK, sdSl, SM::LV, m0, n0, KD);
+        wm::warp_tile<true, false>(c2, sP, 72, sdO, SM::LV, m0, n0, CS);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int r = m0 + (lane >> 2) + 8 * (e >> 1), c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+            const float d = r < ch.n ? scale * c2[j][e] + sE[r] * c1[j][e] : 0.f;
+            snDU[r * SM::LV + c] = f2b(-d);
+            if (r < ch.n) {
+              du[((size_t)(ch.row0 + r) * H + h) * VD + v0 + c] = d;
+              atomicAdd(&sde[r], c1[j][e] * b2f(sU[r * SM::LV + c]));
+            }
+          }
+      }
+    }
+    __syncthreads();
+    // state-dependent gradient pieces (summed over the V blocks with atomics)
+    wm::block_gemm2<false, true>(CS, KD, VB, sdO, SM::LV, sS, sSl, SM::LV, [&](int t, int c, float val) {
+      if (t < ch.n) atomicAdd(&dq[((size_t)(ch.row0 + t) * H + h) * KD + c], scale * sGam[t] * val);
+    });
+    wm::block_gemm2<false, true>(CS, KD, VB, sU, SM::LV, sdS, sdSl, SM::LV, [&](int t, int c, float val) {
+      if (t < ch.n) atomicAdd(&dk[((size_t)(ch.row0 + t) * H + h) * KD + c], sE[t] * val);
+    });
+    wm::block_gemm2<false, true>(CS, KD, VB, snDU, SM::LV, sS, sSl, SM::LV, [&](int t, int c, float val) {
+      if (t < ch.n) atomicAdd(&dwk[((size_t)(ch.row0 + t) * H + h) * KD + c], val);
+    });
+    wm::block_gemm2<false, false>(CS, VB, KD, sQ, SM::LK, sS, sSl, SM::LV, [&](int t, int c, float val) {
+      if (t < ch.n) atomicAdd(&sdG[t], scale * sGam[t] * val * b2f(sdO[t * SM::LV + c]));
+    });
+    // dS0 = Gam_last dS1 + Q^T (scale Gam o dO) - Wk^T dU
+    const float gl = sGam[ch.n - 1];
+#pragma unroll
+    for (int i = 0; i < ST::PER_WARP; ++i) {
+      const int t = warp + 8 * i;
+      if (t >= ST::TILES) continue;
+      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const int m0 = (t / ST::TN) * 16, n0 = (t % ST::TN) * 16;
+      wm::warp_tile<true, false>(c, sQ, SM::LK, sGdO, SM::LV, m0, n0, CS);
+      wm::warp_tile<true, false>(c, sWk, SM::LK, snDU, SM::LV, m0, n0, CS);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ds[i][j][e] = gl * ds[i][j][e] + c[j][e];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float tot = 0.f, dsum = 0.f;
+      for (int w = 0; w < NT / 32; ++w) dsum += sred[w];
+      for (int t = 0; t < ch.n; ++t) tot += sde[t] * sE[t];
+      sdG[ch.n - 1] += dsum * gl + tot;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < ch.n; t += NT)
+      atomicAdd(&dG[(size_t)(ch.row0 + t) * H + h], sdG[t] - sde[t] * sE[t]);
+    __syncthreads();
+  }
+  if (dh0) {
+#pragma unroll
+    for (int i = 0; i < ST::PER_WARP; ++i) {
+      const int t = warp + 8 * i;
+      if (t >= ST::TILES) continue;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = (t / ST::TN) * 16 + (lane >> 2) + 8 * (e >> 1);
+          const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+          dh0[(((size_t)b * H + h) * KD + r) * VD + v0 + c] = ds[i][j][e];
+        }
+    }
+  }
+}
+
+template <int KD, int VD>
+struct BChunkSmem {
+  static constexpr int LK = KD + 8, LV = VD + 8;
+  static constexpr size_t Q = 0;
+  static constexpr size_t K = Q + sizeof(bf) * CS * LK;
+  static constexpr size_t KB = K + sizeof(bf) * CS * LK;
+  static constexpr size_t DWK = KB + sizeof(bf) * CS * LK;
+  static constexpr size_t U = DWK + sizeof(bf) * CS * LK;
+  static constexpr size_t DO = U + sizeof(bf) * CS * LV;
+  static constexpr size_t DU = DO + sizeof(bf) * CS * LV;
+  static constexpr size_t VB = DU + sizeof(bf) * CS * LV;
+  static constexpr size_t TB = VB + sizeof(bf) * CS * LV;
+  static constexpr size_t X1 = TB + sizeof(bf) * CS * 72;   // dP o D, then dT / M
+  static constexpr size_t X2 = X1 + sizeof(bf) * CS * 72;   // dT T^T
+  static constexpr size_t A = X2 + sizeof(bf) * CS * 72;
+  static constexpr size_t TF = A + sizeof(float) * CS * 65;  // T (solve) + scratch, then P
+  static constexpr size_t VEC = TF + sizeof(float) * (CS * 65 + 4 * 16 * 17);  // G Gam E B dG db
+  static constexpr size_t TOTAL = VEC + sizeof(float) * 6 * CS;
+};
+
+template <int KD, int VD>
+__global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
+    const bf* __restrict__ dout, const bf* __restrict__ q, const bf* __restrict__ k, const bf* __restrict__ v,
+    const float* __restrict__ g, const float* __restrict__ beta, const bf* __restrict__ u,
+    const float* __restrict__ du, const float* __restrict__ dwk, const int* __restrict__ chunks,
+    float* __restrict__ dq, float* __restrict__ dk, bf* __restrict__ dv, const float* __restrict__ dG_in,
+    float* __restrict__ dg, float* __restrict__ dbeta, int H, float scale) {
+  using SM = BChunkSmem<KD, VD>;
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf* sQ = reinterpret_cast<bf*>(smem + SM::Q);
+  bf* sK = reinterpret_cast<bf*>(smem + SM::K);
+  bf* sKb = reinterpret_cast<bf*>(smem + SM::KB);
+  bf* sdWk = reinterpret_cast<bf*>(smem + SM::DWK);
+  bf* sU = reinterpret_cast<bf*>(smem + SM::U);
+  bf* sdO = reinterpret_cast<bf*>(smem + SM::DO);
+  bf* sdU = reinterpret_cast<bf*>(smem + SM::DU);
+  bf* sVb = reinterpret_cast<bf*>(smem + SM::VB);
+  bf* sTb = reinterpret_cast<bf*>(smem + SM::TB);
+  bf* sX1 = reinterpret_cast<bf*>(smem + SM::X1);
+  bf* sX2 = reinterpret_cast<bf*>(smem + SM::X2);
+  float* sA = reinterpret_cast<float*>(smem + SM::A);
+  float* sTf = reinterpret_cast<float*>(smem + SM::TF);
+  float* sG = reinterpret_cast<float*>(smem + SM::VEC);
+  float* sGam = sG + CS;
+  float* sE = sGam + CS;
+  float* sB = sE + CS;
+  float* sdG = sB + CS;
+  float* sdb = sdG + CS;
+  const Chunk ch = load_chunk_desc(chunks, blockIdx.x);
+  const int h = blockIdx.y, n = ch.n, row0 = ch.row0;
+  auto rk = [&](int t) { return ((size_t)(row0 + t) * H + h) * KD; };
+  auto rv = [&](int t) { return ((size_t)(row0 + t) * H + h) * VD; };
+
+  load_rows<KD>(sQ, SM::LK, q, row0, n, H, h, KD, 0);
+  load_rows<KD>(sK, SM::LK, k, row0, n, H, h, KD, 0);
+  load_rows<VD>(sU, SM::LV, u, row0, n, H, h, VD, 0);
+  load_rows<VD>(sdO, SM::LV, dout, row0, n, H, h, VD, 0);
+  for (int t = threadIdx.x; t < CS; t += NT) {
+    sB[t] = t < n ? beta[(size_t)(row0 + t) * H + h] : 0.f;
+    sdG[t] = t < n ? dG_in[(size_t)(row0 + t) * H + h] : 0.f;
+    sdb[t] = 0.f;
+  }
+  chunk_decay(g, row0, n, H, h, sG, sGam, sE);
+  for (int i = threadIdx.x; i < CS * KD; i += NT) {
+    const int t = i / KD, c = i % KD;
+    sKb[t * SM::LK + c] = f2b(sB[t] * sGam[t] * b2f(sK[t * SM::LK + c]));
+    sdWk[t * SM::LK + c] = f2b(t < n ? dwk[rk(t) + c] : 0.f);
+  }
+  for (int i = threadIdx.x; i < CS * VD; i += NT) {
+    const int t = i / VD, c = i % VD;
+    sVb[t * SM::LV + c] = f2b(t < n ? sB[t] * b2f(v[rv(t) + c]) : 0.f);
+    sdU[t * SM::LV + c] = f2b(t < n ? du[rv(t) + c] : 0.f);
+  }
+  __syncthreads();
+  build_T<KD>(sK, SM::LK, sG, sB, sA, sTf, sTb, n);          // sA = D o KK^T (strict), sTb = T
+  // P (fp32, into sTf) and dP = scale dO U^T;  dG from P: rowsum(dP o P) - colsum(dP o P)
+  wm::block_gemm<false, true>(CS, CS, KD, sQ, SM::LK, sK, SM::LK, [&](int t, int s, float val) {
+    sTf[t * 65 + s] = (s <= t && t < n) ? __expf(sG[t] - sG[s]) * val : 0.f;
+  });
+  __syncthreads();
+  wm::block_gemm<false, true>(CS, CS, VD, sdO, SM::LV, sU, SM::LV, [&](int t, int s, float val) {
+    const bool ok = s <= t && t < n;
+    const float dp = ok ? scale * val : 0.f;
+    sX1[t * 72 + s] = f2b(ok ? dp * __expf(sG[t] - sG[s]) : 0.f);
+    if (ok && s != t) {
+      const float pp = dp * sTf[t * 65 + s];
+      atomicAdd(&sdG[t], pp);
+      atomicAdd(&sdG[s], -pp);
+    }
+  });
+  __syncthreads();
+  // dq += (dP o D) K ;  dk += (dP o D)^T Q
+  wm::block_gemm<false, false>(CS, KD, CS, sX1, 72, sK, SM::LK, [&](int t, int c, float val) {
+    if (t < n) dq[rk(t) + c] += val;
+  });
+  wm::block_gemm<true, false>(CS, KD, CS, sX1, 72, sQ, SM::LK, [&](int t, int c, float val) {
+    if (t < n) dk[rk(t) + c] += val;
+  });
+  __syncthreads();
+  // dT = dU (beta V)^T + dWk (beta Gam K)^T   (into sX1)
+  {
+    const int tiles = (CS / 16) * (CS / 16);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = warp; t < tiles; t += 8) {
+      const int m0 = (t / 4) * 16, n0 = (t % 4) * 16;
+      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      wm::warp_tile<false, true>(c, sdU, SM::LV, sVb, SM::LV, m0, n0, VD);
+      wm::warp_tile<false, true>(c, sdWk, SM::LK, sKb, SM::LK, m0, n0, KD);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = m0 + (lane >> 2) + 8 * (e >> 1), cc = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+          sX1[r * 72 + cc] = f2b(r < n && cc < n ? c[j][e] : 0.f);
+        }
+    }
+  }
+  __syncthreads();
+  // dVb = T^T dU -> dv = beta dVb, dbeta += <dVb, V>;  dKb = T^T dWk -> dk += beta Gam dKb, dbeta, dG
+  wm::block_gemm<true, false>(CS, VD, CS, sTb, 72, sdU, SM::LV, [&](int s, int c, float val) {
+    if (s < n) {
+      dv[rv(s) + c] = f2b(sB[s] * val);
+      atomicAdd(&sdb[s], val * b2f(v[rv(s) + c]));
+    }
+  });
+  wm::block_gemm<true, false>(CS, KD, CS, sTb, 72, sdWk, SM::LK, [&](int s, int c, float val) {
+    if (s < n) {
+      const float kv = b2f(sK[s * SM::LK + c]);
+      dk[rk(s) + c] += sB[s] * sGam[s] * val;
+      atomicAdd(&sdb[s], sGam[s] * kv * val);
+      atomicAdd(&sdG[s], sB[s] * sGam[s] * kv * val);
+    }
+  });
+  // X2 = dT T^T
+  wm::block_gemm<false, true>(CS, CS, CS, sX1, 72, sTb, 72, [&](int t, int s, float val) {
+    sX2[t * 72 + s] = f2b(val);
+  });
+  __syncthreads();
+  for (int i = threadIdx.x; i < CS * 72; i += NT) sX1[i] = f2b(0.f);
+  __syncthreads();
+  // dL = -T^T X2;  dA_ts = beta_t dL_ts (s < t) -> dbeta, dG, and M = dKK + dKK^T with dKK = dA o D
+  wm::block_gemm<true, false>(CS, CS, CS, sTb, 72, sX2, 72, [&](int t, int s, float val) {
+    if (s < t && t < n) {
+      const float dl = -val;
+      const float a = sA[t * 65 + s];
+      const float da = sB[t] * dl;
+      atomicAdd(&sdb[t], dl * a);
+      atomicAdd(&sdG[t], da * a);
+      atomicAdd(&sdG[s], -da * a);
+      const bf m = f2b(da * __expf(sG[t] - sG[s]));
+      sX1[t * 72 + s] = m;
+      sX1[s * 72 + t] = m;
+    }
+  });
+  __syncthreads();
+  wm::block_gemm<false, false>(CS, KD, CS, sX1, 72, sK, SM::LK, [&](int t, int c, float val) {
+    if (t < n) dk[rk(t) + c] += val;
+  });
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float acc = 0.f;
+    for (int t = n - 1; t >= 0; --t) {
+      acc += sdG[t];
+      dg[(size_t)(row0 + t) * H + h] = acc;
+      dbeta[(size_t)(row0 + t) * H + h] = sdb[t];
+    }
+  }
+}
+
+template <typename Kern>
+void set_smem(Kern kern, size_t bytes) {
   BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
 }
 
+template <int KD, int VD>
+void launch_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& g,
+                const torch::Tensor& beta, const float* h0, const torch::Tensor& chunks, const torch::Tensor& seq0,
+                torch::Tensor& o, torch::Tensor& u, torch::Tensor& hT, torch::Tensor& ckpt, torch::Tensor& wk,
+                torch::Tensor& wv, int H, int B, int nct, int nc_max, float scale) {
+  constexpr int VB = VD > 64 ? 64 : VD;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto prep = gdr_prep_kernel<KD, VD>;
+  set_smem(prep, PrepSmem<KD, VD>::TOTAL);
+  prep<<<dim3(nct, H), NT, PrepSmem<KD, VD>::TOTAL, stream>>>(
+      (const bf*)k.data_ptr(), (const bf*)v.data_ptr(), g.data_ptr<float>(), beta.data_ptr<float>(),
+      chunks.data_ptr<int>(), (bf*)wk.data_ptr(), (bf*)wv.data_ptr(), H);
+  BB_POST_LAUNCH();
+  auto scan = gdr_scan_kernel<KD, VD, VB>;
+  set_smem(scan, ScanSmem<KD, VB>::TOTAL);
+  scan<<<dim3(VD / VB, H, B), NT, ScanSmem<KD, VB>::TOTAL, stream>>>(
+      (const bf*)q.data_ptr(), (const bf*)k.data_ptr(), (const bf*)wk.data_ptr(), (const bf*)wv.data_ptr(),
+      g.data_ptr<float>(), h0, chunks.data_ptr<int>(), seq0.data_ptr<int>(), (bf*)o.data_ptr(), (bf*)u.data_ptr(),
+      hT.data_ptr<float>(), ckpt.data_ptr<float>(), H, nc_max, scale);
+  BB_POST_LAUNCH();
+}
+
+template <int KD, int VD>
+void launch_bwd(const torch::Tensor& dout, const float* dhT, const torch::Tensor& q, const torch::Tensor& k,
+                const torch::Tensor& v, const torch::Tensor& g, const torch::Tensor& beta, const torch::Tensor& ckpt,
+                const torch::Tensor& wk, const torch::Tensor& u, const torch::Tensor& chunks,
+                const torch::Tensor& seq0, torch::Tensor& du, torch::Tensor& dwk, torch::Tensor& dq,
+                torch::Tensor& dk, torch::Tensor& dv, torch::Tensor& dG, torch::Tensor& dg, torch::Tensor& db,
+                float* dh0, int H, int B, int nct, int nc_max, float scale) {
+  constexpr int VB = VD > 64 ? 64 : VD;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto scan = gdr_bwd_scan_kernel<KD, VD, VB>;
+  set_smem(scan, BScanSmem<KD, VB>::TOTAL);
+  scan<<<dim3(VD / VB, H, B), NT, BScanSmem<KD, VB>::TOTAL, stream>>>(
+      (const bf*)dout.data_ptr(), dhT, (const bf*)q.data_ptr(), (const bf*)k.data_ptr(), (const bf*)wk.data_ptr(),
+      (const bf*)u.data_ptr(), g.data_ptr<float>(), ckpt.data_ptr<float>(), chunks.data_ptr<int>(),
+      seq0.data_ptr<int>(), du.data_ptr<float>(), dwk.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr<float>(),
+      dG.data_ptr<float>(), dh0, H, nc_max, scale);
+  BB_POST_LAUNCH();
+  auto chunk = gdr_bwd_chunk_kernel<KD, VD>;
+  set_smem(chunk, BChunkSmem<KD, VD>::TOTAL);
+  chunk<<<dim3(nct, H), NT, BChunkSmem<KD, VD>::TOTAL, stream>>>(
+      (const bf*)dout.data_ptr(), (const bf*)q.data_ptr(), (const bf*)k.data_ptr(), (const bf*)v.data_ptr(),
+      g.data_ptr<float>(), beta.data_ptr<float>(), (const bf*)u.data_ptr(), du.data_ptr<float>(),
+      dwk.data_ptr<float>(), chunks.data_ptr<int>(), dq.data_ptr<float>(), dk.data_ptr<float>(), (bf*)dv.data_ptr(),
+      dG.data_ptr<float>(), dg.data_ptr<float>(), db.data_ptr<float>(), H, scale);
+  BB_POST_LAUNCH();
+}
+
+#define BB_GDR_DISPATCH(KD, VD, CALL)                                                  \
+  if (K == KD && V == VD) {                                                           \
+    CALL;                                                                             \
+    done = true;                                                                      \
+  }
+
 }  // namespace
 
+// chunks: int32 [nct, 4] = (row0, n, sequence, chunk index within the sequence); seq0: int32 [B+1] first
+// chunk of every sequence.  Returns {o, hT, ckpt, wk, u}.
 std::vector<torch::Tensor> gdr_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
-                                   torch::Tensor beta, c10::optional<torch::Tensor> h0, torch::Tensor cu,
-                                   int64_t max_len, double scale, int64_t chunk) {
-  TORCH_CHECK(chunk == CS, "gated delta rule kernel uses chunk 64");
+                                   torch::Tensor beta, c10::optional<torch::Tensor> h0, torch::Tensor chunks,
+                                   torch::Tensor seq0, int64_t max_chunks, double scale) {
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
               "gdr: q/k/v contiguous bf16");
+  TORCH_CHECK(g.scalar_type() == at::kFloat && beta.scalar_type() == at::kFloat && g.is_contiguous() &&
+                  beta.is_contiguous(), "gdr: g / beta fp32 contiguous");
   const int T = q.size(0), H = q.size(1), K = q.size(2), V = v.size(2);
-  TORCH_CHECK(V % VB == 0, "gdr: value dim must be a multiple of 32");
-  const int B = cu.numel() - 1;
-  const int nc = (int)((max_len + CS - 1) / CS);
+  const int B = seq0.numel() - 1, nct = chunks.size(0), ncm = std::max<int>(1, (int)max_chunks);
   auto o = torch::empty_like(v);
+  auto u = torch::empty_like(v);
+  auto wk = torch::empty_like(k);
+  auto wv = torch::empty_like(v);
   auto hT = torch::empty({B, H, K, V}, q.options().dtype(at::kFloat));
-  auto ckpt = torch::empty({B, H, std::max(nc, 1), K, V}, q.options().dtype(at::kFloat));
-  if (T == 0 || B == 0) return {o, hT, ckpt};
-  auto gf = g.to(at::kFloat).contiguous(), bf_ = beta.to(at::kFloat).contiguous();
+  auto ckpt = torch::empty({B, H, ncm, K, V}, q.options().dtype(at::kFloat));
   torch::Tensor h0f;
   if (h0.has_value()) h0f = h0->to(at::kFloat).contiguous();
-  dim3 grid(V / VB, H, B);
-  auto stream = at::cuda::getCurrentCUDAStream();
-#define BB_GF(KK)                                                                                            \
-  {                                                                                                          \
-    auto kern = gdr_fwd_kernel<KK>;                                                                          \
-    set_smem<KK>((const void*)kern, FwdSmem<KK>::TOTAL);                                                     \
-    kern<<<grid, NT, FwdSmem<KK>::TOTAL, stream>>>(                                                          \
-        (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)v.data_ptr(), \
-        gf.data_ptr<float>(), bf_.data_ptr<float>(), h0.has_value() ? h0f.data_ptr<float>() : nullptr,          \
-        cu.data_ptr<int>(), (__nv_bfloat16*)o.data_ptr(), hT.data_ptr<float>(), ckpt.data_ptr<float>(), H, V,  \
-        std::max(nc, 1), (float)scale);                                                                      \
+  if (T == 0 || B == 0) {
+    if (h0.has_value()) hT.copy_(h0f);
+    else hT.zero_();
+    return {o, hT, ckpt, wk, u};
   }
-  if (K == 128) BB_GF(128)
-  else if (K == 64) BB_GF(64)
-  else if (K == 32) BB_GF(32)
-  else TORCH_CHECK(false, "gdr: key dim must be 32, 64 or 128");
-#undef BB_GF
-  BB_POST_LAUNCH();
-  return {o, hT, ckpt};
+  const float* h0p = h0.has_value() ? h0f.data_ptr<float>() : nullptr;
+  bool done = false;
+  const float sc = (float)scale;
+  BB_GDR_DISPATCH(128, 128, (launch_fwd<128, 128>(q, k, v, g, beta, h0p, chunks, seq0, o, u, hT, ckpt, wk, wv, H, B, nct, ncm, sc)))
+  BB_GDR_DISPATCH(64, 64, (launch_fwd<64, 64>(q, k, v, g, beta, h0p, chunks, seq0, o, u, hT, ckpt, wk, wv, H, B, nct, ncm, sc)))
+  BB_GDR_DISPATCH(32, 64, (launch_fwd<32, 64>(q, k, v, g, beta, h0p, chunks, seq0, o, u, hT, ckpt, wk, wv, H, B, nct, ncm, sc)))
+  BB_GDR_DISPATCH(64, 128, (launch_fwd<64, 128>(q, k, v, g, beta, h0p, chunks, seq0, o, u, hT, ckpt, wk, wv, H, B, nct, ncm, sc)))
+  BB_GDR_DISPATCH(32, 32, (launch_fwd<32, 32>(q, k, v, g, beta, h0p, chunks, seq0, o, u, hT, ckpt, wk, wv, H, B, nct, ncm, sc)))
+  TORCH_CHECK(done, "gdr: unsupported (key dim, value dim) = (", K, ", ", V, ")");
+  return {o, hT, ckpt, wk, u};
 }
 
 std::vector<torch::Tensor> gdr_bwd(torch::Tensor dout, c10::optional<torch::Tensor> dhT, torch::Tensor q,
                                    torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
-                                   torch::Tensor ckpt, torch::Tensor cu, int64_t max_len, bool has_h0, double scale) {
+                                   torch::Tensor ckpt, torch::Tensor wk, torch::Tensor u, torch::Tensor chunks,
+                                   torch::Tensor seq0, int64_t max_chunks, bool has_h0, double scale) {
   const int T = q.size(0), H = q.size(1), K = q.size(2), V = v.size(2);
-  const int B = cu.numel() - 1;
-  const int nc = (int)((max_len + CS - 1) / CS);
-  auto dq = torch::zeros({T, H, K}, q.options().dtype(at::kFloat));
-  auto dk = torch::zeros({T, H, K}, q.options().dtype(at::kFloat));
+  const int B = seq0.numel() - 1, nct = chunks.size(0), ncm = std::max<int>(1, (int)max_chunks);
+  auto f32 = q.options().dtype(at::kFloat);
+  auto dq = torch::zeros({T, H, K}, f32);
+  auto dk = torch::zeros({T, H, K}, f32);
   auto dv = torch::empty_like(v);
-  auto dg = torch::zeros({T, H}, q.options().dtype(at::kFloat));
-  auto db = torch::zeros({T, H}, q.options().dtype(at::kFloat));
-  auto dh0 = torch::zeros({B, H, K, V}, q.options().dtype(at::kFloat));
-  if (T == 0 || B == 0) return {dq, dk, dv, dg, db, dh0};
-  auto gf = g.to(at::kFloat).contiguous(), bf_ = beta.to(at::kFloat).contiguous();
+  auto dg = torch::zeros({T, H}, f32);
+  auto db = torch::zeros({T, H}, f32);
+  auto dh0 = torch::zeros({B, H, K, V}, f32);
+  if (T == 0 || B == 0) {
+    if (has_h0 && dhT.has_value()) dh0.copy_(*dhT);
+    return {dq, dk, dv, dg, db, dh0};
+  }
+  auto du = torch::empty({T, H, V}, f32);
+  auto dwk = torch::zeros({T, H, K}, f32);
+  auto dG = torch::zeros({T, H}, f32);
   auto doc = dout.contiguous();
   torch::Tensor dhTf;
   if (dhT.has_value()) dhTf = dhT->to(at::kFloat).contiguous();
-  dim3 grid(V / VB, H, B);
-  auto stream = at::cuda::getCurrentCUDAStream();
-#define BB_GB(KK)                                                                                              \
-  {                                                                                                            \
-    auto kern = gdr_bwd_kernel<KK>;                                                                            \
-    set_smem<KK>((const void*)kern, BwdSmem<KK>::TOTAL);                                                       \
-    kern<<<grid, NT, BwdSmem<KK>::TOTAL, stream>>>(                                                            \
-        (const __nv_bfloat16*)doc.data_ptr(), dhT.has_value() ? dhTf.data_ptr<float>() : nullptr,              \
-        (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)v.data_ptr(), \
-        gf.data_ptr<float>(), bf_.data_ptr<float>(), ckpt.data_ptr<float>(), cu.data_ptr<int>(),                 \
-        dq.data_ptr<float>(), dk.data_ptr<float>(), (__nv_bfloat16*)dv.data_ptr(), dg.data_ptr<float>(),         \
-        db.data_ptr<float>(), has_h0 ? dh0.data_ptr<float>() : nullptr, H, V, std::max(nc, 1), (float)scale);    \
-  }
-  if (K == 128) BB_GB(128)
-  else if (K == 64) BB_GB(64)
-  else if (K == 32) BB_GB(32)
-  else TORCH_CHECK(false, "gdr: key dim must be 32, 64 or 128");
-#undef BB_GB
-  BB_POST_LAUNCH();
+  const float* dhTp = dhT.has_value() ? dhTf.data_ptr<float>() : nullptr;
+  float* dh0p = has_h0 ? dh0.data_ptr<float>() : nullptr;
+  bool done = false;
+  const float sc = (float)scale;
+#define BB_B(KD, VD) launch_bwd<KD, VD>(doc, dhTp, q, k, v, g, beta, ckpt, wk, u, chunks, seq0, du, dwk, dq, dk, dv, dG, dg, db, dh0p, H, B, nct, ncm, sc)
+  BB_GDR_DISPATCH(128, 128, BB_B(128, 128))
+  BB_GDR_DISPATCH(64, 64, BB_B(64, 64))
+  BB_GDR_DISPATCH(32, 64, BB_B(32, 64))
+  BB_GDR_DISPATCH(64, 128, BB_B(64, 128))
+  BB_GDR_DISPATCH(32, 32, BB_B(32, 32))
+#undef BB_B
+  TORCH_CHECK(done, "gdr: unsupported (key dim, value dim) = (", K, ", ", V, ")");
   return {dq, dk, dv, dg, db, dh0};
 }

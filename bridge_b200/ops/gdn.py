@@ -159,44 +159,71 @@ def chunk_gated_delta_rule_reference(q, k, v, g, beta, cu_seqlens: list[int], in
     return torch.cat(outs), torch.stack(finals)
 
 
+_CHUNK_CACHE: dict = {}
+
+
+def _chunk_table(cu_host: tuple, device) -> tuple[Tensor, Tensor, int]:
+    """``(chunks [nct, 4] = (row0, n, seq, chunk), seq0 [B+1], max chunks per sequence)`` for 64-token chunks."""
+    key = (cu_host, str(device))
+    hit = _CHUNK_CACHE.get(key)
+    if hit is not None:
+        return hit
+    rows, seq0, most = [], [0], 1
+    for b, (a, e) in enumerate(zip(cu_host[:-1], cu_host[1:])):
+        nc = (e - a + 63) // 64
+        most = max(most, nc)
+        for c in range(nc):
+            rows.append((a + 64 * c, min(64, e - a - 64 * c), b, c))
+        seq0.append(len(rows))
+    t = torch.tensor(rows if rows else [(0, 0, 0, 0)], dtype=torch.int32).reshape(-1, 4)[:len(rows)]
+    out = (t.to(device), torch.tensor(seq0, dtype=torch.int32, device=device), most)
+    if len(_CHUNK_CACHE) > 256:
+        _CHUNK_CACHE.clear()
+    _CHUNK_CACHE[key] = out
+    return out
+
+
 class _GDRFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, g, beta, h0, cu_dev, cu_host, scale, chunk):
+    def forward(ctx, q, k, v, g, beta, h0, cu_host, scale):
         m = kernels()
         q, k, v = (t.contiguous() for t in (q, k, v))
         gf, bf = g.float().contiguous(), beta.float().contiguous()
-        max_len = max(b - a for a, b in zip(cu_host[:-1], cu_host[1:]))
-        o, hT, ckpt = m.gdr_fwd(q, k, v, gf, bf, h0, cu_dev, max_len, float(scale), int(chunk))
-        ctx.save_for_backward(q, k, v, gf, bf, ckpt, cu_dev)
-        ctx.scale, ctx.max_len, ctx.has_h0 = scale, max_len, h0 is not None
+        chunks, seq0, most = _chunk_table(cu_host, q.device)
+        o, hT, ckpt, wk, u = m.gdr_fwd(q, k, v, gf, bf, h0, chunks, seq0, most, float(scale))
+        ctx.save_for_backward(q, k, v, gf, bf, ckpt, wk, u, chunks, seq0)
+        ctx.scale, ctx.most, ctx.has_h0 = scale, most, h0 is not None
         ctx.dtypes = (g.dtype, beta.dtype, None if h0 is None else h0.dtype)
         return o, hT
 
     @staticmethod
     def backward(ctx, do, dhT):
         m = kernels()
-        q, k, v, g, beta, ckpt, cu = ctx.saved_tensors
+        q, k, v, g, beta, ckpt, wk, u, chunks, seq0 = ctx.saved_tensors
         dq, dk, dv, dg, db, dh0 = m.gdr_bwd(do.contiguous(), dhT.contiguous() if dhT is not None else None,
-                                            q, k, v, g, beta, ckpt, cu, ctx.max_len, ctx.has_h0, float(ctx.scale))
+                                            q, k, v, g, beta, ckpt, wk, u, chunks, seq0, ctx.most, ctx.has_h0,
+                                            float(ctx.scale))
         gdt, bdt, hdt = ctx.dtypes
         return (dq.to(q.dtype), dk.to(k.dtype), dv, dg.to(gdt), db.to(bdt),
-                (dh0.to(hdt) if ctx.has_h0 else None), None, None, None, None)
+                (dh0.to(hdt) if ctx.has_h0 else None), None, None)
+
+
+_GDR_SHAPES = {(128, 128), (64, 64), (32, 64), (64, 128), (32, 32)}
 
 
 def chunk_gated_delta_rule(q, k, v, g, beta, cu_seqlens: list[int], cu_dev: Tensor | None,
                            initial_state: Tensor | None, *, scale: float, chunk_size: int = 64):
     """Packed varlen chunked gated delta rule; ``o [T,H,V]`` (q dtype) and final state ``[B,H,K,V]`` FP32.
 
-    On CUDA this runs the chunked kernel (bf16; key dim 32/64/128; value dim a multiple of 32).  The
-    kernel always works in 64-token chunks: the chunking changes rounding only, not the result, so
-    ``chunk_size`` applies to the PyTorch path.
+    On CUDA this runs the tensor-core chunked kernels (bf16; (key, value) head dims (128, 128),
+    (64, 64), (64, 128), (32, 64), (32, 32)).  The kernels always work in 64-token chunks: the
+    chunking changes rounding only, not the result, so ``chunk_size`` applies to the PyTorch path.
     """
     if on_gpu(q):
-        if q.shape[-1] not in (32, 64, 128) or v.shape[-1] % 32 or q.dtype != torch.bfloat16:
-            raise NotImplementedError("gated delta rule kernel: bf16, key dim 32/64/128, value dim %32")
-        if cu_dev is None:
-            cu_dev = torch.tensor(cu_seqlens, dtype=torch.int32, device=q.device)
-        return _GDRFn.apply(q, k, v, g, beta, initial_state, cu_dev, tuple(cu_seqlens), scale, 64)
+        if (q.shape[-1], v.shape[-1]) not in _GDR_SHAPES or q.dtype != torch.bfloat16:
+            raise NotImplementedError("gated delta rule kernel: bf16 with (key dim, value dim) in "
+                                      f"{sorted(_GDR_SHAPES)}")
+        return _GDRFn.apply(q, k, v, g, beta, initial_state, tuple(cu_seqlens), scale)
     return chunk_gated_delta_rule_reference(q, k, v, g, beta, cu_seqlens, initial_state, scale=scale,
                                             chunk_size=chunk_size)
 

@@ -222,13 +222,16 @@ def bench_gdn(t: Timer, small: bool):
     g = -torch.rand(T, H, device="cuda") * 0.1
     beta = torch.rand(T, H, device="cuda")
     s0 = torch.zeros(len(lens), H, K, V, device="cuda")
+    from bridge_b200.ops.gdn import _chunk_table
+
+    chunks, seq0, most = _chunk_table(tuple(cu_l), torch.device("cuda"))
     # chunk math: A, P (n^2 K), W/U/O/S1 (n K V-ish) per 64-token chunk and head
     fl = 2.0 * T * H * (2 * 64 * K + 64 * V + 3 * K * V)
-    ms = t(lambda: m.gdr_fwd(q, k, v, g, beta, s0, cu, 512, K ** -0.5, 64))
+    ms = t(lambda: m.gdr_fwd(q, k, v, g, beta, s0, chunks, seq0, most, K ** -0.5))
     _report("gated_delta_rule_fwd", {"T": T, "H": H, "K": K, "V": V}, ms, flops=fl)
-    o, hT, ck = m.gdr_fwd(q, k, v, g, beta, s0, cu, 512, K ** -0.5, 64)
+    o, hT, ck, wk, u = m.gdr_fwd(q, k, v, g, beta, s0, chunks, seq0, most, K ** -0.5)
     do = torch.randn_like(o)
-    ms = t(lambda: m.gdr_bwd(do, None, q, k, v, g, beta, ck, cu, 512, True, K ** -0.5))
+    ms = t(lambda: m.gdr_bwd(do, None, q, k, v, g, beta, ck, wk, u, chunks, seq0, most, True, K ** -0.5))
     _report("gated_delta_rule_bwd", {"T": T, "H": H, "K": K, "V": V}, ms, flops=3 * fl)
 
 

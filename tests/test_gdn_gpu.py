@@ -80,7 +80,9 @@ def test_gated_delta_rule_forward_backward(K, V, H, with_h0):
     rs = [t.detach().float().requires_grad_() if t is not None else None for t in (q, k, v, gate, beta, h0)]
     orr, hTr = chunk_gated_delta_rule_reference(*rs[:5], cu, rs[5], scale=scale, chunk_size=64)
     _close(o, orr, 1e-2, 1e-2, "o")
-    _close(hT, hTr, 1e-3, 1e-3, "final state")
+    # the tensor cores see the chunk states as bf16 operands (FP32 accumulation), so the chained
+    # final state carries bf16-level error
+    _close(hT, hTr, 3e-3, 1e-2, "final state")
     do = torch.randn_like(orr)
     dh = torch.randn_like(hTr)
     ((o.float() * do).sum() + (hT * dh).sum()).backward()
@@ -88,6 +90,10 @@ def test_gated_delta_rule_forward_backward(K, V, H, with_h0):
     for name, a, b in zip(("dq", "dk", "dv", "dg", "dbeta", "dh0"), xs, rs):
         if a is not None:
             _close(a.grad, b.grad, 2e-2, 2e-2, name)
+    # no systematic bias: per-head token sums of dg (what a per-head decay parameter's gradient is)
+    sa, sr = xs[3].grad.float().sum(0), rs[3].grad.float().sum(0)
+    mass = rs[3].grad.float().abs().sum(0)
+    assert bool(((sa - sr).abs() <= 1e-2 * mass + 1e-3).all()), (sa, sr, mass)
 
 
 def test_gated_delta_rule_matches_recurrence():
@@ -98,4 +104,4 @@ def test_gated_delta_rule_matches_recurrence():
     o, hT = chunk_gated_delta_rule(q, k, v, gate, beta, cu, None, h0, scale=0.1)
     orr, Sr = gated_delta_rule_recurrent(q.float(), k.float(), v.float(), gate, beta, h0[0], scale=0.1)
     _close(o, orr, 1e-2, 1e-2, "o")
-    _close(hT[0], Sr, 1e-3, 1e-3, "state")
+    _close(hT[0], Sr, 3e-3, 1e-2, "state")
