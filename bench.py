@@ -48,7 +48,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--prefix", type=int, default=512)
     p.add_argument("--siblings", type=int, default=8)
     p.add_argument("--resp", type=int, default=512)
-    p.add_argument("--token-budget", type=int, default=int(os.environ.get("TPR_TOKEN_BUDGET", "8192")))
+    p.add_argument("--token-budget", type=int, default=int(os.environ.get("TPR_TOKEN_BUDGET", "16384")))
     p.add_argument("--mode", default=os.environ.get("TPR_FOREST_MODE", "retain"))
     p.add_argument("--tp", type=int, default=1)
     p.add_argument("--cp", type=int, default=1)
@@ -251,6 +251,7 @@ def main() -> None:
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": launches,
+            "peak_mem_gib": round(torch.cuda.max_memory_allocated() / 2**30, 1),
             "loss": loss,
             "impl": "bridge_b200",
         }
