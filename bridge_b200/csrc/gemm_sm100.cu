@@ -250,6 +250,228 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2): a cluster of two CTAs on two SMs computes a 256 x 256 tile.
+// CTA r stages rows [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the B tile
+// (N half) -- 32 KB per stage instead of 48 KB, so 6 stages fit and every B row is fetched once per
+// pair.  The leader (rank 0) issues the M = 256 MMAs; both CTAs' TMA loads complete on the leader's
+// `full` barrier; the MMA commits arrive on both CTAs' `empty` / `tfull` barriers (multicast commit);
+// both CTAs' epilogue threads arrive on the leader's `tempty`.  Each CTA drains its own TMEM rows.
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK * 2;  // 16 KB
+constexpr int P_B_BYTES = 128 * BK * 2;  // 16 KB (this CTA's half of the 256-row B tile)
+
+struct PairSmem {
+  static constexpr int A_OFF = 0;
+  static constexpr int B_OFF = P_STAGES * P_A_BYTES;
+  static constexpr int BAR_OFF = B_OFF + P_STAGES * P_B_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256;
+};
+
+template <bool A_MN, bool B_MN, bool ACCUM_F32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, void* C,
+                     int M, int N, int K, long ldc, int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem + PairSmem::A_OFF;
+  unsigned char* sB = smem + PairSmem::B_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PairSmem::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + P_STAGES;
+  uint64_t* tfull = bars + 2 * P_STAGES;
+  uint64_t* tempty = bars + 2 * P_STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = sm100::cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m_tiles = (M + 255) / 256, n_tiles = (N + 255) / 256;
+  const int num_tiles = m_tiles * n_tiles;
+  const int nk = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tfull[a], 1);
+      sm100::mbar_init(&tempty[a], 256);
+    }
+    sm100::fence_mbar_init();
+    sm100::prefetch_tmap(&tmap_a);
+    sm100::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) sm100::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();  // both CTAs' barriers are initialised before any remote arrive / TMA
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto tile_coords = [&](int t, int& m0, int& n0) {
+    const int group = 8;
+    const int per_group = group * n_tiles;
+    const int g = t / per_group;
+    const int first_m = g * group;
+    const int gm = min(group, m_tiles - first_m);
+    const int r = t % per_group;
+    m0 = (first_m + r % gm) * 256;
+    n0 = (r / gm) * 256;
+  };
+
+  constexpr uint32_t IDESC = sm100::umma_idesc_bf16(256, 256, A_MN, B_MN);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        int m0, n0;
+        tile_coords(t, m0, n0);
+        const int ma = m0 + 128 * (int)rank, nb = n0 + 128 * (int)rank;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait_cluster(&empty[stage], phase ^ 1, err, 11)) {
+            ok = false;
+            break;
+          }
+          if (leader) sm100::mbar_expect_tx(&full[stage], 2 * (P_A_BYTES + P_B_BYTES));
+          const uint32_t fb = sm100::mapa(sm100::smem_addr(&full[stage]), 0);
+          unsigned char* a_dst = sA + stage * P_A_BYTES;
+          unsigned char* b_dst = sB + stage * P_B_BYTES;
+          if (A_MN) {
+            sm100::tma_load_2d_pair(a_dst, &tmap_a, fb, ma, kb * BK);
+            sm100::tma_load_2d_pair(a_dst + 8192, &tmap_a, fb, ma + 64, kb * BK);
+          } else {
+            sm100::tma_load_2d_pair(a_dst, &tmap_a, fb, kb * BK, ma);
+          }
+          if (B_MN) {
+            sm100::tma_load_2d_pair(b_dst, &tmap_b, fb, nb, kb * BK);
+            sm100::tma_load_2d_pair(b_dst + 8192, &tmap_b, fb, nb + 64, kb * BK);
+          } else {
+            sm100::tma_load_2d_pair(b_dst, &tmap_b, fb, kb * BK, nb);
+          }
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        if (!sm100::mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, err, 12)) break;
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * 256;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait_cluster(&full[stage], phase, err, 13)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t a_base = sm100::smem_addr(sA + stage * P_A_BYTES);
+          const uint32_t b_base = sm100::smem_addr(sB + stage * P_B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sm100::umma_desc_sw128(a_base + kk * 2048, 8192, 1024)
+                                     : sm100::umma_desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sm100::umma_desc_sw128(b_base + kk * 2048, 8192, 1024)
+                                     : sm100::umma_desc_sw128(b_base + kk * 32, 16, 1024);
+            sm100::umma_bf16_pair(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+          }
+          sm100::umma_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        sm100::umma_commit_pair_mc(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < num_tiles; t += npairs) {
+      int m0, n0;
+      tile_coords(t, m0, n0);
+      const bool got = sm100::mbar_wait_cluster(&tfull[acc], acc_phase, err, 14);
+      if (!__all_sync(0xffffffffu, got)) break;
+      sm100::tc_fence_after();
+      const int row = m0 + 128 * (int)rank + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
+#pragma unroll 1
+      for (int c = 0; c < 256 / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(t_row + c * 32, r);
+        sm100::tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (row < M && col0 < N) {
+          if (ACCUM_F32) {
+            float* dst = reinterpret_cast<float*>(C) + (size_t)row * ldc + col0;
+            if (col0 + 32 <= N) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float4 v = reinterpret_cast<float4*>(dst)[j];
+                v.x += __uint_as_float(r[4 * j]);
+                v.y += __uint_as_float(r[4 * j + 1]);
+                v.z += __uint_as_float(r[4 * j + 2]);
+                v.w += __uint_as_float(r[4 * j + 3]);
+                reinterpret_cast<float4*>(dst)[j] = v;
+              }
+            } else {
+              for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] += __uint_as_float(r[j]);
+            }
+          } else {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
+            if (col0 + 32 <= N) {
+              uint32_t p[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                p[j] = *reinterpret_cast<uint32_t*>(&h);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(dst)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+            } else {
+              for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = __float2bfloat16(__uint_as_float(r[j]));
+            }
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive_cluster(sm100::mapa(sm100::smem_addr(&tempty[acc]), 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();  // the peer's smem / barriers stay alive until both CTAs are done
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -330,6 +552,33 @@ void launch(const MapPair* maps, void* c, int M, int N, int K, long ldc) {
   BB_POST_LAUNCH();
 }
 
+template <bool A_MN, bool B_MN, bool ACC>
+void launch_pair(const MapPair* maps, void* c, int M, int N, int K, long ldc) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, ACC>;
+  const int smem = PairSmem::TOTAL + 1024;
+  static bool attr = false;
+  if (!attr) {
+    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int grid = 2 * std::max(1, std::min(tiles, num_sms() / 2));
+  int* err = error_word().data_ptr<int>();
+  void* args[] = {const_cast<CUtensorMap*>(&maps->a), const_cast<CUtensorMap*>(&maps->b), &c, &M, &N, &K, &ldc, &err};
+  BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NUM_THREADS), args, smem,
+                                 at::cuda::getCurrentCUDAStream()));
+  BB_POST_LAUNCH();
+}
+
+bool use_pair(long M, long N) {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("BB_GEMM_PAIR");
+    mode = (e && e[0] == '0') ? 0 : 1;
+  }
+  return mode == 1 && M >= 256 && N >= 256;
+}
+
 }  // namespace
 
 // C = op(A) * op(B)^T where op(A) is [M, K] and op(B) is [N, K].
@@ -371,13 +620,18 @@ torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, c10::
   }
   MapPair* maps = map_storage();
   GTRACE("storage");
+  const bool pair = use_pair(M, N);
   if (a_mn) make_map(&maps->a, a.data_ptr(), K, M, a.stride(0), 64);
   else make_map(&maps->a, a.data_ptr(), M, K, a.stride(0), BM);
   if (b_mn) make_map(&maps->b, b.data_ptr(), K, N, b.stride(0), 64);
-  else make_map(&maps->b, b.data_ptr(), N, K, b.stride(0), BN);
+  else make_map(&maps->b, b.data_ptr(), N, K, b.stride(0), pair ? 128 : BN);
   GTRACE("maps encoded");
   const long ldc = c.stride(0);
-#define BB_G(AM, BMN, ACC) launch<AM, BMN, ACC>(maps, c.data_ptr(), (int)M, (int)N, (int)K, ldc)
+#define BB_G(AM, BMN, ACC)                                                           \
+  do {                                                                               \
+    if (pair) launch_pair<AM, BMN, ACC>(maps, c.data_ptr(), (int)M, (int)N, (int)K, ldc); \
+    else launch<AM, BMN, ACC>(maps, c.data_ptr(), (int)M, (int)N, (int)K, ldc);      \
+  } while (0)
   if (accumulate) {
     if (!a_mn && !b_mn) BB_G(false, false, true);
     else if (!a_mn && b_mn) BB_G(false, true, true);
