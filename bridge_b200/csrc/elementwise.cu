@@ -118,7 +118,37 @@ __global__ void column_sum_kernel(const float* __restrict__ part, float* __restr
 }
 
 // ------------------------------------------------------------------------------- qk-RMSNorm + RoPE
-// One warp per (token, head); D == 128 (4 elems / lane). Rotate-half partner of lane l is lane l^16.
+// One warp per (token, head); E = D/32 elements per lane (one 4-, 8- or 16-byte access). Rotate-half
+// partner of lane l is lane l^16.
+template <int E>
+__device__ __forceinline__ void load_e(const __nv_bfloat16* p, float* f) {
+  if constexpr (E == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  } else if constexpr (E == 8) {
+    bb::unpack8(*reinterpret_cast<const bb::bf16x8*>(p), f);
+  } else {
+#pragma unroll
+    for (int j = 0; j < E; ++j) f[j] = __bfloat162float(p[j]);
+  }
+}
+template <int E>
+__device__ __forceinline__ void store_e(__nv_bfloat16* p, const float* f) {
+  if constexpr (E == 4) {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    h[0] = __floats2bfloat162_rn(f[0], f[1]);
+    h[1] = __floats2bfloat162_rn(f[2], f[3]);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else if constexpr (E == 8) {
+    *reinterpret_cast<bb::bf16x8*>(p) = bb::pack8(f);
+  } else {
+#pragma unroll
+    for (int j = 0; j < E; ++j) p[j] = __float2bfloat16(f[j]);
+  }
+}
 template <int D>
 __device__ __forceinline__ void norm_rope_row(const __nv_bfloat16* __restrict__ in, const float* __restrict__ w,
                                               __nv_bfloat16* __restrict__ out, float* __restrict__ rstd_out,
@@ -126,9 +156,7 @@ __device__ __forceinline__ void norm_rope_row(const __nv_bfloat16* __restrict__ 
                                               int lane) {
   constexpr int E = D / 32;
   float f[E];
-  const __nv_bfloat16* p = in + lane * E;
-#pragma unroll
-  for (int j = 0; j < E; ++j) f[j] = __bfloat162float(p[j]);
+  load_e<E>(in + lane * E, f);
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < E; ++j) ss += f[j] * f[j];
@@ -140,13 +168,14 @@ __device__ __forceinline__ void norm_rope_row(const __nv_bfloat16* __restrict__ 
   // rotate half: first half lanes (0..15) hold x1, partner lanes hold x2 at the same offset.
   const bool lo = lane < 16;
   const int fi = (lane & 15) * E;  // frequency index of element 0
+  float o[E];
 #pragma unroll
   for (int j = 0; j < E; ++j) {
     float other = __shfl_xor_sync(0xffffffffu, f[j], 16);
     float c = cs[fi + j], s = sn[fi + j];
-    float v = lo ? (f[j] * c - other * s) : (f[j] * c + other * s);
-    out[lane * E + j] = __float2bfloat16(v);
+    o[j] = lo ? (f[j] * c - other * s) : (f[j] * c + other * s);
   }
+  store_e<E>(out + lane * E, o);
 }
 
 template <int D>
@@ -155,7 +184,7 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, con
                                         const float* __restrict__ cosb, const float* __restrict__ sinb,
                                         __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko,
                                         float* __restrict__ rq, float* __restrict__ rk, int T, int Hq, int Hk,
-                                        float eps) {
+                                        float eps, long qts, long qhs, long kts, long khs) {
   __shared__ float swq[D], swk[D];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     swq[i] = __bfloat162float(qw[i]);
@@ -171,11 +200,11 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, con
     const float* sn = sinb + (size_t)t * (D / 2);
     if (h < Hq) {
       size_t off = ((size_t)t * Hq + h) * D;
-      norm_rope_row<D>(q + off, swq, qo + off, rq + (size_t)t * Hq + h, cs, sn, eps, lane);
+      norm_rope_row<D>(q + t * qts + h * qhs, swq, qo + off, rq + (size_t)t * Hq + h, cs, sn, eps, lane);
     } else {
       int hh = h - Hq;
       size_t off = ((size_t)t * Hk + hh) * D;
-      norm_rope_row<D>(k + off, swk, ko + off, rk + (size_t)t * Hk + hh, cs, sn, eps, lane);
+      norm_rope_row<D>(k + t * kts + hh * khs, swk, ko + off, rk + (size_t)t * Hk + hh, cs, sn, eps, lane);
     }
   }
 }
@@ -189,15 +218,16 @@ __device__ __forceinline__ void norm_rope_row_bwd(const __nv_bfloat16* __restric
   constexpr int E = D / 32;
   const bool lo = lane < 16;
   const int fi = (lane & 15) * E;
-  float g[E], x[E];
+  float g[E], x[E], dl[E];
+  load_e<E>(dyp + lane * E, dl);
+  load_e<E>(xp + lane * E, x);
 #pragma unroll
   for (int j = 0; j < E; ++j) {
-    float d = __bfloat162float(dyp[lane * E + j]);
+    float d = dl[j];
     float other = __shfl_xor_sync(0xffffffffu, d, 16);
     float c = cs[fi + j], s = sn[fi + j];
     // forward: lo: y = a c - b s ; hi: y = b c + a s  (a = x1, b = x2)
     g[j] = lo ? (d * c + other * s) : (d * c - other * s);
-    x[j] = __bfloat162float(xp[lane * E + j]);
   }
   float dot = 0.f;
 #pragma unroll
@@ -207,8 +237,10 @@ __device__ __forceinline__ void norm_rope_row_bwd(const __nv_bfloat16* __restric
     dwacc[j] += g[j] * xh;
   }
   dot = bb::warp_sum(dot) / D;
+  float o[E];
 #pragma unroll
-  for (int j = 0; j < E; ++j) dxp[lane * E + j] = __float2bfloat16(r * (g[j] * w[lane * E + j] - x[j] * r * dot));
+  for (int j = 0; j < E; ++j) o[j] = r * (g[j] * w[lane * E + j] - x[j] * r * dot);
+  store_e<E>(dxp + lane * E, o);
 }
 
 template <int D>
@@ -218,7 +250,8 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, c
                                         const float* __restrict__ cosb, const float* __restrict__ sinb,
                                         const float* __restrict__ rq, const float* __restrict__ rk,
                                         __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk,
-                                        float* __restrict__ dqw, float* __restrict__ dkw, int T, int Hq, int Hk) {
+                                        float* __restrict__ dqw, float* __restrict__ dkw, int T, int Hq, int Hk,
+                                        long qts, long qhs, long kts, long khs) {
   constexpr int E = D / 32;
   __shared__ float swq[D], swk[D], sdq[D], sdk[D];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -240,11 +273,13 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, c
     const float* sn = sinb + (size_t)t * (D / 2);
     if (h < Hq) {
       size_t off = ((size_t)t * Hq + h) * D;
-      norm_rope_row_bwd<D>(dqo + off, q + off, swq, rq[(size_t)t * Hq + h], cs, sn, dq + off, aq, lane);
+      norm_rope_row_bwd<D>(dqo + off, q + t * qts + h * qhs, swq, rq[(size_t)t * Hq + h], cs, sn, dq + off, aq,
+                           lane);
     } else {
       int hh = h - Hq;
       size_t off = ((size_t)t * Hk + hh) * D;
-      norm_rope_row_bwd<D>(dko + off, k + off, swk, rk[(size_t)t * Hk + hh], cs, sn, dk + off, ak, lane);
+      norm_rope_row_bwd<D>(dko + off, k + t * kts + hh * khs, swk, rk[(size_t)t * Hk + hh], cs, sn, dk + off, ak,
+                           lane);
     }
   }
 #pragma unroll
@@ -592,15 +627,23 @@ std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch:
   return {dx, dw};
 }
 
+// q [T, Hq, D], k [T, Hk, D] may be strided views (e.g. column slices of a fused QKV output): the
+// head dimension must be contiguous, token / head strides 16-byte aligned; outputs are contiguous.
+void check_qk_view(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 3 && t.stride(2) == 1 &&
+                  t.stride(0) % 8 == 0 && t.stride(1) % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0,
+              name, " must be a bf16 [T, H, D] view with a contiguous, 16-byte aligned head dimension");
+}
+
 std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor qw, torch::Tensor kw,
                                             torch::Tensor cosb, torch::Tensor sinb, double eps) {
-  check_bf16(q, "q");
-  check_bf16(k, "k");
+  check_qk_view(q, "q");
+  check_qk_view(k, "k");
   TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && q.size(2) == k.size(2) && q.size(0) == k.size(0), "qk shapes");
   const int T = q.size(0), Hq = q.size(1), Hk = k.size(1), D = q.size(2);
   TORCH_CHECK(cosb.size(0) == T && cosb.size(1) == D / 2 && cosb.scalar_type() == at::kFloat && cosb.is_contiguous(),
               "cos table must be [T, D/2] fp32");
-  auto qo = torch::empty_like(q), ko = torch::empty_like(k);
+  auto qo = torch::empty({T, Hq, D}, q.options()), ko = torch::empty({T, Hk, D}, k.options());
   auto rq = torch::empty({T, Hq}, q.options().dtype(at::kFloat));
   auto rk = torch::empty({T, Hk}, q.options().dtype(at::kFloat));
   if (T == 0) return {qo, ko, rq, rk};
@@ -614,7 +657,7 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor q, torch::Tensor k, to
       (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)qwb.data_ptr(), \
       (const __nv_bfloat16*)kwb.data_ptr(), cosb.data_ptr<float>(), sinb.data_ptr<float>(),                      \
       (__nv_bfloat16*)qo.data_ptr(), (__nv_bfloat16*)ko.data_ptr(), rq.data_ptr<float>(), rk.data_ptr<float>(), T, \
-      Hq, Hk, (float)eps)
+      Hq, Hk, (float)eps, q.stride(0), q.stride(1), k.stride(0), k.stride(1))
   if (D == 128) {
     BB_QKF(128);
   } else if (D == 64) {
@@ -634,8 +677,10 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko
                                             torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk) {
   check_bf16(dqo, "dq");
   check_bf16(dko, "dk");
+  check_qk_view(q, "q");
+  check_qk_view(k, "k");
   const int T = q.size(0), Hq = q.size(1), Hk = k.size(1), D = q.size(2);
-  auto dq = torch::empty_like(q), dk = torch::empty_like(k);
+  auto dq = torch::empty({T, Hq, D}, q.options()), dk = torch::empty({T, Hk, D}, k.options());
   auto dqw = torch::zeros({D}, q.options().dtype(at::kFloat));
   auto dkw = torch::zeros({D}, q.options().dtype(at::kFloat));
   if (T == 0) return {dq, dk, dqw, dkw};
@@ -650,7 +695,7 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko
       (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)qwb.data_ptr(), (const __nv_bfloat16*)kwb.data_ptr(), \
       cosb.data_ptr<float>(), sinb.data_ptr<float>(), rq.data_ptr<float>(), rk.data_ptr<float>(),                \
       (__nv_bfloat16*)dq.data_ptr(), (__nv_bfloat16*)dk.data_ptr(), dqw.data_ptr<float>(), dkw.data_ptr<float>(), T, \
-      Hq, Hk)
+      Hq, Hk, q.stride(0), q.stride(1), k.stride(0), k.stride(1))
   if (D == 128) {
     BB_QKB(128);
   } else if (D == 64) {

@@ -72,11 +72,17 @@ def qk_norm_rope_reference(q, k, q_weight, k_weight, cos, sin, eps):
     return apply_rope_reference(q, cos, sin), apply_rope_reference(k, cos, sin)
 
 
+def _view_ok(t: Tensor) -> bool:
+    return t.stride(2) == 1 and t.stride(0) % 8 == 0 and t.stride(1) % 8 == 0 and t.data_ptr() % 16 == 0
+
+
 class _QKNormRopeFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, qw, kw, cos, sin, eps):
         m = kernels()
-        q_, k_ = q.contiguous(), k.contiguous()
+        # strided views (column slices of the fused QKV output) are read in place
+        q_ = q if _view_ok(q) else q.contiguous()
+        k_ = k if _view_ok(k) else k.contiguous()
         qo, ko, rq, rk = m.qk_norm_rope_fwd(q_, k_, qw, kw, cos, sin, float(eps))
         ctx.save_for_backward(q_, k_, qw, kw, cos, sin, rq, rk)
         ctx.eps = eps

@@ -42,12 +42,22 @@ def test_rmsnorm(rows, H):
 
 
 @pytest.mark.parametrize("D", [64, 128, 256])
-def test_qk_norm_rope(D):
+@pytest.mark.parametrize("fused_view", [False, True])
+def test_qk_norm_rope(D, fused_view):
+    """Contiguous q/k, and q/k read in place as column slices of a fused [q+gate | k | v] projection."""
     from bridge_b200.ops.norm import qk_norm_rope, qk_norm_rope_reference, rope_cos_sin
 
     T, Hq, Hk = 77, 8, 2
-    q = torch.randn(T, Hq, D, device=DEV, dtype=torch.bfloat16, requires_grad=True)
-    k = torch.randn(T, Hk, D, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    if fused_view:
+        qkv = torch.randn(T, Hq * 2 * D + 2 * Hk * D, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+        q_all, k, _ = qkv.split((Hq * 2 * D, Hk * D, Hk * D), dim=-1)
+        q = q_all.view(T, Hq, 2 * D)[..., :D]
+        k = k.view(T, Hk, D)
+        q.retain_grad()
+        k.retain_grad()
+    else:
+        q = torch.randn(T, Hq, D, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+        k = torch.randn(T, Hk, D, device=DEV, dtype=torch.bfloat16, requires_grad=True)
     qw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16).requires_grad_()
     kw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16).requires_grad_()
     cos, sin = rope_cos_sin(torch.arange(1000, 1000 + T, device=DEV), D, 1e6)
