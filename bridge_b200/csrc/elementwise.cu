@@ -599,7 +599,9 @@ std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch:
   auto dw = torch::zeros({H}, x.options().dtype(at::kFloat));
   if (rows == 0) return {dx, dw};
   const int threads = 256;
-  int blocks = (int)std::min<long>((rows + 7) / 8, (long)sm_count() * 2);
+  // per-lane register footprint follows ceil(H / 256) vectors exactly (10 for H = 2560), so
+  // several blocks fit per SM
+  int blocks = (int)std::min<long>((rows + 7) / 8, (long)sm_count() * 4);
   auto part = torch::empty({blocks, H}, x.options().dtype(at::kFloat));
   auto stream = at::cuda::getCurrentCUDAStream();
   const int nv = H / 8;
@@ -614,8 +616,14 @@ std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch:
     BB_RMS_BWD(2);
   } else if (nv <= 128) {
     BB_RMS_BWD(4);
+  } else if (nv <= 192) {
+    BB_RMS_BWD(6);
   } else if (nv <= 256) {
     BB_RMS_BWD(8);
+  } else if (nv <= 320) {
+    BB_RMS_BWD(10);
+  } else if (nv <= 384) {
+    BB_RMS_BWD(12);
   } else {
     TORCH_CHECK(nv <= 512, "rmsnorm_bwd: hidden size too large");
     BB_RMS_BWD(16);
