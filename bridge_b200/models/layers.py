@@ -158,9 +158,15 @@ class TPRGatedDeltaNet(nn.Module):
 
         t = x.shape[0]
         kd, vd = self.hk * self.dk, self.hv * self.dv
+        ctx = get_tpr_attention_context()
+        backend = getattr(ctx, "attention_backend", None) if ctx is not None else None
+        cp_group = getattr(backend, "cp_group", None)
+        if cp_group is not None and torch.distributed.get_world_size(cp_group) > 1:
+            from ..parallel.gdn_state import forward_gdn_cp_tpr
+
+            return forward_gdn_cp_tpr(self, x, ctx, backend)          # CP-sharded tokens: head-parallel
         proj = self.in_proj(x)
         qkv, z, b, a = proj.split((2 * kd + vd, vd, self.hv, self.hv), dim=-1)
-        ctx = get_tpr_attention_context()
         if ctx is not None and ctx.layout is not None:
             cu = [0]
             for n in ctx.layout.seq_lens:

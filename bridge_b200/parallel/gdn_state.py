@@ -135,3 +135,81 @@ def gdn_sequence_chain_states(M: Tensor, C: Tensor, h0: Tensor, cp_group) -> Ten
     for i in range(r):
         S = torch.matmul(Ms[i], S) + Cs[i]
     return S
+
+
+_PERM_CACHE: dict = {}
+
+
+def _shard_permutation(shard, n: int, device):
+    """``(pos, valid_len)``: ``pos[g]`` = row of global token ``g`` in the rank-major layout produced by the
+    sequence->head exchange (rank j's local rows after rank j-1's), for the valid tokens ``g``."""
+    from .cp_p2p import rank_rows
+
+    key = (type(shard).__name__, shard.global_length, shard.padded_length, n, str(device))
+    hit = _PERM_CACHE.get(key)
+    if hit is not None:
+        return hit
+    where = {}
+    base = 0
+    for j in range(n):
+        rows = rank_rows(shard, j)
+        for li, g in enumerate(rows):
+            where[g] = base + li
+        base += len(rows)
+    valid = shard.global_length
+    pos = torch.tensor([where[g] for g in range(valid)], dtype=torch.long, device=device)
+    _PERM_CACHE[key] = (pos, valid, base)
+    return _PERM_CACHE[key]
+
+
+def forward_gdn_cp_tpr(module, hidden_local: Tensor, ctx, backend):
+    """Head-parallel GDN of one TPR segment whose tokens are CP-sharded (contiguous or zigzag).
+
+    The projected ``[q | k | v | z | b | a]`` channels go through a sequence->head exchange; the rows are
+    put back in token order (padding dropped), the stateful conv and chunked delta rule run over the
+    whole segment for this rank's 1/cp of the heads from the parent's head-local state, and the output
+    returns through head->sequence in the shard's row order.  The final conv / recurrent states are
+    head-local, the form every segment of the CP run stores and relays.
+
+    Parity: the six-section cp2hp / hp2cp seam of verl/models/mcore/tpr/parallel/gdn_state.py:25-104
+    and gated_delta_net.py:186-202 (un-zigzag inside the exchange).
+    """
+    from ..tpr.prefix_state import GDNLayerState
+
+    group = backend.cp_group
+    n, r = dist.get_world_size(group), dist.get_rank(group)
+    gdn_cp_state_shapes(module, n)
+    kd, vd = module.hk * module.dk, module.hv * module.dv
+    proj = module.in_proj(hidden_local)                               # [L_local, 2kd+2vd+2hv]
+    sizes = [kd, kd, vd, vd, module.hv, module.hv]
+    per_rank = [_split_channels(proj, sizes, n, j) for j in range(n)]
+    full = sequence_to_head(torch.stack(per_rank, dim=1).contiguous(), group).squeeze(1)   # rank-major rows
+    pos, t, total = _shard_permutation(backend.current_shard, n, full.device)
+    tok = full.index_select(0, pos)                                   # [t, ch/n] in token order
+    kl, vl, hl = kd // n, vd // n, module.hv // n
+    q, k, v, z, b, a = tok.split([kl, kl, vl, vl, hl, hl], dim=-1)
+    w = _split_channels(module.conv_weight.t(), [kd, kd, vd], n, r).t().contiguous()
+    init = ctx.get_initial_gdn_state(module.layer_number)
+    h_conv = init.conv_state if init is not None else None
+    h_rec = init.recurrent_state if init is not None else None
+    y, conv_final = causal_conv1d(torch.cat([q, k, v], -1), w, None, [0, t], None, h_conv, activation=True)
+    q, k, v = y.split([kl, kl, vl], dim=-1)
+    hk, hv = module.hk // n, module.hv // n
+    q = l2norm(q.reshape(t, hk, module.dk))
+    k = l2norm(k.reshape(t, hk, module.dk))
+    v = v.reshape(t, hv, module.dv)
+    rep = hv // hk
+    if rep > 1:
+        q, k = q.repeat_interleave(rep, 1), k.repeat_interleave(rep, 1)
+    A = module.A_log.chunk(n)[r]
+    dt = module.dt_bias.chunk(n)[r]
+    beta = torch.sigmoid(b.float())
+    g = -torch.exp(A.float()) * F.softplus(a.float() + dt.float())
+    o, rec_final = chunk_gated_delta_rule(q, k, v, g, beta, [0, t], None, h_rec, scale=module.scale,
+                                          chunk_size=module.chunk)
+    o = gated_rmsnorm(o, z.reshape(t, hv, module.dv), module.norm_weight, module.eps).reshape(t, hv * module.dv)
+    back = o.new_zeros((total, hv * module.dv)).index_copy(0, pos, o)          # rank-major, padding rows zero
+    o_local = head_to_sequence(back.reshape(total, 1, hv * module.dv), group).reshape(hidden_local.shape[0], -1)
+    if ctx.capture_gdn_final_state:
+        ctx.set_new_gdn_state(module.layer_number, GDNLayerState(conv_final, rec_final))
+    return module.out_proj(o_local)

@@ -7,7 +7,7 @@ import torch
 from tests.dist_utils import run_ranks
 
 
-def _worker(rank, world, backend, n_layers):
+def _worker(rank, world, backend, n_layers, preset="tiny", prefix=128, resp=64):
     import torch
 
     from bridge_b200.engine import EngineConfig, TPREngine
@@ -16,8 +16,8 @@ def _worker(rank, world, backend, n_layers):
     from bridge_b200.parallel.groups import build_parallel_state
     from tests.helpers import flat_ppo_loss, set_old_log_probs, tree_batch
 
-    cfg = get_config("tiny", num_layers=n_layers)
-    batch = tree_batch(n_trees=1, prefix=128, siblings=4, resp=64, seed=0)
+    cfg = get_config(preset, num_layers=n_layers)
+    batch = tree_batch(n_trees=1, prefix=prefix, siblings=4, resp=resp, seed=0)
     ref = build_model(cfg, dtype=torch.float32, seed=0)
     set_old_log_probs(ref, batch)
     loss_ref, lps = flat_ppo_loss(ref, batch)
@@ -46,6 +46,16 @@ def test_cp2_matches_flattened(backend):
 
 def test_hybrid_cp4_matches_flattened():
     res = run_ranks(4, _worker, "hybrid", 1)
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
+
+@pytest.mark.parametrize("prefix,resp", [(128, 64), (131, 63)])
+def test_hybrid_gdn_cp2_ring_matches_flattened(prefix, resp):
+    """GDN layers under ring CP: head-parallel exchange with un-zigzag (and padding), head-local state relay."""
+    res = run_ranks(2, _worker, "ring", 4, "tiny_hybrid", prefix, resp)
     for r in res:
         assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
         worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
