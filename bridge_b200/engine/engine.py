@@ -103,6 +103,15 @@ class TPREngine:
         return self.parallel.dp_group
 
     def finalize_model_grads(self) -> None:
+        """TP sum of replicated-but-partial gradients (qk-norm / GDN norm weights, norms under SP), then
+        the data-parallel reduction."""
+        tp = self.parallel.tp_group
+        if tp is not None and self.parallel.tp > 1:
+            import torch.distributed as dist
+
+            for p in self.model.parameters():
+                if getattr(p, "tp_partial_grad", False):
+                    dist.all_reduce(p.main_grad, group=tp)
         self.grad_reducer.finalize(self.optimizer.grad_buffers())
 
     def zero_grad(self) -> None:

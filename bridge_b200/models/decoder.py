@@ -35,6 +35,10 @@ class DecoderModel(nn.Module):
             for i in range(cfg.num_layers)
         )
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_eps, device=device)
+        if self.sequence_parallel:  # norms see only this rank's token shard: gradients summed over TP
+            for layer in self.layers:
+                layer.input_layernorm.weight.tp_partial_grad = True  # type: ignore[attr-defined]
+                layer.post_attention_layernorm.weight.tp_partial_grad = True  # type: ignore[attr-defined]
         self.rotary_pos_emb = RotaryEmbedding(cfg.head_dim, cfg.rope_theta)
         if cfg.tie_word_embeddings:
             self.lm_head = None

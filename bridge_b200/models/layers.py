@@ -90,6 +90,10 @@ class TPRSelfAttention(nn.Module):
                                         std=scaled_init_std(cfg.init_std, cfg.num_layers), device=device)
         self.q_norm = RMSNorm(cfg.head_dim, cfg.rms_eps, device=device) if cfg.qk_norm else None
         self.k_norm = RMSNorm(cfg.head_dim, cfg.rms_eps, device=device) if cfg.qk_norm else None
+        if n > 1:  # replicated weights that only see this rank's heads: gradients are summed over TP
+            for norm in (self.q_norm, self.k_norm):
+                if norm is not None:
+                    norm.weight.tp_partial_grad = True  # type: ignore[attr-defined]
         self.eps = cfg.rms_eps
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
 
@@ -144,6 +148,8 @@ class TPRGatedDeltaNet(nn.Module):
         self.A_log = nn.Parameter(torch.log(torch.empty(self.hv, device=device).uniform_(1, 16)))
         self.dt_bias = nn.Parameter(torch.zeros(self.hv, device=device))
         self.norm_weight = nn.Parameter(torch.ones(self.dv, device=device, dtype=torch.bfloat16))
+        if n > 1:  # shared across heads; each TP rank sees only its heads
+            self.norm_weight.tp_partial_grad = True  # type: ignore[attr-defined]
         self.out_proj = RowParallelLinear(vd, cfg.hidden_size, group=tp_group,
                                           std=scaled_init_std(cfg.init_std, cfg.num_layers), device=device)
         self.eps = cfg.rms_eps

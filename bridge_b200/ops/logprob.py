@@ -40,7 +40,8 @@ def logprob_entropy_reference(logits: Tensor, targets: Tensor, temperature: Tens
             p = torch.softmax(z, dim=-1)
             ent = lse - (p * z).sum(-1)
         return lp, ent
-    return _VocabParallelLogProb.apply(z, targets, vocab_start, tp_group, with_entropy)
+    lp, ent = _VocabParallelLogProb.apply(z, targets, vocab_start, tp_group, with_entropy)
+    return lp, (ent if with_entropy else None)
 
 
 class _VocabParallelLogProb(torch.autograd.Function):
