@@ -156,10 +156,13 @@ class SegmentPPOObjectiveAdapter:
 
     def ref_table(self, refs: Sequence[SegmentObjectiveRef]) -> RefTable:
         n = len(refs)
-        # One vectorised conversion (a per-element tensor write is a host op per ref).
-        cols = np.fromiter((x for r in refs for x in (r.segment_id, r.query_offset, r.target_token_id,
-                                                      r.sample_row, r.response_offset)),
-                           dtype=np.int64, count=5 * n).reshape(n, 5).T
+        cols = getattr(refs, "columns", None)
+        if cols is not None:          # columnar refs: no per-ref Python objects
+            cols = cols.T
+        else:                         # one vectorised conversion (a per-element tensor write is a host op)
+            cols = np.fromiter((x for r in refs for x in (r.segment_id, r.query_offset, r.target_token_id,
+                                                          r.sample_row, r.response_offset)),
+                               dtype=np.int64, count=5 * n).reshape(n, 5).T
         flat = self._row_offsets_np[cols[3]] + cols[4]
         a = torch.from_numpy(np.vstack([cols, flat[None]]))
         if n and not bool(self._flat["mask"][a[5]].all()):

@@ -35,6 +35,7 @@ from collections import defaultdict
 from dataclasses import dataclass, field
 from typing import Any
 
+import numpy as np
 import torch
 from torch import Tensor, nn
 
@@ -144,9 +145,19 @@ class ForestExecutor:
                 nodes.append(node)
                 order.extend(plan.child_ids(sid))
                 i += 1
-            refs: dict[int, list] = defaultdict(list)
-            for r in tree.objective_refs:
-                refs[r.segment_id].append(r)
+            cols = getattr(tree.objective_refs, "columns", None)
+            if cols is not None:
+                from .tree_plan_builder import ObjectiveRefs
+
+                order_ = np.argsort(cols[:, 0], kind="stable")
+                sorted_cols = cols[order_]
+                sids, starts = np.unique(sorted_cols[:, 0], return_index=True)
+                bounds = list(starts[1:]) + [len(sorted_cols)]
+                refs = {int(sid): ObjectiveRefs(sorted_cols[a:b]) for sid, a, b in zip(sids, starts, bounds)}
+            else:
+                refs = defaultdict(list)
+                for r in tree.objective_refs:
+                    refs[r.segment_id].append(r)
             for sid, lst in refs.items():
                 tab = self.objective.ref_table(lst)
                 n = by_id[sid]

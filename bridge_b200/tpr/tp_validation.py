@@ -45,9 +45,14 @@ def digest_forest_plan(forest) -> str:
                                  list(n.member_rows), list(n.terminal_rows), list(n.children)),
                                 separators=(",", ":")).encode())
         _plan_bytes(h, ex.segment_plan)
-        for r in ex.objective_refs:
-            h.update(json.dumps((r.segment_id, r.query_offset, r.target_token_id, r.sample_row, r.response_offset),
-                                separators=(",", ":")).encode())
+        cols = getattr(ex.objective_refs, "columns", None)
+        if cols is not None:
+            h.update(cols.astype("<i8").tobytes())
+        else:
+            import numpy as np
+
+            h.update(np.asarray([(r.segment_id, r.query_offset, r.target_token_id, r.sample_row, r.response_offset)
+                                 for r in ex.objective_refs], dtype="<i8").reshape(-1, 5).tobytes())
     return h.hexdigest()
 
 

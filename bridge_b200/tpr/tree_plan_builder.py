@@ -12,9 +12,11 @@ Parity: verl/models/mcore/tpr/tree_plan_builder.py:21-212.
 from __future__ import annotations
 
 from bisect import bisect_right
+from collections.abc import Sequence
 from dataclasses import dataclass
 from typing import Any
 
+import numpy as np
 import torch
 
 from .segment_plan import SegmentPlan, SegmentSpec
@@ -30,6 +32,43 @@ class SegmentObjectiveRef:
     response_offset: int
 
 
+class ObjectiveRefs(Sequence):
+    """Immutable sequence of :class:`SegmentObjectiveRef` stored as int64 columns ``[n, 5]``
+    ``(segment_id, query_offset, target_token_id, sample_row, response_offset)``; ref objects are
+    built only when indexed or iterated, and ``columns`` feeds the vectorised consumers directly."""
+
+    __slots__ = ("columns",)
+
+    def __init__(self, columns: np.ndarray) -> None:
+        cols = np.ascontiguousarray(columns, dtype=np.int64).reshape(-1, 5)
+        cols.setflags(write=False)
+        self.columns = cols
+
+    def __len__(self) -> int:
+        return self.columns.shape[0]
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            return ObjectiveRefs(self.columns[i])
+        a = self.columns[i]
+        return SegmentObjectiveRef(int(a[0]), int(a[1]), int(a[2]), int(a[3]), int(a[4]))
+
+    def __iter__(self):
+        for a in self.columns.tolist():
+            yield SegmentObjectiveRef(*a)
+
+    def __eq__(self, other) -> bool:
+        if isinstance(other, ObjectiveRefs):
+            return bool(np.array_equal(self.columns, other.columns))
+        return tuple(self) == tuple(other)
+
+    def __hash__(self) -> int:
+        return hash(self.columns.tobytes())
+
+    def __repr__(self) -> str:
+        return f"ObjectiveRefs(n={len(self)})"
+
+
 @dataclass(frozen=True, slots=True)
 class TreeExecutionPlan:
     tree: TrajectoryTree
@@ -38,6 +77,9 @@ class TreeExecutionPlan:
 
     def refs_for_segment(self, segment_id: int) -> tuple[SegmentObjectiveRef, ...]:
         self.segment_plan.get(segment_id)
+        cols = getattr(self.objective_refs, "columns", None)
+        if cols is not None:
+            return tuple(ObjectiveRefs(cols[cols[:, 0] == segment_id]))
         return tuple(r for r in self.objective_refs if r.segment_id == segment_id)
 
     @property
@@ -107,7 +149,7 @@ def build_tree_execution_plans(
         raise ValueError("keys, input_ids and response_mask must have identical row counts")
     responses = _tensor_rows(batch, "responses") if _has(batch, "responses") else None
 
-    supervised: list[list[int]] = []
+    supervised: list[np.ndarray] = []
     expected = 0
     for row, (tokens, mask) in enumerate(zip(inputs, masks)):
         if mask.numel() > tokens.numel():
@@ -118,11 +160,11 @@ def build_tree_execution_plans(
                 raise ValueError(f"responses/response_mask length mismatch on row {row}")
             if not torch.equal(tokens[tokens.numel() - resp.numel():].cpu(), resp.cpu()):
                 raise ValueError(f"response is not an input_ids suffix on row {row}")
-        offs = torch.nonzero(mask.to(torch.bool).cpu(), as_tuple=False).flatten().tolist()
-        if offs and tokens.numel() - mask.numel() + offs[0] == 0:
+        offs = np.flatnonzero(mask.detach().to(torch.bool).cpu().numpy()).astype(np.int64)
+        if offs.size and tokens.numel() - mask.numel() + int(offs[0]) == 0:
             raise ValueError(f"row {row} has no preceding query token for first supervised token")
         supervised.append(offs)
-        expected += len(offs)
+        expected += int(offs.size)
 
     if require_loss_mask_alignment:
         loss_masks = _tensor_rows(batch, "loss_mask")
@@ -166,29 +208,33 @@ def build_tree_execution_plans(
         if set(path_of) != set(tree.member_rows):
             raise ValueError(f"tree {tree.key} terminal rows do not cover members")
 
-        refs: list[SegmentObjectiveRef] = []
+        # ownership search, vectorised per row: token t (response offset `off`) is predicted by query
+        # q = t - 1, owned by the first node on the row's root-to-terminal path whose end exceeds q
+        parts: list[np.ndarray] = []
         for row in tree.member_rows:
             if row in consumed:
                 raise ValueError(f"row {row} appears in more than one tree")
             consumed.add(row)
+            off = supervised[row]
+            if not off.size:
+                continue
             ids = inputs[row]
             resp_start = ids.numel() - masks[row].numel()
-            path = path_of[row]
-            ends = [tree.get(n).segment.end for n in path]
-            targets = ids.detach().cpu()
-            for off in supervised[row]:
-                t = resp_start + off
-                q = t - 1
-                k = bisect_right(ends, q)
-                if k >= len(path):
-                    raise ValueError(f"row {row} query position {q} is outside tree")
-                owner = tree.get(path[k])
-                if not owner.segment.start <= q < owner.segment.end:
-                    raise ValueError(f"row {row} has uncovered query position {q}")
-                refs.append(SegmentObjectiveRef(segment_id=owner.node_id, query_offset=q - owner.segment.start,
-                                                target_token_id=int(targets[t]), sample_row=row,
-                                                response_offset=off))
-        plans.append(TreeExecutionPlan(tree=tree, segment_plan=plan, objective_refs=tuple(refs)))
+            path = np.asarray(path_of[row], dtype=np.int64)
+            segs = [tree.get(int(n)).segment for n in path]
+            ends = np.asarray([sg.end for sg in segs], dtype=np.int64)
+            starts = np.asarray([sg.start for sg in segs], dtype=np.int64)
+            t = resp_start + off
+            q = t - 1
+            k = np.searchsorted(ends, q, side="right")
+            if bool((k >= len(path)).any()):
+                raise ValueError(f"row {row} query position {int(q[k >= len(path)][0])} is outside tree")
+            if not bool(((starts[k] <= q) & (q < ends[k])).all()):
+                raise ValueError(f"row {row} has uncovered query positions")
+            targets = ids.detach().cpu().numpy().astype(np.int64)[t]
+            parts.append(np.stack([path[k], q - starts[k], targets, np.full_like(off, row), off], axis=1))
+        refs = ObjectiveRefs(np.concatenate(parts) if parts else np.zeros((0, 5), dtype=np.int64))
+        plans.append(TreeExecutionPlan(tree=tree, segment_plan=plan, objective_refs=refs))
 
     if consumed != set(range(len(keys))):
         raise ValueError(f"forest does not cover all input rows: {sorted(set(range(len(keys))) - consumed)}")
