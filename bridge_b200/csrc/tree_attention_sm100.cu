@@ -14,6 +14,7 @@
 // TMEM: S0 | S1 | O = 384 of 512 columns.  Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + P 32 KB.
 // All waits are bounded (sm100_common.cuh).
 #include <torch/extension.h>
+#include <string>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
@@ -301,7 +302,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //   dq   : one CTA = 128 queries x 1 q head (forward-like loop over key tiles): S, dP in TMEM, dS -> smem,
 //          dQ += dS K accumulated in TMEM, written once.
 struct alignas(64) BwdMaps {
-  CUtensorMap q, k, v, pk, pv, dout;
+  CUtensorMap q, k, v, pk, pv, dout, q64, dout64;   // q64 / dout64: 64-row boxes for the pipelined dK/dV
 };
 
 __device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -493,6 +494,249 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       named_sync_softmax();  // lse_s / del_s are rewritten by the next iteration
     }
     const bool g = ok && sm100::mbar_wait(dkv_done, 0, err, 28);
+    if (__all_sync(0xffffffffu, g)) {
+      sm100::tc_fence_after();
+      const size_t kstride = (size_t)Hk * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t rk[32], rv[32];
+        sm100::tmem_ld32(TM_DK + lane_off + c * 32, rk);
+        sm100::tmem_ld32(TM_DV + lane_off + c * 32, rv);
+        sm100::tmem_ld_wait();
+        if (!key_ok) continue;
+        if (mode == 0) {
+          __nv_bfloat16* kd = dk + (size_t)(key_row0 + key) * kstride + (size_t)hk * D + c * 32;
+          __nv_bfloat16* vd = dv + (size_t)(key_row0 + key) * kstride + (size_t)hk * D + c * 32;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            reinterpret_cast<__nv_bfloat162*>(kd)[e] =
+                __floats2bfloat162_rn(__uint_as_float(rk[2 * e]) * scale, __uint_as_float(rk[2 * e + 1]) * scale);
+            reinterpret_cast<__nv_bfloat162*>(vd)[e] =
+                __floats2bfloat162_rn(__uint_as_float(rv[2 * e]), __uint_as_float(rv[2 * e + 1]));
+          }
+        } else {
+          float4* kd = reinterpret_cast<float4*>(dpk_acc + (size_t)(key_row0 + key) * kstride + (size_t)hk * D + c * 32);
+          float4* vd = reinterpret_cast<float4*>(dpv_acc + (size_t)(key_row0 + key) * kstride + (size_t)hk * D + c * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            atomicAdd(kd + e, make_float4(__uint_as_float(rk[4 * e]) * scale, __uint_as_float(rk[4 * e + 1]) * scale,
+                                          __uint_as_float(rk[4 * e + 2]) * scale, __uint_as_float(rk[4 * e + 3]) * scale));
+            atomicAdd(vd + e, make_float4(__uint_as_float(rv[4 * e]), __uint_as_float(rv[4 * e + 1]),
+                                          __uint_as_float(rv[4 * e + 2]), __uint_as_float(rv[4 * e + 3])));
+          }
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Pipelined dK/dV (default): the same math as tree_attn_dkdv_sm100_kernel in 64-row query steps with
+// every per-step buffer doubled -- Q/dO tiles (TMA), S^T/dP^T (TMEM) and P^T/dS^T (smem) -- so the
+// TMA of step i+1 and the S^T/dP^T MMAs of step i+1 run while the softmax warps work on step i, and
+// the MMA warp issues S^T(i+1) before dV/dK(i).  Shared memory: K, V 64 KB + 2 x (Q, dO) 64 KB +
+// 2 x (P^T, dS^T) 64 KB; TMEM: 2 x (S^T 64 | dP^T 64) + dV 128 + dK 128 = 512 columns.
+constexpr int BQ2 = 64;
+constexpr int QT_BYTES = BQ2 * D * 2;   // 16 KB: two 64-column blocks of 64 rows
+constexpr int PT_BYTES = BKV * BQ2 * 2; // 16 KB: one 64-column block of 128 rows
+
+struct SmemDKDV2 {
+  static constexpr int K = 0;
+  static constexpr int V = K + TILE_BYTES;
+  static constexpr int Q0 = V + TILE_BYTES;
+  static constexpr int DO0 = Q0 + 2 * QT_BYTES;
+  static constexpr int PT0 = DO0 + 2 * QT_BYTES;
+  static constexpr int DS0 = PT0 + 2 * PT_BYTES;
+  static constexpr int LSE = DS0 + 2 * PT_BYTES;   // [2][64] floats
+  static constexpr int DEL = LSE + 512;            // [2][64] floats
+  static constexpr int BAR = DEL + 512;
+  static constexpr int TOTAL = BAR + 256;
+};
+
+__device__ __forceinline__ uint64_t kmajor64_desc(uint32_t base, int kk) {   // [64 rows x 128], 8 KB blocks
+  return sm100::umma_desc_sw128(base + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t vmajor64_desc(uint32_t base, int kk) {   // MN-major [64 (K) x 128 (N)]
+  return sm100::umma_desc_sw128(base + kk * 2048, 8192, 1024);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tree_attn_dkdv2_sm100_kernel(const __grid_constant__ BwdMaps maps, const int* __restrict__ cu,
+                                 const int* __restrict__ poff, const int* __restrict__ plen,
+                                 const float* __restrict__ lse, const float* __restrict__ delta,
+                                 __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
+                                 float* __restrict__ dpk_acc, float* __restrict__ dpv_acc, int B, int T, int Hq,
+                                 int Hk, float scale_log2, float scale, int* err) {
+  const int mode = blockIdx.y / B, b = blockIdx.y % B, hk = blockIdx.z, rep = Hq / Hk;
+  const int q0 = cu[b], n = cu[b + 1] - q0;
+  const int key_len = mode == 0 ? n : plen[b];
+  const int key_row0 = mode == 0 ? q0 : poff[b];
+  const int kb = blockIdx.x * BKV;
+  if (kb >= key_len || n <= 0) return;
+  const int it0 = mode == 0 ? kb / BQ2 : 0;
+  const int nq = (n + BQ2 - 1) / BQ2 - it0;
+  const int niter = rep * nq;
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* lse_s = reinterpret_cast<float*>(smem + SmemDKDV2::LSE);
+  float* del_s = reinterpret_cast<float*>(smem + SmemDKDV2::DEL);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemDKDV2::BAR);
+  uint64_t* kv_bar = bars + 0;
+  uint64_t* qdo_full = bars + 1;    // [2]
+  uint64_t* qdo_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;      // [2]
+  uint64_t* st_free = bars + 7;     // [2]
+  uint64_t* p_full = bars + 9;      // [2]
+  uint64_t* dkv_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(kv_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&qdo_full[i], 1);
+      sm100::mbar_init(&qdo_empty[i], 1);
+      sm100::mbar_init(&s_full[i], 1);
+      sm100::mbar_init(&st_free[i], 128);
+      sm100::mbar_init(&p_full[i], 128);
+    }
+    sm100::mbar_init(dkv_done, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, 512);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_DV = tmem + 256, TM_DK = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const CUtensorMap* km = mode == 0 ? &maps.k : &maps.pk;
+      const CUtensorMap* vm = mode == 0 ? &maps.v : &maps.pv;
+      sm100::mbar_expect_tx(kv_bar, 2 * TILE_BYTES);
+      load_tile128(smem + SmemDKDV2::K, km, kv_bar, hk * D, key_row0 + kb);
+      load_tile128(smem + SmemDKDV2::V, vm, kv_bar, hk * D, key_row0 + kb);
+      for (int it = 0; it < niter; ++it) {
+        const int bi = it & 1;
+        const int h = hk * rep + it / nq, qt = it0 + it % nq;
+        if (!sm100::mbar_wait(&qdo_empty[bi], ((it >> 1) & 1) ^ 1, err, 41)) break;
+        sm100::mbar_expect_tx(&qdo_full[bi], 2 * QT_BYTES);
+        unsigned char* qd = smem + SmemDKDV2::Q0 + bi * QT_BYTES;
+        unsigned char* od = smem + SmemDKDV2::DO0 + bi * QT_BYTES;
+        const int row0 = q0 + qt * BQ2;
+        sm100::tma_load_2d(qd, &maps.q64, &qdo_full[bi], h * D, row0);
+        sm100::tma_load_2d(qd + 8192, &maps.q64, &qdo_full[bi], h * D + 64, row0);
+        sm100::tma_load_2d(od, &maps.dout64, &qdo_full[bi], h * D, row0);
+        sm100::tma_load_2d(od + 8192, &maps.dout64, &qdo_full[bi], h * D + 64, row0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = sm100::umma_idesc_bf16(BKV, BQ2, false, false);   // S^T, dP^T: 128 x 64
+      constexpr uint32_t ID_ACC = sm100::umma_idesc_bf16(BKV, D, false, true);    // dV, dK: 128 x 128
+      const uint32_t k_b = sm100::smem_addr(smem + SmemDKDV2::K), v_b = sm100::smem_addr(smem + SmemDKDV2::V);
+      bool ok = sm100::mbar_wait(kv_bar, 0, err, 42);
+      auto issue_s = [&](int j) -> bool {
+        const int bj = j & 1;
+        if (!sm100::mbar_wait(&qdo_full[bj], (j >> 1) & 1, err, 43)) return false;
+        if (!sm100::mbar_wait(&st_free[bj], ((j >> 1) & 1) ^ 1, err, 44)) return false;
+        sm100::tc_fence_after();
+        const uint32_t q_b = sm100::smem_addr(smem + SmemDKDV2::Q0 + bj * QT_BYTES);
+        const uint32_t o_b = sm100::smem_addr(smem + SmemDKDV2::DO0 + bj * QT_BYTES);
+        const uint32_t tm_s = tmem + bj * 128, tm_dp = tmem + bj * 128 + 64;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          sm100::umma_bf16(tm_s, kmajor_desc(k_b, kk), kmajor64_desc(q_b, kk), ID_S, kk > 0);
+          sm100::umma_bf16(tm_dp, kmajor_desc(v_b, kk), kmajor64_desc(o_b, kk), ID_S, kk > 0);
+        }
+        sm100::umma_commit(&s_full[bj]);
+        return true;
+      };
+      if (ok && niter > 0) ok = issue_s(0);
+      for (int it = 0; it < niter && ok; ++it) {
+        if (it + 1 < niter && !issue_s(it + 1)) {
+          ok = false;
+          break;
+        }
+        const int bi = it & 1;
+        if (!sm100::mbar_wait(&p_full[bi], (it >> 1) & 1, err, 45)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t q_b = sm100::smem_addr(smem + SmemDKDV2::Q0 + bi * QT_BYTES);
+        const uint32_t o_b = sm100::smem_addr(smem + SmemDKDV2::DO0 + bi * QT_BYTES);
+        const uint32_t pt_b = sm100::smem_addr(smem + SmemDKDV2::PT0 + bi * PT_BYTES);
+        const uint32_t ds_b = sm100::smem_addr(smem + SmemDKDV2::DS0 + bi * PT_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BQ2 / 16; ++kk) {
+          sm100::umma_bf16(TM_DV, kmajor_desc(pt_b, kk), vmajor64_desc(o_b, kk), ID_ACC, it > 0 || kk > 0);
+          sm100::umma_bf16(TM_DK, kmajor_desc(ds_b, kk), vmajor64_desc(q_b, kk), ID_ACC, it > 0 || kk > 0);
+        }
+        sm100::umma_commit(&qdo_empty[bi]);
+      }
+      if (ok) sm100::umma_commit(dkv_done);
+    }
+  } else {
+    const int quarter = warp & 3, row = quarter * 32 + lane, key = kb + row;
+    const bool key_ok = key < key_len;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int t = threadIdx.x - 64;  // 0..127 among the softmax threads
+    const float LOG2E = 1.4426950408889634f;
+    bool ok = true;
+    for (int it = 0; it < niter && ok; ++it) {
+      const int bi = it & 1;
+      const int h = hk * rep + it / nq, qbase = (it0 + it % nq) * BQ2;
+      if (t < BQ2) {
+        const int q = qbase + t;
+        const bool v = q < n;
+        lse_s[bi * 64 + t] = v ? lse[(size_t)h * T + q0 + q] * LOG2E : INFINITY;
+        del_s[bi * 64 + t] = v ? delta[(size_t)h * T + q0 + q] : 0.f;
+      }
+      named_sync_softmax();
+      bool g = sm100::mbar_wait(&s_full[bi], (it >> 1) & 1, err, 46);
+      if (g && it >= 2) g = sm100::mbar_wait(&qdo_empty[bi], ((it >> 1) & 1) ^ 1, err, 47);  // P^T/dS^T[bi] free
+      if (!named_and_softmax(g)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t tm_s = tmem + bi * 128, tm_dp = tmem + bi * 128 + 64;
+      unsigned char* pt = smem + SmemDKDV2::PT0 + bi * PT_BYTES;
+      unsigned char* dst = smem + SmemDKDV2::DS0 + bi * PT_BYTES;
+#pragma unroll 1
+      for (int c = 0; c < BQ2 / 32; ++c) {
+        uint32_t rs[32], rd[32];
+        sm100::tmem_ld32(tm_s + lane_off + c * 32, rs);
+        sm100::tmem_ld32(tm_dp + lane_off + c * 32, rd);
+        sm100::tmem_ld_wait();
+        float p[32], ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int qq = qbase + c * 32 + e;
+          const bool vis = key_ok && (mode == 1 || key <= qq);  // invalid q rows carry lse=+inf -> p=0
+          const float pe = vis ? exp2f(__uint_as_float(rs[e]) * scale_log2 - lse_s[bi * 64 + c * 32 + e]) : 0.f;
+          p[e] = pe;
+          ds[e] = pe * (__uint_as_float(rd[e]) - del_s[bi * 64 + c * 32 + e]);
+        }
+        store_row32_sw128(pt, row, c, p);
+        store_row32_sw128(dst, row, c, ds);
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&st_free[bi]);
+      sm100::fence_proxy_async_smem();
+      sm100::mbar_arrive(&p_full[bi]);
+    }
+    const bool g = ok && sm100::mbar_wait(dkv_done, 0, err, 48);
     if (__all_sync(0xffffffffu, g)) {
       sm100::tc_fence_after();
       const size_t kstride = (size_t)Hk * D;
@@ -745,12 +989,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Row-major [rows, cols] bf16 -> map with box {64 cols, 128 rows}, 128-byte swizzle.
-void encode_rows(CUtensorMap* m, const void* base, long rows, long cols) {
+// Row-major [rows, cols] bf16 -> map with box {64 cols, box_rows}, 128-byte swizzle.
+void encode_rows(CUtensorMap* m, const void* base, long rows, long cols, int box_rows = 128) {
   TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0 && (cols * 2) % 16 == 0, "attention TMA alignment");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)std::max<long>(rows, 1)};
   cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -868,6 +1112,8 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
   encode_rows(&maps->pk, has_p ? pk.data_ptr() : k.data_ptr(), has_p ? pk.size(0) : T, (long)Hk * D);
   encode_rows(&maps->pv, has_p ? pv.data_ptr() : v.data_ptr(), has_p ? pv.size(0) : T, (long)Hk * D);
   encode_rows(&maps->dout, dout.data_ptr(), T, (long)Hq * D);
+  encode_rows(&maps->q64, q.data_ptr(), T, (long)Hq * D, 64);
+  encode_rows(&maps->dout64, dout.data_ptr(), T, (long)Hq * D, 64);
   const int* cup = cu.data_ptr<int>();
   const int* pop = poff.data_ptr<int>();
   const int* plp = plen.data_ptr<int>();
@@ -877,8 +1123,9 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
   int* err = attn_error_word().data_ptr<int>();
   int Bi = B, Ti = T, Hqi = Hq, Hki = Hk;
   {
-    auto kern = tree_attn_dkdv_sm100_kernel;
-    const int smem = SmemDKDV::TOTAL + 1024;
+    static const bool v1 = getenv("BB_ATTN_DKDV") && std::string(getenv("BB_ATTN_DKDV")) == "v1";
+    auto kern = v1 ? tree_attn_dkdv_sm100_kernel : tree_attn_dkdv2_sm100_kernel;
+    const int smem = (v1 ? SmemDKDV::TOTAL : SmemDKDV2::TOTAL) + 1024;
     static bool attr = false;
     if (!attr) {
       BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
