@@ -65,3 +65,22 @@ def test_capture_env_hook_writes_once_per_minibatch(tmp_path, monkeypatch):
     eng.forward_backward_batch(batch)
     files = sorted(os.listdir(tmp_path))
     assert files == ["step00000003_rank00000_capture000000_batch0.pt", "step00000003_rank00000_capture000001_batch1.pt"]
+
+
+def test_gemm_mshape_tool_reports_split_drift():
+    from bridge_b200.utils.gemm_mshape import mshape_drift
+
+    r = mshape_drift(96, 256, 128, 32, device="cpu")
+    assert r["torch"]["rel_l2"] < 1e-2 and r["torch"]["max_abs"] >= 0.0
+
+
+def test_cp_drift_tool(tmp_path):
+    from bridge_b200.utils.cp_drift import _flat, drift, main
+
+    a = torch.randn(500) - 3
+    b = a + 1e-3 * torch.randn(500)
+    torch.save(a, tmp_path / "a.pt")
+    torch.save({"log_probs": [b[:200], b[200:]]}, tmp_path / "b.pt")
+    out = drift(_flat(torch.load(tmp_path / "a.pt")), _flat(torch.load(tmp_path / "b.pt", weights_only=False)))
+    assert out["cosine"] > 0.999 and out["rel_l2"] < 1e-3
+    main([str(tmp_path / "a.pt"), str(tmp_path / "b.pt")])
