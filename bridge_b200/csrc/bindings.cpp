@@ -5,6 +5,14 @@ int64_t bb_launch_count();
 
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
 std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd);
+std::vector<torch::Tensor> gated_rmsnorm_fwd(torch::Tensor o, torch::Tensor z, torch::Tensor w, double eps);
+std::vector<torch::Tensor> gated_rmsnorm_bwd(torch::Tensor dy, torch::Tensor o, torch::Tensor z, torch::Tensor w,
+                                             torch::Tensor rstd);
+std::vector<torch::Tensor> l2norm_fwd(torch::Tensor x, double eps);
+torch::Tensor l2norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor rn);
+std::vector<torch::Tensor> gdn_gates_fwd(torch::Tensor a, torch::Tensor b, torch::Tensor A_log, torch::Tensor dt);
+std::vector<torch::Tensor> gdn_gates_bwd(torch::Tensor dg, torch::Tensor dbeta, torch::Tensor a, torch::Tensor b,
+                                         torch::Tensor A_log, torch::Tensor dt);
 std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor qw, torch::Tensor kw,
                                             torch::Tensor cosb, torch::Tensor sinb, double eps);
 std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
@@ -87,6 +95,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bridge_b200 sm_100a kernels";
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd, "GDN output gate: RMSNorm(o) * w * silu(z)");
+  m.def("gated_rmsnorm_bwd", &gated_rmsnorm_bwd);
+  m.def("l2norm_fwd", &l2norm_fwd, "row L2 normalisation of a [T, H, D] view");
+  m.def("l2norm_bwd", &l2norm_bwd);
+  m.def("gdn_gates_fwd", &gdn_gates_fwd, "g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)");
+  m.def("gdn_gates_bwd", &gdn_gates_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
   m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
   m.def("swiglu_fwd", &swiglu_fwd);

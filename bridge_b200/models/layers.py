@@ -18,12 +18,11 @@ import math
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 from torch import Tensor
 
 from ..ops.activation import swiglu
 from ..ops.attention import tree_attention
-from ..ops.gdn import causal_conv1d, chunk_gated_delta_rule, gated_rmsnorm, l2norm
+from ..ops.gdn import causal_conv1d, chunk_gated_delta_rule, gated_rmsnorm, gdn_gates, l2norm
 from ..ops.norm import qk_norm_rope, rmsnorm, rope_cos_sin
 from ..parallel.tp import ColumnParallelLinear, RowParallelLinear, tp_size, scaled_init_std
 from ..tpr.context import get_tpr_attention_context, _single_layout
@@ -197,8 +196,7 @@ class TPRGatedDeltaNet(nn.Module):
         if rep > 1:
             q = q.repeat_interleave(rep, dim=1)
             k = k.repeat_interleave(rep, dim=1)
-        beta = torch.sigmoid(b.float())
-        g = -torch.exp(self.A_log.float()) * F.softplus(a.float() + self.dt_bias.float())
+        g, beta = gdn_gates(a, b, self.A_log, self.dt_bias)
         o, rec_final = chunk_gated_delta_rule(q, k, v, g, beta, cu, cu_dev, h_rec, scale=self.scale,
                                               chunk_size=self.chunk)
         if ctx is not None and ctx.capture_gdn_final_state:

@@ -228,13 +228,97 @@ def chunk_gated_delta_rule(q, k, v, g, beta, cu_seqlens: list[int], cu_dev: Tens
                                             chunk_size=chunk_size)
 
 
-def l2norm(x: Tensor, eps: float = 1e-6) -> Tensor:
+def l2norm_reference(x: Tensor, eps: float = 1e-6) -> Tensor:
     xf = x.float()
     return (xf * torch.rsqrt((xf * xf).sum(-1, keepdim=True) + eps)).to(x.dtype)
 
 
-def gated_rmsnorm(o: Tensor, z: Tensor, weight: Tensor, eps: float) -> Tensor:
-    """``RMSNorm(o) * weight * silu(z)`` per head (last dim)."""
+def gated_rmsnorm_reference(o: Tensor, z: Tensor, weight: Tensor, eps: float) -> Tensor:
     of = o.float()
     y = of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps) * weight.float()
     return (y * F.silu(z.float())).to(o.dtype)
+
+
+def gdn_gates_reference(a: Tensor, b: Tensor, A_log: Tensor, dt_bias: Tensor) -> tuple[Tensor, Tensor]:
+    g = -torch.exp(A_log.float()) * F.softplus(a.float() + dt_bias.float())
+    return g, torch.sigmoid(b.float())
+
+
+_ROW_WIDTHS = (32, 64, 128, 256)
+
+
+def _heads_view_ok(x: Tensor) -> bool:
+    return (x.dim() == 3 and x.dtype == torch.bfloat16 and x.shape[-1] in _ROW_WIDTHS and x.stride(2) == 1
+            and (x.shape[1] == 1 or x.stride(1) == x.shape[2]))
+
+
+class _L2NormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, eps):
+        y, rn = kernels().l2norm_fwd(x, eps)
+        ctx.save_for_backward(x, rn)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, rn = ctx.saved_tensors
+        return kernels().l2norm_bwd(dy.contiguous(), x, rn), None
+
+
+class _GatedRMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, o, z, weight, eps):
+        o = o.contiguous()
+        y, rstd = kernels().gated_rmsnorm_fwd(o, z, weight, eps)
+        ctx.save_for_backward(o, z, weight, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        o, z, weight, rstd = ctx.saved_tensors
+        do, dz, dw = kernels().gated_rmsnorm_bwd(dy.contiguous(), o, z, weight, rstd)
+        return do, dz, dw.to(weight.dtype), None
+
+
+class _GatesFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b, A_log, dt_bias):
+        g, beta = kernels().gdn_gates_fwd(a, b, A_log, dt_bias)
+        ctx.save_for_backward(a, b, A_log, dt_bias)
+        return g, beta
+
+    @staticmethod
+    def backward(ctx, dg, dbeta):
+        a, b, A_log, dt_bias = ctx.saved_tensors
+        if dg is None:
+            dg = torch.zeros(a.shape, dtype=torch.float32, device=a.device)
+        if dbeta is None:
+            dbeta = torch.zeros(b.shape, dtype=torch.float32, device=b.device)
+        da, db, dA, ddt = kernels().gdn_gates_bwd(dg, dbeta, a, b, A_log, dt_bias)
+        return da, db, dA.to(A_log.dtype), ddt.to(dt_bias.dtype)
+
+
+def l2norm(x: Tensor, eps: float = 1e-6) -> Tensor:
+    """Row L2 normalisation of ``x [T, H, D]`` (q / k before the delta rule); fused kernel on CUDA.
+
+    ``x`` may be a column slice of the conv output (token stride wider than ``H * D``)."""
+    if on_gpu(x) and _heads_view_ok(x):
+        return _L2NormFn.apply(x, eps)
+    return l2norm_reference(x, eps)
+
+
+def gated_rmsnorm(o: Tensor, z: Tensor, weight: Tensor, eps: float) -> Tensor:
+    """``RMSNorm(o) * weight * silu(z)`` per head (last dim); fused kernel on CUDA."""
+    if on_gpu(o) and _heads_view_ok(o) and _heads_view_ok(z) and o.shape == z.shape:
+        return _GatedRMSNormFn.apply(o, z, weight, eps)
+    return gated_rmsnorm_reference(o, z, weight, eps)
+
+
+def gdn_gates(a: Tensor, b: Tensor, A_log: Tensor, dt_bias: Tensor) -> tuple[Tensor, Tensor]:
+    """Decay and write gates of the delta rule: ``g = -exp(A_log) softplus(a + dt_bias)`` (log-space
+    decay per token and head) and ``beta = sigmoid(b)``, both FP32 ``[T, H]``.  ``a, b`` may be
+    column slices of the fused input projection (unit column stride)."""
+    if (on_gpu(a) and a.dim() == 2 and a.shape == b.shape and a.dtype == torch.bfloat16
+            and b.dtype == torch.bfloat16 and a.stride(1) == 1 and b.stride(1) == 1):
+        return _GatesFn.apply(a, b, A_log, dt_bias)
+    return gdn_gates_reference(a, b, A_log, dt_bias)

@@ -24,10 +24,9 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
 from torch import Tensor
 
-from ..ops.gdn import causal_conv1d, chunk_gated_delta_rule, gated_rmsnorm, l2norm
+from ..ops.gdn import causal_conv1d, chunk_gated_delta_rule, gated_rmsnorm, gdn_gates, l2norm
 from .ulysses_attention import head_to_sequence, sequence_to_head
 
 
@@ -75,8 +74,7 @@ def forward_gdn_cp_with_state(module, hidden_local: Tensor, initial_state, cp_gr
         q, k = q.repeat_interleave(rep, 1), k.repeat_interleave(rep, 1)
     A = module.A_log.chunk(n)[r]
     dt = module.dt_bias.chunk(n)[r]
-    beta = torch.sigmoid(b.float())
-    g = -torch.exp(A.float()) * F.softplus(a.float() + dt.float())
+    g, beta = gdn_gates(a, b, A, dt)
     o, rec_final = chunk_gated_delta_rule(q, k, v, g, beta, [0, t], None, h_rec, scale=module.scale,
                                           chunk_size=module.chunk)
     o = gated_rmsnorm(o, z.reshape(t, hv, module.dv), module.norm_weight, module.eps)
@@ -203,8 +201,7 @@ def forward_gdn_cp_tpr(module, hidden_local: Tensor, ctx, backend):
         q, k = q.repeat_interleave(rep, 1), k.repeat_interleave(rep, 1)
     A = module.A_log.chunk(n)[r]
     dt = module.dt_bias.chunk(n)[r]
-    beta = torch.sigmoid(b.float())
-    g = -torch.exp(A.float()) * F.softplus(a.float() + dt.float())
+    g, beta = gdn_gates(a, b, A, dt)
     o, rec_final = chunk_gated_delta_rule(q, k, v, g, beta, [0, t], None, h_rec, scale=module.scale,
                                           chunk_size=module.chunk)
     o = gated_rmsnorm(o, z.reshape(t, hv, module.dv), module.norm_weight, module.eps).reshape(t, hv * module.dv)

@@ -105,3 +105,67 @@ def test_gated_delta_rule_matches_recurrence():
     orr, Sr = gated_delta_rule_recurrent(q.float(), k.float(), v.float(), gate, beta, h0[0], scale=0.1)
     _close(o, orr, 1e-2, 1e-2, "o")
     _close(hT[0], Sr, 3e-3, 1e-2, "state")
+
+
+@pytest.mark.parametrize("D", [128, 64, 256])
+def test_l2norm_strided_heads(D):
+    """Fused L2 norm on a column slice of a wider projection (the conv output layout) vs FP32."""
+    from bridge_b200.ops.gdn import l2norm, l2norm_reference
+
+    torch.manual_seed(D)
+    T, H = 333, 3
+    base = torch.randn(T, 2 * H * D + 40, device=DEV).to(torch.bfloat16)
+    x = base[:, H * D:2 * H * D].reshape(T, H, D).detach().requires_grad_()
+    xr = x.detach().float().requires_grad_()
+    y = l2norm(x)
+    yr = l2norm_reference(xr)
+    assert y.is_contiguous()
+    _close(y, yr, 1e-2, 1e-2, "y")
+    dy = torch.randn_like(yr)
+    (y.float() * dy).sum().backward()
+    (yr * dy).sum().backward()
+    _close(x.grad, xr.grad, 2e-2, 1e-2, "dx")
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_gated_rmsnorm_matches_fp32(D):
+    from bridge_b200.ops.gdn import gated_rmsnorm, gated_rmsnorm_reference
+
+    torch.manual_seed(D + 1)
+    T, H = 517, 4
+    o = torch.randn(T, H, D, device=DEV).to(torch.bfloat16).requires_grad_()
+    proj = torch.randn(T, H * D + 24, device=DEV).to(torch.bfloat16)
+    z = proj[:, 8:8 + H * D].reshape(T, H, D).detach().requires_grad_()
+    w = (1 + 0.1 * torch.randn(D, device=DEV)).requires_grad_()
+    y = gated_rmsnorm(o, z, w, 1e-6)
+    refs = [t.detach().float().requires_grad_() for t in (o, z, w)]
+    yr = gated_rmsnorm_reference(*refs, 1e-6)
+    _close(y, yr, 2e-2, 1e-2, "y")
+    dy = torch.randn_like(yr)
+    (y.float() * dy).sum().backward()
+    (yr * dy).sum().backward()
+    for name, a, b in zip(("do", "dz", "dw"), (o, z, w), refs):
+        _close(a.grad, b.grad, 3e-2, 1e-2, name)
+
+
+def test_gdn_gates_matches_fp32():
+    from bridge_b200.ops.gdn import gdn_gates, gdn_gates_reference
+
+    torch.manual_seed(7)
+    T, H = 1000, 16
+    proj = (2 * torch.randn(T, 3 * H + 16, device=DEV)).to(torch.bfloat16)
+    a = proj[:, 16:16 + H].detach().requires_grad_()
+    b = proj[:, 16 + H:16 + 2 * H].detach().requires_grad_()
+    A_log = torch.log(torch.empty(H, device=DEV).uniform_(1, 16)).requires_grad_()
+    dt = (0.5 * torch.randn(H, device=DEV)).requires_grad_()
+    g, beta = gdn_gates(a, b, A_log, dt)
+    refs = [t.detach().float().requires_grad_() for t in (a, b, A_log, dt)]
+    gr, br = gdn_gates_reference(*refs)
+    assert g.dtype == torch.float32 and beta.dtype == torch.float32
+    _close(g, gr, 1e-4, 1e-5, "g")
+    _close(beta, br, 1e-6, 1e-5, "beta")
+    dg, db = torch.randn_like(gr), torch.randn_like(br)
+    ((g * dg).sum() + (beta * db).sum()).backward()
+    ((gr * dg).sum() + (br * db).sum()).backward()
+    for name, x, r in zip(("da", "db", "dA_log", "ddt"), (a, b, A_log, dt), refs):
+        _close(x.grad, r.grad, 1e-3, 1e-2, name)
