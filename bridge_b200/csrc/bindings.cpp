@@ -5,6 +5,10 @@ int64_t bb_launch_count();
 
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
 std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd);
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, torch::Tensor w, double eps);
+std::vector<torch::Tensor> add_rmsnorm_bwd(torch::Tensor dy, torch::Tensor h, torch::Tensor w, torch::Tensor rstd,
+                                           torch::Tensor dh);
+void sumsq_into(torch::Tensor x, torch::Tensor out, bool accumulate);
 std::vector<torch::Tensor> gated_rmsnorm_fwd(torch::Tensor o, torch::Tensor z, torch::Tensor w, double eps);
 std::vector<torch::Tensor> gated_rmsnorm_bwd(torch::Tensor dy, torch::Tensor o, torch::Tensor z, torch::Tensor w,
                                              torch::Tensor rstd);
@@ -95,6 +99,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bridge_b200 sm_100a kernels";
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, "h = x + res; y = RMSNorm(h) * w -> (y, rstd, h)");
+  m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd, "residual-sum gradient: RMSNorm backward + dh -> (dx, dw)");
+  m.def("sumsq_into", &sumsq_into, "out[0] (+)= sum(x^2), FP32, deterministic");
   m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd, "GDN output gate: RMSNorm(o) * w * silu(z)");
   m.def("gated_rmsnorm_bwd", &gated_rmsnorm_bwd);
   m.def("l2norm_fwd", &l2norm_fwd, "row L2 normalisation of a [T, H, D] view");

@@ -75,6 +75,19 @@ inline std::atomic<long long>& launch_counter() {
   return c;
 }
 }  // namespace bb
+namespace bb {
+// Grid for a grid-stride kernel: at most the number of blocks that are resident at once on all SMs
+// (a larger grid would run as a partial second wave), and no more than `want`.
+template <typename Kernel>
+inline int resident_grid(Kernel kernel, int threads, size_t smem, long want) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  const long cap = (long)sms * (per_sm > 0 ? per_sm : 1);
+  return (int)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+}  // namespace bb
 #define BB_POST_LAUNCH()                  \
   do {                                    \
     BB_CHECK_CUDA(cudaGetLastError());    \

@@ -13,108 +13,159 @@ using bb::bf16x8;
 namespace {
 
 // ----------------------------------------------------------------------------------------- RMSNorm
-// One warp per row; H % 8 == 0.
-__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
-                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd, int rows, int H,
-                                   float eps) {
+// One warp per row; lane owns the 8-element vectors i = lane + 32 a (a < MAXV), so a whole row stays
+// in registers and HBM is touched once per tensor (all MAXV loads of a row are in flight together).
+// RES = true fuses the residual add that precedes every decoder norm: h = bf16(x + res) is written
+// out and normalised (the same rounding as a separate bf16 add).
+template <int MAXV, bool RES>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ res,
+                                                          const __nv_bfloat16* __restrict__ w,
+                                                          __nv_bfloat16* __restrict__ y,
+                                                          __nv_bfloat16* __restrict__ hout,
+                                                          float* __restrict__ rstd, int rows, int H, float eps) {
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int nv = H / 8;
+  const bf16x8* wr = reinterpret_cast<const bf16x8*>(w);
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
     const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + (size_t)row * H);
-    float ss = 0.f;
-    for (int i = lane; i < H / 8; i += 32) {
-      float f[8];
-      bb::unpack8(xr[i], f);
+    bf16x8 v[MAXV];
+    bf16x8 rv[RES ? MAXV : 1];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+    for (int a = 0; a < MAXV; ++a) {
+      const int i = lane + a * 32;
+      if (i < nv) {
+        v[a] = xr[i];
+        if constexpr (RES) rv[a] = reinterpret_cast<const bf16x8*>(res + (size_t)row * H)[i];
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int a = 0; a < MAXV; ++a) {
+      const int i = lane + a * 32;
+      if (i < nv) {
+        float f[8];
+        bb::unpack8(v[a], f);
+        if constexpr (RES) {
+          float g[8];
+          bb::unpack8(rv[a], g);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] += g[j];
+          v[a] = bb::pack8(f);
+          reinterpret_cast<bf16x8*>(hout + (size_t)row * H)[i] = v[a];
+          bb::unpack8(v[a], f);  // normalise the rounded sum
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+      }
     }
     ss = bb::warp_sum(ss);
     const float r = rsqrtf(ss / H + eps);
     if (lane == 0) rstd[row] = r;
     bf16x8* yr = reinterpret_cast<bf16x8*>(y + (size_t)row * H);
-    const bf16x8* wr = reinterpret_cast<const bf16x8*>(w);
-    for (int i = lane; i < H / 8; i += 32) {
-      float f[8], g[8];
-      bb::unpack8(xr[i], f);
-      bb::unpack8(wr[i], g);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
-      yr[i] = bb::pack8(f);
+    for (int a = 0; a < MAXV; ++a) {
+      const int i = lane + a * 32;
+      if (i < nv) {
+        float f[8], g[8];
+        bb::unpack8(v[a], f);
+        bb::unpack8(wr[i], g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
+        yr[i] = bb::pack8(f);
+      }
     }
   }
 }
 
-// dx = r * (dy*w - xhat * mean(dy*w*xhat)); dw partials per block -> [gridDim.x, H] (FP32).
-template <int MAXV>
-__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
-                                   const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
-                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int rows, int H) {
-  extern __shared__ float sdw[];  // [H]
+// dx = r * (dy*w - xhat * mean(dy*w*xhat)) (+ dres: the gradient that reached the residual sum
+// directly).  dw: every warp accumulates its rows into a private FP32 row of shared memory (each lane
+// owns fixed columns, so no atomics), the block sums its warps' rows and adds one FP32 atomic per
+// column into dw (zero-initialised by the caller).
+template <int MAXV, bool RES>
+__global__ void __launch_bounds__(256, 2) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                             const __nv_bfloat16* __restrict__ x,
+                                                             const __nv_bfloat16* __restrict__ w,
+                                                             const float* __restrict__ rstd,
+                                                             const __nv_bfloat16* __restrict__ dres,
+                                                             __nv_bfloat16* __restrict__ dx, float* __restrict__ dw,
+                                                             int rows, int H) {
+  extern __shared__ __align__(16) float smem[];  // [H] weight (FP32), [warps][H] dw partials
   const int warps = blockDim.x >> 5;
-  const int lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sw = smem;
+  float* sdw = smem + H + (size_t)warp * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) sw[i] = __bfloat162float(w[i]);
+  for (int i = threadIdx.x; i < warps * H; i += blockDim.x) smem[H + i] = 0.f;
   __syncthreads();
   const int nv = H / 8;
-  float acc[MAXV][8];
-#pragma unroll
-  for (int a = 0; a < MAXV; ++a)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[a][j] = 0.f;
-  const bf16x8* wr = reinterpret_cast<const bf16x8*>(w);
-  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
+  for (int row = blockIdx.x * warps + warp; row < rows; row += gridDim.x * warps) {
     const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + (size_t)row * H);
     const bf16x8* gr = reinterpret_cast<const bf16x8*>(dy + (size_t)row * H);
+    bf16x8 xv[MAXV], gv[MAXV];
+#pragma unroll
+    for (int a = 0; a < MAXV; ++a) {
+      const int i = lane + a * 32;
+      if (i < nv) {
+        xv[a] = xr[i];
+        gv[a] = gr[i];
+      }
+    }
     const float r = rstd[row];
     float dot = 0.f;
 #pragma unroll
     for (int a = 0; a < MAXV; ++a) {
-      int i = lane + a * 32;
+      const int i = lane + a * 32;
       if (i < nv) {
-        float f[8], g[8], ww[8];
-        bb::unpack8(xr[i], f);
-        bb::unpack8(gr[i], g);
-        bb::unpack8(wr[i], ww);
+        float f[8], g[8];
+        bb::unpack8(xv[a], f);
+        bb::unpack8(gv[a], g);
+        float4* acc = reinterpret_cast<float4*>(sdw + i * 8);
+        const float4* wv = reinterpret_cast<const float4*>(sw + i * 8);
+        float4 a0 = acc[0], a1 = acc[1];
+        const float4 w0 = wv[0], w1 = wv[1];
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float* ap0 = &a0.x;
+        float* ap1 = &a1.x;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          float xh = f[j] * r;
+          const float xh = f[j] * r;
           dot += g[j] * ww[j] * xh;
-          acc[a][j] += g[j] * xh;
+          (j < 4 ? ap0[j] : ap1[j - 4]) += g[j] * xh;
         }
+        acc[0] = a0;
+        acc[1] = a1;
       }
     }
     dot = bb::warp_sum(dot) / H;
     bf16x8* dxr = reinterpret_cast<bf16x8*>(dx + (size_t)row * H);
 #pragma unroll
     for (int a = 0; a < MAXV; ++a) {
-      int i = lane + a * 32;
+      const int i = lane + a * 32;
       if (i < nv) {
-        float f[8], g[8], ww[8], o[8];
-        bb::unpack8(xr[i], f);
-        bb::unpack8(gr[i], g);
-        bb::unpack8(wr[i], ww);
+        float f[8], g[8], o[8], d[8];
+        bb::unpack8(xv[a], f);
+        bb::unpack8(gv[a], g);
+        const float4* wv = reinterpret_cast<const float4*>(sw + i * 8);
+        const float4 w0 = wv[0], w1 = wv[1];
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        if constexpr (RES) bb::unpack8(reinterpret_cast<const bf16x8*>(dres + (size_t)row * H)[i], d);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = r * (g[j] * ww[j] - f[j] * r * dot);
+        for (int j = 0; j < 8; ++j) {
+          o[j] = r * (g[j] * ww[j] - f[j] * r * dot);
+          if constexpr (RES) o[j] += d[j];
+        }
         dxr[i] = bb::pack8(o);
       }
     }
   }
-#pragma unroll
-  for (int a = 0; a < MAXV; ++a) {
-    int i = lane + a * 32;
-    if (i < nv)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) atomicAdd(&sdw[i * 8 + j], acc[a][j]);
-  }
   __syncthreads();
-  for (int i = threadIdx.x; i < H; i += blockDim.x) dw_part[(size_t)blockIdx.x * H + i] = sdw[i];
-}
-
-__global__ void column_sum_kernel(const float* __restrict__ part, float* __restrict__ out, int nrows, int H) {
-  int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= H) return;
-  float s = 0.f;
-  for (int r = 0; r < nrows; ++r) s += part[(size_t)r * H + c];
-  out[c] = s;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float t = 0.f;
+    for (int k = 0; k < warps; ++k) t += smem[H + (size_t)k * H + i];
+    atomicAdd(&dw[i], t);
+  }
 }
 
 // ------------------------------------------------------------------------------- qk-RMSNorm + RoPE
@@ -149,14 +200,12 @@ __device__ __forceinline__ void store_e(__nv_bfloat16* p, const float* f) {
     for (int j = 0; j < E; ++j) p[j] = __float2bfloat16(f[j]);
   }
 }
+// Normalise + rotate one preloaded head row f (E = D / 32 elements per lane) and store it.
 template <int D>
-__device__ __forceinline__ void norm_rope_row(const __nv_bfloat16* __restrict__ in, const float* __restrict__ w,
-                                              __nv_bfloat16* __restrict__ out, float* __restrict__ rstd_out,
-                                              const float* __restrict__ cs, const float* __restrict__ sn, float eps,
-                                              int lane) {
+__device__ __forceinline__ void norm_rope_apply(float* f, const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                                float* __restrict__ rstd_out, const float* __restrict__ cs,
+                                                const float* __restrict__ sn, float eps, int lane) {
   constexpr int E = D / 32;
-  float f[E];
-  load_e<E>(in + lane * E, f);
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < E; ++j) ss += f[j] * f[j];
@@ -178,6 +227,11 @@ __device__ __forceinline__ void norm_rope_row(const __nv_bfloat16* __restrict__ 
   store_e<E>(out + lane * E, o);
 }
 
+// A warp handles one token and kQKRows of its heads per iteration: all rows are loaded before any is
+// reduced (kQKRows x 256 B in flight per warp for D = 128), and one 32-bit division per group maps
+// the work item to (token, first head).
+constexpr int kQKRows = 4;
+
 template <int D>
 __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                                         const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
@@ -191,36 +245,48 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, con
     swk[i] = __bfloat162float(kw[i]);
   }
   __syncthreads();
+  constexpr int E = D / 32;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  const long total = (long)T * (Hq + Hk);
-  for (long item = (long)blockIdx.x * warps + (threadIdx.x >> 5); item < total; item += (long)gridDim.x * warps) {
-    const int t = (int)(item / (Hq + Hk));
-    const int h = (int)(item % (Hq + Hk));
+  const int HH = Hq + Hk, G = (HH + kQKRows - 1) / kQKRows;  // head groups per token
+  const int total = T * G;                                  // < 2^31, checked on the host
+  for (int item = blockIdx.x * warps + (threadIdx.x >> 5); item < total; item += gridDim.x * warps) {
+    const int t = item / G, h0 = (item - t * G) * kQKRows;
+    float f[kQKRows][E];
+#pragma unroll
+    for (int u = 0; u < kQKRows; ++u) {
+      const int h = h0 + u;
+      if (h < HH) {
+        const __nv_bfloat16* src = h < Hq ? q + t * qts + h * qhs : k + t * kts + (h - Hq) * khs;
+        load_e<E>(src + lane * E, f[u]);
+      }
+    }
     const float* cs = cosb + (size_t)t * (D / 2);
     const float* sn = sinb + (size_t)t * (D / 2);
-    if (h < Hq) {
-      size_t off = ((size_t)t * Hq + h) * D;
-      norm_rope_row<D>(q + t * qts + h * qhs, swq, qo + off, rq + (size_t)t * Hq + h, cs, sn, eps, lane);
-    } else {
-      int hh = h - Hq;
-      size_t off = ((size_t)t * Hk + hh) * D;
-      norm_rope_row<D>(k + t * kts + hh * khs, swk, ko + off, rk + (size_t)t * Hk + hh, cs, sn, eps, lane);
+#pragma unroll
+    for (int u = 0; u < kQKRows; ++u) {
+      const int h = h0 + u;
+      if (h < HH) {
+        if (h < Hq)
+          norm_rope_apply<D>(f[u], swq, qo + ((size_t)t * Hq + h) * D, rq + (size_t)t * Hq + h, cs, sn, eps, lane);
+        else
+          norm_rope_apply<D>(f[u], swk, ko + ((size_t)t * Hk + h - Hq) * D, rk + (size_t)t * Hk + h - Hq, cs, sn,
+                             eps, lane);
+      }
     }
   }
 }
 
-// Backward of y = rope(rmsnorm(x) * w): un-rotate dy, then RMSNorm backward; dw accumulated per block.
+// Backward of y = rope(rmsnorm(x) * w) for one preloaded row (dl = dy, x): un-rotate dy, then the
+// RMSNorm backward; dw accumulated per lane.
 template <int D>
-__device__ __forceinline__ void norm_rope_row_bwd(const __nv_bfloat16* __restrict__ dyp,
-                                                  const __nv_bfloat16* __restrict__ xp, const float* __restrict__ w,
-                                                  float r, const float* __restrict__ cs, const float* __restrict__ sn,
-                                                  __nv_bfloat16* __restrict__ dxp, float* dwacc, int lane) {
+__device__ __forceinline__ void norm_rope_apply_bwd(const float* dl, const float* x, const float* __restrict__ w,
+                                                    float r, const float* __restrict__ cs,
+                                                    const float* __restrict__ sn, __nv_bfloat16* __restrict__ dxp,
+                                                    float* dwacc, int lane) {
   constexpr int E = D / 32;
   const bool lo = lane < 16;
   const int fi = (lane & 15) * E;
-  float g[E], x[E], dl[E];
-  load_e<E>(dyp + lane * E, dl);
-  load_e<E>(xp + lane * E, x);
+  float g[E];
 #pragma unroll
   for (int j = 0; j < E; ++j) {
     float d = dl[j];
@@ -265,21 +331,37 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, c
 #pragma unroll
   for (int j = 0; j < E; ++j) aq[j] = ak[j] = 0.f;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  const long total = (long)T * (Hq + Hk);
-  for (long item = (long)blockIdx.x * warps + (threadIdx.x >> 5); item < total; item += (long)gridDim.x * warps) {
-    const int t = (int)(item / (Hq + Hk));
-    const int h = (int)(item % (Hq + Hk));
+  const int HH = Hq + Hk, G = (HH + kQKRows - 1) / kQKRows;
+  const int total = T * G;
+  for (int item = blockIdx.x * warps + (threadIdx.x >> 5); item < total; item += gridDim.x * warps) {
+    const int t = item / G, h0 = (item - t * G) * kQKRows;
+    float dl[kQKRows][E], xv[kQKRows][E], rr[kQKRows];
+#pragma unroll
+    for (int u = 0; u < kQKRows; ++u) {
+      const int h = h0 + u;
+      if (h < HH) {
+        if (h < Hq) {
+          load_e<E>(dqo + ((size_t)t * Hq + h) * D + lane * E, dl[u]);
+          load_e<E>(q + t * qts + h * qhs + lane * E, xv[u]);
+          rr[u] = rq[(size_t)t * Hq + h];
+        } else {
+          load_e<E>(dko + ((size_t)t * Hk + h - Hq) * D + lane * E, dl[u]);
+          load_e<E>(k + t * kts + (h - Hq) * khs + lane * E, xv[u]);
+          rr[u] = rk[(size_t)t * Hk + h - Hq];
+        }
+      }
+    }
     const float* cs = cosb + (size_t)t * (D / 2);
     const float* sn = sinb + (size_t)t * (D / 2);
-    if (h < Hq) {
-      size_t off = ((size_t)t * Hq + h) * D;
-      norm_rope_row_bwd<D>(dqo + off, q + t * qts + h * qhs, swq, rq[(size_t)t * Hq + h], cs, sn, dq + off, aq,
-                           lane);
-    } else {
-      int hh = h - Hq;
-      size_t off = ((size_t)t * Hk + hh) * D;
-      norm_rope_row_bwd<D>(dko + off, k + t * kts + hh * khs, swk, rk[(size_t)t * Hk + hh], cs, sn, dk + off, ak,
-                           lane);
+#pragma unroll
+    for (int u = 0; u < kQKRows; ++u) {
+      const int h = h0 + u;
+      if (h < HH) {
+        if (h < Hq)
+          norm_rope_apply_bwd<D>(dl[u], xv[u], swq, rr[u], cs, sn, dq + ((size_t)t * Hq + h) * D, aq, lane);
+        else
+          norm_rope_apply_bwd<D>(dl[u], xv[u], swk, rr[u], cs, sn, dk + ((size_t)t * Hk + h - Hq) * D, ak, lane);
+      }
     }
   }
 #pragma unroll
@@ -300,8 +382,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfl
   const int nv = F / 8;
   const long total = rows * nv;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    long r = i / nv;
-    int c = (int)(i % nv);
+    const int r = (int)i / nv, c = (int)i - r * nv;  // rows * nv < 2^31 (host check)
     const bf16x8* g = reinterpret_cast<const bf16x8*>(gu + (size_t)r * 2 * F) + c;
     const bf16x8* u = reinterpret_cast<const bf16x8*>(gu + (size_t)r * 2 * F + F) + c;
     float a[8], b[8];
@@ -318,8 +399,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __
   const int nv = F / 8;
   const long total = rows * nv;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    long r = i / nv;
-    int c = (int)(i % nv);
+    const int r = (int)i / nv, c = (int)i - r * nv;  // rows * nv < 2^31 (host check)
     float a[8], b[8], d[8], da[8], db[8];
     bb::unpack8(reinterpret_cast<const bf16x8*>(gu + (size_t)r * 2 * F)[c], a);
     bb::unpack8(reinterpret_cast<const bf16x8*>(gu + (size_t)r * 2 * F + F)[c], b);
@@ -534,23 +614,88 @@ __global__ void ppo_loss_kernel(const float* __restrict__ x, const float* __rest
 template <typename P>
 __global__ void adamw_kernel(float* __restrict__ master, P* __restrict__ param, const float* __restrict__ grad,
                              float* __restrict__ m, float* __restrict__ v, const float* __restrict__ clip, long n,
-                             float lr, float b1, float b2, float eps, float wd, float bc1, float bc2) {
+                             float lr, float b1, float b2, float eps, float wd, float bc1, float bc2, bool vec) {
   const float c = clip[0];
   const float inv_bc1 = 1.f / bc1, inv_sqrt_bc2 = rsqrtf(bc2);
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    float g = grad[i] * c;
-    float mi = b1 * m[i] + (1.f - b1) * g;
-    float vi = b2 * v[i] + (1.f - b2) * g * g;
+  auto step = [&](float g, float& mi, float& vi, float& w) {
+    g *= c;
+    mi = b1 * mi + (1.f - b1) * g;
+    vi = b2 * vi + (1.f - b2) * g * g;
+    w = w * (1.f - lr * wd) - lr * (mi * inv_bc1) / (sqrtf(vi) * inv_sqrt_bc2 + eps);
+  };
+  // 16-byte vectors when every pointer allows them (decided on the host), then a scalar tail
+  const long n4 = vec ? n / 4 : 0;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const float4 g = reinterpret_cast<const float4*>(grad)[i];
+    float4 mi = reinterpret_cast<float4*>(m)[i], vi = reinterpret_cast<float4*>(v)[i];
+    float4 w = reinterpret_cast<float4*>(master)[i];
+    step(g.x, mi.x, vi.x, w.x);
+    step(g.y, mi.y, vi.y, w.y);
+    step(g.z, mi.z, vi.z, w.z);
+    step(g.w, mi.w, vi.w, w.w);
+    reinterpret_cast<float4*>(m)[i] = mi;
+    reinterpret_cast<float4*>(v)[i] = vi;
+    reinterpret_cast<float4*>(master)[i] = w;
+    if constexpr (std::is_same<P, float>::value) {
+      reinterpret_cast<float4*>(param)[i] = w;
+    } else {
+      uint2 u;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+      h[0] = __floats2bfloat162_rn(w.x, w.y);
+      h[1] = __floats2bfloat162_rn(w.z, w.w);
+      reinterpret_cast<uint2*>(param)[i] = u;
+    }
+  }
+  const long stride = vec ? blockDim.x : (long)gridDim.x * blockDim.x;
+  const long first = vec ? (blockIdx.x == 0 ? n4 * 4 + threadIdx.x : n) : (long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (long i = first; i < n; i += stride) {
+    float mi = m[i], vi = v[i], w = master[i];
+    step(grad[i], mi, vi, w);
     m[i] = mi;
     v[i] = vi;
-    float w = master[i];
-    w = w * (1.f - lr * wd) - lr * (mi * inv_bc1) / (sqrtf(vi) * inv_sqrt_bc2 + eps);
     master[i] = w;
     if constexpr (std::is_same<P, float>::value) {
       param[i] = w;
     } else {
       param[i] = __float2bfloat16(w);
     }
+  }
+}
+
+// Sum of squares of an FP32 vector in one read: per-block partials (float4 loads, FP32 accumulation
+// per thread, fixed-order block reduction), then one block sums the partials in a fixed order, so the
+// result is deterministic.
+__global__ void sumsq_partial_kernel(const float* __restrict__ x, long n, bool vec, float* __restrict__ part) {
+  float acc = 0.f;
+  const long n4 = vec ? n / 4 : 0;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(x)[i];
+    acc += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+  }
+  for (long i = n4 * 4 + (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    acc += x[i] * x[i];
+  __shared__ float sw[32];
+  acc = bb::warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) sw[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sw[threadIdx.x] : 0.f;
+    t = bb::warp_sum(t);
+    if (threadIdx.x == 0) part[blockIdx.x] = t;
+  }
+}
+
+__global__ void sum_partials_kernel(const float* __restrict__ part, int n, float* __restrict__ out, bool accumulate) {
+  __shared__ float sw[32];
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) acc += part[i];
+  acc = bb::warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) sw[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sw[threadIdx.x] : 0.f;
+    t = bb::warp_sum(t);
+    if (threadIdx.x == 0) out[0] = accumulate ? out[0] + t : t;
   }
 }
 
@@ -572,7 +717,31 @@ void check_bf16(const torch::Tensor& t, const char* name) {
 }  // namespace
 
 // ============================================================================================ host
-std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
+// MAXV = ceil(H / 256) 16-byte vectors per lane (10 for H = 2560); H % 8 == 0, H <= 4096.
+#define BB_RMS_DISPATCH(nv, MACRO)                                                 \
+  if (nv <= 32) {                                                                  \
+    MACRO(1);                                                                      \
+  } else if (nv <= 64) {                                                           \
+    MACRO(2);                                                                      \
+  } else if (nv <= 128) {                                                          \
+    MACRO(4);                                                                      \
+  } else if (nv <= 192) {                                                          \
+    MACRO(6);                                                                      \
+  } else if (nv <= 256) {                                                          \
+    MACRO(8);                                                                      \
+  } else if (nv <= 320) {                                                          \
+    MACRO(10);                                                                     \
+  } else if (nv <= 384) {                                                          \
+    MACRO(12);                                                                     \
+  } else if (nv <= 512) {                                                          \
+    MACRO(16);                                                                     \
+  } else {                                                                         \
+    TORCH_CHECK(false, "rmsnorm: hidden size above 4096 is not supported");        \
+  }
+
+namespace {
+std::vector<torch::Tensor> rmsnorm_fwd_impl(torch::Tensor x, c10::optional<torch::Tensor> res, torch::Tensor w,
+                                            double eps) {
   check_bf16(x, "x");
   check_bf16(w, "weight");
   const int H = x.size(-1);
@@ -580,59 +749,90 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   const long rows = x.numel() / H;
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({rows}, x.options().dtype(at::kFloat));
-  if (rows == 0) return {y, rstd};
+  torch::Tensor h;
+  if (res) {
+    check_bf16(*res, "residual");
+    TORCH_CHECK(res->sizes() == x.sizes(), "rmsnorm: residual shape must match x");
+    h = torch::empty_like(x);
+  }
+  if (rows == 0) return res ? std::vector<torch::Tensor>{y, rstd, h} : std::vector<torch::Tensor>{y, rstd};
   const int threads = 256;
-  int blocks = (int)std::min<long>((rows + 7) / 8, (long)sm_count() * 8);
-  rmsnorm_fwd_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
-      rstd.data_ptr<float>(), rows, H, (float)eps);
+  const int nv = H / 8;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const __nv_bfloat16* rp = res ? (const __nv_bfloat16*)res->data_ptr() : nullptr;
+  __nv_bfloat16* hp = res ? (__nv_bfloat16*)h.data_ptr() : nullptr;
+#define BB_RMS_FWD(MV)                                                                                        \
+  const int blocks = res ? bb::resident_grid(rmsnorm_fwd_kernel<MV, true>, threads, 0, (rows + 7) / 8)         \
+                         : bb::resident_grid(rmsnorm_fwd_kernel<MV, false>, threads, 0, (rows + 7) / 8);       \
+  if (res)                                                                                                    \
+    rmsnorm_fwd_kernel<MV, true><<<blocks, threads, 0, stream>>>(                                             \
+        (const __nv_bfloat16*)x.data_ptr(), rp, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(), \
+        hp, rstd.data_ptr<float>(), rows, H, (float)eps);                                                     \
+  else                                                                                                        \
+    rmsnorm_fwd_kernel<MV, false><<<blocks, threads, 0, stream>>>(                                            \
+        (const __nv_bfloat16*)x.data_ptr(), nullptr, (const __nv_bfloat16*)w.data_ptr(),                      \
+        (__nv_bfloat16*)y.data_ptr(), nullptr, rstd.data_ptr<float>(), rows, H, (float)eps)
+  BB_RMS_DISPATCH(nv, BB_RMS_FWD)
+#undef BB_RMS_FWD
   BB_POST_LAUNCH();
-  return {y, rstd};
+  return res ? std::vector<torch::Tensor>{y, rstd, h} : std::vector<torch::Tensor>{y, rstd};
 }
 
-std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd) {
+std::vector<torch::Tensor> rmsnorm_bwd_impl(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
+                                            c10::optional<torch::Tensor> dres) {
   check_bf16(dy, "dy");
   check_bf16(x, "x");
   const int H = x.size(-1);
   const long rows = x.numel() / H;
   auto dx = torch::empty_like(x);
   auto dw = torch::zeros({H}, x.options().dtype(at::kFloat));
+  if (dres) {
+    check_bf16(*dres, "dres");
+    TORCH_CHECK(dres->sizes() == x.sizes(), "rmsnorm_bwd: residual gradient shape must match x");
+  }
   if (rows == 0) return {dx, dw};
   const int threads = 256;
-  // per-lane register footprint follows ceil(H / 256) vectors exactly (10 for H = 2560), so
-  // several blocks fit per SM
-  int blocks = (int)std::min<long>((rows + 7) / 8, (long)sm_count() * 4);
-  auto part = torch::empty({blocks, H}, x.options().dtype(at::kFloat));
   auto stream = at::cuda::getCurrentCUDAStream();
   const int nv = H / 8;
-  size_t smem = H * sizeof(float);
+  const size_t smem = (1 + threads / 32) * (size_t)H * sizeof(float);
+  const __nv_bfloat16* dp = dres ? (const __nv_bfloat16*)dres->data_ptr() : nullptr;
 #define BB_RMS_BWD(MV)                                                                                        \
-  rmsnorm_bwd_kernel<MV><<<blocks, threads, smem, stream>>>(                                                  \
-      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), \
-      rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), rows, H)
-  if (nv <= 32) {
-    BB_RMS_BWD(1);
-  } else if (nv <= 64) {
-    BB_RMS_BWD(2);
-  } else if (nv <= 128) {
-    BB_RMS_BWD(4);
-  } else if (nv <= 192) {
-    BB_RMS_BWD(6);
-  } else if (nv <= 256) {
-    BB_RMS_BWD(8);
-  } else if (nv <= 320) {
-    BB_RMS_BWD(10);
-  } else if (nv <= 384) {
-    BB_RMS_BWD(12);
-  } else {
-    TORCH_CHECK(nv <= 512, "rmsnorm_bwd: hidden size too large");
-    BB_RMS_BWD(16);
-  }
+  cudaFuncSetAttribute(rmsnorm_bwd_kernel<MV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);  \
+  cudaFuncSetAttribute(rmsnorm_bwd_kernel<MV, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+  const int blocks = dres ? bb::resident_grid(rmsnorm_bwd_kernel<MV, true>, threads, smem, (rows + 7) / 8)    \
+                          : bb::resident_grid(rmsnorm_bwd_kernel<MV, false>, threads, smem, (rows + 7) / 8);  \
+  if (dres)                                                                                                   \
+    rmsnorm_bwd_kernel<MV, true><<<blocks, threads, smem, stream>>>(                                          \
+        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), \
+        rstd.data_ptr<float>(), dp, (__nv_bfloat16*)dx.data_ptr(), dw.data_ptr<float>(), rows, H);           \
+  else                                                                                                        \
+    rmsnorm_bwd_kernel<MV, false><<<blocks, threads, smem, stream>>>(                                         \
+        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), \
+        rstd.data_ptr<float>(), nullptr, (__nv_bfloat16*)dx.data_ptr(), dw.data_ptr<float>(), rows, H)
+  BB_RMS_DISPATCH(nv, BB_RMS_BWD)
 #undef BB_RMS_BWD
   BB_POST_LAUNCH();
-  column_sum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(part.data_ptr<float>(), dw.data_ptr<float>(), blocks, H);
-  BB_POST_LAUNCH();
   return {dx, dw};
+}
+}  // namespace
+
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
+  return rmsnorm_fwd_impl(x, c10::nullopt, w, eps);
+}
+
+std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd) {
+  return rmsnorm_bwd_impl(dy, x, w, rstd, c10::nullopt);
+}
+
+// h = x + res; y = RMSNorm(h) * w  ->  {y, rstd, h}
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, torch::Tensor w, double eps) {
+  return rmsnorm_fwd_impl(x, res, w, eps);
+}
+
+// d(x) = d(res) = rmsnorm_bwd(dy) + dh  ->  {dsum, dw}
+std::vector<torch::Tensor> add_rmsnorm_bwd(torch::Tensor dy, torch::Tensor h, torch::Tensor w, torch::Tensor rstd,
+                                           torch::Tensor dh) {
+  return rmsnorm_bwd_impl(dy, h, w, rstd, dh);
 }
 
 // q [T, Hq, D], k [T, Hk, D] may be strided views (e.g. column slices of a fused QKV output): the
@@ -656,11 +856,12 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor q, torch::Tensor k, to
   auto rk = torch::empty({T, Hk}, q.options().dtype(at::kFloat));
   if (T == 0) return {qo, ko, rq, rk};
   const int threads = 256;
-  long items = (long)T * (Hq + Hk);
-  int blocks = (int)std::min<long>((items + 7) / 8, (long)sm_count() * 8);
+  const long items = (long)T * ((Hq + Hk + kQKRows - 1) / kQKRows);
+  TORCH_CHECK(items < (1l << 31), "qk_norm_rope: too many rows");
   auto stream = at::cuda::getCurrentCUDAStream();
   auto qwb = qw.contiguous(), kwb = kw.contiguous();
 #define BB_QKF(DD)                                                                                               \
+  const int blocks = bb::resident_grid(qk_norm_rope_fwd_kernel<DD>, threads, 0, (items + 7) / 8);                 \
   qk_norm_rope_fwd_kernel<DD><<<blocks, threads, 0, stream>>>(                                                   \
       (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)qwb.data_ptr(), \
       (const __nv_bfloat16*)kwb.data_ptr(), cosb.data_ptr<float>(), sinb.data_ptr<float>(),                      \
@@ -693,11 +894,12 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko
   auto dkw = torch::zeros({D}, q.options().dtype(at::kFloat));
   if (T == 0) return {dq, dk, dqw, dkw};
   const int threads = 256;
-  long items = (long)T * (Hq + Hk);
-  int blocks = (int)std::min<long>((items + 7) / 8, (long)sm_count() * 4);
+  const long items = (long)T * ((Hq + Hk + kQKRows - 1) / kQKRows);
+  TORCH_CHECK(items < (1l << 31), "qk_norm_rope: too many rows");
   auto stream = at::cuda::getCurrentCUDAStream();
   auto qwb = qw.contiguous(), kwb = kw.contiguous();
 #define BB_QKB(DD)                                                                                               \
+  const int blocks = bb::resident_grid(qk_norm_rope_bwd_kernel<DD>, threads, 0, (items + 7) / 8);                 \
   qk_norm_rope_bwd_kernel<DD><<<blocks, threads, 0, stream>>>(                                                   \
       (const __nv_bfloat16*)dqo.data_ptr(), (const __nv_bfloat16*)dko.data_ptr(), (const __nv_bfloat16*)q.data_ptr(), \
       (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)qwb.data_ptr(), (const __nv_bfloat16*)kwb.data_ptr(), \
@@ -729,6 +931,7 @@ torch::Tensor swiglu_fwd(torch::Tensor gu) {
   auto y = torch::empty(sizes, gu.options());
   if (rows == 0) return y;
   long total = rows * (F / 8);
+  TORCH_CHECK(total < (1l << 31), "swiglu: too many elements");
   int blocks = (int)std::min<long>((total + 255) / 256, (long)sm_count() * 16);
   swiglu_fwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)y.data_ptr(), rows, F);
@@ -744,6 +947,7 @@ torch::Tensor swiglu_bwd(torch::Tensor dy, torch::Tensor gu) {
   auto dgu = torch::empty_like(gu);
   if (rows == 0) return dgu;
   long total = rows * (F / 8);
+  TORCH_CHECK(total < (1l << 31), "swiglu: too many elements");
   int blocks = (int)std::min<long>((total + 255) / 256, (long)sm_count() * 16);
   swiglu_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)dgu.data_ptr(), rows,
@@ -813,20 +1017,39 @@ void adamw_step(torch::Tensor master, torch::Tensor param, torch::Tensor grad, t
   const long n = master.numel();
   if (!n) return;
   auto clipf = clip.to(at::kFloat).contiguous();
-  int blocks = (int)std::min<long>((n + 255) / 256, (long)sm_count() * 16);
   auto stream = at::cuda::getCurrentCUDAStream();
+  auto al = [](const torch::Tensor& t, uintptr_t a) { return (reinterpret_cast<uintptr_t>(t.data_ptr()) % a) == 0; };
+  const bool vec = al(master, 16) && al(grad, 16) && al(m, 16) && al(v, 16) &&
+                   al(param, param.scalar_type() == at::kBFloat16 ? 8 : 16);
+  const long work = vec ? (n + 3) / 4 : n;
+  int blocks = (int)std::min<long>((work + 255) / 256, (long)sm_count() * 8);
   if (param.scalar_type() == at::kBFloat16) {
     adamw_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
         master.data_ptr<float>(), (__nv_bfloat16*)param.data_ptr(), grad.data_ptr<float>(), m.data_ptr<float>(),
         v.data_ptr<float>(), clipf.data_ptr<float>(), n, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
-        (float)bc1, (float)bc2);
+        (float)bc1, (float)bc2, vec);
   } else {
     adamw_kernel<float><<<blocks, 256, 0, stream>>>(
         master.data_ptr<float>(), param.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(),
         v.data_ptr<float>(), clipf.data_ptr<float>(), n, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
-        (float)bc1, (float)bc2);
+        (float)bc1, (float)bc2, vec);
   }
   BB_POST_LAUNCH();
 }
 
 int64_t bb_launch_count() { return (int64_t)bb::launch_counter().load(); }
+
+// out[0] (+)= sum(x^2) over an FP32 tensor (deterministic; no host sync)
+void sumsq_into(torch::Tensor x, torch::Tensor out, bool accumulate) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous(), "sumsq: contiguous CUDA fp32");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.numel() >= 1, "sumsq: fp32 output");
+  const long n = x.numel();
+  const bool vec = (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) == 0;
+  const int blocks = (int)std::max<long>(1, std::min<long>(((vec ? n / 4 : n) + 255) / 256, (long)sm_count() * 8));
+  auto part = torch::empty({blocks}, x.options());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  sumsq_partial_kernel<<<blocks, 256, 0, stream>>>(x.data_ptr<float>(), n, vec, part.data_ptr<float>());
+  BB_POST_LAUNCH();
+  sum_partials_kernel<<<1, 1024, 0, stream>>>(part.data_ptr<float>(), blocks, out.data_ptr<float>(), accumulate);
+  BB_POST_LAUNCH();
+}

@@ -19,7 +19,11 @@ namespace {
 struct RowMap {
   long st;
   int H;
-  __device__ __forceinline__ long off(long r, int D) const { return (r / H) * st + (long)(r % H) * D; }
+  // rows < 2^31 (checked on the host): 32-bit division
+  __device__ __forceinline__ long off(long r, int D) const {
+    const int ri = (int)r, t = ri / H;
+    return (long)t * st + (long)(ri - t * H) * D;
+  }
 };
 
 template <int E>
@@ -138,9 +142,8 @@ __global__ void gdn_gates_fwd_kernel(const __nv_bfloat16* __restrict__ a, long l
                                      float* __restrict__ g, float* __restrict__ beta, long T, int H) {
   const long n = T * H;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long t = i / H;
-    const int h = (int)(i % H);
-    const float av = __bfloat162float(a[t * lda + h]), bv = __bfloat162float(b[t * ldb + h]);
+    const int t = (int)i / H, h = (int)i - t * H;  // n < 2^31 (host check)
+    const float av = __bfloat162float(a[(long)t * lda + h]), bv = __bfloat162float(b[(long)t * ldb + h]);
     g[i] = -__expf(A_log[h]) * softplus_f(av + dt[h]);
     beta[i] = bb::sigmoidf_(bv);
   }
@@ -156,9 +159,8 @@ __global__ void gdn_gates_bwd_kernel(const float* __restrict__ dg, const float* 
   __syncthreads();
   const long n = T * H;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long t = i / H;
-    const int h = (int)(i % H);
-    const float av = __bfloat162float(a[t * lda + h]), bv = __bfloat162float(b[t * ldb + h]);
+    const int t = (int)i / H, h = (int)i - t * H;  // n < 2^31 (host check)
+    const float av = __bfloat162float(a[(long)t * lda + h]), bv = __bfloat162float(b[(long)t * ldb + h]);
     const float x = av + dt[h], e = __expf(A_log[h]);
     const float sp = softplus_f(x), sg = bb::sigmoidf_(x);
     const float d = dg[i];
@@ -176,13 +178,6 @@ __global__ void gdn_gates_bwd_kernel(const float* __restrict__ dg, const float* 
   }
 }
 
-int blocks_for(long work) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return (int)std::max<long>(1, std::min<long>((work + 255) / 256, (long)sms * 8));
-}
-
 void check_rows(const torch::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), name, ": contiguous CUDA bf16");
 }
@@ -192,17 +187,24 @@ RowMap row_map(const torch::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 3, name, ": CUDA bf16 [T, H, D]");
   const long D = t.size(2), H = t.size(1);
   TORCH_CHECK(t.stride(2) == 1 && (H == 1 || t.stride(1) == D), name, ": heads must be contiguous rows");
+  TORCH_CHECK(t.size(0) * H < (1l << 31), name, ": too many rows");
   return RowMap{t.size(0) > 1 ? t.stride(0) : H * D, (int)H};
 }
 
 }  // namespace
 
-#define BB_ROWS_DISPATCH(D, MACRO)                                      \
-  if (D == 32) MACRO(1);                                                \
-  else if (D == 64) MACRO(2);                                           \
-  else if (D == 128) MACRO(4);                                          \
-  else if (D == 256) MACRO(8);                                          \
-  else TORCH_CHECK(false, "GDN element-wise kernels: row width must be 32, 64, 128 or 256");
+#define BB_ROWS_DISPATCH(D, MACRO)                                                        \
+  if (D == 32) {                                                                          \
+    MACRO(1);                                                                             \
+  } else if (D == 64) {                                                                   \
+    MACRO(2);                                                                             \
+  } else if (D == 128) {                                                                  \
+    MACRO(4);                                                                             \
+  } else if (D == 256) {                                                                  \
+    MACRO(8);                                                                             \
+  } else {                                                                                \
+    TORCH_CHECK(false, "GDN element-wise kernels: row width must be 32, 64, 128 or 256"); \
+  }
 
 // o: contiguous [T, H, D]; z: [T, H, D] view with contiguous heads
 std::vector<torch::Tensor> gated_rmsnorm_fwd(torch::Tensor o, torch::Tensor z, torch::Tensor w, double eps) {
@@ -216,8 +218,8 @@ std::vector<torch::Tensor> gated_rmsnorm_fwd(torch::Tensor o, torch::Tensor z, t
   if (rows == 0) return {y, rstd};
   auto wb = w.to(at::kBFloat16).contiguous();
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int blocks = blocks_for(rows * 32);
 #define BB_GRF(E)                                                                                       \
+  const int blocks = bb::resident_grid(gated_rmsnorm_fwd_kernel<E>, 256, 0, (rows + 7) / 8);                            \
   gated_rmsnorm_fwd_kernel<E><<<blocks, 256, 0, stream>>>(                                              \
       (const __nv_bfloat16*)o.data_ptr(), (const __nv_bfloat16*)z.data_ptr(), zm,                       \
       (const __nv_bfloat16*)wb.data_ptr(), (__nv_bfloat16*)y.data_ptr(), rstd.data_ptr<float>(), rows, \
@@ -240,8 +242,8 @@ std::vector<torch::Tensor> gated_rmsnorm_bwd(torch::Tensor dy, torch::Tensor o, 
   if (rows == 0) return {d_o, dz, dw};
   auto wb = w.to(at::kBFloat16).contiguous();
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int blocks = blocks_for(rows * 32);
 #define BB_GRB(E)                                                                                           \
+  const int blocks = bb::resident_grid(gated_rmsnorm_bwd_kernel<E>, 256, 0, (rows + 7) / 8);                            \
   gated_rmsnorm_bwd_kernel<E><<<blocks, 256, 0, stream>>>(                                                  \
       (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)o.data_ptr(),                              \
       (const __nv_bfloat16*)z.data_ptr(), zm, (const __nv_bfloat16*)wb.data_ptr(), rstd.data_ptr<float>(), \
@@ -261,8 +263,8 @@ std::vector<torch::Tensor> l2norm_fwd(torch::Tensor x, double eps) {
   auto rn = torch::empty({rows}, x.options().dtype(at::kFloat));
   if (rows == 0) return {y, rn};
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int blocks = blocks_for(rows * 32);
 #define BB_L2F(E)                                                                                          \
+  const int blocks = bb::resident_grid(l2norm_fwd_kernel<E>, 256, 0, (rows + 7) / 8);                            \
   l2norm_fwd_kernel<E><<<blocks, 256, 0, stream>>>((const __nv_bfloat16*)x.data_ptr(), xm,                 \
                                                    (__nv_bfloat16*)y.data_ptr(), rn.data_ptr<float>(), rows, \
                                                    (float)eps)
@@ -280,8 +282,8 @@ torch::Tensor l2norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor rn) {
   auto dx = torch::empty(x.sizes(), x.options());
   if (rows == 0) return dx;
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int blocks = blocks_for(rows * 32);
 #define BB_L2B(E)                                                                                             \
+  const int blocks = bb::resident_grid(l2norm_bwd_kernel<E>, 256, 0, (rows + 7) / 8);                            \
   l2norm_bwd_kernel<E><<<blocks, 256, 0, stream>>>((const __nv_bfloat16*)dy.data_ptr(),                        \
                                                    (const __nv_bfloat16*)x.data_ptr(), xm, rn.data_ptr<float>(), \
                                                    (__nv_bfloat16*)dx.data_ptr(), rows)
@@ -298,11 +300,13 @@ std::vector<torch::Tensor> gdn_gates_fwd(torch::Tensor a, torch::Tensor b, torch
               "gdn_gates: a, b must be bf16 [T, H] with contiguous columns");
   const long T = a.size(0);
   const int H = a.size(1);
+  TORCH_CHECK(T * H < (1l << 31), "gdn_gates: too many elements");
   auto g = torch::empty({T, H}, a.options().dtype(at::kFloat));
   auto beta = torch::empty({T, H}, a.options().dtype(at::kFloat));
   if (T == 0) return {g, beta};
   auto Af = A_log.to(at::kFloat).contiguous(), dtf = dt.to(at::kFloat).contiguous();
-  gdn_gates_fwd_kernel<<<blocks_for(T * H), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  const int blocks = bb::resident_grid(gdn_gates_fwd_kernel, 256, 0, (T * H + 255) / 256);
+  gdn_gates_fwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)a.data_ptr(), a.stride(0), (const __nv_bfloat16*)b.data_ptr(), b.stride(0),
       Af.data_ptr<float>(), dtf.data_ptr<float>(), g.data_ptr<float>(), beta.data_ptr<float>(), T, H);
   BB_POST_LAUNCH();
@@ -313,6 +317,7 @@ std::vector<torch::Tensor> gdn_gates_bwd(torch::Tensor dg, torch::Tensor dbeta, 
                                          torch::Tensor A_log, torch::Tensor dt) {
   const long T = a.size(0);
   const int H = a.size(1);
+  TORCH_CHECK(T * H < (1l << 31), "gdn_gates: too many elements");
   auto da = torch::empty({T, H}, a.options());
   auto db = torch::empty({T, H}, a.options());
   auto dA = torch::zeros({H}, a.options().dtype(at::kFloat));
@@ -320,7 +325,9 @@ std::vector<torch::Tensor> gdn_gates_bwd(torch::Tensor dg, torch::Tensor dbeta, 
   if (T == 0) return {da, db, dA, ddt};
   auto Af = A_log.to(at::kFloat).contiguous(), dtf = dt.to(at::kFloat).contiguous();
   auto dgc = dg.to(at::kFloat).contiguous(), dbc = dbeta.to(at::kFloat).contiguous();
-  gdn_gates_bwd_kernel<<<blocks_for(T * H), 256, 2 * H * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
+  const size_t smem = 2 * H * sizeof(float);
+  const int blocks = bb::resident_grid(gdn_gates_bwd_kernel, 256, smem, (T * H + 255) / 256);
+  gdn_gates_bwd_kernel<<<blocks, 256, smem, at::cuda::getCurrentCUDAStream()>>>(
       dgc.data_ptr<float>(), dbc.data_ptr<float>(), (const __nv_bfloat16*)a.data_ptr(), a.stride(0),
       (const __nv_bfloat16*)b.data_ptr(), b.stride(0), Af.data_ptr<float>(), dtf.data_ptr<float>(),
       (__nv_bfloat16*)da.data_ptr(), (__nv_bfloat16*)db.data_ptr(), dA.data_ptr<float>(), ddt.data_ptr<float>(), T, H);

@@ -92,7 +92,13 @@ class MixedPrecisionAdamW:
         return [a.main_grad for a in self.arenas]
 
     def grad_norm(self) -> Tensor:
-        sq = [a.main_grad.float().pow(2).sum() for a in self.arenas]
+        grads = [a.main_grad for a in self.arenas]
+        if grads and all(on_gpu(g) and g.dtype == torch.float32 and g.is_contiguous() for g in grads):
+            acc = torch.zeros(1, dtype=torch.float32, device=grads[0].device)
+            for i, g in enumerate(grads):     # one read of each FP32 arena, no squared copy
+                kernels().sumsq_into(g, acc, i > 0)
+            return torch.sqrt(acc[0])
+        sq = [g.float().pow(2).sum() for g in grads]
         return torch.sqrt(torch.stack(sq).sum())
 
     def step(self, *, grad_norm: Tensor | None = None) -> Tensor:

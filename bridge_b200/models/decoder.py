@@ -15,6 +15,7 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
+from ..ops.norm import add_rmsnorm
 from ..parallel.tp import VocabParallelEmbedding, copy_to_tp, gather_from_sp, tp_rank, tp_size
 from .config import ModelConfig
 from .layers import DecoderLayer, RMSNorm, RotaryEmbedding
@@ -77,9 +78,10 @@ class DecoderModel(nn.Module):
             if x.shape[0] % n:
                 raise ValueError("sequence-parallel segments must be divisible by the TP size")
             x = x.chunk(n)[r]
+        pending = None      # each block's MLP output is added inside the next block's first norm
         for layer in self.layers:
-            x = layer(x, rope)
-        x = self.norm(x)
+            x, pending = layer(x, rope, pending, True)
+        x = self.norm(x) if pending is None else add_rmsnorm(x, pending, self.norm.weight, self.norm.eps)[1]
         if self.sequence_parallel:
             x = gather_from_sp(x, self.tp_group)
         return x

@@ -23,7 +23,7 @@ from torch import Tensor
 from ..ops.activation import swiglu
 from ..ops.attention import tree_attention
 from ..ops.gdn import causal_conv1d, chunk_gated_delta_rule, gated_rmsnorm, gdn_gates, l2norm
-from ..ops.norm import qk_norm_rope, rmsnorm, rope_cos_sin
+from ..ops.norm import add_rmsnorm, qk_norm_rope, rmsnorm, rope_cos_sin
 from ..parallel.tp import ColumnParallelLinear, RowParallelLinear, tp_size, scaled_init_std
 from ..tpr.context import get_tpr_attention_context, _single_layout
 from .config import ModelConfig
@@ -244,6 +244,18 @@ class DecoderLayer(nn.Module):
                                  sequence_parallel=sequence_parallel, std=cfg.init_std,
                                  out_std=scaled_init_std(cfg.init_std, cfg.num_layers), device=device)
 
-    def forward(self, x: Tensor, rope) -> Tensor:
-        x = x + self.self_attention(self.input_layernorm(x), rope)
-        return x + self.mlp(self.post_attention_layernorm(x))
+    def forward(self, x: Tensor, rope, pending: Tensor | None = None, defer_residual: bool = False):
+        """Pre-norm block ``x + attn(norm1(x))`` then ``+ mlp(norm2(.))``.
+
+        Each residual add is fused into the RMSNorm that reads its result.  With ``pending`` (the
+        previous block's MLP output, not yet added) the block computes ``x + pending`` inside its
+        first norm; with ``defer_residual`` it returns ``(h, mlp_out)`` and leaves the last add to
+        the next block (or the final norm) instead of returning ``h + mlp_out``."""
+        ln1, ln2 = self.input_layernorm, self.post_attention_layernorm
+        if pending is None:
+            y = ln1(x)
+        else:
+            x, y = add_rmsnorm(x, pending, ln1.weight, ln1.eps)
+        h, y = add_rmsnorm(x, self.self_attention(y, rope), ln2.weight, ln2.eps)
+        out = self.mlp(y)
+        return (h, out) if defer_residual else h + out

@@ -48,6 +48,44 @@ def rmsnorm(x: Tensor, weight: Tensor, eps: float = 1e-6) -> Tensor:
     return rmsnorm_reference(x, weight, eps)
 
 
+class _AddRMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, res, weight, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        r2 = res.reshape(x2.shape).contiguous()
+        y, rstd, h = kernels().add_rmsnorm_fwd(x2, r2, weight.contiguous(), float(eps))
+        ctx.save_for_backward(h, weight, rstd)
+        ctx.shape = shape
+        return h.view(shape), y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dh, dy):
+        h, weight, rstd = ctx.saved_tensors
+        m = kernels()
+        if dy is None:
+            return dh, dh, None, None
+        dy2 = dy.reshape(h.shape).contiguous()
+        if dh is None:
+            d, dw = m.rmsnorm_bwd(dy2, h, weight.contiguous(), rstd)
+        else:
+            d, dw = m.add_rmsnorm_bwd(dy2, h, weight.contiguous(), rstd, dh.reshape(h.shape).contiguous())
+        d = d.view(ctx.shape)
+        return d, d, dw.to(weight.dtype), None
+
+
+def add_rmsnorm(x: Tensor, res: Tensor, weight: Tensor, eps: float = 1e-6) -> tuple[Tensor, Tensor]:
+    """Residual add fused with the RMSNorm that follows it: ``h = x + res``, ``y = RMSNorm(h) * w``.
+
+    Returns ``(h, y)``.  ``h`` is rounded to the activation dtype before it is normalised, exactly as
+    a separate add would; the backward returns ``RMSNorm'(dy) + dh`` for both ``x`` and ``res`` in one
+    pass (the residual-gradient add is folded into the norm backward)."""
+    if on_gpu(x) and x.dtype == torch.bfloat16 and res.dtype == torch.bfloat16:
+        return _AddRMSNormFn.apply(x, res, weight, eps)
+    h = x + res
+    return h, rmsnorm_reference(h, weight, eps)
+
+
 # --------------------------------------------------------------------------- RoPE
 def rope_cos_sin(positions: Tensor, head_dim: int, theta: float) -> tuple[Tensor, Tensor]:
     """FP32 ``cos, sin [T, head_dim/2]`` for integer positions."""

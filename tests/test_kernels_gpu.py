@@ -41,6 +41,29 @@ def test_rmsnorm(rows, H):
     _close(w.grad, wr.grad, 1e-1, 2e-2, "dw")
 
 
+@pytest.mark.parametrize("rows,H", [(1000, 2560), (333, 64), (97, 4096), (50, 1000)])
+def test_add_rmsnorm(rows, H):
+    """Residual add fused into RMSNorm: h, y and the shared gradient of both addends vs FP32."""
+    from bridge_b200.ops.norm import add_rmsnorm, rmsnorm_reference
+
+    torch.manual_seed(rows + H)
+    x = torch.randn(rows, H, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    r = torch.randn(rows, H, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16).requires_grad_()
+    h, y = add_rmsnorm(x, r, w, 1e-6)
+    xr, rr, wr = (t.detach().float().requires_grad_() for t in (x, r, w))
+    hr = xr + rr
+    yr = rmsnorm_reference(hr, wr, 1e-6)
+    _close(h, hr, 2e-2, 1e-2, "h")
+    _close(y, yr, 2e-2, 1e-2, "y")
+    gh, gy = torch.randn_like(hr), torch.randn_like(yr)
+    ((h.float() * gh).sum() + (y.float() * gy).sum()).backward()
+    ((hr * gh).sum() + (yr * gy).sum()).backward()
+    _close(x.grad, xr.grad, 3e-2, 2e-2, "dx")
+    _close(r.grad, rr.grad, 3e-2, 2e-2, "dres")
+    _close(w.grad, wr.grad, 1e-1, 2e-2, "dw")
+
+
 @pytest.mark.parametrize("D", [64, 128, 256])
 @pytest.mark.parametrize("fused_view", [False, True])
 def test_qk_norm_rope(D, fused_view):
@@ -129,15 +152,18 @@ def test_ppo_loss():
     _close(x.grad, xr.grad, 1e-6, 1e-4, "dx")
 
 
-def test_adamw_kernel():
+@pytest.mark.parametrize("off", [0, 1])
+def test_adamw_kernel(off):
+    """16-byte vector path with a scalar tail (off = 0) and the scalar path for unaligned views (off = 1)."""
     from bridge_b200.ops._ext import kernels
 
     n = 10001
-    master = torch.randn(n, device=DEV)
-    param = master.to(torch.bfloat16)
-    grad = torch.randn(n, device=DEV)
-    m = torch.randn(n, device=DEV).abs() * 0.1
-    v = torch.rand(n, device=DEV) * 0.01
+    master = torch.randn(n + off, device=DEV)[off:]
+    param = torch.empty(n + off, device=DEV, dtype=torch.bfloat16)[off:]
+    param.copy_(master)
+    grad = torch.randn(n + off, device=DEV)[off:]
+    m = torch.randn(n + off, device=DEV)[off:].abs() * 0.1
+    v = torch.rand(n + off, device=DEV)[off:] * 0.01
     ref = [t.clone() for t in (master, m, v)]
     clip = torch.tensor([0.5], device=DEV)
     kernels().adamw_step(master, param, grad, m, v, clip, 1e-3, 0.9, 0.999, 1e-8, 0.01, 0.19, 0.002)
@@ -259,3 +285,16 @@ def test_tree_attention_sm100_backward(lens, spans, P, hq, hkv):
     if P:
         _close(dpk, ref[3].grad, 1e-2, 3e-2, "dpk")
         _close(dpv, ref[4].grad, 1e-2, 3e-2, "dpv")
+
+
+@pytest.mark.parametrize("n", [1, 1003, 4 * 1000 + 3, 1 << 22])
+def test_sumsq_into(n):
+    from bridge_b200.ops._ext import kernels
+
+    x = torch.randn(n + 1, device=DEV)[1:] if n % 2 else torch.randn(n, device=DEV)   # odd n: unaligned start
+    out = torch.full((1,), 5.0, device=DEV)
+    kernels().sumsq_into(x, out, False)
+    ref = (x.double() ** 2).sum()
+    assert abs(out.item() - ref.item()) <= 1e-5 * ref.item() + 1e-6
+    kernels().sumsq_into(x, out, True)
+    assert abs(out.item() - 2 * ref.item()) <= 2e-5 * ref.item() + 1e-6

@@ -85,14 +85,25 @@ def test_hybrid_tpr_vs_flat_bf16(preset, head_dim):
         assert _cos(a, b) > 0.99
         return
     assert abs(out["loss"][0] - float(loss_ref)) <= 1e-3 * scale
+    # Per-head scalars (A_log, dt_bias: a handful of values, each a long cancelling token sum) carry
+    # far more bf16 noise than the matrices, in the flat path as much as in TPR.  They are judged
+    # against an FP32 CPU run of the same weights: TPR may not be much noisier than the flat path.
+    small = {n for n, p in eng.model.named_parameters() if p.numel() < 64 and gr[n] is not None}
+    if small:
+        ref32 = build_model(cfg, device="cpu", seed=0, dtype=torch.float32)
+        ref32.load_state_dict({k: v.detach().float().cpu() for k, v in ref.state_dict().items()})
+        loss32, _ = flat_ppo_loss(ref32, batch)
+        loss32.backward()
+        g32 = {n: p.grad for n, p in ref32.named_parameters()}
     for n, p in eng.model.named_parameters():
         b = gr[n]
         if b is None:
             continue
         a = p.main_grad.float()
+        if n in small:
+            e_tpr = float((a.cpu() - g32[n]).norm())
+            e_flat = float((b.float().cpu() - g32[n]).norm())
+            assert e_tpr <= 2 * e_flat + 0.05 * float(g32[n].norm()), (n, e_tpr, e_flat)
+            continue
         rel = float((a - b.float()).norm() / (b.float().norm() + 1e-12))
-        # per-head scalars (A_log, dt_bias: a handful of values, each a long cancelling token sum) carry
-        # more bf16 noise than the matrices
-        # (the kernel itself shows no bias: tests/test_gdn_gpu.py checks per-head sums of dg)
-        small = p.numel() < 64
-        assert rel < (0.35 if small else 5e-2) and _cos(a, b) > (0.95 if small else 0.998), (n, rel)
+        assert rel < 5e-2 and _cos(a, b) > 0.998, (n, rel)
