@@ -57,6 +57,9 @@ class EngineConfig:
     # MoE expert-parallel dispatch / combine: "auto" (NVLink P2P gathers on a single-node CUDA group,
     # NCCL all-to-all otherwise), "nvlink" or "nccl"
     ep_comm: str = "auto"
+    # Gated DeltaNet under CP: "head" (head-parallel exchange, head-local state) or "sequence"
+    # (sequence-sharded: per-piece affine state maps exchanged, no token activations moved)
+    gdn_cp_mode: str = "head"
     extra: dict = field(default_factory=dict)
 
     def with_env(self) -> "EngineConfig":
@@ -86,6 +89,8 @@ class EngineConfig:
             kw["tp_comm"] = os.environ["TPR_TP_COMM"]
         if "TPR_DP_COMM" in os.environ:
             kw["dp_comm"] = os.environ["TPR_DP_COMM"]
+        if "TPR_GDN_CP_MODE" in os.environ:
+            kw["gdn_cp_mode"] = os.environ["TPR_GDN_CP_MODE"]
         cfg = replace(self, **kw) if kw else self
         if cfg.tree_policy not in ("exact", "qwen_turn"):
             raise ValueError(f"unknown TPR tree_policy: {cfg.tree_policy!r}")
@@ -97,6 +102,8 @@ class EngineConfig:
             raise ValueError(f"unknown tp_comm: {cfg.tp_comm!r}")
         if cfg.dp_comm not in ("auto", "nvlink", "nccl"):
             raise ValueError(f"unknown dp_comm: {cfg.dp_comm!r}")
+        if cfg.gdn_cp_mode not in ("head", "sequence"):
+            raise ValueError(f"unknown gdn_cp_mode: {cfg.gdn_cp_mode!r}")
         if cfg.log_prob_chunk_tokens < 0:
             raise ValueError("TPR_PPO_LOGPROB_CHUNK_TOKENS must be nonnegative")
         if cfg.turn_min_segment_tokens < 1:

@@ -57,11 +57,13 @@ class TPREngine:
                                                                ec.expert_model_parallel_size)
         from ..parallel.cp_p2p import set_cp_comm_mode
         from ..parallel.ep_p2p import set_ep_comm_mode
+        from ..parallel.gdn_state import set_gdn_cp_mode
         from ..parallel.tp_fused import set_tp_comm_mode
 
         set_tp_comm_mode(ec.tp_comm)
         set_cp_comm_mode(ec.cp_comm)
         set_ep_comm_mode(ec.ep_comm)
+        set_gdn_cp_mode(ec.gdn_cp_mode)
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)

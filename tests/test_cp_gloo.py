@@ -7,7 +7,7 @@ import torch
 from tests.dist_utils import run_ranks
 
 
-def _worker(rank, world, backend, n_layers, preset="tiny", prefix=128, resp=64):
+def _worker(rank, world, backend, n_layers, preset="tiny", prefix=128, resp=64, gdn_cp_mode="head"):
     import torch
 
     from bridge_b200.engine import EngineConfig, TPREngine
@@ -24,7 +24,7 @@ def _worker(rank, world, backend, n_layers, preset="tiny", prefix=128, resp=64):
     loss_ref.backward()
     ps = build_parallel_state(tp=1, cp=world)
     model = build_model(cfg, dtype=torch.float32, seed=0)
-    ec = EngineConfig(context_parallel_size=world, tpr_cp_backend=backend)
+    ec = EngineConfig(context_parallel_size=world, tpr_cp_backend=backend, gdn_cp_mode=gdn_cp_mode)
     eng = TPREngine(cfg, ec, device="cpu", model=model, parallel_state=ps)
     batch["tpr_capture_log_probs"] = True
     out = eng.forward_backward_batch(batch)
@@ -59,6 +59,108 @@ def test_hybrid_gdn_cp2_ring_matches_flattened(prefix, resp):
     for r in res:
         assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
         worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
+
+@pytest.mark.parametrize("prefix,resp", [(128, 64), (131, 63)])
+def test_hybrid_gdn_cp2_sequence_sharded_matches_flattened(prefix, resp):
+    """GDN layers sequence-sharded under ring CP (zigzag pieces, padding): exchanged per-piece state maps
+    and conv halos, full-head state relayed between segments."""
+    res = run_ranks(2, _worker, "ring", 4, "tiny_hybrid", prefix, resp, "sequence")
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
+
+def _seq_layer_worker(rank, world):
+    """forward_gdn_cp_sequence on contiguous shards vs the whole segment on one rank (FP32)."""
+    import torch
+
+    from bridge_b200.models import get_config
+    from bridge_b200.models.layers import TPRGatedDeltaNet
+    from bridge_b200.parallel.gdn_state import forward_gdn_cp_sequence
+    from bridge_b200.tpr.prefix_state import GDNLayerState
+
+    cfg = get_config("tiny_hybrid")
+    torch.manual_seed(0)
+    layer = TPRGatedDeltaNet(cfg, 1).float()
+    L = 48
+    x = torch.randn(world * L, cfg.hidden_size)
+    cc = 2 * layer.hk * layer.dk + layer.hv * layer.dv
+    h_conv = torch.randn(1, cc, layer.w)
+    h_conv[:, :, 0] = 0
+    h_rec = 0.1 * torch.randn(1, layer.hv, layer.dk, layer.dv)
+    # reference: whole segment, one process
+    xr, hc_r, hr_r = (t.clone().requires_grad_() for t in (x, h_conv, h_rec))
+    ref_layer = TPRGatedDeltaNet(cfg, 1).float()
+    ref_layer.load_state_dict(layer.state_dict())
+    out_r, fin_r = _whole_segment(ref_layer, xr, GDNLayerState(hc_r, hr_r))
+    w_out = torch.randn_like(out_r)
+    w_rec = torch.randn_like(fin_r.recurrent_state)
+    w_conv = torch.randn_like(fin_r.conv_state)
+    ((out_r * w_out).sum() + (fin_r.recurrent_state * w_rec).sum() + (fin_r.conv_state * w_conv).sum()).backward()
+    # sequence-sharded
+    xs = x[rank * L:(rank + 1) * L].clone().requires_grad_()
+    hc, hr = h_conv.clone().requires_grad_(), h_rec.clone().requires_grad_()
+    out, fin = forward_gdn_cp_sequence(layer, xs, GDNLayerState(hc, hr), _world(), capture_final_state=True)
+    loss = (out * w_out[rank * L:(rank + 1) * L]).sum()
+    # the final state is replicated: one rank's copy carries the state loss, as in the single-process run
+    if rank == 0:
+        loss = loss + (fin.recurrent_state * w_rec).sum() + (fin.conv_state * w_conv).sum()
+    loss.backward()
+    # dh0 partials: rank 1 never reads the initial conv state (its halo is rank 0's tail)
+    d_hc = hc.grad if hc.grad is not None else torch.zeros_like(hc)
+    d_hr = hr.grad if hr.grad is not None else torch.zeros_like(hr)
+    torch.distributed.all_reduce(d_hc)
+    torch.distributed.all_reduce(d_hr)
+    rel = lambda a, b: float((a - b).norm() / (b.norm() + 1e-12))  # noqa: E731
+    errs = {"out": rel(out.detach(), out_r.detach()[rank * L:(rank + 1) * L]),
+            "rec": rel(fin.recurrent_state.detach(), fin_r.recurrent_state.detach()),
+            "conv": rel(fin.conv_state.detach(), fin_r.conv_state.detach()),
+            "dx": rel(xs.grad, xr.grad[rank * L:(rank + 1) * L]),
+            "dh_conv": rel(d_hc, hc_r.grad), "dh_rec": rel(d_hr, hr_r.grad)}
+    pg = {n: (p.grad if p.grad is not None else torch.zeros_like(p)).clone() for n, p in layer.named_parameters()}
+    for t in pg.values():
+        torch.distributed.all_reduce(t)
+    for n, p in ref_layer.named_parameters():
+        errs["param:" + n] = rel(pg[n], p.grad)
+    return errs
+
+
+def _world():
+    import torch.distributed as dist
+
+    return dist.group.WORLD
+
+
+def _whole_segment(layer, x, state):
+    """The layer's own single-process path with an explicit initial state (no TPR context)."""
+    from bridge_b200.ops.gdn import (causal_conv1d, chunk_gated_delta_rule, gated_rmsnorm, gdn_gates,
+                                     l2norm)
+    from bridge_b200.tpr.prefix_state import GDNLayerState
+
+    t = x.shape[0]
+    kd, vd = layer.hk * layer.dk, layer.hv * layer.dv
+    qkv, z, b, a = layer.in_proj(x).split((2 * kd + vd, vd, layer.hv, layer.hv), dim=-1)
+    y, conv_final = causal_conv1d(qkv, layer.conv_weight, None, [0, t], None, state.conv_state, activation=True)
+    q, k, v = y.split((kd, kd, vd), dim=-1)
+    q = l2norm(q.reshape(t, layer.hk, layer.dk))
+    k = l2norm(k.reshape(t, layer.hk, layer.dk))
+    v = v.reshape(t, layer.hv, layer.dv)
+    if layer.hv // layer.hk > 1:
+        q, k = q.repeat_interleave(layer.hv // layer.hk, 1), k.repeat_interleave(layer.hv // layer.hk, 1)
+    g, beta = gdn_gates(a, b, layer.A_log, layer.dt_bias)
+    o, rec = chunk_gated_delta_rule(q, k, v, g, beta, [0, t], None, state.recurrent_state, scale=layer.scale,
+                                    chunk_size=layer.chunk)
+    o = gated_rmsnorm(o, z.reshape(t, layer.hv, layer.dv), layer.norm_weight, layer.eps)
+    return layer.out_proj(o.reshape(t, vd)), GDNLayerState(conv_final, rec)
+
+
+def test_gdn_sequence_sharded_layer_matches_whole_segment():
+    """Outputs, final conv / recurrent state and every gradient (input, parameters, dh0 of both states)."""
+    for r in run_ranks(2, _seq_layer_worker):
+        worst = max(r.items(), key=lambda kv: kv[1])
         assert worst[1] < 1e-4, worst
 
 

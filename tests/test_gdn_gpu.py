@@ -169,3 +169,55 @@ def test_gdn_gates_matches_fp32():
     ((gr * dg).sum() + (br * db).sum()).backward()
     for name, x, r in zip(("da", "db", "dA_log", "ddt"), (a, b, A_log, dt), refs):
         _close(x.grad, r.grad, 1e-3, 1e-2, name)
+
+
+def _seq_gpu_worker(rank, world):
+    """One-rank sequence-sharded GDN on the GPU: O = O0 + O_I S0 and S_end = M S0 + C from the two
+    tensor-core passes (the identity pass runs the (K, K) kernel) vs the direct stateful path."""
+    import torch
+    import torch.distributed as dist
+
+    from bridge_b200.models import get_config
+    from bridge_b200.models.layers import TPRGatedDeltaNet
+    from bridge_b200.parallel.gdn_state import forward_gdn_cp_sequence
+    from bridge_b200.tpr.prefix_state import GDNLayerState
+    from tests.test_cp_gloo import _whole_segment
+
+    group = dist.new_group(ranks=[0], backend="nccl")
+    dev = torch.device("cuda", 0)
+    cfg = get_config("tiny_hybrid", gdn_head_dim=64)
+    torch.manual_seed(0)
+    layer = TPRGatedDeltaNet(cfg, 1, device=dev)
+    ref = TPRGatedDeltaNet(cfg, 1, device=dev)
+    ref.load_state_dict(layer.state_dict())
+    T = 200
+    x = torch.randn(T, cfg.hidden_size, device=dev).to(torch.bfloat16)
+    cc = 2 * layer.hk * layer.dk + layer.hv * layer.dv
+    h_conv = torch.randn(1, cc, layer.w, device=dev).to(torch.bfloat16)
+    h_conv[:, :, 0] = 0
+    h_rec = 0.2 * torch.randn(1, layer.hv, layer.dk, layer.dv, device=dev)
+    outs = {}
+    for name, mod in (("seq", layer), ("ref", ref)):
+        xs, hc, hr = (t.clone().requires_grad_() for t in (x, h_conv, h_rec))
+        if name == "seq":
+            o, fin = forward_gdn_cp_sequence(mod, xs, GDNLayerState(hc, hr), group)
+        else:
+            o, fin = _whole_segment(mod, xs, GDNLayerState(hc, hr))
+        g = torch.Generator(device=dev).manual_seed(1)
+        wo = torch.randn(o.shape, device=dev, generator=g)
+        wr = torch.randn(fin.recurrent_state.shape, device=dev, generator=g)
+        ((o.float() * wo).sum() + (fin.recurrent_state.float() * wr).sum()).backward()
+        outs[name] = {"o": o.detach().float(), "rec": fin.recurrent_state.detach().float(),
+                      "conv": fin.conv_state.detach().float(), "dx": xs.grad.float(), "dh_rec": hr.grad.float(),
+                      "dh_conv": hc.grad.float(), **{"p:" + n: p.grad.float() for n, p in mod.named_parameters()}}
+    return {k: float((outs["seq"][k] - outs["ref"][k]).norm() / (outs["ref"][k].norm() + 1e-12))
+            for k in outs["ref"]}
+
+
+def test_gdn_sequence_sharded_gpu_kernels():
+    from tests.dist_utils import run_ranks
+
+    (errs,) = run_ranks(1, _seq_gpu_worker)
+    worst = max(errs.items(), key=lambda kv: kv[1])
+    # bf16 activations; the identity pass adds one bf16 rounding of O_I before the FP32 correction
+    assert worst[1] < 3e-2, errs
