@@ -200,6 +200,44 @@ __device__ __forceinline__ void store_e(__nv_bfloat16* p, const float* f) {
     for (int j = 0; j < E; ++j) p[j] = __float2bfloat16(f[j]);
   }
 }
+// Packed bf16 row slice of E elements held in registers until use (half the registers of floats).
+template <int E>
+struct RawBf16 {
+  using T = typename std::conditional<E == 8, uint4, typename std::conditional<E == 4, uint2, uint32_t>::type>::type;
+};
+template <int E>
+__device__ __forceinline__ typename RawBf16<E>::T load_raw(const __nv_bfloat16* p) {
+  return *reinterpret_cast<const typename RawBf16<E>::T*>(p);
+}
+template <int E>
+__device__ __forceinline__ void unpack_raw(const typename RawBf16<E>::T& u, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < E / 2; ++j) {
+    const float2 v = __bfloat1622float2(h[j]);
+    f[2 * j] = v.x;
+    f[2 * j + 1] = v.y;
+  }
+}
+
+// E consecutive floats with the widest aligned vector loads (p aligned to 4 * E bytes, E in {2, 4, 8}).
+template <int E>
+__device__ __forceinline__ void load_f(const float* p, float* f) {
+  if constexpr (E % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < E; j += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(p + j);
+      f[j] = v.x; f[j + 1] = v.y; f[j + 2] = v.z; f[j + 3] = v.w;
+    }
+  } else if constexpr (E == 2) {
+    const float2 v = *reinterpret_cast<const float2*>(p);
+    f[0] = v.x; f[1] = v.y;
+  } else {
+#pragma unroll
+    for (int j = 0; j < E; ++j) f[j] = p[j];
+  }
+}
+
 // Normalise + rotate one preloaded head row f (E = D / 32 elements per lane) and store it.
 template <int D>
 __device__ __forceinline__ void norm_rope_apply(float* f, const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
@@ -212,17 +250,20 @@ __device__ __forceinline__ void norm_rope_apply(float* f, const float* __restric
   ss = bb::warp_sum(ss);
   const float r = rsqrtf(ss / D + eps);
   if (lane == 0) *rstd_out = r;
+  float wv[E], cv[E], sv[E];
+  load_f<E>(w + lane * E, wv);
 #pragma unroll
-  for (int j = 0; j < E; ++j) f[j] = f[j] * r * w[lane * E + j];
+  for (int j = 0; j < E; ++j) f[j] = f[j] * r * wv[j];
   // rotate half: first half lanes (0..15) hold x1, partner lanes hold x2 at the same offset.
   const bool lo = lane < 16;
   const int fi = (lane & 15) * E;  // frequency index of element 0
+  load_f<E>(cs + fi, cv);
+  load_f<E>(sn + fi, sv);
   float o[E];
 #pragma unroll
   for (int j = 0; j < E; ++j) {
     float other = __shfl_xor_sync(0xffffffffu, f[j], 16);
-    float c = cs[fi + j], s = sn[fi + j];
-    o[j] = lo ? (f[j] * c - other * s) : (f[j] * c + other * s);
+    o[j] = lo ? (f[j] * cv[j] - other * sv[j]) : (f[j] * cv[j] + other * sv[j]);
   }
   store_e<E>(out + lane * E, o);
 }
@@ -233,13 +274,13 @@ __device__ __forceinline__ void norm_rope_apply(float* f, const float* __restric
 constexpr int kQKRows = 4;
 
 template <int D>
-__global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+__global__ void __launch_bounds__(256, D >= 256 ? 2 : 4) qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                                         const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
                                         const float* __restrict__ cosb, const float* __restrict__ sinb,
                                         __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko,
                                         float* __restrict__ rq, float* __restrict__ rk, int T, int Hq, int Hk,
                                         float eps, long qts, long qhs, long kts, long khs) {
-  __shared__ float swq[D], swk[D];
+  __shared__ __align__(16) float swq[D], swk[D];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     swq[i] = __bfloat162float(qw[i]);
     swk[i] = __bfloat162float(kw[i]);
@@ -251,13 +292,13 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, con
   const int total = T * G;                                  // < 2^31, checked on the host
   for (int item = blockIdx.x * warps + (threadIdx.x >> 5); item < total; item += gridDim.x * warps) {
     const int t = item / G, h0 = (item - t * G) * kQKRows;
-    float f[kQKRows][E];
+    typename RawBf16<E>::T raw[kQKRows];
 #pragma unroll
     for (int u = 0; u < kQKRows; ++u) {
       const int h = h0 + u;
       if (h < HH) {
         const __nv_bfloat16* src = h < Hq ? q + t * qts + h * qhs : k + t * kts + (h - Hq) * khs;
-        load_e<E>(src + lane * E, f[u]);
+        raw[u] = load_raw<E>(src + lane * E);
       }
     }
     const float* cs = cosb + (size_t)t * (D / 2);
@@ -266,10 +307,12 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ q, con
     for (int u = 0; u < kQKRows; ++u) {
       const int h = h0 + u;
       if (h < HH) {
+        float f[E];
+        unpack_raw<E>(raw[u], f);
         if (h < Hq)
-          norm_rope_apply<D>(f[u], swq, qo + ((size_t)t * Hq + h) * D, rq + (size_t)t * Hq + h, cs, sn, eps, lane);
+          norm_rope_apply<D>(f, swq, qo + ((size_t)t * Hq + h) * D, rq + (size_t)t * Hq + h, cs, sn, eps, lane);
         else
-          norm_rope_apply<D>(f[u], swk, ko + ((size_t)t * Hk + h - Hq) * D, rk + (size_t)t * Hk + h - Hq, cs, sn,
+          norm_rope_apply<D>(f, swk, ko + ((size_t)t * Hk + h - Hq) * D, rk + (size_t)t * Hk + h - Hq, cs, sn,
                              eps, lane);
       }
     }
@@ -286,31 +329,33 @@ __device__ __forceinline__ void norm_rope_apply_bwd(const float* dl, const float
   constexpr int E = D / 32;
   const bool lo = lane < 16;
   const int fi = (lane & 15) * E;
-  float g[E];
+  float g[E], wv[E], cv[E], sv[E];
+  load_f<E>(cs + fi, cv);
+  load_f<E>(sn + fi, sv);
+  load_f<E>(w + lane * E, wv);
 #pragma unroll
   for (int j = 0; j < E; ++j) {
     float d = dl[j];
     float other = __shfl_xor_sync(0xffffffffu, d, 16);
-    float c = cs[fi + j], s = sn[fi + j];
     // forward: lo: y = a c - b s ; hi: y = b c + a s  (a = x1, b = x2)
-    g[j] = lo ? (d * c + other * s) : (d * c - other * s);
+    g[j] = lo ? (d * cv[j] + other * sv[j]) : (d * cv[j] - other * sv[j]);
   }
   float dot = 0.f;
 #pragma unroll
   for (int j = 0; j < E; ++j) {
     float xh = x[j] * r;
-    dot += g[j] * w[lane * E + j] * xh;
+    dot += g[j] * wv[j] * xh;
     dwacc[j] += g[j] * xh;
   }
   dot = bb::warp_sum(dot) / D;
   float o[E];
 #pragma unroll
-  for (int j = 0; j < E; ++j) o[j] = r * (g[j] * w[lane * E + j] - x[j] * r * dot);
+  for (int j = 0; j < E; ++j) o[j] = r * (g[j] * wv[j] - x[j] * r * dot);
   store_e<E>(dxp + lane * E, o);
 }
 
 template <int D>
-__global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, const __nv_bfloat16* __restrict__ dko,
+__global__ void __launch_bounds__(256, D >= 256 ? 2 : 4) qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, const __nv_bfloat16* __restrict__ dko,
                                         const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                                         const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
                                         const float* __restrict__ cosb, const float* __restrict__ sinb,
@@ -319,7 +364,7 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, c
                                         float* __restrict__ dqw, float* __restrict__ dkw, int T, int Hq, int Hk,
                                         long qts, long qhs, long kts, long khs) {
   constexpr int E = D / 32;
-  __shared__ float swq[D], swk[D], sdq[D], sdk[D];
+  __shared__ __align__(16) float swq[D], swk[D], sdq[D], sdk[D];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     swq[i] = __bfloat162float(qw[i]);
     swk[i] = __bfloat162float(kw[i]);
@@ -335,18 +380,19 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, c
   const int total = T * G;
   for (int item = blockIdx.x * warps + (threadIdx.x >> 5); item < total; item += gridDim.x * warps) {
     const int t = item / G, h0 = (item - t * G) * kQKRows;
-    float dl[kQKRows][E], xv[kQKRows][E], rr[kQKRows];
+    typename RawBf16<E>::T rd[kQKRows], rx[kQKRows];
+    float rr[kQKRows];
 #pragma unroll
     for (int u = 0; u < kQKRows; ++u) {
       const int h = h0 + u;
       if (h < HH) {
         if (h < Hq) {
-          load_e<E>(dqo + ((size_t)t * Hq + h) * D + lane * E, dl[u]);
-          load_e<E>(q + t * qts + h * qhs + lane * E, xv[u]);
+          rd[u] = load_raw<E>(dqo + ((size_t)t * Hq + h) * D + lane * E);
+          rx[u] = load_raw<E>(q + t * qts + h * qhs + lane * E);
           rr[u] = rq[(size_t)t * Hq + h];
         } else {
-          load_e<E>(dko + ((size_t)t * Hk + h - Hq) * D + lane * E, dl[u]);
-          load_e<E>(k + t * kts + (h - Hq) * khs + lane * E, xv[u]);
+          rd[u] = load_raw<E>(dko + ((size_t)t * Hk + h - Hq) * D + lane * E);
+          rx[u] = load_raw<E>(k + t * kts + (h - Hq) * khs + lane * E);
           rr[u] = rk[(size_t)t * Hk + h - Hq];
         }
       }
@@ -357,10 +403,13 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqo, c
     for (int u = 0; u < kQKRows; ++u) {
       const int h = h0 + u;
       if (h < HH) {
+        float dl[E], xv[E];
+        unpack_raw<E>(rd[u], dl);
+        unpack_raw<E>(rx[u], xv);
         if (h < Hq)
-          norm_rope_apply_bwd<D>(dl[u], xv[u], swq, rr[u], cs, sn, dq + ((size_t)t * Hq + h) * D, aq, lane);
+          norm_rope_apply_bwd<D>(dl, xv, swq, rr[u], cs, sn, dq + ((size_t)t * Hq + h) * D, aq, lane);
         else
-          norm_rope_apply_bwd<D>(dl[u], xv[u], swk, rr[u], cs, sn, dk + ((size_t)t * Hk + h - Hq) * D, ak, lane);
+          norm_rope_apply_bwd<D>(dl, xv, swk, rr[u], cs, sn, dk + ((size_t)t * Hk + h - Hq) * D, ak, lane);
       }
     }
   }
@@ -849,8 +898,10 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor q, torch::Tensor k, to
   check_qk_view(k, "k");
   TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && q.size(2) == k.size(2) && q.size(0) == k.size(0), "qk shapes");
   const int T = q.size(0), Hq = q.size(1), Hk = k.size(1), D = q.size(2);
-  TORCH_CHECK(cosb.size(0) == T && cosb.size(1) == D / 2 && cosb.scalar_type() == at::kFloat && cosb.is_contiguous(),
-              "cos table must be [T, D/2] fp32");
+  TORCH_CHECK(cosb.size(0) == T && cosb.size(1) == D / 2 && cosb.scalar_type() == at::kFloat && cosb.is_contiguous() &&
+                  sinb.is_contiguous() && (reinterpret_cast<uintptr_t>(cosb.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(sinb.data_ptr()) & 15) == 0,
+              "cos / sin tables must be contiguous, 16-byte aligned [T, D/2] fp32");
   auto qo = torch::empty({T, Hq, D}, q.options()), ko = torch::empty({T, Hk, D}, k.options());
   auto rq = torch::empty({T, Hq}, q.options().dtype(at::kFloat));
   auto rk = torch::empty({T, Hk}, q.options().dtype(at::kFloat));
@@ -888,6 +939,9 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko
   check_bf16(dko, "dk");
   check_qk_view(q, "q");
   check_qk_view(k, "k");
+  TORCH_CHECK(cosb.is_contiguous() && sinb.is_contiguous() && (reinterpret_cast<uintptr_t>(cosb.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(sinb.data_ptr()) & 15) == 0,
+              "cos / sin tables must be contiguous and 16-byte aligned");
   const int T = q.size(0), Hq = q.size(1), Hk = k.size(1), D = q.size(2);
   auto dq = torch::empty({T, Hq, D}, q.options()), dk = torch::empty({T, Hk, D}, k.options());
   auto dqw = torch::zeros({D}, q.options().dtype(at::kFloat));

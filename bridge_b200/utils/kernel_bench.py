@@ -139,6 +139,11 @@ def bench_elementwise(t: Timer, small: bool):
     _report("rmsnorm_fwd", {"T": T, "H": H}, ms, bytes_=2 * x.numel() * 2)
     ms = t(lambda: m.rmsnorm_bwd(y, x, w, rstd))
     _report("rmsnorm_bwd", {"T": T, "H": H}, ms, bytes_=3 * x.numel() * 2)
+    r = torch.randn_like(x)
+    ms = t(lambda: m.add_rmsnorm_fwd(x, r, w, 1e-6))
+    _report("add_rmsnorm_fwd", {"T": T, "H": H}, ms, bytes_=4 * x.numel() * 2)
+    ms = t(lambda: m.add_rmsnorm_bwd(y, x, w, rstd, r))
+    _report("add_rmsnorm_bwd", {"T": T, "H": H}, ms, bytes_=4 * x.numel() * 2)
     F = 9728
     Ts = T // 4
     gu = torch.randn(Ts, 2 * F, device="cuda", dtype=torch.bfloat16)
@@ -148,8 +153,10 @@ def bench_elementwise(t: Timer, small: bool):
     ms = t(lambda: m.swiglu_bwd(dy, gu))
     _report("swiglu_bwd", {"T": Ts, "F": F}, ms, bytes_=5 * Ts * F * 2)
     Tq = T // 2
-    q = torch.randn(Tq, 32, 128, device="cuda", dtype=torch.bfloat16)
-    k = torch.randn(Tq, 8, 128, device="cuda", dtype=torch.bfloat16)
+    # q and k read in place from the fused QKV projection output, as the attention layer does
+    qkv = torch.randn(Tq, 48 * 128, device="cuda", dtype=torch.bfloat16)
+    q = qkv[:, :32 * 128].view(Tq, 32, 128)
+    k = qkv[:, 32 * 128:40 * 128].view(Tq, 8, 128)
     qw = torch.ones(128, device="cuda", dtype=torch.bfloat16)
     cos, sin = rope_cos_sin(torch.arange(Tq, device="cuda"), 128, 1e6)
     qo, ko, rq, rk = m.qk_norm_rope_fwd(q, k, qw, qw, cos, sin, 1e-6)
