@@ -13,7 +13,8 @@ written here loads in HF and vice versa:
 * MoE: ``mlp.gate.weight`` (router), ``mlp.experts.{e}.{gate,up,down}_proj.weight``,
   ``mlp.shared_expert.{gate,up,down}_proj.weight``, ``mlp.shared_expert_gate.weight``;
 * GDN layers: ``linear_attn.in_proj.weight`` (rows ``[q|k|v|z|b|a]``), ``linear_attn.conv1d.weight``
-  (``[C, 1, W]``), ``linear_attn.{A_log,dt_bias,norm.weight,out_proj.weight}``.
+  (``[C, 1, W]``, channels ``[q|k|v]``), ``linear_attn.{A_log,dt_bias,norm.weight,out_proj.weight}``;
+  under TP every rank holds its heads' slice of each section, in the same section order.
 
 Optimizer state is saved per rank (``optim_rank{r}.pt``: FP32 master, Adam
 moments, step) next to ``model.safetensors`` and a ``meta.json`` with the step
@@ -48,6 +49,27 @@ def _gather(t: Tensor, dim: int, group) -> Tensor:
     return torch.cat(parts, dim=dim)
 
 
+def _split_sections(t: Tensor, sizes: list[int], group) -> Tensor:
+    """Rank's slice of every section of dim 0 (global section sizes ``sizes``), concatenated."""
+    if tp_size(group) == 1:
+        return t
+    return torch.cat([s_.chunk(tp_size(group), 0)[tp_rank(group)] for s_ in t.split(sizes, 0)], 0).contiguous()
+
+
+def _gather_sections(t: Tensor, sizes_local: list[int], group) -> Tensor:
+    """Inverse of :func:`_split_sections`: every section gathered over TP, sections concatenated."""
+    if tp_size(group) == 1:
+        return t
+    return torch.cat([_gather(s_, 0, group) for s_ in t.split(sizes_local, 0)], 0)
+
+
+def _gdn_sections(cfg, n: int) -> tuple[list[int], list[int]]:
+    """Global row sections of the GDN input projection ``[q|k|v|z|b|a]`` and conv channels ``[q|k|v]``
+    (each rank holds its heads' slice of every section, in that order)."""
+    kd, vd = cfg.gdn_num_qk_heads * cfg.gdn_head_dim, cfg.gdn_num_v_heads * cfg.gdn_head_dim
+    return [kd, kd, vd, vd, cfg.gdn_num_v_heads, cfg.gdn_num_v_heads], [kd, kd, vd]
+
+
 def _qkv_rows(cfg, n: int):
     d = cfg.head_dim
     q = cfg.num_heads * d * (2 if cfg.attention_output_gate else 1) // n
@@ -79,8 +101,11 @@ def hf_state_dict(model) -> dict[str, Tensor]:
                 out[p + "self_attn.q_norm.weight"] = mix.q_norm.weight.data
                 out[p + "self_attn.k_norm.weight"] = mix.k_norm.weight.data
         else:
-            out[p + "linear_attn.in_proj.weight"] = _gather(mix.in_proj.weight.data, 0, g)
-            out[p + "linear_attn.conv1d.weight"] = _gather(mix.conv_weight.data, 0, g).unsqueeze(1)
+            proj_s, conv_s = _gdn_sections(cfg, n)
+            out[p + "linear_attn.in_proj.weight"] = _gather_sections(mix.in_proj.weight.data,
+                                                                     [x // n for x in proj_s], g)
+            out[p + "linear_attn.conv1d.weight"] = _gather_sections(mix.conv_weight.data, [x // n for x in conv_s],
+                                                                    g).unsqueeze(1)
             out[p + "linear_attn.A_log"] = _gather(mix.A_log.data, 0, g)
             out[p + "linear_attn.dt_bias"] = _gather(mix.dt_bias.data, 0, g)
             out[p + "linear_attn.norm.weight"] = mix.norm_weight.data
@@ -160,8 +185,9 @@ def load_hf_state_dict(model, sd: dict[str, Tensor], *, strict: bool = True) -> 
                 put(mix.q_norm.weight, take(p + "self_attn.q_norm.weight"))
                 put(mix.k_norm.weight, take(p + "self_attn.k_norm.weight"))
         else:
-            put(mix.in_proj.weight, _split(take(p + "linear_attn.in_proj.weight"), 0, g))
-            put(mix.conv_weight, _split(take(p + "linear_attn.conv1d.weight").squeeze(1), 0, g))
+            proj_s, conv_s = _gdn_sections(cfg, tp_size(g))
+            put(mix.in_proj.weight, _split_sections(take(p + "linear_attn.in_proj.weight"), proj_s, g))
+            put(mix.conv_weight, _split_sections(take(p + "linear_attn.conv1d.weight").squeeze(1), conv_s, g))
             put(mix.A_log, _split(take(p + "linear_attn.A_log"), 0, g))
             put(mix.dt_bias, _split(take(p + "linear_attn.dt_bias"), 0, g))
             put(mix.norm_weight, take(p + "linear_attn.norm.weight"))

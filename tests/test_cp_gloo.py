@@ -164,7 +164,7 @@ def test_gdn_sequence_sharded_layer_matches_whole_segment():
         assert worst[1] < 1e-4, worst
 
 
-def _tpcp_worker(rank, world, backend):
+def _tpcp_worker(rank, world, backend, preset="tiny", gdn_cp_mode="head"):
     import torch
 
     from bridge_b200.engine import EngineConfig, TPREngine
@@ -173,7 +173,7 @@ def _tpcp_worker(rank, world, backend):
     from bridge_b200.parallel.groups import build_parallel_state
     from tests.helpers import flat_ppo_loss, set_old_log_probs, tree_batch
 
-    cfg = get_config("tiny", num_layers=2)
+    cfg = get_config(preset, num_layers=2 if preset == "tiny" else 4)
     batch = tree_batch(n_trees=1, prefix=128, siblings=4, resp=64, seed=0)
     ref = build_model(cfg, dtype=torch.float32, seed=0)
     set_old_log_probs(ref, batch)
@@ -184,8 +184,8 @@ def _tpcp_worker(rank, world, backend):
     ps = build_parallel_state(tp=2, cp=2)
     model = build_model(cfg, dtype=torch.float32, seed=1, tp_group=ps.tp_group)
     load_hf_state_dict(model, hf_state_dict(ref))          # TP shards of the reference weights
-    eng = TPREngine(cfg, EngineConfig(tensor_model_parallel_size=2, context_parallel_size=2, tpr_cp_backend=backend),
-                    device="cpu", model=model, parallel_state=ps)
+    eng = TPREngine(cfg, EngineConfig(tensor_model_parallel_size=2, context_parallel_size=2, tpr_cp_backend=backend,
+                                      gdn_cp_mode=gdn_cp_mode), device="cpu", model=model, parallel_state=ps)
     out = eng.forward_backward_batch(batch)
     # expected TP-sharded gradients: the reference gradients sharded by the same HF -> Megatron loader
     import copy
@@ -212,3 +212,23 @@ def test_tp2_cp2_matches_flattened(backend):
         assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
         worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
         assert worst[1] < 1e-4, worst
+
+
+def test_tp2_cp2_hybrid_gdn_sequence_sharded_matches_flattened():
+    """Config #4's axes on the hybrid model: TP2 x CP2 ring with sequence-sharded GDN (one key head per
+    TP rank, which the head-parallel schedule cannot split over CP) against the flattened batch."""
+    res = run_ranks(4, _tpcp_worker, "ring", "tiny_hybrid", "sequence")
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
+
+def test_hybrid_gdn_cp4_sequence_sharded_matches_flattened():
+    """GDN under ring CP4 (eight zigzag pieces chained through the exchanged state maps)."""
+    res = run_ranks(4, _worker, "ring", 4, "tiny_hybrid", 64, 32, "sequence")
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
