@@ -303,6 +303,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //          dQ += dS K accumulated in TMEM, written once.
 struct alignas(64) BwdMaps {
   CUtensorMap q, k, v, pk, pv, dout, q64, dout64;   // q64 / dout64: 64-row boxes for the pipelined dK/dV
+  CUtensorMap k64, v64, pk64, pv64;                 // 64-row key / value boxes for the pipelined dQ
 };
 
 __device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -952,6 +953,210 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Pipelined dQ (default): 64-key tiles with a three-stage K/V ring and every per-tile buffer doubled --
+// S / dP in TMEM (2 x (64 | 64) columns) and dS in shared memory (2 x 16 KB) -- so the MMA warp issues
+// S(j+1), dP(j+1) before dQ += dS(j) K(j) and the tensor pipe works while the softmax warps form dS(j).
+// Eight softmax warps (each TMEM lane quarter served twice, one 32-key half each) keep the exp / dS
+// work of a tile shorter than its MMAs.
+// Shared memory: Q, dO 64 KB + 3 x (K, V) 96 KB + 2 x dS 32 KB; TMEM: 256 (S, dP) + 128 (dQ) columns.
+constexpr int BKV2 = 64;
+constexpr int KT_BYTES = BKV2 * D * 2;   // 16 KB: two 64-column blocks of 64 rows
+constexpr int DS2_BYTES = BQ * BKV2 * 2; // 16 KB: one 64-column block of 128 rows
+constexpr int DQ_STAGES = 3;
+constexpr int DQ2_THREADS = 320;  // TMA warp, MMA warp, 8 softmax warps (two per TMEM lane quarter)
+
+struct SmemDQ2 {
+  static constexpr int Q = 0;
+  static constexpr int DO = Q + TILE_BYTES;
+  static constexpr int K0 = DO + TILE_BYTES;
+  static constexpr int V0 = K0 + DQ_STAGES * KT_BYTES;
+  static constexpr int DS0 = V0 + DQ_STAGES * KT_BYTES;
+  static constexpr int BAR = DS0 + 2 * DS2_BYTES;
+  static constexpr int TOTAL = BAR + 256;
+};
+
+__global__ void __launch_bounds__(DQ2_THREADS, 1)
+    tree_attn_dq2_sm100_kernel(const __grid_constant__ BwdMaps maps, const int* __restrict__ cu,
+                               const int* __restrict__ poff, const int* __restrict__ plen,
+                               const float* __restrict__ lse, const float* __restrict__ delta,
+                               __nv_bfloat16* __restrict__ dq, int T, int Hq, int Hk, float scale_log2, float scale,
+                               int* err) {
+  const int seq = blockIdx.y, h = blockIdx.z, hk = h / (Hq / Hk);
+  const int q0 = cu[seq], n = cu[seq + 1] - q0;
+  const int m0 = blockIdx.x * BQ;
+  if (m0 >= n) return;
+  const int po = poff[seq], pl = plen[seq];
+  const int n_pre = (pl + BKV2 - 1) / BKV2;
+  const int n_self = (min(n, m0 + BQ) + BKV2 - 1) / BKV2;
+  const int ntiles = n_pre + n_self;
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemDQ2::BAR);
+  uint64_t* qdo_bar = bars + 0;
+  uint64_t* kv_full = bars + 1;    // [3]
+  uint64_t* kv_empty = bars + 4;   // [3]
+  uint64_t* s_full = bars + 7;     // [2] S, dP of a tile landed in TMEM
+  uint64_t* sd_free = bars + 9;    // [2] softmax warps read S, dP of the buffer
+  uint64_t* ds_full = bars + 11;   // [2] dS of the buffer written to smem
+  uint64_t* ds_done = bars + 13;   // [2] dQ MMA of the buffer completed (dS smem reusable)
+  uint64_t* dq_done = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(qdo_bar, 1);
+    for (int i = 0; i < DQ_STAGES; ++i) {
+      sm100::mbar_init(&kv_full[i], 1);
+      sm100::mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&s_full[i], 1);
+      sm100::mbar_init(&sd_free[i], 256);
+      sm100::mbar_init(&ds_full[i], 256);
+      sm100::mbar_init(&ds_done[i], 1);
+    }
+    sm100::mbar_init(dq_done, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, 512);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_DQ = tmem + 256;  // S(b) at tmem + 64 b, dP(b) at tmem + 128 + 64 b
+
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::mbar_expect_tx(qdo_bar, 2 * TILE_BYTES);
+      load_tile128(smem + SmemDQ2::Q, &maps.q, qdo_bar, h * D, q0 + m0);
+      load_tile128(smem + SmemDQ2::DO, &maps.dout, qdo_bar, h * D, q0 + m0);
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % DQ_STAGES;
+        if (!sm100::mbar_wait(&kv_empty[st], ((j / DQ_STAGES) & 1) ^ 1, err, 51)) break;
+        sm100::mbar_expect_tx(&kv_full[st], 2 * KT_BYTES);
+        const bool pre = j < n_pre;
+        const int r0 = pre ? po + j * BKV2 : q0 + (j - n_pre) * BKV2;
+        const CUtensorMap* km = pre ? &maps.pk64 : &maps.k64;
+        const CUtensorMap* vm = pre ? &maps.pv64 : &maps.v64;
+        unsigned char* kd = smem + SmemDQ2::K0 + st * KT_BYTES;
+        unsigned char* vd = smem + SmemDQ2::V0 + st * KT_BYTES;
+        sm100::tma_load_2d(kd, km, &kv_full[st], hk * D, r0);
+        sm100::tma_load_2d(kd + 8192, km, &kv_full[st], hk * D + 64, r0);
+        sm100::tma_load_2d(vd, vm, &kv_full[st], hk * D, r0);
+        sm100::tma_load_2d(vd + 8192, vm, &kv_full[st], hk * D + 64, r0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = sm100::umma_idesc_bf16(BQ, BKV2, false, false);  // S, dP: 128 x 64
+      constexpr uint32_t ID_DQ = sm100::umma_idesc_bf16(BQ, D, false, true);     // dQ: 128 x 128
+      const uint32_t q_b = sm100::smem_addr(smem + SmemDQ2::Q), o_b = sm100::smem_addr(smem + SmemDQ2::DO);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % DQ_STAGES, b = j & 1;
+        if (!sm100::mbar_wait(&kv_full[st], (j / DQ_STAGES) & 1, err, 52)) return false;
+        if (!sm100::mbar_wait(&sd_free[b], ((j >> 1) & 1) ^ 1, err, 53)) return false;
+        sm100::tc_fence_after();
+        const uint32_t k_b = sm100::smem_addr(smem + SmemDQ2::K0 + st * KT_BYTES);
+        const uint32_t v_b = sm100::smem_addr(smem + SmemDQ2::V0 + st * KT_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          sm100::umma_bf16(tmem + b * 64, kmajor_desc(q_b, kk), kmajor64_desc(k_b, kk), ID_S, kk > 0);
+          sm100::umma_bf16(tmem + 128 + b * 64, kmajor_desc(o_b, kk), kmajor64_desc(v_b, kk), ID_S, kk > 0);
+        }
+        sm100::umma_commit(&s_full[b]);
+        return true;
+      };
+      auto issue_dq = [&](int j) -> bool {
+        const int st = j % DQ_STAGES, b = j & 1;
+        if (!sm100::mbar_wait(&ds_full[b], (j >> 1) & 1, err, 54)) return false;
+        sm100::tc_fence_after();
+        const uint32_t k_b = sm100::smem_addr(smem + SmemDQ2::K0 + st * KT_BYTES);
+        const uint32_t ds_b = sm100::smem_addr(smem + SmemDQ2::DS0 + b * DS2_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BKV2 / 16; ++kk)
+          sm100::umma_bf16(TM_DQ, kmajor_desc(ds_b, kk), vmajor64_desc(k_b, kk), ID_DQ, j > 0 || kk > 0);
+        sm100::umma_commit(&kv_empty[st]);
+        sm100::umma_commit(&ds_done[b]);
+        return true;
+      };
+      bool ok = sm100::mbar_wait(qdo_bar, 0, err, 55) && issue_s(0);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        if (j + 1 < ntiles) ok = issue_s(j + 1);
+        if (ok) ok = issue_dq(j);
+      }
+      if (ok) sm100::umma_commit(dq_done);
+    }
+  } else {
+    // eight softmax warps: warp w serves TMEM lanes 32 (w % 4) .. (rows) and the 32-key half (w - 2) / 4
+    const int quarter = warp & 3, half = (warp - 2) >> 2, row = quarter * 32 + lane, qi = m0 + row;
+    const bool row_ok = qi < n;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float LOG2E = 1.4426950408889634f;
+    const float lse_r = row_ok ? lse[(size_t)h * T + q0 + qi] * LOG2E : 0.f;
+    const float del_r = row_ok ? delta[(size_t)h * T + q0 + qi] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int b = j & 1;
+      bool g = sm100::mbar_wait(&s_full[b], (j >> 1) & 1, err, 56);
+      if (g && j >= 2) g = sm100::mbar_wait(&ds_done[b], ((j >> 1) & 1) ^ 1, err, 57);  // dS[b] of j-2 consumed
+      if (!__all_sync(0xffffffffu, g)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const bool pre = j < n_pre;
+      const int kbase = pre ? j * BKV2 : (j - n_pre) * BKV2;
+      const int klim = pre ? pl : min(n, qi + 1);
+      unsigned char* ds_tile = smem + SmemDQ2::DS0 + b * DS2_BYTES;
+      {
+        const int c = half;
+        uint32_t rs[32], rd[32];
+        sm100::tmem_ld32(tmem + b * 64 + lane_off + c * 32, rs);
+        sm100::tmem_ld32(tmem + 128 + b * 64 + lane_off + c * 32, rd);
+        sm100::tmem_ld_wait();
+        float ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const bool vis = row_ok && (kbase + c * 32 + e) < klim;
+          const float pe = vis ? exp2f(__uint_as_float(rs[e]) * scale_log2 - lse_r) : 0.f;
+          ds[e] = pe * (__uint_as_float(rd[e]) - del_r);
+        }
+        store_row32_sw128(ds_tile, row, c, ds);
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&sd_free[b]);
+      sm100::fence_proxy_async_smem();
+      sm100::mbar_arrive(&ds_full[b]);
+    }
+    const bool g = ok && sm100::mbar_wait(dq_done, 0, err, 58);
+    if (__all_sync(0xffffffffu, g)) {
+      sm100::tc_fence_after();
+      __nv_bfloat16* dst = dq + (size_t)(q0 + qi) * Hq * D + (size_t)h * D;
+#pragma unroll 1
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(TM_DQ + lane_off + c * 32, r);
+        sm100::tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            reinterpret_cast<__nv_bfloat162*>(dst + c * 32)[e] =
+                __floats2bfloat162_rn(__uint_as_float(r[2 * e]) * scale, __uint_as_float(r[2 * e + 1]) * scale);
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
 __global__ void delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
                              float* __restrict__ delta, int T, int Hq) {
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
@@ -1114,6 +1319,10 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
   encode_rows(&maps->dout, dout.data_ptr(), T, (long)Hq * D);
   encode_rows(&maps->q64, q.data_ptr(), T, (long)Hq * D, 64);
   encode_rows(&maps->dout64, dout.data_ptr(), T, (long)Hq * D, 64);
+  encode_rows(&maps->k64, k.data_ptr(), T, (long)Hk * D, 64);
+  encode_rows(&maps->v64, v.data_ptr(), T, (long)Hk * D, 64);
+  encode_rows(&maps->pk64, has_p ? pk.data_ptr() : k.data_ptr(), has_p ? pk.size(0) : T, (long)Hk * D, 64);
+  encode_rows(&maps->pv64, has_p ? pv.data_ptr() : v.data_ptr(), has_p ? pv.size(0) : T, (long)Hk * D, 64);
   const int* cup = cu.data_ptr<int>();
   const int* pop = poff.data_ptr<int>();
   const int* plp = plen.data_ptr<int>();
@@ -1142,8 +1351,9 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
     BB_POST_LAUNCH();
   }
   {
-    auto kern = tree_attn_dq_sm100_kernel;
-    const int smem = SmemDQ::TOTAL + 1024;
+    static const bool dq_v1 = getenv("BB_ATTN_DQ") && std::string(getenv("BB_ATTN_DQ")) == "v1";
+    auto kern = dq_v1 ? tree_attn_dq_sm100_kernel : tree_attn_dq2_sm100_kernel;
+    const int smem = (dq_v1 ? SmemDQ::TOTAL : SmemDQ2::TOTAL) + 1024;
     static bool attr = false;
     if (!attr) {
       BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -1152,7 +1362,8 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
     dim3 grid((unsigned)((max_seqlen + BQ - 1) / BQ), (unsigned)B, (unsigned)Hq);
     __nv_bfloat16* dqp = (__nv_bfloat16*)dq.data_ptr();
     void* args[] = {maps, &cup, &pop, &plp, &lsep, &delp, &dqp, &Ti, &Hqi, &Hki, &sl2, &sc, &err};
-    BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(NUM_THREADS), args, smem, stream));
+    BB_CHECK_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(dq_v1 ? NUM_THREADS : DQ2_THREADS), args,
+                                   smem, stream));
     BB_POST_LAUNCH();
   }
   if (has_p) {
