@@ -9,6 +9,12 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, t
 std::vector<torch::Tensor> add_rmsnorm_bwd(torch::Tensor dy, torch::Tensor h, torch::Tensor w, torch::Tensor rstd,
                                            torch::Tensor dh);
 void sumsq_into(torch::Tensor x, torch::Tensor out, bool accumulate);
+torch::Tensor rmsnorm_bwd_acc(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dres,
+                              torch::Tensor dw_acc);
+std::vector<torch::Tensor> qk_norm_rope_bwd_acc(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
+                                                torch::Tensor qw, torch::Tensor kw, torch::Tensor cosb,
+                                                torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk,
+                                                torch::Tensor dqw_acc, torch::Tensor dkw_acc);
 std::vector<torch::Tensor> gated_rmsnorm_fwd(torch::Tensor o, torch::Tensor z, torch::Tensor w, double eps);
 std::vector<torch::Tensor> gated_rmsnorm_bwd(torch::Tensor dy, torch::Tensor o, torch::Tensor z, torch::Tensor w,
                                              torch::Tensor rstd);
@@ -101,6 +107,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, "h = x + res; y = RMSNorm(h) * w -> (y, rstd, h)");
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd, "residual-sum gradient: RMSNorm backward + dh -> (dx, dw)");
+  m.def("rmsnorm_bwd_acc", &rmsnorm_bwd_acc, "RMSNorm backward (+ residual grad) with dw accumulated in place");
+  m.def("qk_norm_rope_bwd_acc", &qk_norm_rope_bwd_acc, "qk-norm + RoPE backward with weight grads accumulated in place");
   m.def("sumsq_into", &sumsq_into, "out[0] (+)= sum(x^2), FP32, deterministic");
   m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd, "GDN output gate: RMSNorm(o) * w * silu(z)");
   m.def("gated_rmsnorm_bwd", &gated_rmsnorm_bwd);

@@ -828,13 +828,21 @@ std::vector<torch::Tensor> rmsnorm_fwd_impl(torch::Tensor x, c10::optional<torch
 }
 
 std::vector<torch::Tensor> rmsnorm_bwd_impl(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
-                                            c10::optional<torch::Tensor> dres) {
+                                            c10::optional<torch::Tensor> dres,
+                                            c10::optional<torch::Tensor> dw_acc = c10::nullopt) {
   check_bf16(dy, "dy");
   check_bf16(x, "x");
   const int H = x.size(-1);
   const long rows = x.numel() / H;
   auto dx = torch::empty_like(x);
-  auto dw = torch::zeros({H}, x.options().dtype(at::kFloat));
+  torch::Tensor dw;
+  if (dw_acc) {  // accumulate straight into an FP32 gradient buffer (e.g. the weight's main_grad)
+    TORCH_CHECK(dw_acc->is_cuda() && dw_acc->scalar_type() == at::kFloat && dw_acc->is_contiguous() &&
+                    dw_acc->numel() == H, "rmsnorm_bwd: dw accumulator must be a contiguous FP32 [H] tensor");
+    dw = *dw_acc;
+  } else {
+    dw = torch::zeros({H}, x.options().dtype(at::kFloat));
+  }
   if (dres) {
     check_bf16(*dres, "dres");
     TORCH_CHECK(dres->sizes() == x.sizes(), "rmsnorm_bwd: residual gradient shape must match x");
@@ -876,6 +884,13 @@ std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch:
 // h = x + res; y = RMSNorm(h) * w  ->  {y, rstd, h}
 std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, torch::Tensor w, double eps) {
   return rmsnorm_fwd_impl(x, res, w, eps);
+}
+
+// dx (+ dres when given, i.e. non-empty) with dw accumulated into dw_acc (FP32 [H]) -> dx
+torch::Tensor rmsnorm_bwd_acc(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dres,
+                              torch::Tensor dw_acc) {
+  c10::optional<torch::Tensor> r = dres.numel() ? c10::optional<torch::Tensor>(dres) : c10::nullopt;
+  return rmsnorm_bwd_impl(dy, x, w, rstd, r, dw_acc)[0];
 }
 
 // d(x) = d(res) = rmsnorm_bwd(dy) + dh  ->  {dsum, dw}
@@ -932,9 +947,11 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor q, torch::Tensor k, to
   return {qo, ko, rq, rk};
 }
 
-std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
-                                            torch::Tensor qw, torch::Tensor kw, torch::Tensor cosb,
-                                            torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk) {
+namespace {
+std::vector<torch::Tensor> qk_norm_rope_bwd_impl(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
+                                                 torch::Tensor qw, torch::Tensor kw, torch::Tensor cosb,
+                                                 torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk,
+                                                 torch::Tensor dqw_acc, torch::Tensor dkw_acc) {
   check_bf16(dqo, "dq");
   check_bf16(dko, "dk");
   check_qk_view(q, "q");
@@ -944,8 +961,14 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko
               "cos / sin tables must be contiguous and 16-byte aligned");
   const int T = q.size(0), Hq = q.size(1), Hk = k.size(1), D = q.size(2);
   auto dq = torch::empty({T, Hq, D}, q.options()), dk = torch::empty({T, Hk, D}, k.options());
-  auto dqw = torch::zeros({D}, q.options().dtype(at::kFloat));
-  auto dkw = torch::zeros({D}, q.options().dtype(at::kFloat));
+  auto acc_ok = [&](const torch::Tensor& t) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous() && t.numel() == D,
+                "qk_norm_rope_bwd: weight-gradient accumulators must be contiguous FP32 [D] tensors");
+    return t;
+  };
+  // empty accumulators: fresh zeroed outputs; otherwise accumulate into them (e.g. the weights' main_grad)
+  auto dqw = dqw_acc.numel() ? acc_ok(dqw_acc) : torch::zeros({D}, q.options().dtype(at::kFloat));
+  auto dkw = dkw_acc.numel() ? acc_ok(dkw_acc) : torch::zeros({D}, q.options().dtype(at::kFloat));
   if (T == 0) return {dq, dk, dqw, dkw};
   const int threads = 256;
   const long items = (long)T * ((Hq + Hk + kQKRows - 1) / kQKRows);
@@ -972,6 +995,23 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko
 #undef BB_QKB
   BB_POST_LAUNCH();
   return {dq, dk, dqw, dkw};
+}
+}  // namespace
+
+std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
+                                            torch::Tensor qw, torch::Tensor kw, torch::Tensor cosb,
+                                            torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk) {
+  auto none = torch::empty({0}, q.options().dtype(at::kFloat));
+  return qk_norm_rope_bwd_impl(dqo, dko, q, k, qw, kw, cosb, sinb, rq, rk, none, none);
+}
+
+// As qk_norm_rope_bwd, with the q / k norm weight gradients accumulated into dqw_acc / dkw_acc -> {dq, dk}
+std::vector<torch::Tensor> qk_norm_rope_bwd_acc(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
+                                                torch::Tensor qw, torch::Tensor kw, torch::Tensor cosb,
+                                                torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk,
+                                                torch::Tensor dqw_acc, torch::Tensor dkw_acc) {
+  auto r = qk_norm_rope_bwd_impl(dqo, dko, q, k, qw, kw, cosb, sinb, rq, rk, dqw_acc, dkw_acc);
+  return {r[0], r[1]};
 }
 
 torch::Tensor swiglu_fwd(torch::Tensor gu) {

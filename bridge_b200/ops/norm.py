@@ -17,6 +17,15 @@ from torch import Tensor
 from ._ext import kernels, on_gpu
 
 
+def _main_grad(w: Tensor):
+    """The weight's FP32 gradient accumulator when it has one (the engine's ``main_grad`` arena view):
+    the backward kernels then add the weight gradient into it and autograd gets ``None`` for it."""
+    g = getattr(w, "main_grad", None)
+    if g is not None and g.dtype == torch.float32 and g.is_cuda and g.is_contiguous():
+        return g.view(-1)
+    return None
+
+
 def rmsnorm_reference(x: Tensor, weight: Tensor, eps: float) -> Tensor:
     xf = x.float()
     y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
@@ -38,7 +47,12 @@ class _RMSNormFn(torch.autograd.Function):
     def backward(ctx, dy):
         m = kernels()
         x2, weight, rstd = ctx.saved_tensors
-        dx, dw = m.rmsnorm_bwd(dy.reshape(x2.shape).contiguous(), x2, weight.contiguous(), rstd)
+        dy2 = dy.reshape(x2.shape).contiguous()
+        acc = _main_grad(weight)
+        if acc is not None:
+            dx = m.rmsnorm_bwd_acc(dy2, x2, weight.contiguous(), rstd, dy2.new_empty(0), acc)
+            return dx.view(ctx.shape), None, None
+        dx, dw = m.rmsnorm_bwd(dy2, x2, weight.contiguous(), rstd)
         return dx.view(ctx.shape), dw.to(weight.dtype), None
 
 
@@ -66,10 +80,15 @@ class _AddRMSNormFn(torch.autograd.Function):
         if dy is None:
             return dh, dh, None, None
         dy2 = dy.reshape(h.shape).contiguous()
+        dh2 = dh.reshape(h.shape).contiguous() if dh is not None else dy2.new_empty(0)
+        acc = _main_grad(weight)
+        if acc is not None:
+            d = m.rmsnorm_bwd_acc(dy2, h, weight.contiguous(), rstd, dh2, acc).view(ctx.shape)
+            return d, d, None, None
         if dh is None:
             d, dw = m.rmsnorm_bwd(dy2, h, weight.contiguous(), rstd)
         else:
-            d, dw = m.add_rmsnorm_bwd(dy2, h, weight.contiguous(), rstd, dh.reshape(h.shape).contiguous())
+            d, dw = m.add_rmsnorm_bwd(dy2, h, weight.contiguous(), rstd, dh2)
         d = d.view(ctx.shape)
         return d, d, dw.to(weight.dtype), None
 
@@ -130,6 +149,10 @@ class _QKNormRopeFn(torch.autograd.Function):
     def backward(ctx, dqo, dko):
         m = kernels()
         q, k, qw, kw, cos, sin, rq, rk = ctx.saved_tensors
+        aq, ak = _main_grad(qw), _main_grad(kw)
+        if aq is not None and ak is not None:
+            dq, dk = m.qk_norm_rope_bwd_acc(dqo.contiguous(), dko.contiguous(), q, k, qw, kw, cos, sin, rq, rk, aq, ak)
+            return dq, dk, None, None, None, None, None
         dq, dk, dqw, dkw = m.qk_norm_rope_bwd(dqo.contiguous(), dko.contiguous(), q, k, qw, kw, cos, sin, rq, rk)
         return dq, dk, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None
 

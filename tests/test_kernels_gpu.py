@@ -298,3 +298,48 @@ def test_sumsq_into(n):
     assert abs(out.item() - ref.item()) <= 1e-5 * ref.item() + 1e-6
     kernels().sumsq_into(x, out, True)
     assert abs(out.item() - 2 * ref.item()) <= 2e-5 * ref.item() + 1e-6
+
+
+def test_norm_weight_grads_accumulate_into_main_grad():
+    """With an FP32 ``main_grad`` on the weight (the engine's gradient arena), the RMSNorm, fused add +
+    RMSNorm and qk-norm + RoPE backward kernels add the weight gradient into it in place and hand
+    autograd no gradient for the weight."""
+    from bridge_b200.ops.norm import add_rmsnorm, qk_norm_rope, rmsnorm, rope_cos_sin
+
+    torch.manual_seed(3)
+    T, H = 300, 2560
+
+    def grads(use_main):
+        w1 = (1 + 0.1 * torch.randn(H, device=DEV, generator=torch.Generator(device=DEV).manual_seed(1))).to(
+            torch.bfloat16).requires_grad_()
+        w2 = w1.detach().clone().requires_grad_()
+        qw = torch.linspace(0.5, 1.5, 128, device=DEV).to(torch.bfloat16).requires_grad_()
+        kw = torch.linspace(1.5, 0.5, 128, device=DEV).to(torch.bfloat16).requires_grad_()
+        base = {}
+        for name, w in (("w1", w1), ("w2", w2), ("qw", qw), ("kw", kw)):
+            base[name] = torch.full(w.shape, 0.25, device=DEV)
+            if use_main:
+                w.main_grad = base[name].clone()
+        g = torch.Generator(device=DEV).manual_seed(2)
+        x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16).requires_grad_()
+        r = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
+        q = torch.randn(T, 8, 128, device=DEV, generator=g).to(torch.bfloat16).requires_grad_()
+        k = torch.randn(T, 2, 128, device=DEV, generator=g).to(torch.bfloat16).requires_grad_()
+        cos, sin = rope_cos_sin(torch.arange(T, device=DEV), 128, 1e6)
+        y1 = rmsnorm(x, w1, 1e-6)
+        h, y2 = add_rmsnorm(x, r, w2, 1e-6)
+        qo, ko = qk_norm_rope(q, k, qw, kw, cos, sin, 1e-6)
+        loss = (y1.float() ** 2).sum() + (y2.float() * h.float()).sum() + (qo.float() ** 2).sum() + ko.float().sum()
+        loss.backward()
+        out = {"dx": x.grad.float(), "dq": q.grad.float(), "dk": k.grad.float()}
+        for name, w in (("w1", w1), ("w2", w2), ("qw", qw), ("kw", kw)):
+            if use_main:
+                assert w.grad is None, name
+                out[name] = w.main_grad - base[name]
+            else:
+                out[name] = w.grad.float()
+        return out
+
+    a, b = grads(True), grads(False)
+    for name in a:
+        _close(a[name], b[name], 1e-3, 2e-2, name)
