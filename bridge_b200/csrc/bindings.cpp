@@ -9,6 +9,8 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, t
 std::vector<torch::Tensor> add_rmsnorm_bwd(torch::Tensor dy, torch::Tensor h, torch::Tensor w, torch::Tensor rstd,
                                            torch::Tensor dh);
 void sumsq_into(torch::Tensor x, torch::Tensor out, bool accumulate);
+torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w, int64_t start);
+void embedding_bwd_acc(torch::Tensor ids, torch::Tensor dy, torch::Tensor grad, int64_t start);
 torch::Tensor rmsnorm_bwd_acc(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dres,
                               torch::Tensor dw_acc);
 std::vector<torch::Tensor> qk_norm_rope_bwd_acc(torch::Tensor dqo, torch::Tensor dko, torch::Tensor q, torch::Tensor k,
@@ -109,6 +111,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd, "residual-sum gradient: RMSNorm backward + dh -> (dx, dw)");
   m.def("rmsnorm_bwd_acc", &rmsnorm_bwd_acc, "RMSNorm backward (+ residual grad) with dw accumulated in place");
   m.def("qk_norm_rope_bwd_acc", &qk_norm_rope_bwd_acc, "qk-norm + RoPE backward with weight grads accumulated in place");
+  m.def("embedding_fwd", &embedding_fwd, "vocab-parallel embedding lookup (zero rows outside this rank)");
+  m.def("embedding_bwd_acc", &embedding_bwd_acc, "embedding backward: scatter-add dy rows into an FP32 grad");
   m.def("sumsq_into", &sumsq_into, "out[0] (+)= sum(x^2), FP32, deterministic");
   m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd, "GDN output gate: RMSNorm(o) * w * silu(z)");
   m.def("gated_rmsnorm_bwd", &gated_rmsnorm_bwd);

@@ -748,6 +748,48 @@ __global__ void sum_partials_kernel(const float* __restrict__ part, int n, float
   }
 }
 
+// ------------------------------------------------------------------------------------ embedding
+// Vocab-parallel lookup (rows [start, start + rows) of the full table live here; other ids give zero
+// rows) and its backward as a scatter-add of dy rows into the FP32 gradient buffer (16-byte float4
+// atomics; repeated ids add in arbitrary order).  One warp per token, 16-byte accesses.
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
+                                     __nv_bfloat16* __restrict__ out, int T, int H, long start, long rows) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31, nv = H / 8;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    const long r = ids[t] - start;
+    const bool ok = r >= 0 && r < rows;
+    bf16x8* dst = reinterpret_cast<bf16x8*>(out + (size_t)t * H);
+    const bf16x8* src = reinterpret_cast<const bf16x8*>(w + (size_t)(ok ? r : 0) * H);
+    for (int i = lane; i < nv; i += 32) {
+      bf16x8 v;
+      if (ok) {
+        v = src[i];
+      } else {
+        float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        v = bb::pack8(z);
+      }
+      dst[i] = v;
+    }
+  }
+}
+
+__global__ void embedding_bwd_acc_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dy,
+                                         float* __restrict__ g, int T, int H, long start, long rows) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31, nv = H / 8;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    const long r = ids[t] - start;
+    if (r < 0 || r >= rows) continue;
+    const bf16x8* src = reinterpret_cast<const bf16x8*>(dy + (size_t)t * H);
+    float4* dst = reinterpret_cast<float4*>(g + (size_t)r * H);
+    for (int i = lane; i < nv; i += 32) {
+      float f[8];
+      bb::unpack8(src[i], f);
+      atomicAdd(dst + 2 * i, make_float4(f[0], f[1], f[2], f[3]));
+      atomicAdd(dst + 2 * i + 1, make_float4(f[4], f[5], f[6], f[7]));
+    }
+  }
+}
+
 int sm_count() {
   static int n = 0;
   if (!n) {
@@ -1145,5 +1187,36 @@ void sumsq_into(torch::Tensor x, torch::Tensor out, bool accumulate) {
   sumsq_partial_kernel<<<blocks, 256, 0, stream>>>(x.data_ptr<float>(), n, vec, part.data_ptr<float>());
   BB_POST_LAUNCH();
   sum_partials_kernel<<<1, 1024, 0, stream>>>(part.data_ptr<float>(), blocks, out.data_ptr<float>(), accumulate);
+  BB_POST_LAUNCH();
+}
+
+// out[t] = weight[ids[t] - start] (zero rows for ids outside this rank's [start, start + rows))
+torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w, int64_t start) {
+  check_bf16(w, "embedding weight");
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.dim() == 1,
+              "embedding: ids must be a contiguous CUDA int64 vector");
+  const int T = ids.numel(), H = w.size(1);
+  TORCH_CHECK(H % 8 == 0, "embedding: hidden size must be a multiple of 8");
+  auto out = torch::empty({T, H}, w.options());
+  if (T == 0) return out;
+  const int blocks = bb::resident_grid(embedding_fwd_kernel, 256, 0, (T + 7) / 8);
+  embedding_fwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)out.data_ptr(), T, H, start,
+      w.size(0));
+  BB_POST_LAUNCH();
+  return out;
+}
+
+// grad[ids[t] - start] += dy[t] for ids inside this rank's rows; grad is FP32 [rows, H] (e.g. main_grad)
+void embedding_bwd_acc(torch::Tensor ids, torch::Tensor dy, torch::Tensor grad, int64_t start) {
+  check_bf16(dy, "embedding dy");
+  TORCH_CHECK(grad.is_cuda() && grad.scalar_type() == at::kFloat && grad.is_contiguous() && grad.dim() == 2 &&
+                  grad.size(1) == dy.size(1) && (reinterpret_cast<uintptr_t>(grad.data_ptr()) & 15) == 0,
+              "embedding_bwd: grad must be a contiguous, 16-byte aligned FP32 [rows, H] tensor");
+  const int T = ids.numel(), H = dy.size(1);
+  if (T == 0) return;
+  const int blocks = bb::resident_grid(embedding_bwd_acc_kernel, 256, 0, (T + 7) / 8);
+  embedding_bwd_acc_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>(), (const __nv_bfloat16*)dy.data_ptr(), grad.data_ptr<float>(), T, H, start, grad.size(0));
   BB_POST_LAUNCH();
 }

@@ -180,13 +180,10 @@ class VocabParallelEmbedding(nn.Module):
         self.weight.tp_split_dim = 0  # type: ignore[attr-defined]
 
     def forward(self, ids: Tensor) -> Tensor:
-        if tp_size(self.group) == 1:
-            return torch.nn.functional.embedding(ids, self.weight)
-        local = ids - self.start
-        outside = (local < 0) | (local >= self.per_rank)
-        out = torch.nn.functional.embedding(local.clamp(0, self.per_rank - 1), self.weight)
-        out = out.masked_fill(outside[:, None], 0.0)
-        return reduce_from_tp(out, self.group)
+        from ..ops.embedding import embedding
+
+        out = embedding(ids, self.weight, self.start)
+        return out if tp_size(self.group) == 1 else reduce_from_tp(out, self.group)
 
 
 def scaled_init_std(std: float, num_layers: int) -> float:

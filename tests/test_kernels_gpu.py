@@ -343,3 +343,31 @@ def test_norm_weight_grads_accumulate_into_main_grad():
     a, b = grads(True), grads(False)
     for name in a:
         _close(a[name], b[name], 1e-3, 2e-2, name)
+
+
+@pytest.mark.parametrize("start,use_main", [(0, True), (0, False), (500, True)])
+def test_embedding_lookup_and_scatter_add(start, use_main):
+    """Vocab-parallel lookup (ids outside this rank's rows give zero rows) and the backward's scatter-add
+    into main_grad (or a fresh gradient) against torch's embedding, repeated ids included."""
+    from bridge_b200.ops.embedding import embedding
+
+    torch.manual_seed(start + int(use_main))
+    V, H, T = 1000, 256, 4000
+    w = (0.1 * torch.randn(V, H, device=DEV)).to(torch.bfloat16).requires_grad_()
+    ids = torch.randint(0, 1500, (T,), device=DEV)
+    if use_main:
+        w.main_grad = torch.full((V, H), 0.5, device=DEV)
+    out = embedding(ids, w, start)
+    local = ids - start
+    inside = (local >= 0) & (local < V)
+    ref = torch.zeros(T, H, device=DEV)
+    ref[inside] = w.detach().float()[local[inside]]
+    _close(out, ref, 0, 0, "out")
+    dy = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    out.backward(dy)
+    g_ref = torch.zeros(V, H, device=DEV).index_add_(0, local[inside], dy.float()[inside])
+    if use_main:
+        assert w.grad is None
+        _close(w.main_grad - 0.5, g_ref, 1e-4, 1e-5, "main_grad")
+    else:
+        _close(w.grad, g_ref, 1e-2, 1e-2, "grad")
