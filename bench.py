@@ -1,11 +1,15 @@
 #!/usr/bin/env python
 """PPO actor-update throughput with tree-prefix reuse on B200.
 
-Config (BASELINE config #2 shape): Qwen3-4B (36 layers, hidden 2560, 32q/8kv heads of 128,
-FFN 9728, vocab 151936, qk-RMSNorm, RoPE 1e6), bf16 weights with FP32 master weights and Adam
-state; every tree is a 512-token prompt with 8 sibling responses of 512 tokens; ids uniform from a
-seed, advantages ~ N(0,1), response mask all ones; random-init weights (no checkpoint access).
+Config (BASELINE config #2): Qwen3-4B (36 layers, hidden 2560, 32q/8kv heads of 128, FFN 9728,
+vocab 151936, qk-RMSNorm, RoPE 1e6), bf16 weights with FP32 master weights and Adam state; every
+tree is a 512-token prompt with 8 sibling responses of 512 tokens; ids uniform from a seed,
+advantages ~ N(0,1), response mask all ones; random-init weights (no checkpoint access).
 Weak scaling: ``--trees-per-gpu`` trees per GPU (8 -> 64 trees on 8 GPUs, the named config).
+
+Parallel layout: by default the named config's TP2 x CP4 at 8 GPUs, scaled down along the same axes
+(1 GPU: none, 2: TP2, 4: TP2 x CP2, 8: TP2 x CP4); TP runs with sequence parallelism.  ``--tp`` /
+``--cp`` override it (``--tp 1 --cp 1`` = pure data parallelism).
 
 One step = plan the token-trie forest, forward + backward of every segment (prefix KV relayed),
 PPO loss over all supervised tokens, DP gradient finalisation, fused AdamW update.
@@ -50,13 +54,37 @@ def parse() -> argparse.Namespace:
     p.add_argument("--resp", type=int, default=512)
     p.add_argument("--token-budget", type=int, default=int(os.environ.get("TPR_TOKEN_BUDGET", "16384")))
     p.add_argument("--mode", default=os.environ.get("TPR_FOREST_MODE", "retain"))
-    p.add_argument("--tp", type=int, default=1)
-    p.add_argument("--cp", type=int, default=1)
+    p.add_argument("--tp", type=int, default=None, help="default: the config-#2 layout for --gpus")
+    p.add_argument("--cp", type=int, default=None, help="default: the config-#2 layout for --gpus")
+    p.add_argument("--no-sp", action="store_true", help="TP without sequence parallelism")
     p.add_argument("--dp-comm", default="auto", choices=["auto", "nvlink", "nccl"],
                    help="DP gradient path: fused NVLink P2P kernels + sharded optimizer, or NCCL all-reduce")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
+
+
+DEFAULT_LAYOUT = {1: (1, 1), 2: (2, 1), 4: (2, 2), 8: (2, 4)}   # gpus -> (tp, cp), config #2 scaled down
+
+
+def layout(args) -> tuple[int, int]:
+    tp_d, cp_d = DEFAULT_LAYOUT.get(args.gpus, (1, 1))
+    return (tp_d if args.tp is None else args.tp), (cp_d if args.cp is None else args.cp)
+
+
+def parallelism_name(tp: int, cp: int, dp: int) -> str:
+    parts = [f"tp{tp}"] if tp > 1 else []
+    parts += [f"cp{cp}"] if cp > 1 else []
+    parts += [f"dp{dp}"] if dp > 1 or not parts else []
+    return "".join(parts)
+
+
+def local_gpu_indices() -> str | None:
+    """nvidia-smi indices of the GPUs this node's ranks use (local rank i -> visible device i)."""
+    n = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    ids = [x.strip() for x in vis.split(",") if x.strip()] if vis else [str(i) for i in range(n)]
+    return ",".join(ids[:n]) if ids else None
 
 
 def reference_unavailable(args) -> None:
@@ -70,10 +98,11 @@ def reference_unavailable(args) -> None:
         }), flush=True)
 
 
-def synthetic_batch(args, rank: int, dp: int, vocab: int, device_pin: bool) -> dict:
+def synthetic_batch(args, n_trees: int, rank: int, dp: int, vocab: int, device_pin: bool) -> dict:
+    """``n_trees`` trees for data-parallel rank ``rank`` (the mini-batch of one model replica)."""
     g = torch.Generator().manual_seed(args.seed * 1000003 + rank)
     ids, masks, old, adv, uids = [], [], [], [], []
-    for t in range(args.trees_per_gpu):
+    for t in range(n_trees):
         prompt = torch.randint(0, vocab, (args.prefix,), generator=g)
         for s in range(args.siblings):
             resp = torch.randint(0, vocab, (args.resp,), generator=g)
@@ -87,7 +116,7 @@ def synthetic_batch(args, rank: int, dp: int, vocab: int, device_pin: bool) -> d
         masks = [x.pin_memory() for x in masks]
         old = [x.pin_memory() for x in old]
         adv = [x.pin_memory() for x in adv]
-    per_rank = args.trees_per_gpu * args.siblings * args.resp
+    per_rank = n_trees * args.siblings * args.resp
     return {"input_ids": ids, "response_mask": masks, "old_log_probs": old, "advantages": adv, "uid": uids,
             "temperature": 1.0, "batch_num_tokens": per_rank * dp, "dp_size": dp}
 
@@ -161,14 +190,17 @@ def main() -> None:
     if world > 1:
         collective_probe(device=dev)
     cfg = get_config(args.model)
-    ec = EngineConfig(tensor_model_parallel_size=args.tp, context_parallel_size=args.cp,
+    tp, cp = layout(args)
+    sp = tp > 1 and not args.no_sp
+    ec = EngineConfig(tensor_model_parallel_size=tp, context_parallel_size=cp, sequence_parallel=sp,
                       token_budget=args.token_budget, forest_mode=args.mode,
-                      tpr_cp_backend="ring" if args.cp > 1 else None, dp_comm=args.dp_comm)
+                      tpr_cp_backend="ring" if cp > 1 else None, dp_comm=args.dp_comm)
     eng = TPREngine(cfg, ec, AdamWConfig(lr=1e-6), device=dev, seed=args.seed)
     dp = eng.parallel.dp
-    batch = synthetic_batch(args, eng.parallel.dp_rank, dp, cfg.vocab_size, device_pin=True)
+    n_trees = args.trees_per_gpu * world                  # weak scaling: trees per GPU fixed
+    batch = synthetic_batch(args, n_trees // dp, eng.parallel.dp_rank, dp, cfg.vocab_size, device_pin=True)
     prepared = prepare_tpr_batch(eng, batch)
-    ppo_tokens_global = args.trees_per_gpu * args.siblings * args.resp * dp
+    ppo_tokens_global = n_trees * args.siblings * args.resp
     m = ext()
 
     def device_step():
@@ -181,7 +213,7 @@ def main() -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES")) if rank == 0 else None
+    sampler = ClockSampler(local_gpu_indices()) if rank == 0 else None
     launches0 = m.launch_count()
     torch.cuda.synchronize()
     if world > 1:
@@ -225,6 +257,9 @@ def main() -> None:
 
     if rank == 0:
         value = ppo_tokens_global / (ms / 1e3)
+        par = parallelism_name(tp, cp, dp)
+        named = (args.model, par, world, n_trees, args.prefix, args.siblings, args.resp) == \
+            ("qwen3_4b", "tp2cp4", 8, 64, 512, 8, 512)
         line = {
             "metric": METRIC,
             "value": value,
@@ -235,14 +270,15 @@ def main() -> None:
             "ms_per_step": ms,
             "higher_is_better": True,
             "scaling": "weak",
-            "vs_baseline": value / PUBLISHED_TPR_TOKENS_PER_S,
+            # the published figure is TPR at TP2 x CP4 on 8 Ascend 910B; it is quoted only for that layout
+            "vs_baseline": value / PUBLISHED_TPR_TOKENS_PER_S if named else None,
             "dtype": "bf16",
             "data": "synthetic (uniform token ids from seed, advantages N(0,1), random-init weights)",
             "config": {
-                "model": args.model, "global_batch": args.trees_per_gpu * args.siblings * dp, "seq_len":
-                args.prefix + args.resp, "parallelism": f"dp{dp}" + (f"tp{args.tp}" if args.tp > 1 else "") +
-                (f"cp{args.cp}" if args.cp > 1 else ""),
-                "trees": args.trees_per_gpu * dp, "prefix": args.prefix, "siblings": args.siblings,
+                "model": args.model, "global_batch": n_trees * args.siblings, "seq_len": args.prefix + args.resp,
+                "parallelism": par, "sequence_parallel": sp,
+                "cp_placement": "segment-granular (forest executor)" if cp > 1 else None,
+                "trees": n_trees, "prefix": args.prefix, "siblings": args.siblings,
                 "response": args.resp, "ppo_tokens_per_step": ppo_tokens_global, "forest_mode": args.mode,
                 "token_budget": args.token_budget,
                 "dp_comm": "nvlink-p2p-fused" if eng.symm_heap is not None else ("nccl" if world > 1 else "none"),

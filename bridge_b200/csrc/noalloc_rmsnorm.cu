@@ -1,43 +1,34 @@
-// RMSNorm backward that allocates nothing: C entry point for callers that cannot allocate.
+// RMSNorm backward that allocates nothing: the C entry point declared in noalloc.h (which states
+// who needs it, its limits and its contract).
 //
 // NOTE: this entry point has no counterpart in the reference implementation; it is an addition of
 // this library.
 //
-// Who needs it.  Some callers cannot call cudaMalloc (or torch's caching allocator) at the point
-// where they run this op: a C/C++ host runtime that owns every device allocation itself and hands
-// kernels only pre-planned buffers, or a serving / training loop that forbids allocation after
-// start-up because a cudaMalloc can synchronize the device and stall the other streams.  Such a
-// caller passes its inputs and outputs; the FP32 reduction scratch this kernel needs lives in a
-// fixed static device array instead of a per-call allocation.
-//
-// Contract.
-//   * Scratch: `g_noalloc_rms_scratch`, kNoAllocScratchFloats FP32 values (4 MiB).  Every GPU that
-//     loads this library holds it until the process exits.
-//   * Limits: 8 <= H <= 32768 with H % 8 == 0.  The kernel uses nblocks x H scratch floats and picks
-//     nblocks so that it fits; H above the limit is rejected (cudaErrorInvalidValue, nothing launched,
-//     message available from bb_noalloc_last_error()).
-//   * The first call on a device, with that device current, resolves the device address of the
-//     scratch array (cudaGetSymbolAddress) and caches it per device.  Make that first call before any
-//     stream capture.
-//   * Every call shares the one array and it keeps the previous call's contents.  Each call fully
-//     overwrites the part it reads, so nothing has to start at zero; but calls that overlap on the
-//     GPU (different streams without ordering) race on the scratch and must be serialized by the
-//     caller.
-//   * No cudaMalloc, cudaFree or allocating library routine is called.
+// The FP32 weight-gradient partials live in `g_noalloc_rms_scratch` (BB_NOALLOC_SCRATCH_BYTES).  The
+// partial kernel uses nblocks x H of it and nblocks is capped so that it fits.  Host code must not use
+// the array's name as a device address: the first call on each device resolves it with
+// cudaGetSymbolAddress (once per device, std::call_once) and every call passes that pointer.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
+#include <mutex>
+
+#include "noalloc.h"
+
 namespace {
 
-constexpr long kNoAllocScratchFloats = 1l << 20;  // 4 MiB
+constexpr long kNoAllocScratchFloats = BB_NOALLOC_SCRATCH_BYTES / sizeof(float);
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_rms_scratch[kNoAllocScratchFloats];
 
-float* g_scratch_ptr[kMaxDevices] = {nullptr};
-char g_last_error[256] = "";
+std::once_flag g_scratch_once[kMaxDevices];
+std::atomic<float*> g_scratch_ptr[kMaxDevices];
+std::atomic<int> g_scratch_err[kMaxDevices];
+thread_local char g_last_error[256] = "";
 
 __device__ __forceinline__ float wsum(float v) {
 #pragma unroll
@@ -87,28 +78,31 @@ int fail(cudaError_t e, const char* msg) {
 
 extern "C" {
 
-// Last error message of the no-allocation entry points (empty after a successful call).
-const char* bb_noalloc_last_error() { return g_last_error; }
+const char* bb_noalloc_last_error(void) { return g_last_error; }
 
-// dx[rows, H] (bf16) and dw[H] (FP32, overwritten) of y = x * rstd * w given dy, x, w, rstd.
-// Returns 0 (cudaSuccess) or a cudaError_t value; see the contract at the top of this file.
 int bb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw,
                            long rows, int H, cudaStream_t stream) {
   g_last_error[0] = '\0';
-  if (H < 8 || H > 32768 || (H % 8) != 0)
+  if (H < 8 || H > BB_NOALLOC_MAX_HIDDEN || (H % 8) != 0)
     return fail(cudaErrorInvalidValue, "bb_rmsnorm_bwd_noalloc: H must be a multiple of 8 in [8, 32768]");
   if (rows < 0) return fail(cudaErrorInvalidValue, "bb_rmsnorm_bwd_noalloc: rows must be >= 0");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(e, "bb_rmsnorm_bwd_noalloc: cudaGetDevice failed");
   if (dev < 0 || dev >= kMaxDevices) return fail(cudaErrorInvalidDevice, "bb_rmsnorm_bwd_noalloc: device index");
-  if (g_scratch_ptr[dev] == nullptr) {
-    // One-time set-up on this device (the device is current): host code may not use the symbol
-    // itself as a device address, so resolve it.
+  // One-time set-up on this device (the device is current): host code may not use the symbol itself
+  // as a device address, so resolve it.  call_once makes concurrent first calls from several host
+  // threads safe.
+  std::call_once(g_scratch_once[dev], [dev]() {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_rms_scratch);
-    if (e != cudaSuccess || p == nullptr) return fail(e, "bb_rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed");
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+    const cudaError_t se = cudaGetSymbolAddress(&p, g_noalloc_rms_scratch);
+    g_scratch_err[dev].store(se == cudaSuccess && p == nullptr ? (int)cudaErrorInvalidSymbol : (int)se);
+    g_scratch_ptr[dev].store(static_cast<float*>(p));
+  });
+  float* scratch = g_scratch_ptr[dev].load();
+  if (scratch == nullptr) {
+    const int se = g_scratch_err[dev].load();
+    return fail(se ? (cudaError_t)se : cudaErrorInvalidSymbol, "bb_rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed");
   }
   if (rows == 0) {
     e = cudaMemsetAsync(dw, 0, sizeof(float) * (size_t)H, stream);
@@ -127,10 +121,10 @@ int bb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void* w, const f
   }
   rms_bwd_partial<<<nblocks, threads, smem, stream>>>(
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
-      rstd, static_cast<__nv_bfloat16*>(dx), g_scratch_ptr[dev], rows, H);
+      rstd, static_cast<__nv_bfloat16*>(dx), scratch, rows, H);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(e, "bb_rmsnorm_bwd_noalloc: partial kernel launch failed");
-  rms_bwd_colsum<<<(H + 255) / 256, 256, 0, stream>>>(g_scratch_ptr[dev], dw, nblocks, H);
+  rms_bwd_colsum<<<(H + 255) / 256, 256, 0, stream>>>(scratch, dw, nblocks, H);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(e, "bb_rmsnorm_bwd_noalloc: column-sum kernel launch failed");
   return 0;

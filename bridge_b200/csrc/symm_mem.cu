@@ -303,7 +303,7 @@ void symm_clear_error() {
 // Row-indexed P2P movement over symmetric buffers (context-parallel KV exchange, MoE dispatch):
 //   p2p_gather_rows  out[i, :] = peer[src_rank[i]][src_row[i], :]              (bf16 rows)
 //   p2p_reduce_rows  out[i, :] = sum_r peer[r][src_row[i], :]  (+ add[i, :])    (bf16 or fp32 rows,
-//                    fixed rank order, FP32 accumulation, bf16 out)
+//                    fixed rank order, FP32 accumulation, bf16 or fp32 out)
 // One warp per row, 16-byte vectors, several loads in flight per lane.
 namespace {
 
@@ -332,9 +332,9 @@ __global__ void p2p_gather_rows_kernel(PeerPtrs peers, const int* __restrict__ s
   }
 }
 
-template <bool SRC_F32>
+template <bool SRC_F32, bool OUT_F32>
 __global__ void p2p_reduce_rows_kernel(PeerPtrs peers, int n, const int* __restrict__ src_row,
-                                       const bb::bf16x8* __restrict__ add, bb::bf16x8* __restrict__ out, int rows,
+                                       const bb::bf16x8* __restrict__ add, void* __restrict__ out_raw, int rows,
                                        int vecs /* 8-element vectors per row */) {
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
@@ -358,7 +358,13 @@ __global__ void p2p_reduce_rows_kernel(PeerPtrs peers, int n, const int* __restr
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] += f[e];
       }
-      out[(size_t)i * vecs + v] = bb::pack8(acc);
+      if (OUT_F32) {
+        float4* o = reinterpret_cast<float4*>(out_raw) + 2 * ((size_t)i * vecs + v);
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      } else {
+        reinterpret_cast<bb::bf16x8*>(out_raw)[(size_t)i * vecs + v] = bb::pack8(acc);
+      }
     }
   }
 }
@@ -383,28 +389,36 @@ void p2p_gather_rows(torch::Tensor out, std::vector<int64_t> peers, torch::Tenso
 
 void p2p_reduce_rows(torch::Tensor out, std::vector<int64_t> peers, torch::Tensor src_row, bool src_f32,
                      c10::optional<torch::Tensor> add) {
-  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.dim() == 2 && out.scalar_type() == at::kBFloat16,
-              "p2p_reduce_rows: bf16 out [rows, width]");
+  const bool out_f32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.dim() == 2 &&
+                  (out.scalar_type() == at::kBFloat16 || out_f32),
+              "p2p_reduce_rows: bf16 or fp32 out [rows, width]");
+  TORCH_CHECK(!out_f32 || src_f32, "p2p_reduce_rows: an fp32 out needs fp32 source rows");
   TORCH_CHECK(out.size(1) % 8 == 0, "p2p_reduce_rows: width must be a multiple of 8");
   const int rows = (int)out.size(0);
   TORCH_CHECK(src_row.numel() == rows && src_row.scalar_type() == at::kInt && src_row.is_cuda(),
               "p2p_reduce_rows: int32 row index on the device");
   const bb::bf16x8* addp = nullptr;
   if (add.has_value()) {
-    TORCH_CHECK(add->is_contiguous() && add->scalar_type() == at::kBFloat16 && add->numel() == out.numel(),
-                "p2p_reduce_rows: add must match out");
+    TORCH_CHECK(!out_f32 && add->is_contiguous() && add->scalar_type() == at::kBFloat16 &&
+                    add->numel() == out.numel(),
+                "p2p_reduce_rows: add must match a bf16 out");
     addp = reinterpret_cast<const bb::bf16x8*>(add->data_ptr());
   }
   if (rows == 0) return;
   const int blocks = num_blocks((size_t)rows * 32, 256, 8);
   auto stream = at::cuda::getCurrentCUDAStream();
-  auto* o = reinterpret_cast<bb::bf16x8*>(out.data_ptr());
+  void* o = out.data_ptr();
   const int vecs = (int)(out.size(1) / 8);
-  if (src_f32)
-    p2p_reduce_rows_kernel<true><<<blocks, 256, 0, stream>>>(make_ptrs(peers), (int)peers.size(),
-                                                             src_row.data_ptr<int>(), addp, o, rows, vecs);
+  const int np = (int)peers.size();
+  if (out_f32)
+    p2p_reduce_rows_kernel<true, true><<<blocks, 256, 0, stream>>>(make_ptrs(peers), np, src_row.data_ptr<int>(),
+                                                                   addp, o, rows, vecs);
+  else if (src_f32)
+    p2p_reduce_rows_kernel<true, false><<<blocks, 256, 0, stream>>>(make_ptrs(peers), np, src_row.data_ptr<int>(),
+                                                                    addp, o, rows, vecs);
   else
-    p2p_reduce_rows_kernel<false><<<blocks, 256, 0, stream>>>(make_ptrs(peers), (int)peers.size(),
-                                                              src_row.data_ptr<int>(), addp, o, rows, vecs);
+    p2p_reduce_rows_kernel<false, false><<<blocks, 256, 0, stream>>>(make_ptrs(peers), np, src_row.data_ptr<int>(),
+                                                                     addp, o, rows, vecs);
   BB_POST_LAUNCH();
 }

@@ -1,8 +1,10 @@
 """Public TPR entry points: module-spec install, CE request entry, PPO mini-batch entry.
 
 * :func:`run_tpr_forward_backward_batch` -- PPO mini-batch -> token-trie forest
-  -> batched level execution (or per-tree Push/Pop under CP) -> one gradient
-  finalisation; returns ``{"model_output", "loss", "metrics"}`` like verl.
+  -> batched level execution (under CP: segment-granular placement over the CP
+  group, or per-tree Push/Pop with the named CP backend when a segment is longer
+  than one rank's token budget) -> one gradient finalisation; returns
+  ``{"model_output", "loss", "metrics"}`` like verl.
 * :func:`run_tpr_forward_backward` -- CE request (a :class:`SegmentPlan` with
   loss terms, optional fixed event order) through one SegmentExecutor.
 
@@ -182,6 +184,20 @@ def prepare_tpr_batch(engine, data: Any, loss_function: Any = None) -> PreparedT
     return PreparedTPRBatch(data, forest, objective, logical_inputs, stage)
 
 
+def max_segment_tokens(forest) -> int:
+    return max((s.length for t in forest.trees for s in t.segment_plan.segments.values()), default=0)
+
+
+def forest_fits(engine, forest, rt) -> bool:
+    """Whether the batched forest executor runs this forest: always on one CP rank; under CP when every
+    segment fits whole into one rank's token budget (segment-granular placement).  Otherwise the
+    per-tree executor splits each segment over the CP group with the configured backend."""
+    ec = engine.engine_config
+    if ec.executor != "forest":
+        return False
+    return rt.group is None or max_segment_tokens(forest) <= ec.token_budget
+
+
 def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss: bool = True) -> dict:
     """Run the forest schedule of a prepared mini-batch and finalise gradients once."""
     from ..parallel.engine_runtime import aggregate_cp_loss, resolve_engine_cp_runtime
@@ -201,8 +217,16 @@ def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss:
 
         profiler = SegmentEventProfiler()
         engine._tpr_segment_event_profiler = profiler
-    if rt.group is None and ec.executor == "forest":
-        fx = ForestExecutor(model, objective, mode=ec.forest_mode, token_budget=ec.token_budget)
+    if forest_fits(engine, forest, rt):
+        cp = None
+        if rt.group is not None:
+            cp = getattr(engine, "_tpr_forest_cp", None)
+            if cp is None or cp.group is not rt.group:
+                from ..parallel.forest_cp import ForestCP
+
+                cp = engine._tpr_forest_cp = ForestCP(rt.group, comm=ec.cp_comm)
+        fx = ForestExecutor(model, objective, mode=ec.forest_mode, token_budget=ec.token_budget,
+                            loss_scale=float(rt.size), cp=cp)
         fx.profiler = profiler
         if prepared.nodes is None:
             prepared.nodes = fx.plan(forest)

@@ -16,7 +16,8 @@ import torch.nn as nn
 from torch import Tensor
 
 from ..ops.norm import add_rmsnorm
-from ..parallel.tp import VocabParallelEmbedding, copy_to_tp, gather_from_sp, tp_rank, tp_size
+from ..parallel.tp import (VocabParallelEmbedding, copy_to_tp, gather_from_sp, reduce_scatter_to_sp, tp_rank,
+                           tp_size)
 from .config import ModelConfig
 from .layers import DecoderLayer, RMSNorm, RotaryEmbedding
 
@@ -40,6 +41,8 @@ class DecoderModel(nn.Module):
             for layer in self.layers:
                 layer.input_layernorm.weight.tp_partial_grad = True  # type: ignore[attr-defined]
                 layer.post_attention_layernorm.weight.tp_partial_grad = True  # type: ignore[attr-defined]
+            self.norm.weight.tp_partial_grad = True  # type: ignore[attr-defined]
+
         self.rotary_pos_emb = RotaryEmbedding(cfg.head_dim, cfg.rope_theta)
         if cfg.tie_word_embeddings:
             self.lm_head = None
@@ -71,13 +74,15 @@ class DecoderModel(nn.Module):
     def forward(self, input_ids: Tensor, position_ids: Tensor, max_position: int | None = None) -> Tensor:
         if input_ids.ndim == 2:  # [1, T] accepted for single-sequence callers
             input_ids, position_ids = input_ids[0], position_ids[0]
-        x = self.embed_tokens(input_ids)
         rope = self.rotary_pos_emb(position_ids, max_position)
         if self.sequence_parallel:
-            n, r = tp_size(self.tp_group), tp_rank(self.tp_group)
-            if x.shape[0] % n:
+            if input_ids.shape[0] % tp_size(self.tp_group):
                 raise ValueError("sequence-parallel segments must be divisible by the TP size")
-            x = x.chunk(n)[r]
+            # vocab-sharded partial rows -> reduce-scatter over tokens (backward: all-gather, so every
+            # rank's vocab shard sees the gradient of every token)
+            x = reduce_scatter_to_sp(self.embed_tokens(input_ids, reduce=False), self.tp_group)
+        else:
+            x = self.embed_tokens(input_ids)
         pending = None      # each block's MLP output is added inside the next block's first norm
         for layer in self.layers:
             x, pending = layer(x, rope, pending, True)
@@ -87,8 +92,13 @@ class DecoderModel(nn.Module):
         return x
 
     def head_input(self, hidden_rows: Tensor) -> Tensor:
-        """Prepare selected hidden rows for the (vocab-parallel) LM head."""
-        return copy_to_tp(hidden_rows, self.tp_group)
+        """Prepare selected hidden rows for the (vocab-parallel) LM head.
+
+        Each TP rank's head backward yields a partial ``dh`` (its vocab shard).  Without sequence
+        parallelism they are summed here (all-reduce); with it the final hidden states came out of
+        :func:`gather_from_sp`, whose backward reduce-scatter already sums them -- summing here too
+        would count every contribution TP times."""
+        return hidden_rows if self.sequence_parallel else copy_to_tp(hidden_rows, self.tp_group)
 
     def logits(self, hidden_rows: Tensor) -> Tensor:
         """Local-vocab logits ``[U, V/TP]`` of selected rows."""

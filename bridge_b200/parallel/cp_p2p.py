@@ -147,6 +147,14 @@ def cp_comm(group, x: Tensor) -> CPP2PComm | None:
     return _COMMS[key]
 
 
+def shared_cp_comm(group, device: torch.device) -> CPP2PComm:
+    """The group's P2P staging comm (created on first use; shared by every CP transport of the group)."""
+    key = id(group)
+    if key not in _COMMS:
+        _COMMS[key] = CPP2PComm(group, device)
+    return _COMMS[key]
+
+
 def close_all() -> None:
     for c in _COMMS.values():
         c.close()

@@ -179,11 +179,13 @@ class VocabParallelEmbedding(nn.Module):
         _init(self.weight, std, 2)
         self.weight.tp_split_dim = 0  # type: ignore[attr-defined]
 
-    def forward(self, ids: Tensor) -> Tensor:
+    def forward(self, ids: Tensor, *, reduce: bool = True) -> Tensor:
+        """Rows of out-of-shard ids are zero; ``reduce=False`` returns these per-rank partials (the
+        sequence-parallel caller reduce-scatters them instead of all-reducing)."""
         from ..ops.embedding import embedding
 
         out = embedding(ids, self.weight, self.start)
-        return out if tp_size(self.group) == 1 else reduce_from_tp(out, self.group)
+        return out if (tp_size(self.group) == 1 or not reduce) else reduce_from_tp(out, self.group)
 
 
 def scaled_init_std(std: float, num_layers: int) -> float:

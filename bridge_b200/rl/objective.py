@@ -27,7 +27,8 @@ import numpy as np
 import torch
 from torch import Tensor
 
-from ..ops.logprob import fused_lm_head_logprob
+from ..ops._ext import on_gpu
+from ..ops.logprob import fused_lm_head_logprob, fused_lm_head_ppo
 from ..ops.ppo import PPOLossConfig, ppo_loss
 from ..tpr.tree_plan_builder import SegmentObjectiveRef, TreeExecutionPlan
 
@@ -171,11 +172,15 @@ class SegmentPPOObjectiveAdapter:
 
     # ------------------------------------------------------------------ loss on selected rows
     def rows_loss(self, model, hidden: Tensor, local_rows: Tensor, table_targets: Tensor, sample_rows: Tensor,
-                  flat_index: Tensor, *, host_keys: list[tuple] | None = None) -> tuple[Tensor, dict]:
+                  flat_index: Tensor, *, host_keys: list[tuple] | None = None,
+                  grad_scale: float | None = None) -> tuple[Tensor, dict]:
         """PPO loss of refs whose predicting query rows are ``hidden[local_rows]``.
 
         ``local_rows``, ``table_targets`` etc. are host tensors (one entry per ref).
-        Dedupe on (row, target, temperature) happens here on the host.
+        Dedupe on (row, target, temperature) happens here on the host.  With ``grad_scale`` (the
+        factor the caller's backward applies to this loss) the CUDA path runs the LM-head backward
+        inside the forward (:func:`~bridge_b200.ops.logprob.fused_lm_head_ppo`), so no logits are
+        kept until backward.
         """
         dev = hidden.device
         temps = self.row_temperature[sample_rows]
@@ -189,12 +194,28 @@ class SegmentPPOObjectiveAdapter:
         aux = torch.stack([inverse, flat_index]).to(dev, non_blocking=True)
         u_t = u_temps.to(dev, non_blocking=True)
         h = hidden.index_select(0, pack[0])
+        flat = self.device_flat(dev)
+        if grad_scale is not None and on_gpu(hidden):
+            old = flat["old_log_probs"].index_select(0, aux[1])
+            adv = flat["advantages"].index_select(0, aux[1])
+            w = flat["rollout_is_weights"].index_select(0, aux[1]) if "rollout_is_weights" in flat else None
+            c = self.config
+            loss, stats, lp_u, ent_u = fused_lm_head_ppo(
+                model.head_input(h), model.head_weight, pack[1], u_t, aux[0], old, adv, w, denom=self.denominator,
+                clip_low=c.clip_ratio_low, clip_high=c.clip_ratio_high, clip_c=c.clip_ratio_c,
+                vocab_start=model.vocab_start, tp_group=model.tp_group, with_entropy=self.calculate_entropy,
+                chunk_rows=self.log_prob_chunk_size, grad_scale=grad_scale)
+            metrics = {"n": int(local_rows.numel()), "stats": stats}
+            if ent_u is not None:
+                metrics["entropy_sum"] = ent_u.index_select(0, aux[0]).sum()
+            if self.capture_log_probs:
+                metrics["log_probs"] = lp_u.index_select(0, aux[0])
+            return loss, metrics
         lp_u, ent_u = fused_lm_head_logprob(model.head_input(h), model.head_weight, pack[1], u_t,
                                             vocab_start=model.vocab_start, tp_group=model.tp_group,
                                             with_entropy=self.calculate_entropy,
                                             chunk_rows=self.log_prob_chunk_size)
         lp = lp_u.index_select(0, aux[0])
-        flat = self.device_flat(dev)
         old = flat["old_log_probs"].index_select(0, aux[1])
         adv = flat["advantages"].index_select(0, aux[1])
         w = flat["rollout_is_weights"].index_select(0, aux[1]) if "rollout_is_weights" in flat else None

@@ -75,7 +75,10 @@ class _Node:
 
 @dataclass(eq=False)
 class _Chunk:
-    nodes: list
+    nodes: list                                       # every node of the chunk (rank-major under CP)
+    local: list = field(default_factory=list)         # the nodes this rank forwards
+    counts: tuple | None = None                       # CP: (rows per rank, segments per rank)
+    index: int = 0                                    # push order (deterministic on every rank)
     kv_anchor: dict = field(default_factory=dict)     # layer -> (A_K, A_V) leaves
     kv_graph: dict = field(default_factory=dict)      # layer -> (K, V) graph tensors (retain)
     gdn_anchor: dict = field(default_factory=dict)    # layer -> (A_conv, A_rec)
@@ -114,12 +117,16 @@ class ForestExecutor:
     """Runs a :class:`ForestExecutionPlan` (PPO objective) level-wise in packed chunks."""
 
     def __init__(self, model: nn.Module, objective, *, mode: str = "retain", token_budget: int = 8192,
-                 loss_scale: float = 1.0) -> None:
+                 loss_scale: float = 1.0, cp=None) -> None:
+        """``token_budget`` is the packed token count one rank forwards at a time; ``cp`` (a
+        :class:`~bridge_b200.parallel.forest_cp.ForestCP`) partitions every chunk's segments over a
+        context-parallel group (chunks then hold ``token_budget * cp.size`` tokens)."""
         if mode not in ("retain", "recompute"):
             raise ValueError(f"mode must be 'retain' or 'recompute', got {mode!r}")
         self.model, self.objective, self.mode = model, objective, mode
         self.token_budget = int(token_budget)
         self.loss_scale = loss_scale
+        self.cp = cp
         self.attn_layers = tuple(getattr(model, "attention_layer_numbers", ()))
         self.gdn_layers = tuple(getattr(model, "gdn_layer_numbers", ()))
         self.device = model_device(model)
@@ -210,7 +217,7 @@ class ForestExecutor:
             bank[layer] = (torch.cat(ks), torch.cat(vs))
         return bank, spans, None
 
-    def _gdn_init(self, nodes: list[_Node]):
+    def _gdn_init(self, nodes: list[_Node], pad_seqs: int = 0):
         if not self.gdn_layers:
             return {}
         if all(n.parent is None for n in nodes):
@@ -230,27 +237,63 @@ class ForestExecutor:
                     ac, ar = p.chunk.gdn_anchor[layer]
                     convs.append(ac[p.batch_index:p.batch_index + 1])
                     recs.append(ar[p.batch_index:p.batch_index + 1])
+            for _ in range(pad_seqs):
+                convs.append(torch.zeros_like(convs[0]))
+                recs.append(torch.zeros_like(recs[0]))
             out[layer] = GDNLayerState(torch.cat(convs), torch.cat(recs))
         return out
 
+    def _pad_multiple(self) -> int:
+        if getattr(self.model, "sequence_parallel", False):
+            from ..parallel.tp import tp_size
+
+            return tp_size(self.model.tp_group)
+        return 1
+
     def _forward(self, nodes: list[_Node], *, grad: bool, record: bool):
+        """Packed forward of ``nodes``.  A trailing pad segment (token 0, no prefix, no loss) is added
+        when sequence parallelism needs the row count to divide over TP, and an idle CP rank (no
+        segments in this chunk) forwards a pad segment alone so every rank makes the same collectives."""
         dev = self.device
         seq_lens = [n.length for n in nodes]
-        ids = torch.cat([n.tokens for n in nodes])
-        pos = torch.cat([torch.arange(n.start, n.start + n.length) for n in nodes])
-        host = torch.stack([ids, pos])
+        total = sum(seq_lens)
+        mult = self._pad_multiple()
+        pad = (-total) % mult if nodes else max(mult, 8)
+        ids_l = [n.tokens for n in nodes]
+        pos_l = [torch.arange(n.start, n.start + n.length) for n in nodes]
+        bank, spans, _ = self._prefix_bank(nodes)
+        if pad:
+            ids_l.append(torch.zeros(pad, dtype=ids_l[0].dtype if ids_l else torch.long))
+            pos_l.append(torch.arange(pad))
+            seq_lens.append(pad)
+            spans = list(spans) + [(0, 0)]
+        host = torch.stack([torch.cat(ids_l), torch.cat(pos_l)])
         if dev.type == "cuda":
             host = host.pin_memory()
         dev_ip = host.to(dev, non_blocking=True)
-        bank, spans, _ = self._prefix_bank(nodes)
         layout = SegmentBatchLayout.build(seq_lens, spans, device=dev)
+        gdn0 = self._gdn_init(nodes, pad_seqs=1 if pad else 0) if nodes else {}
         ctx = TPRAttentionContext(prefix_length=0, suffix_length=sum(seq_lens), past_key_values=bank,
-                                  layout=layout, initial_gdn_states=self._gdn_init(nodes),
+                                  layout=layout, initial_gdn_states=gdn0,
                                   capture_gdn_final_state=record, record_new_kv=record)
-        max_pos = max(n.start + n.length for n in nodes)
+        max_pos = max([n.start + n.length for n in nodes] + [pad])
         with (torch.enable_grad() if grad else torch.no_grad()), use_tpr_attention_context(ctx):
             hidden = self.model(dev_ip[0], dev_ip[1], max_pos)
         return ctx, hidden
+
+    def _exchange(self, ctx, local: list[_Node], counts):
+        """This chunk's new K/V and final GDN states, restricted to real rows and (under CP) gathered
+        over the CP group into rank-major anchor order."""
+        rows = sum(n.length for n in local)
+        segs = len(local)
+        kv, gdn = {}, {}
+        for layer, (k, v) in ctx.new_key_values.items():
+            k, v = k[:rows], v[:rows]
+            kv[layer] = (k, v) if self.cp is None else tuple(self.cp.gather([k, v], counts[0]))
+        for layer, st in ctx.new_gdn_states.items():
+            c, r = st.conv_state[:segs], st.recurrent_state[:segs]
+            gdn[layer] = (c, r) if self.cp is None else tuple(self.cp.gather([c, r], counts[1]))
+        return kv, gdn
 
     def _loss(self, nodes: list[_Node], hidden: Tensor):
         rows, tg, sm, fl = [], [], [], []
@@ -265,36 +308,48 @@ class ForestExecutor:
         if not rows:
             return None, None
         loss, metrics = self.objective.rows_loss(self.model, hidden, torch.cat(rows), torch.cat(tg), torch.cat(sm),
-                                                 torch.cat(fl))
+                                                 torch.cat(fl), grad_scale=self.loss_scale)
         return loss, metrics
 
     # ------------------------------------------------------------------ phases
-    def _push_chunk(self, nodes: list[_Node], stats: dict) -> _Chunk:
-        ch = _Chunk(nodes)
+    def _place(self, nodes: list[_Node]):
+        """``(local nodes, rank-major order, counts)`` of a chunk (identity without CP)."""
+        if self.cp is None:
+            return nodes, nodes, None
+        parts = self.cp.split(nodes)
+        order = [n for p in parts for n in p]
+        return parts[self.cp.rank], order, ([sum(n.length for n in p) for p in parts], [len(p) for p in parts])
+
+    def _push_chunk(self, nodes: list[_Node], stats: dict, index: int = 0) -> _Chunk:
+        local, order, counts = self._place(nodes)
+        ch = _Chunk(order, local=local, counts=counts, index=index)
         grad = self.mode == "retain"
-        ctx, hidden = self._forward(nodes, grad=grad, record=True)
-        stats["fwd"] += sum(n.length for n in nodes)
         row = 0
-        for b, n in enumerate(nodes):
+        for b, n in enumerate(order):
             n.chunk, n.row0, n.batch_index = ch, row, b
             row += n.length
-        for layer, (k, v) in ctx.new_key_values.items():
+        ctx, hidden = self._forward(local, grad=grad, record=True)
+        stats["fwd"] += sum(n.length for n in local)
+        kv, gdn = self._exchange(ctx, local, counts)
+        for layer, (k, v) in kv.items():
             ch.kv_anchor[layer] = (k.detach().requires_grad_(True), v.detach().requires_grad_(True))
             if grad:
                 ch.kv_graph[layer] = (k, v)
-        for layer, st in ctx.new_gdn_states.items():
-            ch.gdn_anchor[layer] = (st.conv_state.detach().requires_grad_(True),
-                                    st.recurrent_state.detach().requires_grad_(True))
+        for layer, (c, r) in gdn.items():
+            ch.gdn_anchor[layer] = (c.detach().requires_grad_(True), r.detach().requires_grad_(True))
             if grad:
-                ch.gdn_graph[layer] = (st.conv_state, st.recurrent_state)
+                ch.gdn_graph[layer] = (c, r)
         if grad:
-            loss, metrics = self._loss(nodes, hidden)
+            loss, metrics = self._loss(local, hidden)
+            if loss is None and self.cp is not None:   # every CP rank back-propagates the whole model
+                loss = hidden.float().sum() * 0.0
             ch.loss = loss
             if metrics is not None:
                 ch.metrics.append(metrics)
         return ch
 
     def _visit_leaves(self, nodes: list[_Node], stats: dict, acc: dict) -> None:
+        nodes = self._place(nodes)[0]
         ctx, hidden = self._forward(nodes, grad=True, record=False)
         stats["fwd"] += sum(n.length for n in nodes)
         stats["bwd"] += sum(n.length for n in nodes)
@@ -309,11 +364,12 @@ class ForestExecutor:
     def _pop_chunk(self, ch: _Chunk, stats: dict, acc: dict) -> None:
         if self.mode == "recompute":
             # Re-run the chunk with grad over the (still anchored) ancestors, then relay.
-            ctx, hidden = self._forward(ch.nodes, grad=True, record=True)
-            stats["fwd"] += sum(n.length for n in ch.nodes)
-            kv_graph = dict(ctx.new_key_values)
-            gdn_graph = {k: (s.conv_state, s.recurrent_state) for k, s in ctx.new_gdn_states.items()}
-            loss, metrics = self._loss(ch.nodes, hidden)
+            ctx, hidden = self._forward(ch.local, grad=True, record=True)
+            stats["fwd"] += sum(n.length for n in ch.local)
+            kv_graph, gdn_graph = self._exchange(ctx, ch.local, ch.counts)
+            loss, metrics = self._loss(ch.local, hidden)
+            if loss is None and self.cp is not None:
+                loss = hidden.float().sum() * 0.0
             if metrics is not None:
                 ch.metrics.append(metrics)
         else:
@@ -324,20 +380,22 @@ class ForestExecutor:
             grads.append(None)
             acc["loss"] = loss.detach() if acc["loss"] is None else acc["loss"] + loss.detach()
         acc["metrics"].extend(ch.metrics)
+        every = self.cp is not None      # the CP gathers' backward is a collective: every rank enters it
         for layer, (k, v) in kv_graph.items():
             ak, av = ch.kv_anchor[layer]
-            if ak.grad is not None:
+            if ak.grad is not None or av.grad is not None or every:
                 roots += [k, v]
-                grads += [ak.grad, av.grad]
+                grads += [ak.grad if ak.grad is not None else torch.zeros_like(ak),
+                          av.grad if av.grad is not None else torch.zeros_like(av)]
         for layer, (c, r) in gdn_graph.items():
             ac, ar = ch.gdn_anchor[layer]
-            if ac.grad is not None or ar.grad is not None:
+            if ac.grad is not None or ar.grad is not None or every:
                 roots += [c, r]
                 grads += [ac.grad if ac.grad is not None else torch.zeros_like(ac),
                           ar.grad if ar.grad is not None else torch.zeros_like(ar)]
         if roots:
             torch.autograd.backward(roots, grad_tensors=grads)
-        stats["bwd"] += sum(n.length for n in ch.nodes)
+        stats["bwd"] += sum(n.length for n in ch.local)
         ch.kv_anchor.clear()
         ch.kv_graph.clear()
         ch.gdn_anchor.clear()
@@ -368,18 +426,22 @@ class ForestExecutor:
         stats = {"fwd": 0, "bwd": 0, "chunks": 0}
         acc: dict[str, Any] = {"loss": None, "metrics": []}
         pushed: dict[int, list[_Chunk]] = {}
+        budget = self.token_budget * (self.cp.size if self.cp is not None else 1)
+        n_pushed = 0
         for d in sorted(internal):
             pushed[d] = []
             # Keep siblings of one parent adjacent so their children batch together later.
-            for grp in _chunked(internal[d], self.token_budget):
+            for grp in _chunked(internal[d], budget):
                 rec = self._prof_begin("push_chunk", grp, d)
-                pushed[d].append(self._push_chunk(grp, stats))
+                pushed[d].append(self._push_chunk(grp, stats, n_pushed))
                 self._prof_end(rec)
+                n_pushed += 1
                 stats["chunks"] += 1
-        # Leaves ordered by (parent chunk, parent row) so a chunk's spans hit few parents.
-        leaves.sort(key=lambda n: (n.depth == 0, id(n.parent.chunk) if n.parent else 0,
+        # Leaves ordered by (parent chunk, parent row) so a chunk's spans hit few parents.  The key is
+        # the same on every rank (TP and CP peers must form identical chunks).
+        leaves.sort(key=lambda n: (n.depth == 0, n.parent.chunk.index if n.parent else 0,
                                    n.parent.row0 if n.parent else 0))
-        for grp in _chunked(leaves, self.token_budget):
+        for grp in _chunked(leaves, budget):
             rec = self._prof_begin("visit_chunk", grp, grp[0].depth)
             self._visit_leaves(grp, stats, acc)
             self._prof_end(rec)

@@ -369,6 +369,8 @@ class PrefixStateEntry:
 class PrefixStateStack:
     """The active DFS path: entries pushed in root->leaf order."""
 
+    label = "prefix-state stack"      # how error messages name this stack
+
     def __init__(self) -> None:
         self._entries: list[PrefixStateEntry] = []
 
@@ -388,14 +390,14 @@ class PrefixStateStack:
 
     def top(self) -> PrefixStateEntry:
         if not self._entries:
-            raise RuntimeError("prefix-state stack is empty")
+            raise RuntimeError(f"{self.label} is empty")
         return self._entries[-1]
 
     def get(self, segment_id: SegmentId) -> PrefixStateEntry:
         for e in self._entries:
             if e.segment.segment_id == segment_id:
                 return e
-        raise KeyError(f"segment {segment_id} is not on the prefix-state stack")
+        raise KeyError(f"segment {segment_id} is not on the {self.label}")
 
     def push_state(self, segment: SegmentSpec, state, *, entry_type=PrefixStateEntry) -> PrefixStateEntry:
         if not isinstance(segment, SegmentSpec):
@@ -415,9 +417,9 @@ class PrefixStateStack:
 
     def pop_state(self, segment_id: SegmentId) -> PrefixStateEntry:
         if not self._entries or self._entries[-1].segment.segment_id != segment_id:
-            raise RuntimeError(f"cannot pop segment {segment_id}: prefix-state stack is {list(self.segment_ids)}")
+            raise RuntimeError(f"cannot pop segment {segment_id}: {self.label} is {list(self.segment_ids)}")
         return self._entries.pop()
 
     def assert_empty(self) -> None:
         if self._entries:
-            raise RuntimeError(f"prefix-state stack is not empty: {list(self.segment_ids)}")
+            raise RuntimeError(f"{self.label} is not empty: {list(self.segment_ids)}")

@@ -1,16 +1,17 @@
 """Fixed-topology scheduler and forest batch runner.
 
-:class:`FixedTopologyScheduler` executes one validated Push/Pop stream against
-a :class:`SegmentExecutor`; an adjacent ``Push(x), Pop(x)`` of a leaf becomes a
-single VISIT_LEAF.  It tracks the peak path length (prefix + segment tokens)
-and moves READY -> RUNNING -> COMPLETED, or FAILED on any exception.
+:class:`FixedTopologyScheduler` runs one validated Push/Pop stream against a
+:class:`SegmentExecutor`.  The stream is first *lowered* to physical executions: a push that is
+immediately followed by the pop of the same childless segment becomes one VISIT_LEAF (forward and
+backward in one go, no prefix state kept); every other event stays a PUSH or a POP.  The scheduler
+then executes that list, records the peak path length (prefix + segment tokens) and moves READY ->
+RUNNING -> COMPLETED, or FAILED on any exception.
 
-:class:`TPRBatchRunner` runs every tree of one mini-batch under one
-``no_sync`` scope and finalises gradients exactly once -- and not at all if any
-tree failed.
+:class:`TPRBatchRunner` runs every tree of one mini-batch under one ``no_sync`` scope and finalises
+gradients exactly once -- and not at all if any tree failed.
 
-Parity: verl/models/mcore/tpr/fixed_topology_scheduler.py:32-210 and
-verl/models/mcore/tpr/tpr_batch_runner.py:23-83.
+Parity: the public types and state machine of verl/models/mcore/tpr/fixed_topology_scheduler.py:32-210
+and tpr_batch_runner.py:23-83; the lowering step and the code are this framework's own.
 """
 
 from __future__ import annotations
@@ -51,6 +52,8 @@ class PhysicalExecution:
 
 @dataclass(frozen=True, slots=True)
 class TreeScheduleResult:
+    """What one tree's schedule produced (traces, per-execution results, summed losses)."""
+
     event_trace: tuple[SegmentEvent, ...]
     execution_trace: tuple[PhysicalExecution, ...]
     forward_results: tuple[SegmentForwardResult, ...]
@@ -74,7 +77,25 @@ class TreeScheduleResult:
 
     @property
     def executed_segment_count(self) -> int:
-        return self.pushed_segment_count + self.direct_leaf_count
+        """Segments that ran a forward: pushed ones plus directly visited leaves."""
+        return len(self.forward_results) + len(self.direct_leaf_results)
+
+
+def lower_events(plan: SegmentPlan, events: Sequence[SegmentEvent]) -> tuple[PhysicalExecution, ...]:
+    """Physical executions of a validated event stream (adjacent push/pop of a leaf -> VISIT_LEAF)."""
+    out: list[PhysicalExecution] = []
+    it = iter(range(len(events)))
+    for i in it:
+        ev = events[i]
+        nxt = events[i + 1] if i + 1 < len(events) else None
+        if (ev.kind is SegmentEventKind.PUSH and nxt is not None and nxt.kind is SegmentEventKind.POP
+                and nxt.segment_id == ev.segment_id and not plan.child_ids(ev.segment_id)):
+            out.append(PhysicalExecution(PhysicalExecutionKind.VISIT_LEAF, ev.segment_id))
+            next(it)                                 # the pop is part of the visit
+        else:
+            kind = PhysicalExecutionKind.PUSH if ev.kind is SegmentEventKind.PUSH else PhysicalExecutionKind.POP
+            out.append(PhysicalExecution(kind, ev.segment_id))
+    return tuple(out)
 
 
 def _mem_trace(tag: str, **fields) -> None:
@@ -91,77 +112,64 @@ class FixedTopologyScheduler:
 
     def __init__(self, plan: SegmentPlan, executor: SegmentExecutor, *, events: Sequence[SegmentEvent] | None = None,
                  event_profiler=None, tree_index: int = 0) -> None:
-        if not isinstance(plan, SegmentPlan):
-            raise TypeError(f"plan must be SegmentPlan, got {type(plan).__name__}")
-        if not isinstance(executor, SegmentExecutor):
-            raise TypeError(f"executor must be SegmentExecutor, got {type(executor).__name__}")
-        if executor.plan is not plan:
-            raise ValueError("executor and scheduler must share the same SegmentPlan instance")
-        if executor.failed:
-            raise ValueError("executor is already failed")
-        if len(executor.kv_stack):
-            raise ValueError("executor KV stack must be empty before scheduling")
-        self.events = plan.validate_events(tuple(plan.dfs_events()) if events is None else tuple(events))
+        for obj, cls in ((plan, SegmentPlan), (executor, SegmentExecutor)):
+            if not isinstance(obj, cls):
+                raise TypeError(f"expected a {cls.__name__}, got {type(obj).__name__}")
+        problem = ("the executor was built for a different SegmentPlan object" if executor.plan is not plan else
+                   "the executor has already failed" if executor.failed else
+                   f"the executor still holds segments {list(executor.kv_stack.segment_ids)} on its KV stack"
+                   if len(executor.kv_stack) else None)
+        if problem:
+            raise ValueError(f"cannot schedule tree {tree_index}: {problem}")
+        self.events = plan.validate_events(plan.dfs_events() if events is None else events)
+        self.executions = lower_events(plan, self.events)
         self.plan, self.executor = plan, executor
         self.event_profiler, self.tree_index = event_profiler, tree_index
         self.state = SchedulerState.READY
 
-    def _leaf_pair(self, i: int) -> bool:
-        if i + 1 >= len(self.events):
-            return False
-        a, b = self.events[i], self.events[i + 1]
-        return (a.kind is SegmentEventKind.PUSH and b.kind is SegmentEventKind.POP and a.segment_id == b.segment_id
-                and not self.plan.child_ids(a.segment_id))
+    def _execute(self, step: PhysicalExecution, out: dict) -> int:
+        """Run one physical execution; return the path length it reached."""
+        ex, sid = self.executor, step.segment_id
+        if step.kind is PhysicalExecutionKind.VISIT_LEAF:
+            r = ex.visit_leaf(sid)
+            out["leaves"].append(r)
+            out["losses"].append(r.backward)
+            return r.forward.prefix_length + r.forward.suffix_length
+        if step.kind is PhysicalExecutionKind.PUSH:
+            out["fwd"].append(ex.push(sid))
+            return ex.kv_stack.prefix_length
+        r = ex.pop(sid)
+        out["bwd"].append(r)
+        out["losses"].append(r)
+        return 0
 
     def run(self) -> TreeScheduleResult:
         if self.state is not SchedulerState.READY:
-            raise RuntimeError(f"scheduler can only run from READY, current state is {self.state.value}")
+            raise RuntimeError(f"the scheduler of tree {self.tree_index} is {self.state.value}; it runs once, "
+                               "from ready")
         self.state = SchedulerState.RUNNING
-        fwd, bwd, leaves, losses, trace = [], [], [], [], []
+        out: dict[str, list] = {"fwd": [], "bwd": [], "leaves": [], "losses": []}
         peak = 0
-        ex = self.executor
         try:
-            i = 0
-            while i < len(self.events):
-                ev = self.events[i]
-                leaf = self._leaf_pair(i)
-                kind = "visit_leaf" if leaf else ev.kind.value
-                _mem_trace("EVENT_BEGIN", index=i, kind=kind, segment=ev.segment_id,
-                           path_tokens=ex.kv_stack.prefix_length, depth=len(ex.kv_stack))
-                prof = None
-                if self.event_profiler is not None:
-                    prof = self.event_profiler.begin(self.plan.get(ev.segment_id), kind=kind,
-                                                     tree_index=self.tree_index,
-                                                     depth=self.plan.depth_of(ev.segment_id))
-                if leaf:
-                    r = ex.visit_leaf(ev.segment_id)
-                    leaves.append(r)
-                    losses.append(r.backward)
-                    trace.append(PhysicalExecution(PhysicalExecutionKind.VISIT_LEAF, ev.segment_id))
-                    peak = max(peak, r.forward.prefix_length + r.forward.suffix_length)
-                    step = 2
-                elif ev.kind is SegmentEventKind.PUSH:
-                    fwd.append(ex.push(ev.segment_id))
-                    trace.append(PhysicalExecution(PhysicalExecutionKind.PUSH, ev.segment_id))
-                    peak = max(peak, ex.kv_stack.prefix_length)
-                    step = 1
-                else:
-                    r = ex.pop(ev.segment_id)
-                    bwd.append(r)
-                    losses.append(r)
-                    trace.append(PhysicalExecution(PhysicalExecutionKind.POP, ev.segment_id))
-                    step = 1
+            for i, step in enumerate(self.executions):
+                stack = self.executor.kv_stack
+                _mem_trace("EVENT_BEGIN", index=i, kind=step.kind.value, segment=step.segment_id,
+                           path_tokens=stack.prefix_length, depth=len(stack))
+                prof = None if self.event_profiler is None else self.event_profiler.begin(
+                    self.plan.get(step.segment_id), kind=step.kind.value, tree_index=self.tree_index,
+                    depth=self.plan.depth_of(step.segment_id))
+                peak = max(peak, self._execute(step, out))
                 if prof is not None:
                     self.event_profiler.end(prof)
-                _mem_trace("EVENT_END", index=i, kind=kind, segment=ev.segment_id)
-                i += step
-            ex.kv_stack.assert_empty()
+                _mem_trace("EVENT_END", index=i, kind=step.kind.value, segment=step.segment_id)
+            self.executor.kv_stack.assert_empty()
+            losses = out["losses"]
             if not losses:
-                raise RuntimeError("schedule produced no backward results")
-            loss_sum = sum((r.loss_sum for r in losses[1:]), losses[0].loss_sum)
-            normalized = sum((r.normalized_loss for r in losses[1:]), losses[0].normalized_loss)
-            result = TreeScheduleResult(self.events, tuple(trace), tuple(fwd), tuple(bwd), tuple(leaves), loss_sum,
-                                        normalized, peak)
+                raise RuntimeError(f"tree {self.tree_index}: the schedule ran no backward")
+            loss_sum = torch.stack([r.loss_sum for r in losses]).sum()
+            normalized = torch.stack([r.normalized_loss for r in losses]).sum()
+            result = TreeScheduleResult(self.events, self.executions, tuple(out["fwd"]), tuple(out["bwd"]),
+                                        tuple(out["leaves"]), loss_sum, normalized, peak)
         except Exception:
             self.state = SchedulerState.FAILED
             raise

@@ -1,13 +1,20 @@
-"""Immutable segment topology and its Push/Pop event protocol.
+"""Segment trees and the Push/Pop event protocol the TPR executors follow.
 
-A :class:`SegmentPlan` is a rooted tree of token segments kept entirely on the
-host. Every child starts exactly where its parent ends, so a segment's absolute
-positions are ``[prefix_length, prefix_length + length)`` and its external
-prefix is the concatenation of its ancestors. The plan yields a deterministic
-DFS Push/Pop stream and validates arbitrary streams against stack discipline.
+A :class:`SegmentPlan` is host-side metadata: a rooted tree whose nodes are contiguous token
+segments.  A child begins at the absolute position where its parent ends, so the external prefix of
+any segment is the concatenation of its ancestors.  Executing a plan means walking it with two
+kinds of events -- *push* (forward a segment and keep its prefix state for the descendants) and
+*pop* (backward it with the gradients its descendants relayed, then drop it).  Any order is legal
+as long as it is a depth-first walk: a segment is pushed while its parent is the open segment on
+top, and popped only after all of its children were popped.
 
-Parity: verl/models/mcore/tpr/segment_plan.py:36-313 (SegmentLossTerm,
-SegmentSpec, SegmentEvent, SegmentPlan.dfs_events / validate_events).
+Internally the plan keeps the tree as a parent map plus ordered child tuples; the canonical walk
+(:meth:`SegmentPlan.dfs_events`) is derived from the preorder with depths, and
+:meth:`SegmentPlan.validate_events` replays a caller's stream against the open path.
+
+Parity: the public types of verl/models/mcore/tpr/segment_plan.py:36-313 (SegmentLossTerm,
+SegmentSpec, SegmentEvent(Kind), Push/PopSegment, SegmentPlan with dfs_events /
+validate_events); the implementation and messages are this framework's own.
 """
 
 from __future__ import annotations
@@ -29,17 +36,22 @@ def _is_int(value) -> bool:
 
 
 def check_nonneg_int(value, name: str) -> int:
-    if not _is_int(value) or value < 0:
-        raise ValueError(f"{name} must be a non-negative integer, got {value!r}")
-    return value
+    """``value`` if it is a plain non-negative int (bools rejected), else ``ValueError``."""
+    if _is_int(value) and value >= 0:
+        return value
+    raise ValueError(f"{name}: expected an int >= 0, got {value!r}")
+
+
+def _finite_number(value) -> bool:
+    return isinstance(value, (int, float)) and not isinstance(value, bool) and math.isfinite(value)
 
 
 @dataclass(frozen=True, slots=True)
 class SegmentLossTerm:
     """A weighted next-token CE term predicted by one query row of a segment.
 
-    Several terms may share a ``query_offset``: the last row of a branching
-    segment predicts the first token of each child.
+    Several terms may share a ``query_offset``: the last row of a branching segment predicts the
+    first token of each child.
     """
 
     query_offset: int
@@ -50,17 +62,15 @@ class SegmentLossTerm:
     def __post_init__(self) -> None:
         check_nonneg_int(self.query_offset, "query_offset")
         check_nonneg_int(self.target_token_id, "target_token_id")
-        if isinstance(self.weight, bool) or not isinstance(self.weight, (int, float)):
-            raise ValueError(f"weight must be a finite number, got {self.weight!r}")
-        if not math.isfinite(self.weight) or self.weight < 0:
-            raise ValueError(f"weight must be finite and non-negative, got {self.weight!r}")
+        if not _finite_number(self.weight) or self.weight < 0:
+            raise ValueError(f"weight: expected a finite number >= 0, got {self.weight!r}")
         if self.sample_id is not None:
             check_nonneg_int(self.sample_id, "sample_id")
 
 
 @dataclass(frozen=True, slots=True)
 class SegmentSpec:
-    """One non-empty contiguous token segment (CPU ``int64`` token ids)."""
+    """One non-empty contiguous token segment (CPU ``int64`` token ids, privately copied)."""
 
     segment_id: SegmentId
     parent_id: SegmentId | None
@@ -70,37 +80,36 @@ class SegmentSpec:
     loss_terms: tuple[SegmentLossTerm, ...] = field(default_factory=tuple)
 
     def __post_init__(self) -> None:
-        check_nonneg_int(self.segment_id, "segment_id")
-        if self.parent_id is not None:
-            check_nonneg_int(self.parent_id, "parent_id")
-            if self.parent_id == self.segment_id:
-                raise ValueError(f"segment {self.segment_id} cannot be its own parent")
+        for name in ("segment_id", "position_start", "prefix_length"):
+            check_nonneg_int(getattr(self, name), name)
+        if self.parent_id is not None and check_nonneg_int(self.parent_id, "parent_id") == self.segment_id:
+            raise ValueError(f"segment {self.segment_id} names itself as parent")
         tok = self.token_ids
         if not isinstance(tok, Tensor):
-            raise TypeError("token_ids must be a torch.Tensor")
-        if tok.device.type != "cpu" or tok.dtype != torch.long or tok.ndim != 1:
-            raise ValueError(
-                "token_ids must be a 1-D CPU torch.long tensor, got "
-                f"shape={tuple(tok.shape)} dtype={tok.dtype} device={tok.device}"
-            )
-        if tok.numel() == 0:
-            raise ValueError("token_ids must contain at least one token")
-        if bool((tok < 0).any()):
-            raise ValueError("token_ids must be non-negative")
-        check_nonneg_int(self.position_start, "position_start")
-        check_nonneg_int(self.prefix_length, "prefix_length")
+            raise TypeError(f"token_ids: expected a torch.Tensor, got {type(tok).__name__}")
+        problems = []
+        if tok.ndim != 1:
+            problems.append(f"{tok.ndim} dims")
+        if tok.dtype != torch.long:
+            problems.append(f"dtype {tok.dtype}")
+        if tok.device.type != "cpu":
+            problems.append(f"device {tok.device}")
+        if problems:
+            raise ValueError("token_ids: expected a 1-D int64 CPU tensor, got " + ", ".join(problems))
+        n = int(tok.numel())
+        if n == 0:
+            raise ValueError(f"segment {self.segment_id} has no tokens")
+        if int(tok.min()) < 0:
+            raise ValueError(f"segment {self.segment_id} contains a negative token id")
         terms = tuple(self.loss_terms)
-        for term in terms:
-            if not isinstance(term, SegmentLossTerm):
-                raise TypeError(f"loss_terms must hold SegmentLossTerm, got {type(term).__name__}")
-            if term.query_offset >= tok.numel():
-                raise ValueError(
-                    f"segment {self.segment_id} loss query_offset {term.query_offset} "
-                    f"is outside length {tok.numel()}"
-                )
+        bad = [t for t in terms if not isinstance(t, SegmentLossTerm)]
+        if bad:
+            raise TypeError(f"loss_terms: expected SegmentLossTerm items, got {type(bad[0]).__name__}")
+        late = [t.query_offset for t in terms if t.query_offset >= n]
+        if late:
+            raise ValueError(f"segment {self.segment_id}: loss term query offset {late[0]} is past its {n} rows")
         object.__setattr__(self, "loss_terms", terms)
-        # The plan owns a private copy: later caller mutation cannot leak in.
-        object.__setattr__(self, "token_ids", tok.detach().clone())
+        object.__setattr__(self, "token_ids", tok.detach().clone())   # caller mutations cannot leak in
 
     @property
     def length(self) -> int:
@@ -123,7 +132,7 @@ class SegmentEvent:
 
     def __post_init__(self) -> None:
         if not isinstance(self.kind, SegmentEventKind):
-            raise TypeError(f"kind must be SegmentEventKind, got {type(self.kind).__name__}")
+            raise TypeError(f"kind: expected a SegmentEventKind, got {type(self.kind).__name__}")
         check_nonneg_int(self.segment_id, "segment_id")
 
 
@@ -137,12 +146,55 @@ def PopSegment(segment_id: SegmentId) -> SegmentEvent:  # noqa: N802 (public API
     return SegmentEvent(SegmentEventKind.POP, segment_id)
 
 
+def _index_specs(segments) -> dict[SegmentId, SegmentSpec]:
+    items = segments.values() if isinstance(segments, Mapping) else segments
+    by_id: dict[SegmentId, SegmentSpec] = {}
+    for spec in items:
+        if not isinstance(spec, SegmentSpec):
+            raise TypeError(f"segments: expected SegmentSpec items, got {type(spec).__name__}")
+        if by_id.setdefault(spec.segment_id, spec) is not spec:
+            raise ValueError(f"segment id {spec.segment_id} appears twice")
+    if not by_id:
+        raise ValueError("a segment plan needs at least one segment")
+    return by_id
+
+
+def _check_geometry(by_id: dict[SegmentId, SegmentSpec], root_id: SegmentId) -> None:
+    """The root starts at position 0; every other segment starts exactly where its parent ends."""
+    for spec in by_id.values():
+        if spec.parent_id is None:
+            if spec.segment_id != root_id:
+                raise ValueError(f"segment {spec.segment_id} has no parent but the root is {root_id}")
+            if (spec.prefix_length, spec.position_start) != (0, 0):
+                raise ValueError(f"root segment {root_id} must start at position 0 with no prefix, got "
+                                 f"position_start={spec.position_start}, prefix_length={spec.prefix_length}")
+            continue
+        parent = by_id.get(spec.parent_id)
+        if parent is None:
+            raise ValueError(f"segment {spec.segment_id} refers to parent {spec.parent_id}, which is not in the plan")
+        end = parent.position_end
+        if spec.position_start != end or spec.prefix_length != end:
+            raise ValueError(f"segment {spec.segment_id} starts at position {spec.position_start} with prefix "
+                             f"{spec.prefix_length}; its parent {parent.segment_id} ends at {end}")
+
+
+def _preorder(root_id: SegmentId, children: Mapping[SegmentId, tuple[SegmentId, ...]]) -> list[tuple[SegmentId, int]]:
+    """``(segment, depth)`` in preorder (child insertion order), iterative."""
+    out: list[tuple[SegmentId, int]] = []
+    todo = [(root_id, 0)]
+    while todo:
+        sid, depth = todo.pop()
+        out.append((sid, depth))
+        todo.extend((c, depth + 1) for c in reversed(children[sid]))
+    return out
+
+
 @dataclass(frozen=True, slots=True)
 class SegmentPlan:
     """Validated rooted segment tree, host metadata only.
 
-    ``topology_only`` plans carry no CE terms: an external objective (PPO)
-    owns the loss and its normaliser.
+    ``topology_only`` plans carry no CE terms: an external objective (PPO) owns the loss and its
+    normaliser.
     """
 
     segments: Mapping[SegmentId, SegmentSpec] | Sequence[SegmentSpec]
@@ -153,97 +205,62 @@ class SegmentPlan:
 
     def __post_init__(self) -> None:
         check_nonneg_int(self.root_id, "root_id")
-        items = self.segments.values() if isinstance(self.segments, Mapping) else self.segments
-        by_id: dict[SegmentId, SegmentSpec] = {}
-        for spec in items:
-            if not isinstance(spec, SegmentSpec):
-                raise TypeError(f"segments must hold SegmentSpec, got {type(spec).__name__}")
-            if spec.segment_id in by_id:
-                raise ValueError(f"duplicate segment_id {spec.segment_id}")
-            by_id[spec.segment_id] = spec
-        if not by_id:
-            raise ValueError("segments must not be empty")
+        by_id = _index_specs(self.segments)
         if self.root_id not in by_id:
-            raise ValueError(f"root_id {self.root_id} does not exist")
-        roots = sorted(s.segment_id for s in by_id.values() if s.parent_id is None)
-        if roots != [self.root_id]:
-            raise ValueError(f"plan must have exactly root {self.root_id}, got roots={roots}")
-
-        children: dict[SegmentId, list[SegmentId]] = {sid: [] for sid in by_id}
+            raise ValueError(f"root_id {self.root_id} is not one of the plan's segments")
+        _check_geometry(by_id, self.root_id)
+        kids: dict[SegmentId, list[SegmentId]] = {sid: [] for sid in by_id}
         for spec in by_id.values():
-            if spec.parent_id is None:
-                if spec.prefix_length != 0 or spec.position_start != 0:
-                    raise ValueError("root segment must have prefix_length=0 and position_start=0")
-                continue
-            parent = by_id.get(spec.parent_id)
-            if parent is None:
-                raise ValueError(f"segment {spec.segment_id} has missing parent {spec.parent_id}")
-            if spec.prefix_length != parent.position_end or spec.position_start != parent.position_end:
-                raise ValueError(
-                    f"segment {spec.segment_id} must start at parent {parent.segment_id} end "
-                    f"{parent.position_end}, got prefix_length={spec.prefix_length}, "
-                    f"position_start={spec.position_start}"
-                )
-            children[spec.parent_id].append(spec.segment_id)
-
-        # Reachability (the position rule already excludes cycles through the root,
-        # but a detached cycle of non-root segments must still be rejected).
-        seen: set[SegmentId] = set()
-        stack = [self.root_id]
-        while stack:
-            sid = stack.pop()
-            if sid in seen:
-                raise ValueError(f"cycle detected at segment {sid}")
-            seen.add(sid)
-            stack.extend(children[sid])
-        if seen != set(by_id):
-            raise ValueError(f"segments are not reachable from root: {sorted(set(by_id) - seen)}")
-
-        inferred = sum(t.weight for s in by_id.values() for t in s.loss_terms)
+            if spec.parent_id is not None:
+                kids[spec.parent_id].append(spec.segment_id)
+        children = {sid: tuple(v) for sid, v in kids.items()}
+        # Every segment has one parent and positions grow along edges, so a segment missing from the
+        # root's preorder sits in a cycle detached from the root.
+        reached = {sid for sid, _ in _preorder(self.root_id, children)}
+        if reached != set(by_id):
+            raise ValueError(f"segments {sorted(set(by_id) - reached)} cannot be reached from root {self.root_id}")
+        has_terms = any(spec.loss_terms for spec in by_id.values())
         if self.topology_only:
-            if any(s.loss_terms for s in by_id.values()) or self.total_loss_weight is not None:
-                raise ValueError("topology_only plans must not carry CE loss terms or total_loss_weight")
+            if has_terms or self.total_loss_weight is not None:
+                raise ValueError("a topology_only plan describes structure only: it takes no loss terms and no "
+                                 "total_loss_weight")
             total = None
         else:
-            total = inferred if self.total_loss_weight is None else self.total_loss_weight
-            if (
-                isinstance(total, bool)
-                or not isinstance(total, (int, float))
-                or not math.isfinite(total)
-                or total <= 0
-            ):
-                raise ValueError(f"total_loss_weight must be finite and positive, got {total!r}")
+            total = self.total_loss_weight
+            if total is None:
+                total = sum(t.weight for spec in by_id.values() for t in spec.loss_terms)
+            if not _finite_number(total) or total <= 0:
+                raise ValueError(f"total_loss_weight: expected a finite number > 0, got {total!r}")
             total = float(total)
         object.__setattr__(self, "segments", MappingProxyType(by_id))
-        object.__setattr__(self, "_children", MappingProxyType({k: tuple(v) for k, v in children.items()}))
+        object.__setattr__(self, "_children", MappingProxyType(children))
         object.__setattr__(self, "total_loss_weight", total)
 
     # ------------------------------------------------------------------ queries
     def get(self, segment_id: SegmentId) -> SegmentSpec:
-        try:
-            return self.segments[segment_id]
-        except KeyError as exc:
-            raise KeyError(f"unknown segment_id {segment_id}") from exc
+        spec = self.segments.get(segment_id)
+        if spec is None:
+            raise KeyError(f"segment {segment_id} is not in this plan")
+        return spec
 
     def parent_of(self, segment_id: SegmentId) -> SegmentSpec | None:
-        spec = self.get(segment_id)
-        return None if spec.parent_id is None else self.segments[spec.parent_id]
-
-    def children_of(self, segment_id: SegmentId) -> tuple[SegmentSpec, ...]:
-        self.get(segment_id)
-        return tuple(self.segments[c] for c in self._children[segment_id])
+        pid = self.get(segment_id).parent_id
+        return None if pid is None else self.segments[pid]
 
     def child_ids(self, segment_id: SegmentId) -> tuple[SegmentId, ...]:
         self.get(segment_id)
         return self._children[segment_id]
 
+    def children_of(self, segment_id: SegmentId) -> tuple[SegmentSpec, ...]:
+        return tuple(self.segments[c] for c in self.child_ids(segment_id))
+
     def path_to(self, segment_id: SegmentId) -> tuple[SegmentSpec, ...]:
-        path = []
-        spec: SegmentSpec | None = self.get(segment_id)
-        while spec is not None:
-            path.append(spec)
-            spec = None if spec.parent_id is None else self.segments[spec.parent_id]
-        return tuple(reversed(path))
+        """Root-to-``segment_id`` specs."""
+        chain = [self.get(segment_id)]
+        while chain[-1].parent_id is not None:
+            chain.append(self.segments[chain[-1].parent_id])
+        chain.reverse()
+        return tuple(chain)
 
     def depth_of(self, segment_id: SegmentId) -> int:
         return len(self.path_to(segment_id)) - 1
@@ -254,50 +271,51 @@ class SegmentPlan:
 
     # ------------------------------------------------------------------ events
     def dfs_events(self) -> Iterator[SegmentEvent]:
-        """Deterministic DFS in child insertion order (iterative, no recursion limit)."""
-        stack: list[tuple[SegmentId, bool]] = [(self.root_id, False)]
-        while stack:
-            sid, done = stack.pop()
-            if done:
-                yield PopSegment(sid)
-                continue
+        """Canonical depth-first walk in child insertion order.
+
+        From the preorder with depths: before entering a segment at depth ``d`` every open segment
+        at depth ``>= d`` is closed (popped), and the walk ends by closing the remaining path."""
+        open_path: list[SegmentId] = []
+        for sid, depth in _preorder(self.root_id, self._children):
+            while len(open_path) > depth:
+                yield PopSegment(open_path.pop())
             yield PushSegment(sid)
-            stack.append((sid, True))
-            for child in reversed(self._children[sid]):
-                stack.append((child, False))
+            open_path.append(sid)
+        while open_path:
+            yield PopSegment(open_path.pop())
 
     def validate_events(self, events: Iterable[SegmentEvent]) -> tuple[SegmentEvent, ...]:
-        """Check stack discipline and that every segment is pushed and popped once."""
+        """Replay ``events`` against the open path; return them as a tuple if they form a complete
+        depth-first walk of this plan (every segment pushed and popped exactly once)."""
         seq = tuple(events)
-        stack: list[SegmentId] = []
-        pushed: set[SegmentId] = set()
-        popped: set[SegmentId] = set()
-        for ev in seq:
+        open_path: list[SegmentId] = []
+        state: dict[SegmentId, str] = {}                                 # "open" | "closed"
+        unfinished = {sid: len(c) for sid, c in self._children.items()}  # children not yet closed
+        for i, ev in enumerate(seq):
             if not isinstance(ev, SegmentEvent):
-                raise TypeError(f"events must hold SegmentEvent, got {type(ev).__name__}")
+                raise TypeError(f"event {i}: expected a SegmentEvent, got {type(ev).__name__}")
             spec = self.get(ev.segment_id)
+            sid = ev.segment_id
             if ev.kind is SegmentEventKind.PUSH:
-                if ev.segment_id in pushed:
-                    raise ValueError(f"segment {ev.segment_id} is pushed more than once")
-                top = stack[-1] if stack else None
-                if spec.parent_id != top:
-                    raise ValueError(
-                        f"cannot push segment {ev.segment_id}: expected parent on stack "
-                        f"{spec.parent_id}, got {top}"
-                    )
-                stack.append(ev.segment_id)
-                pushed.add(ev.segment_id)
-            else:
-                if not stack or stack[-1] != ev.segment_id:
-                    raise ValueError(f"cannot pop segment {ev.segment_id}: current stack is {stack}")
-                if any(c not in popped for c in self._children[ev.segment_id]):
-                    raise ValueError(f"cannot pop segment {ev.segment_id} before all children")
-                stack.pop()
-                popped.add(ev.segment_id)
-        every = set(self.segments)
-        if stack or pushed != every or popped != every:
-            raise ValueError(
-                f"incomplete event stream: stack={stack}, unpushed={sorted(every - pushed)}, "
-                f"unpopped={sorted(every - popped)}"
-            )
+                if sid in state:
+                    raise ValueError(f"event {i}: segment {sid} was already pushed")
+                on_top = open_path[-1] if open_path else None
+                if on_top != spec.parent_id:
+                    raise ValueError(f"event {i}: push of segment {sid} needs its parent {spec.parent_id} on top "
+                                     f"of the open path, found {on_top}")
+                open_path.append(sid)
+                state[sid] = "open"
+                continue
+            if not open_path or open_path[-1] != sid:
+                raise ValueError(f"event {i}: pop of segment {sid} while the open path is {open_path}")
+            if unfinished[sid]:
+                raise ValueError(f"event {i}: segment {sid} still has {unfinished[sid]} child(ren) to pop")
+            open_path.pop()
+            state[sid] = "closed"
+            if spec.parent_id is not None:
+                unfinished[spec.parent_id] -= 1
+        missing = sorted(sid for sid in self.segments if state.get(sid) != "closed")
+        if open_path or missing:
+            raise ValueError(f"the event stream ends early: open path {open_path}, segments not completed "
+                             f"{missing}")
         return seq

@@ -27,21 +27,24 @@ import torch
 from .segment_plan import _is_int
 
 
+def _need(ok: bool, message: str) -> None:
+    if not ok:
+        raise ValueError(message)
+
+
 @dataclass(frozen=True, slots=True)
 class SegmentRef:
-    """Zero-copy reference ``input_ids[row][start:end]``."""
+    """Zero-copy reference ``input_ids[row][start:end]`` (``end > start``)."""
 
     row: int
     start: int
     end: int
 
     def __post_init__(self) -> None:
-        if not _is_int(self.row) or self.row < 0:
-            raise ValueError(f"row must be a non-negative integer, got {self.row!r}")
-        if not _is_int(self.start) or self.start < 0:
-            raise ValueError(f"start must be a non-negative integer, got {self.start!r}")
-        if not _is_int(self.end) or self.end <= self.start:
-            raise ValueError(f"end must be an integer > start, got {self.end!r}")
+        for name in ("row", "start", "end"):
+            v = getattr(self, name)
+            _need(_is_int(v) and v >= 0, f"SegmentRef.{name}: expected an int >= 0, got {v!r}")
+        _need(self.end > self.start, f"SegmentRef [{self.start}, {self.end}) is empty")
 
     @property
     def length(self) -> int:
@@ -50,6 +53,8 @@ class SegmentRef:
 
 @dataclass(frozen=True, slots=True)
 class TrajectoryNode:
+    """One trie node: the token span its member rows share, the rows that end here, its children."""
+
     node_id: int
     parent_id: int | None
     segment: SegmentRef
@@ -58,18 +63,16 @@ class TrajectoryNode:
     children: tuple[int, ...]
 
     def __post_init__(self) -> None:
-        if not _is_int(self.node_id) or self.node_id < 0:
-            raise ValueError(f"node_id must be a non-negative integer, got {self.node_id!r}")
-        if self.parent_id is not None and (
-            not _is_int(self.parent_id) or self.parent_id < 0 or self.parent_id == self.node_id
-        ):
-            raise ValueError(f"invalid parent_id {self.parent_id!r} for node {self.node_id}")
-        if not self.member_rows:
-            raise ValueError(f"node {self.node_id} must contain at least one member row")
-        if len(set(self.member_rows)) != len(self.member_rows):
-            raise ValueError(f"node {self.node_id} member_rows must be unique")
-        if not set(self.terminal_rows) <= set(self.member_rows):
-            raise ValueError(f"node {self.node_id} terminal_rows must be a subset of member_rows")
+        nid = self.node_id
+        _need(_is_int(nid) and nid >= 0, f"node_id: expected an int >= 0, got {nid!r}")
+        if self.parent_id is not None:
+            _need(_is_int(self.parent_id) and self.parent_id >= 0 and self.parent_id != nid,
+                  f"trie node {nid}: parent_id {self.parent_id!r} is not another node's id")
+        members = set(self.member_rows)
+        _need(len(members) == len(self.member_rows) > 0,
+              f"trie node {nid}: member_rows must be distinct and non-empty, got {self.member_rows}")
+        _need(members.issuperset(self.terminal_rows),
+              f"trie node {nid}: terminal rows {sorted(set(self.terminal_rows) - members)} are not members")
 
 
 @dataclass(frozen=True, slots=True)
@@ -83,43 +86,36 @@ class TrajectoryTree:
     nodes: Mapping[int, TrajectoryNode]
 
     def __post_init__(self) -> None:
-        nodes = dict(self.nodes)
-        root = nodes.get(self.root_id)
-        if root is None:
-            raise ValueError(f"root_id {self.root_id} does not exist")
-        if root.parent_id is not None:
-            raise ValueError("trajectory tree root must not have a parent")
-        if root.segment.start != 0:
-            raise ValueError("trajectory tree executable root must start at token position 0")
-        if tuple(root.member_rows) != tuple(self.member_rows):
-            raise ValueError("trajectory tree member_rows must match root member_rows")
-        for nid, node in nodes.items():
-            if nid != node.node_id:
-                raise ValueError(f"node mapping key {nid} does not match node_id {node.node_id}")
-            if node.parent_id is not None and node.parent_id not in nodes:
-                raise ValueError(f"node {nid} has missing parent {node.parent_id}")
+        table = dict(self.nodes)
+        _need(all(k == n.node_id for k, n in table.items()), "trie nodes must be keyed by their node_id")
+        root = table.get(self.root_id)
+        _need(root is not None, f"trie root {self.root_id} is not among the nodes")
+        _need(root.parent_id is None and root.segment.start == 0,
+              f"trie root {self.root_id} must be parentless and begin at token 0")
+        _need(tuple(root.member_rows) == tuple(self.member_rows),
+              f"tree rows {self.member_rows} differ from its root's rows {root.member_rows}")
+        # Edges must agree from both ends, and each child continues where its parent stops.
+        for nid, node in table.items():
+            _need(node.parent_id is None or node.parent_id in table,
+                  f"trie node {nid} points at parent {node.parent_id}, which is not in the tree")
             for cid in node.children:
-                child = nodes.get(cid)
-                if child is None:
-                    raise ValueError(f"node {nid} has missing child {cid}")
-                if child.parent_id != nid:
-                    raise ValueError(f"node {nid} child {cid} has inconsistent parent")
-                if child.segment.start != node.segment.end:
-                    raise ValueError(
-                        f"node {cid} must start at parent {nid} end {node.segment.end}, "
-                        f"got {child.segment.start}"
-                    )
-        object.__setattr__(self, "nodes", MappingProxyType(nodes))
+                child = table.get(cid)
+                _need(child is not None and child.parent_id == nid,
+                      f"trie node {nid} lists child {cid}, which does not name {nid} as its parent")
+                _need(child.segment.start == node.segment.end,
+                      f"trie node {cid} begins at token {child.segment.start}, not where its parent {nid} "
+                      f"ends ({node.segment.end})")
+        object.__setattr__(self, "nodes", MappingProxyType(table))
 
     @property
     def key(self) -> str:
         return f"{self.uid}:{self.tree_index}"
 
     def get(self, node_id: int) -> TrajectoryNode:
-        try:
-            return self.nodes[node_id]
-        except KeyError as exc:
-            raise KeyError(f"unknown trajectory node {node_id}") from exc
+        node = self.nodes.get(node_id)
+        if node is None:
+            raise KeyError(f"trie {self.key} has no node {node_id}")
+        return node
 
     @property
     def unique_tokens(self) -> int:

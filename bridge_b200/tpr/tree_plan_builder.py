@@ -6,12 +6,16 @@ may sit in the *parent* segment when ``t`` is the first token of a child.  Every
 supervised logical token maps to exactly one :class:`SegmentObjectiveRef`;
 duplicate trajectories keep separate refs.
 
-Parity: verl/models/mcore/tpr/tree_plan_builder.py:21-212.
+Lowering runs in three stages: per-row supervised offsets (with the optional loss-mask check),
+one topology-only :class:`SegmentPlan` per trie, and a vectorised ownership search per row over
+the row's root-to-terminal node chain (found by walking parent links up from the terminal node).
+
+Parity: the data contract of verl/models/mcore/tpr/tree_plan_builder.py:21-212 (same public types,
+same batch fields and the same ownership rule); the implementation is this framework's own.
 """
 
 from __future__ import annotations
 
-from bisect import bisect_right
 from collections.abc import Sequence
 from dataclasses import dataclass
 from typing import Any
@@ -106,13 +110,15 @@ class ForestExecutionPlan:
 
 
 def _tensor_rows(batch: Any, key: str) -> list[torch.Tensor]:
+    """Rows of ``batch[key]`` as 1-D tensors (a list/tuple of rows or a tensor split along dim 0)."""
     try:
         value = batch[key]
     except (KeyError, TypeError) as exc:
-        raise ValueError(f"batch is missing {key!r}") from exc
+        raise ValueError(f"the mini-batch has no {key!r} field") from exc
     rows = list(value) if isinstance(value, (list, tuple)) else list(value.unbind())
-    if not all(isinstance(r, torch.Tensor) and r.ndim == 1 for r in rows):
-        raise ValueError(f"{key!r} must contain one-dimensional tensor rows")
+    odd = next((i for i, r in enumerate(rows) if not (isinstance(r, torch.Tensor) and r.ndim == 1)), None)
+    if odd is not None:
+        raise ValueError(f"{key}[{odd}] is not a 1-D tensor")
     return rows
 
 
@@ -121,6 +127,92 @@ def _has(batch: Any, key: str) -> bool:
         return key in batch
     except TypeError:
         return False
+
+
+def _supervised_offsets(inputs, masks, responses) -> list[np.ndarray]:
+    """Per row: response offsets whose mask is set (the tokens that carry a PPO term)."""
+    out = []
+    for row, (tokens, mask) in enumerate(zip(inputs, masks)):
+        n_tok, n_resp = tokens.numel(), mask.numel()
+        if n_resp > n_tok:
+            raise ValueError(f"row {row}: response_mask has {n_resp} entries for only {n_tok} input tokens")
+        if responses is not None:
+            resp = responses[row]
+            if resp.numel() != n_resp:
+                raise ValueError(f"row {row}: responses has {resp.numel()} tokens, response_mask {n_resp}")
+            if not torch.equal(tokens[n_tok - n_resp:].cpu(), resp.cpu()):
+                raise ValueError(f"row {row}: responses differ from the tail of input_ids")
+        offs = np.flatnonzero(mask.detach().to(torch.bool).cpu().numpy()).astype(np.int64)
+        if offs.size and n_tok - n_resp + int(offs[0]) == 0:
+            raise ValueError(f"row {row}: token 0 is supervised, but no earlier token can predict it")
+        out.append(offs)
+    return out
+
+
+def _check_loss_mask(batch, inputs, masks) -> None:
+    """``loss_mask`` (response-aligned or full-length) must select exactly the response-mask tokens."""
+    lms = _tensor_rows(batch, "loss_mask")
+    if len(lms) != len(masks):
+        raise ValueError(f"loss_mask has {len(lms)} rows, response_mask {len(masks)}")
+    for row, (lm, rm) in enumerate(zip(lms, masks)):
+        lm, rm = lm.to(torch.bool).cpu(), rm.to(torch.bool).cpu()
+        n_prompt = inputs[row].numel() - rm.numel()
+        if lm.numel() == inputs[row].numel() and lm.numel() != rm.numel():
+            if bool(lm[:n_prompt].any()):
+                raise ValueError(f"row {row}: loss_mask selects prompt tokens")
+            lm = lm[n_prompt:]
+        if lm.numel() != rm.numel():
+            raise ValueError(f"row {row}: loss_mask length {lm.numel()} fits neither the response "
+                             f"({rm.numel()}) nor the whole row ({inputs[row].numel()})")
+        if not torch.equal(lm, rm):
+            raise ValueError(f"row {row}: loss_mask and response_mask select different tokens")
+
+
+def _tree_segment_plan(tree: TrajectoryTree, inputs) -> SegmentPlan:
+    specs = []
+    for node in tree.nodes.values():
+        ref = node.segment
+        ids = inputs[ref.row][ref.start:ref.end].detach().to("cpu", torch.long)
+        specs.append(SegmentSpec(segment_id=node.node_id, parent_id=node.parent_id, token_ids=ids,
+                                 position_start=ref.start, prefix_length=ref.start))
+    return SegmentPlan(specs, root_id=tree.root_id, topology_only=True)
+
+
+def _row_chains(tree: TrajectoryTree) -> dict[int, np.ndarray]:
+    """Member row -> node ids from the root down to the node where the row ends."""
+    chains: dict[int, np.ndarray] = {}
+    for node in tree.nodes.values():
+        if not node.terminal_rows:
+            continue
+        up = [node.node_id]
+        while tree.get(up[-1]).parent_id is not None:
+            up.append(tree.get(up[-1]).parent_id)
+        chain = np.asarray(up[::-1], dtype=np.int64)
+        for row in node.terminal_rows:
+            if row in chains:
+                raise ValueError(f"tree {tree.key}: row {row} ends at two different nodes")
+            chains[row] = chain
+    if set(chains) != set(tree.member_rows):
+        raise ValueError(f"tree {tree.key}: rows {sorted(set(tree.member_rows) - set(chains))} end at no node")
+    return chains
+
+
+def _row_refs(tree: TrajectoryTree, chain: np.ndarray, row: int, tokens, n_resp: int, off: np.ndarray) -> np.ndarray:
+    """Ref columns of one row: the token at response offset ``off`` (absolute position ``t``) is
+    predicted by query ``t - 1``, owned by the first node of the chain whose span contains it."""
+    spans = np.asarray([(tree.get(int(n)).segment.start, tree.get(int(n)).segment.end) for n in chain],
+                       dtype=np.int64).reshape(-1, 2)
+    t = tokens.numel() - n_resp + off
+    q = t - 1
+    k = np.searchsorted(spans[:, 1], q, side="right")
+    outside = k >= len(chain)
+    if bool(outside.any()):
+        raise ValueError(f"row {row}: query position {int(q[outside][0])} lies past the row's last node")
+    kk = np.minimum(k, len(chain) - 1)
+    if not bool((spans[kk, 0] <= q).all()):
+        raise ValueError(f"row {row}: a query position falls between node spans")
+    targets = tokens.detach().cpu().numpy().astype(np.int64)[t]
+    return np.stack([chain[k], q - spans[k, 0], targets, np.full_like(off, row), off], axis=1)
 
 
 def build_tree_execution_plans(
@@ -145,97 +237,26 @@ def build_tree_execution_plans(
             trees = build_trajectory_trees(keys, batch)
     inputs = _tensor_rows(batch, "input_ids")
     masks = _tensor_rows(batch, "response_mask")
-    if len(keys) != len(inputs) or len(keys) != len(masks):
-        raise ValueError("keys, input_ids and response_mask must have identical row counts")
+    if not len(keys) == len(inputs) == len(masks):
+        raise ValueError(f"row counts differ: {len(keys)} keys, {len(inputs)} input_ids, {len(masks)} response_mask")
     responses = _tensor_rows(batch, "responses") if _has(batch, "responses") else None
-
-    supervised: list[np.ndarray] = []
-    expected = 0
-    for row, (tokens, mask) in enumerate(zip(inputs, masks)):
-        if mask.numel() > tokens.numel():
-            raise ValueError(f"response_mask[{row}] is longer than input_ids[{row}]")
-        if responses is not None:
-            resp = responses[row]
-            if resp.numel() != mask.numel():
-                raise ValueError(f"responses/response_mask length mismatch on row {row}")
-            if not torch.equal(tokens[tokens.numel() - resp.numel():].cpu(), resp.cpu()):
-                raise ValueError(f"response is not an input_ids suffix on row {row}")
-        offs = np.flatnonzero(mask.detach().to(torch.bool).cpu().numpy()).astype(np.int64)
-        if offs.size and tokens.numel() - mask.numel() + int(offs[0]) == 0:
-            raise ValueError(f"row {row} has no preceding query token for first supervised token")
-        supervised.append(offs)
-        expected += int(offs.size)
-
+    supervised = _supervised_offsets(inputs, masks, responses)
     if require_loss_mask_alignment:
-        loss_masks = _tensor_rows(batch, "loss_mask")
-        if len(loss_masks) != len(keys):
-            raise ValueError("loss_mask rows do not match keys")
-        for row, (lm, rm) in enumerate(zip(loss_masks, masks)):
-            if lm.numel() == rm.numel():
-                aligned = lm
-            elif lm.numel() == inputs[row].numel():
-                aligned = lm[lm.numel() - rm.numel():]
-                if bool(lm[: lm.numel() - rm.numel()].to(torch.bool).any()):
-                    raise ValueError(f"row {row} loss_mask includes prompt tokens")
-            else:
-                raise ValueError(f"row {row} loss_mask shape is incompatible with response_mask")
-            if not torch.equal(aligned.to(torch.bool).cpu(), rm.to(torch.bool).cpu()):
-                raise ValueError(f"row {row} response_mask and loss_mask disagree")
+        _check_loss_mask(batch, inputs, masks)
 
-    consumed: set[int] = set()
+    owner_tree: dict[int, int] = {}
     plans: list[TreeExecutionPlan] = []
-    for tree in trees:
-        specs = []
-        for node in tree.nodes.values():
-            ref = node.segment
-            ids = inputs[ref.row][ref.start:ref.end].detach().to("cpu", torch.long)
-            specs.append(SegmentSpec(segment_id=node.node_id, parent_id=node.parent_id, token_ids=ids,
-                                     position_start=ref.start, prefix_length=ref.start))
-        plan = SegmentPlan(specs, root_id=tree.root_id, topology_only=True)
-
-        # Root-to-terminal path of every member row.
-        path_of: dict[int, tuple[int, ...]] = {}
-        stack = [(tree.root_id, ())]
-        while stack:
-            nid, path = stack.pop()
-            node = tree.get(nid)
-            here = (*path, nid)
-            for row in node.terminal_rows:
-                if row in path_of:
-                    raise ValueError(f"trajectory row {row} has multiple terminal nodes")
-                path_of[row] = here
-            stack.extend((c, here) for c in node.children)
-        if set(path_of) != set(tree.member_rows):
-            raise ValueError(f"tree {tree.key} terminal rows do not cover members")
-
-        # ownership search, vectorised per row: token t (response offset `off`) is predicted by query
-        # q = t - 1, owned by the first node on the row's root-to-terminal path whose end exceeds q
-        parts: list[np.ndarray] = []
+    for ti, tree in enumerate(trees):
+        chains = _row_chains(tree)
+        parts = []
         for row in tree.member_rows:
-            if row in consumed:
-                raise ValueError(f"row {row} appears in more than one tree")
-            consumed.add(row)
-            off = supervised[row]
-            if not off.size:
-                continue
-            ids = inputs[row]
-            resp_start = ids.numel() - masks[row].numel()
-            path = np.asarray(path_of[row], dtype=np.int64)
-            segs = [tree.get(int(n)).segment for n in path]
-            ends = np.asarray([sg.end for sg in segs], dtype=np.int64)
-            starts = np.asarray([sg.start for sg in segs], dtype=np.int64)
-            t = resp_start + off
-            q = t - 1
-            k = np.searchsorted(ends, q, side="right")
-            if bool((k >= len(path)).any()):
-                raise ValueError(f"row {row} query position {int(q[k >= len(path)][0])} is outside tree")
-            if not bool(((starts[k] <= q) & (q < ends[k])).all()):
-                raise ValueError(f"row {row} has uncovered query positions")
-            targets = ids.detach().cpu().numpy().astype(np.int64)[t]
-            parts.append(np.stack([path[k], q - starts[k], targets, np.full_like(off, row), off], axis=1))
+            if owner_tree.setdefault(row, ti) != ti:
+                raise ValueError(f"row {row} belongs to trees {owner_tree[row]} and {ti}")
+            if supervised[row].size:
+                parts.append(_row_refs(tree, chains[row], row, inputs[row], masks[row].numel(), supervised[row]))
         refs = ObjectiveRefs(np.concatenate(parts) if parts else np.zeros((0, 5), dtype=np.int64))
-        plans.append(TreeExecutionPlan(tree=tree, segment_plan=plan, objective_refs=refs))
-
-    if consumed != set(range(len(keys))):
-        raise ValueError(f"forest does not cover all input rows: {sorted(set(range(len(keys))) - consumed)}")
-    return ForestExecutionPlan(tuple(plans), logical_loss_tokens=expected)
+        plans.append(TreeExecutionPlan(tree=tree, segment_plan=_tree_segment_plan(tree, inputs), objective_refs=refs))
+    orphans = sorted(set(range(len(keys))) - set(owner_tree))
+    if orphans:
+        raise ValueError(f"rows {orphans} are in no tree")
+    return ForestExecutionPlan(tuple(plans), logical_loss_tokens=sum(int(o.size) for o in supervised))

@@ -38,6 +38,30 @@ def tree_batch(*, n_trees=1, prefix=128, siblings=4, resp=64, vocab=1024, seed=0
     return batch
 
 
+def nested_tree_batch(*, n_trees=2, prefix=128, branches=2, mid=32, siblings=2, resp=32, vocab=1024, seed=0):
+    """Two-level trees: prompt -> ``branches`` shared middle turns -> ``siblings`` responses each.
+
+    The response of a row is its middle turn plus its own tail (all supervised), so internal segments
+    below the root own loss terms too."""
+    g = torch.Generator().manual_seed(seed)
+    ids, rmask, old, adv, uids = [], [], [], [], []
+    for t in range(n_trees):
+        p = torch.randint(0, vocab, (prefix,), generator=g)
+        for b in range(branches):
+            m = torch.randint(0, vocab, (mid,), generator=g)
+            for s in range(siblings):
+                r = torch.randint(0, vocab, (resp,), generator=g)
+                ids.append(torch.cat([p, m, r]))
+                rmask.append(torch.ones(mid + resp, dtype=torch.bool))
+                adv.append(torch.randn(mid + resp, generator=g))
+                old.append(torch.zeros(mid + resp))
+                uids.append(f"n{t}")
+    batch = {"input_ids": ids, "response_mask": rmask, "old_log_probs": old, "advantages": adv, "uid": uids,
+             "temperature": 1.0, "dp_size": 1}
+    batch["batch_num_tokens"] = int(sum(int(m.sum()) for m in rmask))
+    return batch
+
+
 @torch.no_grad()
 def set_old_log_probs(model, batch, *, jitter=0.01, seed=1):
     """old_log_probs = current log-probs minus U(0, jitter) (the config #1 recipe)."""

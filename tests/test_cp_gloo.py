@@ -7,7 +7,8 @@ import torch
 from tests.dist_utils import run_ranks
 
 
-def _worker(rank, world, backend, n_layers, preset="tiny", prefix=128, resp=64, gdn_cp_mode="head"):
+def _worker(rank, world, backend, n_layers, preset="tiny", prefix=128, resp=64, gdn_cp_mode="head",
+            executor="segment"):
     import torch
 
     from bridge_b200.engine import EngineConfig, TPREngine
@@ -24,7 +25,8 @@ def _worker(rank, world, backend, n_layers, preset="tiny", prefix=128, resp=64, 
     loss_ref.backward()
     ps = build_parallel_state(tp=1, cp=world)
     model = build_model(cfg, dtype=torch.float32, seed=0)
-    ec = EngineConfig(context_parallel_size=world, tpr_cp_backend=backend, gdn_cp_mode=gdn_cp_mode)
+    ec = EngineConfig(context_parallel_size=world, tpr_cp_backend=backend, gdn_cp_mode=gdn_cp_mode,
+                      executor=executor)
     eng = TPREngine(cfg, ec, device="cpu", model=model, parallel_state=ps)
     batch["tpr_capture_log_probs"] = True
     out = eng.forward_backward_batch(batch)
@@ -164,7 +166,7 @@ def test_gdn_sequence_sharded_layer_matches_whole_segment():
         assert worst[1] < 1e-4, worst
 
 
-def _tpcp_worker(rank, world, backend, preset="tiny", gdn_cp_mode="head"):
+def _tpcp_worker(rank, world, backend, preset="tiny", gdn_cp_mode="head", executor="segment", nested=False):
     import torch
 
     from bridge_b200.engine import EngineConfig, TPREngine
@@ -173,8 +175,10 @@ def _tpcp_worker(rank, world, backend, preset="tiny", gdn_cp_mode="head"):
     from bridge_b200.parallel.groups import build_parallel_state
     from tests.helpers import flat_ppo_loss, set_old_log_probs, tree_batch
 
+    from tests.helpers import nested_tree_batch
+
     cfg = get_config(preset, num_layers=2 if preset == "tiny" else 4)
-    batch = tree_batch(n_trees=1, prefix=128, siblings=4, resp=64, seed=0)
+    batch = nested_tree_batch() if nested else tree_batch(n_trees=1, prefix=128, siblings=4, resp=64, seed=0)
     ref = build_model(cfg, dtype=torch.float32, seed=0)
     set_old_log_probs(ref, batch)
     loss_ref, _ = flat_ppo_loss(ref, batch)
@@ -182,10 +186,12 @@ def _tpcp_worker(rank, world, backend, preset="tiny", gdn_cp_mode="head"):
     from bridge_b200.models.checkpoint import hf_state_dict, load_hf_state_dict
 
     ps = build_parallel_state(tp=2, cp=2)
-    model = build_model(cfg, dtype=torch.float32, seed=1, tp_group=ps.tp_group)
+    model = build_model(cfg, dtype=torch.float32, seed=1, tp_group=ps.tp_group, sequence_parallel=nested)
     load_hf_state_dict(model, hf_state_dict(ref))          # TP shards of the reference weights
     eng = TPREngine(cfg, EngineConfig(tensor_model_parallel_size=2, context_parallel_size=2, tpr_cp_backend=backend,
-                                      gdn_cp_mode=gdn_cp_mode), device="cpu", model=model, parallel_state=ps)
+                                      gdn_cp_mode=gdn_cp_mode, executor=executor, token_budget=160,
+                                      sequence_parallel=nested),
+                    device="cpu", model=model, parallel_state=ps)
     out = eng.forward_backward_batch(batch)
     # expected TP-sharded gradients: the reference gradients sharded by the same HF -> Megatron loader
     import copy
@@ -232,3 +238,73 @@ def test_hybrid_gdn_cp4_sequence_sharded_matches_flattened():
         worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
         assert worst[1] < 1e-4, worst
 
+
+
+# --------------------------------------------------------------------------- forest executor under CP
+def _forest_worker(rank, world, preset, n_layers, budget, mode):
+    """Segment-granular CP in the batched forest executor vs the flattened batch (FP32, gloo): two
+    two-level trees, a per-rank budget small enough that parents and children land on different ranks."""
+    import torch
+
+    from bridge_b200.engine import EngineConfig, TPREngine
+    from bridge_b200.models import get_config
+    from bridge_b200.models.decoder import build_model
+    from bridge_b200.parallel.groups import build_parallel_state
+    from tests.helpers import flat_ppo_loss, nested_tree_batch, set_old_log_probs
+
+    cfg = get_config(preset, num_layers=n_layers)
+    batch = nested_tree_batch()
+    ref = build_model(cfg, dtype=torch.float32, seed=0)
+    set_old_log_probs(ref, batch)
+    loss_ref, _ = flat_ppo_loss(ref, batch)
+    loss_ref.backward()
+    ps = build_parallel_state(tp=1, cp=world)
+    model = build_model(cfg, dtype=torch.float32, seed=0)
+    ec = EngineConfig(context_parallel_size=world, tpr_cp_backend="ring", executor="forest", token_budget=budget,
+                      forest_mode=mode)
+    eng = TPREngine(cfg, ec, device="cpu", model=model, parallel_state=ps)
+    out = eng.forward_backward_batch(batch)
+    errs = {}
+    for n, p in eng.model.named_parameters():
+        g_ref = dict(ref.named_parameters())[n].grad
+        errs[n] = float((p.main_grad - g_ref).norm() / (g_ref.norm() + 1e-12))
+    return {"loss": out["loss"][0], "loss_ref": float(loss_ref), "grad_rel": errs,
+            "chunks": out["metrics"]["tpr/chunks"][0]}
+
+
+@pytest.mark.parametrize("mode", ["retain", "recompute"])
+def test_forest_cp2_matches_flattened(mode):
+    res = run_ranks(2, _forest_worker, "tiny", 2, 160, mode)
+    for r in res:
+        assert r["chunks"] >= 3, r
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
+
+def test_forest_cp2_hybrid_gdn_matches_flattened():
+    """GDN final states of pushed segments are gathered over CP and seed children on the other rank."""
+    res = run_ranks(2, _forest_worker, "tiny_hybrid", 4, 160, "retain")
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
+
+def test_forest_cp3_idle_rank_matches_flattened():
+    """More ranks than segments at some level: an idle rank forwards a pad segment and still joins every
+    collective."""
+    res = run_ranks(3, _forest_worker, "tiny", 2, 4096, "retain")
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
+
+def test_forest_tp2_cp2_sequence_parallel_matches_flattened():
+    """BASELINE config #2's axes through the forest executor: TP2 (sequence parallel) x CP2."""
+    res = run_ranks(4, _tpcp_worker, "ring", "tiny", "head", "forest", True)
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst

@@ -134,6 +134,39 @@ def test_fused_lm_head_logprob(entropy):
     _close(W.grad, Wr.grad, 5e-2, 3e-2, "dW")
 
 
+@pytest.mark.parametrize("main_grad", [False, True])
+def test_fused_lm_head_ppo(main_grad):
+    """Head + log-prob + PPO loss with the head backward run inside the forward, against FP32 torch: loss,
+    dh (scaled by the loss gradient) and dW (into an FP32 main_grad, or returned to autograd)."""
+    from bridge_b200.ops.logprob import fused_lm_head_ppo, logprob_entropy_reference
+    from bridge_b200.ops.ppo import PPOLossConfig, ppo_loss_reference
+
+    U, H, V, R = 300, 256, 5000, 420
+    h = (torch.randn(U, H, device=DEV) * 0.5).to(torch.bfloat16).requires_grad_()
+    W = (torch.randn(V, H, device=DEV) * 0.05).to(torch.bfloat16).requires_grad_()
+    if main_grad:
+        W.main_grad = torch.zeros(V, H, device=DEV)
+    tg = torch.randint(0, V, (U,), device=DEV)
+    temp = torch.rand(U, device=DEV) + 0.5
+    inv = torch.randint(0, U, (R,), device=DEV)         # duplicate refs share a row
+    old = torch.randn(R, device=DEV) * 0.3 - 9.0
+    adv = torch.randn(R, device=DEV)
+    wts = torch.rand(R, device=DEV)
+    scale = 4.0
+    loss, stats, lp, _ = fused_lm_head_ppo(h, W, tg, temp, inv, old, adv, wts, denom=777.0, clip_low=0.2,
+                                           clip_high=0.2, clip_c=3.0, chunk_rows=128, grad_scale=scale)
+    (loss * scale).backward()
+    hr, Wr = h.detach().float().requires_grad_(), W.detach().float().requires_grad_()
+    lpr, _ = logprob_entropy_reference(hr @ Wr.t(), tg, temp)
+    lr, sr = ppo_loss_reference(lpr[inv], old, adv, 777.0, PPOLossConfig(), wts)
+    (lr * scale).backward()
+    _close(lp, lpr, 5e-2, 1e-2, "lp")
+    _close(loss, lr, 1e-3, 1e-2, "loss")
+    _close(stats, sr, 1e-3, 1e-2, "stats")
+    _close(h.grad, hr.grad, 5e-2, 3e-2, "dh")
+    _close(W.main_grad if main_grad else W.grad, Wr.grad, 5e-2, 3e-2, "dW")
+
+
 def test_ppo_loss():
     from bridge_b200.ops.ppo import PPOLossConfig, ppo_loss, ppo_loss_reference
 
