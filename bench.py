@@ -11,6 +11,12 @@ Parallel layout: by default the named config's TP2 x CP4 at 8 GPUs, scaled down 
 (1 GPU: none, 2: TP2, 4: TP2 x CP2, 8: TP2 x CP4); TP runs with sequence parallelism.  ``--tp`` /
 ``--cp`` override it (``--tp 1 --cp 1`` = pure data parallelism).
 
+``--config 3|4|5`` runs the other BASELINE configs (same metric, same timing): #3 multi-turn session
+trees (qwen_turn policy, 50 % loss mask) on Qwen3-4B at CP = N with activation offload; #4 the hybrid
+GDN/attention model (24 layers, 3 GDN : 1 gated attention, head_dim 256) on 512 + 8 x 512 trees at
+the #2 layout; #5 the Qwen3-Next-shape hybrid MoE (512 experts, top-10, 24 layers) on 1024 + 8 x 1024
+trees at CP2 x EP(N) (CP only from 2 GPUs).
+
 One step = plan the token-trie forest, forward + backward of every segment (prefix KV relayed),
 PPO loss over all supervised tokens, DP gradient finalisation, fused AdamW update.
 
@@ -47,12 +53,13 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="bridge", choices=["bridge", "reference"])
-    p.add_argument("--model", default="qwen3_4b")
-    p.add_argument("--trees-per-gpu", type=int, default=8)
-    p.add_argument("--prefix", type=int, default=512)
+    p.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5], help="BASELINE config number")
+    p.add_argument("--model", default=None, help="default: the config's model")
+    p.add_argument("--trees-per-gpu", type=int, default=None, help="default: the config's (8, #3: 2 sessions)")
+    p.add_argument("--prefix", type=int, default=None)
     p.add_argument("--siblings", type=int, default=8)
-    p.add_argument("--resp", type=int, default=512)
-    p.add_argument("--token-budget", type=int, default=int(os.environ.get("TPR_TOKEN_BUDGET", "16384")))
+    p.add_argument("--resp", type=int, default=None)
+    p.add_argument("--token-budget", type=int, default=int(os.environ.get("TPR_TOKEN_BUDGET", "0")) or None)
     p.add_argument("--mode", default=os.environ.get("TPR_FOREST_MODE", "retain"))
     p.add_argument("--tp", type=int, default=None, help="default: the config-#2 layout for --gpus")
     p.add_argument("--cp", type=int, default=None, help="default: the config-#2 layout for --gpus")
@@ -61,21 +68,47 @@ def parse() -> argparse.Namespace:
                    help="DP gradient path: fused NVLink P2P kernels + sharded optimizer, or NCCL all-reduce")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--seed", type=int, default=0)
-    return p.parse_args()
+    p.add_argument("--ep", type=int, default=None, help="expert parallel size (MoE; default: config #5 layout)")
+    p.add_argument("--profile-step", default=None, metavar="PATH",
+                   help="instead of timing: profile one step after the warm-up (torch.profiler CUDA activity) and "
+                        "write the per-kernel self device time table of each rank to PATH.rank<r>.txt")
+    a = p.parse_args()
+    d = CONFIG_DEFAULTS[a.config]
+    for k, v in d.items():
+        if getattr(a, k) is None:
+            setattr(a, k, v)
+    return a
 
 
-DEFAULT_LAYOUT = {1: (1, 1), 2: (2, 1), 4: (2, 2), 8: (2, 4)}   # gpus -> (tp, cp), config #2 scaled down
+# per-config defaults: model, tree shape, per-rank token budget
+CONFIG_DEFAULTS = {
+    2: dict(model="qwen3_4b", trees_per_gpu=8, prefix=512, resp=512, token_budget=16384),
+    3: dict(model="qwen3_4b", trees_per_gpu=2, prefix=0, resp=0, token_budget=32768),
+    4: dict(model="hybrid_gdn_2b", trees_per_gpu=8, prefix=512, resp=512, token_budget=16384),
+    5: dict(model="qwen3_next_24l", trees_per_gpu=4, prefix=1024, resp=1024, token_budget=16384),
+}
 
 
-def layout(args) -> tuple[int, int]:
-    tp_d, cp_d = DEFAULT_LAYOUT.get(args.gpus, (1, 1))
-    return (tp_d if args.tp is None else args.tp), (cp_d if args.cp is None else args.cp)
+# gpus -> (tp, cp, ep): each config's named layout at 8 GPUs, scaled down along the same axes
+DEFAULT_LAYOUT = {
+    2: {1: (1, 1, 1), 2: (2, 1, 1), 4: (2, 2, 1), 8: (2, 4, 1)},
+    3: {1: (1, 1, 1), 2: (1, 2, 1), 4: (1, 4, 1), 8: (1, 8, 1)},
+    4: {1: (1, 1, 1), 2: (2, 1, 1), 4: (2, 2, 1), 8: (2, 4, 1)},
+    5: {1: (1, 1, 1), 2: (1, 2, 2), 4: (1, 2, 4), 8: (1, 2, 8)},
+}
 
 
-def parallelism_name(tp: int, cp: int, dp: int) -> str:
+def layout(args) -> tuple[int, int, int]:
+    tp_d, cp_d, ep_d = DEFAULT_LAYOUT[args.config].get(args.gpus, (1, 1, 1))
+    pick = lambda v, d: d if v is None else v  # noqa: E731
+    return pick(args.tp, tp_d), pick(args.cp, cp_d), pick(args.ep, ep_d)
+
+
+def parallelism_name(tp: int, cp: int, dp: int, ep: int = 1) -> str:
     parts = [f"tp{tp}"] if tp > 1 else []
     parts += [f"cp{cp}"] if cp > 1 else []
-    parts += [f"dp{dp}"] if dp > 1 or not parts else []
+    parts += [f"ep{ep}"] if ep > 1 else []
+    parts += [f"dp{dp}"] if (dp > 1 and ep == 1) or not parts else []
     return "".join(parts)
 
 
@@ -119,6 +152,45 @@ def synthetic_batch(args, n_trees: int, rank: int, dp: int, vocab: int, device_p
     per_rank = n_trees * args.siblings * args.resp
     return {"input_ids": ids, "response_mask": masks, "old_log_probs": old, "advantages": adv, "uid": uids,
             "temperature": 1.0, "batch_num_tokens": per_rank * dp, "dp_size": dp}
+
+
+IM_END = 151645          # Qwen ChatML <|im_end|>: the turn boundary the qwen_turn trie policy cuts at
+
+
+def session_batch(args, n_sessions: int, rank: int, dp: int, vocab: int, device_pin: bool) -> dict:
+    """Config #3: multi-turn agent sessions.  Six turns of U[2k, 6k] tokens (each ending in <|im_end|>);
+    every session forks into 4 branches at each of its last two turn boundaries (16 rows per session),
+    capped at 48k tokens; the prompt is turn 1 and the loss covers a random half of the response
+    tokens (the assistant spans)."""
+    g = torch.Generator().manual_seed(args.seed * 1000003 + 7919 * rank + 3)
+
+    def turn():
+        n = int(torch.randint(2048, 6145, (1,), generator=g))
+        t = torch.randint(0, vocab - 1, (n,), generator=g)
+        t[t == IM_END] = IM_END - 1
+        t[-1] = IM_END
+        return t
+
+    ids, masks, old, adv, uids = [], [], [], [], []
+    for sess in range(n_sessions):
+        shared = [turn() for _ in range(4)]
+        for b in range(4):
+            t5 = turn()
+            for c in range(4):
+                t6 = turn()
+                row = torch.cat(shared + [t5, t6])[:48 * 1024]
+                n_resp = row.numel() - shared[0].numel()
+                m = torch.rand(n_resp, generator=g) < 0.5
+                ids.append(row)
+                masks.append(m)
+                adv.append(torch.randn(n_resp, generator=g))
+                old.append(torch.full((n_resp,), -11.93) - torch.rand(n_resp, generator=g) * 0.01)
+                uids.append(f"r{rank}s{sess}")
+    if device_pin and torch.cuda.is_available():
+        ids, masks, old, adv = ([x.pin_memory() for x in lst] for lst in (ids, masks, old, adv))
+    local = sum(int(m.sum()) for m in masks)
+    return {"input_ids": ids, "response_mask": masks, "old_log_probs": old, "advantages": adv, "uid": uids,
+            "temperature": 1.0, "batch_num_tokens": local, "dp_size": dp}
 
 
 class ClockSampler:
@@ -171,6 +243,32 @@ class ClockSampler:
                 "sm_max_mhz": max(maxes) if maxes else None, "reasons": sorted(reasons), "samples": len(clocks)}
 
 
+def profile_one_step(args, device_step, rank: int, world: int) -> None:
+    """Per-kernel self device time of one step (the number a profiled run prints is not a bench value)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        device_step()
+        torch.cuda.synchronize()
+    rows = []
+    for evt in prof.key_averages():
+        t = getattr(evt, "self_device_time_total", None)
+        if t is None:
+            t = getattr(evt, "self_cuda_time_total", 0)
+        if t > 0:
+            rows.append((t / 1e3, evt.count, evt.key))
+    rows.sort(reverse=True)
+    total = sum(r[0] for r in rows)
+    lines = [f"# one step, rank {rank} of {world}, config #{args.config}, model {args.model}",
+             f"# TOTAL device ms {total:.2f}", "| kernel | ms / step | launches |", "|---|---|---|"]
+    lines += [f"| {k[:90]} | {ms:.2f} | {n} |" for ms, n, k in rows[:60]]
+    with open(f"{args.profile_step}.rank{rank}.txt", "w") as f:
+        f.write("\n".join(lines) + "\n")
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -190,17 +288,25 @@ def main() -> None:
     if world > 1:
         collective_probe(device=dev)
     cfg = get_config(args.model)
-    tp, cp = layout(args)
+    tp, cp, ep = layout(args)
     sp = tp > 1 and not args.no_sp
-    ec = EngineConfig(tensor_model_parallel_size=tp, context_parallel_size=cp, sequence_parallel=sp,
-                      token_budget=args.token_budget, forest_mode=args.mode,
-                      tpr_cp_backend="ring" if cp > 1 else None, dp_comm=args.dp_comm)
+    ec = EngineConfig(tensor_model_parallel_size=tp, context_parallel_size=cp, expert_model_parallel_size=ep,
+                      sequence_parallel=sp, token_budget=args.token_budget, forest_mode=args.mode,
+                      tpr_cp_backend="ring" if cp > 1 else None, dp_comm=args.dp_comm,
+                      activation_offload=args.config == 3,
+                      tree_policy="qwen_turn" if args.config == 3 else "exact",
+                      gdn_cp_mode="sequence" if args.config in (4, 5) else "head")
     eng = TPREngine(cfg, ec, AdamWConfig(lr=1e-6), device=dev, seed=args.seed)
     dp = eng.parallel.dp
-    n_trees = args.trees_per_gpu * world                  # weak scaling: trees per GPU fixed
-    batch = synthetic_batch(args, n_trees // dp, eng.parallel.dp_rank, dp, cfg.vocab_size, device_pin=True)
+    n_trees = args.trees_per_gpu * world                  # weak scaling: trees (sessions) per GPU fixed
+    make = session_batch if args.config == 3 else synthetic_batch
+    batch = make(args, n_trees // dp, eng.parallel.dp_rank, dp, cfg.vocab_size, device_pin=True)
+    tok = torch.tensor([float(batch["batch_num_tokens"])], device=dev)
+    if dp > 1 and args.config == 3:                       # random loss masks: the global count is a sum
+        dist.all_reduce(tok, group=eng.parallel.dp_group)
+        batch["batch_num_tokens"] = int(tok.item())
+    ppo_tokens_global = int(batch["batch_num_tokens"])
     prepared = prepare_tpr_batch(eng, batch)
-    ppo_tokens_global = n_trees * args.siblings * args.resp
     m = ext()
 
     def device_step():
@@ -213,6 +319,9 @@ def main() -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    if args.profile_step:
+        profile_one_step(args, device_step, rank, world)
+        return
     sampler = ClockSampler(local_gpu_indices()) if rank == 0 else None
     launches0 = m.launch_count()
     torch.cuda.synchronize()
@@ -257,9 +366,9 @@ def main() -> None:
 
     if rank == 0:
         value = ppo_tokens_global / (ms / 1e3)
-        par = parallelism_name(tp, cp, dp)
-        named = (args.model, par, world, n_trees, args.prefix, args.siblings, args.resp) == \
-            ("qwen3_4b", "tp2cp4", 8, 64, 512, 8, 512)
+        par = parallelism_name(tp, cp, dp, ep)
+        named = (args.config, args.model, par, world, n_trees, args.prefix, args.siblings, args.resp) == \
+            (2, "qwen3_4b", "tp2cp4", 8, 64, 512, 8, 512)
         line = {
             "metric": METRIC,
             "value": value,
@@ -275,8 +384,10 @@ def main() -> None:
             "dtype": "bf16",
             "data": "synthetic (uniform token ids from seed, advantages N(0,1), random-init weights)",
             "config": {
-                "model": args.model, "global_batch": n_trees * args.siblings, "seq_len": args.prefix + args.resp,
-                "parallelism": par, "sequence_parallel": sp,
+                "baseline_config": args.config, "model": args.model,
+                "global_batch": n_trees * (16 if args.config == 3 else args.siblings),
+                "seq_len": "6 turns of 2k-6k, <= 48k" if args.config == 3 else args.prefix + args.resp,
+                "parallelism": par, "sequence_parallel": sp, "activation_offload": ec.activation_offload,
                 "cp_placement": "segment-granular (forest executor)" if cp > 1 else None,
                 "trees": n_trees, "prefix": args.prefix, "siblings": args.siblings,
                 "response": args.resp, "ppo_tokens_per_step": ppo_tokens_global, "forest_mode": args.mode,

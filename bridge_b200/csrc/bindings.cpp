@@ -31,6 +31,10 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(torch::Tensor dqo, torch::Tensor dko
                                             torch::Tensor qw, torch::Tensor kw, torch::Tensor cosb,
                                             torch::Tensor sinb, torch::Tensor rq, torch::Tensor rk);
 torch::Tensor swiglu_fwd(torch::Tensor gu);
+std::vector<torch::Tensor> moe_route(torch::Tensor logits, int64_t k);
+torch::Tensor moe_combine(torch::Tensor ys, torch::Tensor pos, torch::Tensor w, int64_t T);
+std::vector<torch::Tensor> moe_combine_bwd(torch::Tensor dy, torch::Tensor ys, torch::Tensor pos, torch::Tensor w);
+torch::Tensor moe_route_bwd(torch::Tensor idx, torch::Tensor w, torch::Tensor dw, int64_t E);
 torch::Tensor swiglu_bwd(torch::Tensor dy, torch::Tensor gu);
 void logprob_stats(torch::Tensor logits, torch::Tensor targets, torch::Tensor inv_temp, int64_t vocab_start,
                    torch::Tensor stats);
@@ -123,6 +127,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
   m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
   m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("moe_route", &moe_route, "MoE top-k routing + stable expert sort (idx, w, counts, offsets, pos, order)");
+  m.def("moe_combine", &moe_combine, "y[t] = sum_j w[t,j] ys[pos[t,j]]");
+  m.def("moe_combine_bwd", &moe_combine_bwd);
+  m.def("moe_route_bwd", &moe_route_bwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("logprob_stats", &logprob_stats);
   m.def("logprob_finalize", &logprob_finalize);

@@ -88,6 +88,19 @@ inline int resident_grid(Kernel kernel, int threads, size_t smem, long want) {
   return (int)(want < 1 ? 1 : (want < cap ? want : cap));
 }
 }  // namespace bb
+namespace bb {
+// Sets a kernel's dynamic shared-memory limit once per device (the attribute is per-device state:
+// a process that drives several GPUs must set it on each).
+template <typename Kernel>
+inline void set_smem_attr_once(Kernel kernel, int smem, unsigned long long& done_mask) {
+  int dev = 0;
+  BB_CHECK_CUDA(cudaGetDevice(&dev));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done_mask & bit) return;
+  BB_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  done_mask |= bit;
+}
+}  // namespace bb
 #define BB_POST_LAUNCH()                  \
   do {                                    \
     BB_CHECK_CUDA(cudaGetLastError());    \

@@ -1213,6 +1213,10 @@ void embedding_bwd_acc(torch::Tensor ids, torch::Tensor dy, torch::Tensor grad, 
   TORCH_CHECK(grad.is_cuda() && grad.scalar_type() == at::kFloat && grad.is_contiguous() && grad.dim() == 2 &&
                   grad.size(1) == dy.size(1) && (reinterpret_cast<uintptr_t>(grad.data_ptr()) & 15) == 0,
               "embedding_bwd: grad must be a contiguous, 16-byte aligned FP32 [rows, H] tensor");
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.dim() == 1,
+              "embedding_bwd: ids must be a contiguous CUDA int64 vector");
+  TORCH_CHECK(dy.dim() == 2 && dy.size(0) == ids.numel() && dy.is_contiguous(),
+              "embedding_bwd: dy must be a contiguous [ids.numel(), H] tensor");
   const int T = ids.numel(), H = dy.size(1);
   if (T == 0) return;
   const int blocks = bb::resident_grid(embedding_bwd_acc_kernel, 256, 0, (T + 7) / 8);

@@ -534,11 +534,8 @@ template <bool A_MN, bool B_MN, bool ACC>
 void launch(const MapPair* maps, void* c, int M, int N, int K, long ldc) {
   auto kern = gemm_kernel<A_MN, B_MN, ACC>;
   const int smem = SmemLayout::TOTAL + 1024;
-  static bool attr = false;
-  if (!attr) {
-    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  bb::set_smem_attr_once(kern, smem, attr_done);
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, num_sms()));
   GTRACE("launch: attr ok");
@@ -556,11 +553,8 @@ template <bool A_MN, bool B_MN, bool ACC>
 void launch_pair(const MapPair* maps, void* c, int M, int N, int K, long ldc) {
   auto kern = gemm_pair_kernel<A_MN, B_MN, ACC>;
   const int smem = PairSmem::TOTAL + 1024;
-  static bool attr = false;
-  if (!attr) {
-    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  bb::set_smem_attr_once(kern, smem, attr_done);
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
   const int grid = 2 * std::max(1, std::min(tiles, num_sms() / 2));
   int* err = error_word().data_ptr<int>();
@@ -970,11 +964,8 @@ template <int MODE, bool B_MN>
 void tp_launch(const MapPair* maps, void* c, int M, int N, int K, long ldc, const TpArgs& tp) {
   auto kern = tp_gemm_kernel<MODE, B_MN>;
   const int smem = (MODE == 2 ? SmemLayout::TOTAL_EPI : SmemLayout::TOTAL) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  bb::set_smem_attr_once(kern, smem, attr_done);
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   // AG: every CTA must be resident (CTAs wait on rows copied by other CTAs): at most one per SM
   const int grid = std::max(1, std::min(tiles, num_sms()));
@@ -1357,11 +1348,8 @@ template <int MODE>
 void grouped_launch(const MapPair* maps, void* c, const int* offsets, int E, int N, int K, long ldc, int grid) {
   auto kern = grouped_gemm_kernel<MODE>;
   const int smem = SmemLayout::TOTAL + 4 * (kMaxExperts + 1) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  bb::set_smem_attr_once(kern, smem, attr_done);
   int* err = error_word().data_ptr<int>();
   void* args[] = {const_cast<CUtensorMap*>(&maps->a), const_cast<CUtensorMap*>(&maps->b), &c,
                   const_cast<int**>(&offsets), &E, &N, &K, &ldc, &err};

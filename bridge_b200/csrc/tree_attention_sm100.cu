@@ -1252,11 +1252,8 @@ std::vector<torch::Tensor> tree_attn_fwd_sm100(torch::Tensor q, torch::Tensor k,
   encode_rows(&maps->pv, has_p ? pv.data_ptr() : v.data_ptr(), has_p ? pv.size(0) : T, (long)Hk * D);
   const int smem = Smem::TOTAL + 1024;
   auto kern = tree_attn_fwd_sm100_kernel;
-  static bool attr = false;
-  if (!attr) {
-    BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  bb::set_smem_attr_once(kern, smem, attr_done);
   dim3 grid((max_seqlen + BQ - 1) / BQ, B, Hq);
   const int* cup = cu.data_ptr<int>();
   const int* pop = poff.data_ptr<int>();
@@ -1335,11 +1332,8 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
     static const bool v1 = getenv("BB_ATTN_DKDV") && std::string(getenv("BB_ATTN_DKDV")) == "v1";
     auto kern = v1 ? tree_attn_dkdv_sm100_kernel : tree_attn_dkdv2_sm100_kernel;
     const int smem = (v1 ? SmemDKDV::TOTAL : SmemDKDV2::TOTAL) + 1024;
-    static bool attr = false;
-    if (!attr) {
-      BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr = true;
-    }
+    static unsigned long long attr_done = 0;
+    bb::set_smem_attr_once(kern, smem, attr_done);
     const long xt = std::max<long>((max_seqlen + BKV - 1) / BKV, has_p ? (max_prefix + BKV - 1) / BKV : 0);
     dim3 grid((unsigned)std::max<long>(xt, 1), (unsigned)(has_p ? 2 * B : B), (unsigned)Hk);
     __nv_bfloat16* dkp = (__nv_bfloat16*)dk.data_ptr();
@@ -1354,11 +1348,8 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
     static const bool dq_v1 = getenv("BB_ATTN_DQ") && std::string(getenv("BB_ATTN_DQ")) == "v1";
     auto kern = dq_v1 ? tree_attn_dq_sm100_kernel : tree_attn_dq2_sm100_kernel;
     const int smem = (dq_v1 ? SmemDQ::TOTAL : SmemDQ2::TOTAL) + 1024;
-    static bool attr = false;
-    if (!attr) {
-      BB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr = true;
-    }
+    static unsigned long long attr_done = 0;
+    bb::set_smem_attr_once(kern, smem, attr_done);
     dim3 grid((unsigned)((max_seqlen + BQ - 1) / BQ), (unsigned)B, (unsigned)Hq);
     __nv_bfloat16* dqp = (__nv_bfloat16*)dq.data_ptr();
     void* args[] = {maps, &cup, &pop, &plp, &lsep, &delp, &dqp, &Ti, &Hqi, &Hki, &sl2, &sc, &err};

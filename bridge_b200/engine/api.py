@@ -184,6 +184,15 @@ def prepare_tpr_batch(engine, data: Any, loss_function: Any = None) -> PreparedT
     return PreparedTPRBatch(data, forest, objective, logical_inputs, stage)
 
 
+def offload_config(ec):
+    """``EngineConfig.activation_offload`` as the executors' offload config (None when off)."""
+    if not ec.activation_offload:
+        return None
+    from ..tpr.activation_offload import OffloadConfig
+
+    return OffloadConfig(enabled=True)
+
+
 def max_segment_tokens(forest) -> int:
     return max((s.length for t in forest.trees for s in t.segment_plan.segments.values()), default=0)
 
@@ -226,7 +235,7 @@ def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss:
 
                 cp = engine._tpr_forest_cp = ForestCP(rt.group, comm=ec.cp_comm)
         fx = ForestExecutor(model, objective, mode=ec.forest_mode, token_budget=ec.token_budget,
-                            loss_scale=float(rt.size), cp=cp)
+                            loss_scale=float(rt.size), cp=cp, offload=offload_config(ec))
         fx.profiler = profiler
         if prepared.nodes is None:
             prepared.nodes = fx.plan(forest)
@@ -238,6 +247,8 @@ def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss:
         metrics["tpr/forward_tokens"] = [res.forward_tokens]
         metrics["tpr/backward_tokens"] = [res.backward_tokens]
         metrics["tpr/chunks"] = [res.chunks]
+        if fx.offload is not None:
+            metrics["tpr/offloaded_bytes"] = [fx.offloaded_bytes]
         if objective.calculate_entropy and "entropy_sum" in res.metrics:
             metrics["actor/entropy"] = [res.metrics["entropy_sum"] / forest.logical_loss_tokens]
     else:
@@ -247,7 +258,7 @@ def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss:
         def run_tree(tree_plan):
             fn, counts = objective.bind_tree(tree_plan, shard_for_segment=shard_for, model=model)
             ex = SegmentExecutor(model, tree_plan.segment_plan, segment_loss_fn=fn, segment_loss_term_counts=counts,
-                                 cp_group=rt.group, cp_backend=rt.backend)
+                                 cp_group=rt.group, cp_backend=rt.backend, activation_offload=offload_config(ec))
             out = FixedTopologyScheduler(tree_plan.segment_plan, ex, event_profiler=profiler,
                                          tree_index=len(seg_stats)).run()
             if sync_loss and not bool(torch.isfinite(out.normalized_loss).item()):

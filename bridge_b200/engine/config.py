@@ -89,6 +89,8 @@ class EngineConfig:
             kw["tp_comm"] = os.environ["TPR_TP_COMM"]
         if "TPR_DP_COMM" in os.environ:
             kw["dp_comm"] = os.environ["TPR_DP_COMM"]
+        if "TPR_ACTIVATION_OFFLOAD" in os.environ:
+            kw["activation_offload"] = os.environ["TPR_ACTIVATION_OFFLOAD"] == "1"
         if "TPR_GDN_CP_MODE" in os.environ:
             kw["gdn_cp_mode"] = os.environ["TPR_GDN_CP_MODE"]
         cfg = replace(self, **kw) if kw else self

@@ -24,6 +24,40 @@ from ..ops.gemm import linear
 from .config import ModelConfig
 
 
+class _RouteFn(torch.autograd.Function):
+    """Device top-k routing (``csrc/moe_route.cu``): kept weights are a softmax over the k selected
+    logits; also returns the stable expert-sorted placement of every routed row."""
+
+    @staticmethod
+    def forward(ctx, logits, k):
+        idx, w, counts, offsets, pos, order = kernels().moe_route(logits.contiguous(), int(k))
+        ctx.save_for_backward(idx, w)
+        ctx.E = logits.shape[1]
+        ctx.mark_non_differentiable(idx, counts, offsets, pos, order)
+        return w, idx, counts, offsets, pos, order
+
+    @staticmethod
+    def backward(ctx, dw, *_):
+        idx, w = ctx.saved_tensors
+        return kernels().moe_route_bwd(idx, w, dw.float().contiguous(), ctx.E), None
+
+
+class _CombineFn(torch.autograd.Function):
+    """``y[t] = sum_j w[t, j] * ys[pos[t, j]]`` (gather-reduce, no atomics) and its backward."""
+
+    @staticmethod
+    def forward(ctx, ys, w, pos, t):
+        ys = ys.contiguous()
+        ctx.save_for_backward(ys, w, pos)
+        return kernels().moe_combine(ys, pos, w.contiguous(), int(t))
+
+    @staticmethod
+    def backward(ctx, dy):
+        ys, w, pos = ctx.saved_tensors
+        dys, dw = kernels().moe_combine_bwd(dy.contiguous(), ys, pos, w.contiguous())
+        return dys, dw, None, None
+
+
 def _ep_size(group) -> int:
     return 1 if group is None else dist.get_world_size(group)
 
@@ -140,12 +174,19 @@ class MoELayer(nn.Module):
 
     def forward(self, x: Tensor) -> Tensor:
         t, h = x.shape
-        w, idx = self.route(x)
-        flat_e = idx.reshape(-1)                                   # [T*k]
-        order = torch.argsort(flat_e, stable=True)
-        rows = order // self.top_k
+        device_route = on_gpu(x) and x.dtype == torch.bfloat16 and h % 8 == 0
+        if device_route:
+            # routing, expert sort and the combine run as this framework's kernels
+            logits = linear(x, self.router).float()
+            w, idx, counts_all, _, pos, order = _RouteFn.apply(logits, self.top_k)
+            rows = order.long() // self.top_k
+        else:
+            w, idx = self.route(x)
+            flat_e = idx.reshape(-1)                                   # [T*k]
+            order = torch.argsort(flat_e, stable=True)
+            rows = order // self.top_k
+            counts_all = torch.bincount(flat_e, minlength=self.num_experts)
         xs = x.index_select(0, rows)
-        counts_all = torch.bincount(flat_e, minlength=self.num_experts)
         self.last_load = counts_all.detach()
         ep = _ep_size(self.ep_group)
         comm = None
@@ -185,10 +226,13 @@ class MoELayer(nn.Module):
             inv = torch.empty_like(perm_t)
             inv[perm_t] = torch.arange(perm_t.numel(), device=x.device)
             y_sorted = _AllToAll.apply(ye.index_select(0, inv), recv_l, send_l, self.ep_group)
-        gate = w.reshape(-1).index_select(0, order).to(y_sorted.dtype)[:, None]
-        y = torch.zeros((t, h), device=x.device, dtype=torch.float32)
-        y.index_add_(0, rows, (y_sorted * gate).float())
-        y = y.to(x.dtype)
+        if device_route:
+            y = _CombineFn.apply(y_sorted, w.reshape(-1), pos, t)
+        else:
+            gate = w.reshape(-1).index_select(0, order).to(y_sorted.dtype)[:, None]
+            y = torch.zeros((t, h), device=x.device, dtype=torch.float32)
+            y.index_add_(0, rows, (y_sorted * gate).float())
+            y = y.to(x.dtype)
         if self.shared:
             sh = linear(swiglu(linear(x, self.shared_w1)), self.shared_w2)
             y = y + sh * torch.sigmoid(linear(x, self.shared_gate).float()).to(sh.dtype)

@@ -1,11 +1,13 @@
 """Data-parallel gradient finalisation over the FP32 main-gradient arenas.
 
 ``finalize`` averages every arena across the DP (x CP) group in fixed-size
-buckets.  Each bucket is cast to bf16 for the wire (halving NVLink bytes), all-
-reduced on a side stream while the next bucket is being cast, then scaled by
-``1/dp`` and accumulated back into the FP32 arena -- the cast, scale and
-write-back are one fused elementwise kernel per bucket.  ``comm_dtype=float32``
-keeps the wire in FP32.
+buckets.  Each bucket is cast to bf16 for the wire (halving NVLink bytes) on the
+compute stream and all-reduced by NCCL on a side stream while the next bucket is
+being cast; afterwards each reduced bucket is copied back into the FP32 arena and
+scaled by ``1/dp`` (two torch elementwise ops).  ``comm_dtype=float32`` keeps the
+wire in FP32.  This is the NCCL baseline path; the fused path (P2P reduce-scatter
+with the scale applied in the same kernel, then sharded AdamW) is
+:class:`~bridge_b200.engine.optim.ShardedNVLinkAdamW`.
 
 Parity: the once-per-forest ``finalize_model_grads(force_all_reduce=True)``
 call of verl/models/mcore/tpr/tpr_batch_runner.py:75 and

@@ -14,6 +14,17 @@ reduce-scatter (every slot has landed).  With two alternating buffers that one b
 guarantees no rank overwrites a buffer a peer is still reading from the call before.  Every TP
 rank must make the same sequence of calls (true for SPMD model code).
 
+Two implementations of the same pair of collectives (``TPR_TP_OVERLAP``):
+
+* ``kernel`` -- the single-launch fused tcgen05 kernels described above;
+* ``split`` (default) -- the CTA-pair tcgen05 GEMM (the fastest GEMM of this framework) on row blocks,
+  with the NVLink traffic on a side stream under it.  AG: the local rows' GEMM starts at once while
+  a P2P row-copy kernel pulls the peers' rows; the remote rows' GEMM follows.  RS: the GEMMs of the
+  peers' row blocks write into this rank's symmetric send slots first; after one barrier the side
+  stream sums the peers' slots for this rank's rows (P2P loads, FP32) while the local block's GEMM
+  runs; one add finishes.  Each call still uses one barrier; the side stream always rejoins the
+  compute stream before the call returns, so the two-buffer argument above still holds.
+
 Parity: Megatron sequence-parallel ColumnParallelLinear / RowParallelLinear as used by the
 reference's TP2 path (verl/models/mcore/tpr/attention.py:117-126, 195-221).
 """
@@ -30,6 +41,7 @@ from ..ops._ext import kernels
 from ..ops.gemm import gemm
 
 _MODE = os.environ.get("TPR_TP_COMM", "auto")  # auto | nvlink | nccl
+_OVERLAP = os.environ.get("TPR_TP_OVERLAP", "split")  # split | kernel
 _COMMS: dict = {}
 
 
@@ -87,6 +99,75 @@ class TPFusedComm:
         self.heap.barrier()
         return kernels().tp_sum_slots(buf.view(torch.bfloat16), self.n, ms, nout)
 
+    # ---------------------------------------------------------------- split variant
+    def _side(self):
+        if getattr(self, "_side_stream", None) is None:
+            self._side_stream = torch.cuda.Stream(device=self.heap.device)
+            self._idx: dict = {}
+        return self._side_stream
+
+    def _rows_index(self, ms: int, device):
+        key = ("ag", ms)
+        got = self._idx.get(key)
+        if got is None:
+            ranks = torch.arange(self.n, dtype=torch.int32).repeat_interleave(ms)
+            rows = torch.arange(ms, dtype=torch.int32).repeat(self.n)
+            own = torch.arange(ms, dtype=torch.int32)
+            got = self._idx[key] = (ranks.to(device), rows.to(device), own.to(device))
+        return got
+
+    def ag_gemm_split(self, x_local: Tensor, w: Tensor, *, b_mn: bool) -> tuple[Tensor, Tensor]:
+        ms, k = x_local.shape
+        n, r = self.n, self.rank
+        nout = w.shape[1] if b_mn else w.shape[0]
+        buf = self._next(ms * k * 2)
+        buf.view(torch.bfloat16, ms * k).view(ms, k).copy_(x_local)
+        gather = torch.empty((ms * n, k), dtype=x_local.dtype, device=x_local.device)
+        y = torch.empty((ms * n, nout), dtype=x_local.dtype, device=x_local.device)
+        self.heap.barrier()                                   # every rank's staging is written
+        side, main = self._side(), torch.cuda.current_stream()
+        ranks, rows, _ = self._rows_index(ms, x_local.device)
+        ev = torch.cuda.Event()
+        ev.record(main)
+        with torch.cuda.stream(side):
+            side.wait_event(ev)
+            kernels().p2p_gather_rows(gather, buf.ptrs, ranks, rows)   # all rows, own ones locally
+        gemm(x_local, w, b_mn=b_mn, out=y[r * ms:(r + 1) * ms])          # local rows meanwhile
+        main.wait_stream(side)
+        for j in range(n):
+            if j != r:
+                gemm(gather[j * ms:(j + 1) * ms], w, b_mn=b_mn, out=y[j * ms:(j + 1) * ms])
+        gather.record_stream(side)
+        return y, gather
+
+    def gemm_rs_split(self, a: Tensor, w: Tensor, *, b_mn: bool) -> Tensor:
+        m, _ = a.shape
+        n, r = self.n, self.rank
+        if m % n:
+            raise ValueError("token count must divide by the TP size under sequence parallelism")
+        ms = m // n
+        nout = w.shape[1] if b_mn else w.shape[0]
+        slot = ms * nout
+        buf = self._next(n * slot * 2)
+        slots = buf.view(torch.bfloat16, n * slot).view(n, ms, nout)
+        for d in range(1, n):                                   # peers' blocks first
+            j = (r + d) % n
+            gemm(a[j * ms:(j + 1) * ms], w, b_mn=b_mn, out=slots[j])
+        self.heap.barrier()                                   # every rank's blocks for every owner landed
+        side, main = self._side(), torch.cuda.current_stream()
+        _, _, own_rows = self._rows_index(ms, a.device)
+        peers = [p + r * slot * 2 for j, p in enumerate(buf.ptrs) if j != r]
+        part = torch.empty((ms, nout), dtype=a.dtype, device=a.device)
+        ev = torch.cuda.Event()
+        ev.record(main)
+        with torch.cuda.stream(side):
+            side.wait_event(ev)
+            kernels().p2p_reduce_rows(part, peers, own_rows, False, None)   # sum of the peers' partials
+        own = gemm(a[r * ms:(r + 1) * ms], w, b_mn=b_mn)                    # local block meanwhile
+        main.wait_stream(side)
+        part.record_stream(side)
+        return own.add_(part)
+
     def close(self) -> None:
         self.heap.close()
 
@@ -121,10 +202,18 @@ def _wgrad(w: Tensor, dy: Tensor, x: Tensor):
     return gemm(dy, x, a_mn=True, b_mn=True)
 
 
+def _ag(comm, x, w, b_mn):
+    return (comm.ag_gemm_split if _OVERLAP == "split" else comm.ag_gemm)(x, w, b_mn=b_mn)
+
+
+def _rs(comm, a, w, b_mn):
+    return (comm.gemm_rs_split if _OVERLAP == "split" else comm.gemm_rs)(a, w, b_mn=b_mn)
+
+
 class _AGLinear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, comm):
-        y, gather = comm.ag_gemm(x.contiguous(), w, b_mn=False)
+        y, gather = _ag(comm, x.contiguous(), w, False)
         ctx.save_for_backward(gather, w)
         ctx.comm = comm
         return y
@@ -133,7 +222,7 @@ class _AGLinear(torch.autograd.Function):
     def backward(ctx, dy):
         gather, w = ctx.saved_tensors
         dy = dy.contiguous()
-        dx = ctx.comm.gemm_rs(dy, w, b_mn=True)           # reduce_scatter(dy @ W)
+        dx = _rs(ctx.comm, dy, w, True)                   # reduce_scatter(dy @ W)
         dw = _wgrad(w, dy, gather)
         return dx, dw, None
 
@@ -142,7 +231,7 @@ class _LinearRS(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, comm):
         x = x.contiguous()
-        y = comm.gemm_rs(x, w, b_mn=False)
+        y = _rs(comm, x, w, False)
         ctx.save_for_backward(x, w)
         ctx.comm = comm
         return y
@@ -150,7 +239,7 @@ class _LinearRS(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         x, w = ctx.saved_tensors
-        dx, dy_full = ctx.comm.ag_gemm(dy.contiguous(), w, b_mn=True)   # all_gather(dy) @ W
+        dx, dy_full = _ag(ctx.comm, dy.contiguous(), w, True)          # all_gather(dy) @ W
         dw = _wgrad(w, dy_full, x)
         return dx, dw, None
 

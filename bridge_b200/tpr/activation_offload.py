@@ -22,16 +22,20 @@ from __future__ import annotations
 
 import functools
 import os
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 from torch import Tensor, nn
 
 
+def _env_min_bytes() -> int:
+    return int(os.environ.get("TPR_OFFLOAD_MIN_BYTES", str(1 << 20)))
+
+
 @dataclass(frozen=True)
 class OffloadConfig:
     enabled: bool = False
-    min_bytes: int = 1 << 20
+    min_bytes: int = field(default_factory=_env_min_bytes)     # smaller saved tensors stay on the device
     prefetch: bool = True
     force_restore_sync: bool = os.environ.get("TPR_OFFLOAD_B_FORCE_RESTORE_SYNC", "0") == "1"
 
@@ -151,9 +155,14 @@ class ActivationOffloader:
             self._restore(s, self.h2d)
 
     def release(self) -> None:
+        """Return the pinned buffers to the pool once no copy can still touch them: the D2H copies
+        have finished, and so has every H2D prefetch (one that was issued but never unpacked may
+        still be reading its host buffer)."""
         if self.cuda:
             torch.cuda.current_stream().wait_stream(self.d2h)
+            torch.cuda.current_stream().wait_stream(self.h2d)
             self.d2h.synchronize()
+            self.h2d.synchronize()
         for lst in self.by_layer.values():
             for s in lst:
                 _POOL.put(s.host)
@@ -183,6 +192,54 @@ class _LayerTracker:
     def remove(self) -> None:
         for h in self.handles:
             h.remove()
+
+
+class DeferredOffload:
+    """Offload for a forward whose backward runs later (the forest executor's retained push chunks).
+
+    ``capture()`` wraps the forward (saved tensors go to host as they are produced); ``backward()``
+    wraps the later backward (layer-ahead prefetch hooks) and releases the pinned buffers after it."""
+
+    def __init__(self, model: nn.Module, cfg: OffloadConfig, protected=()) -> None:
+        self.model = model
+        self.off = ActivationOffloader(cfg, protected)
+
+    def capture(self):
+        import contextlib
+
+        @contextlib.contextmanager
+        def scope():
+            tracker = _ForwardTracker(self.model, self.off)
+            try:
+                with torch.autograd.graph.saved_tensors_hooks(self.off.pack, self.off.unpack):
+                    yield self.off
+            finally:
+                tracker.remove()
+
+        return scope()
+
+    def backward(self):
+        import contextlib
+
+        @contextlib.contextmanager
+        def scope():
+            tracker = _LayerTracker(self.model, self.off)
+            try:
+                yield self.off
+            finally:
+                tracker.remove()
+                self.off.release()
+
+        return scope()
+
+
+class _ForwardTracker(_LayerTracker):
+    """Only the forward pre-hooks (layer bookkeeping for the later prefetch)."""
+
+    def __init__(self, model: nn.Module, off: ActivationOffloader) -> None:
+        self.handles = []
+        for i, layer in enumerate(getattr(model, "layers", ()) or ()):
+            self.handles.append(layer.register_forward_pre_hook(functools.partial(self._enter, off, i)))
 
 
 def offload_scope(model: nn.Module, cfg: OffloadConfig, protected=()):

@@ -136,6 +136,7 @@ class TPRAttentionContext:
     capture_gdn_final_state: bool = True
     layout: SegmentBatchLayout | None = None
     record_new_kv: bool = True
+    new_kv_observer: Any = None    # called with (key, value) as a layer records its new K/V
     _new_key_values: dict[int, KVPair] = field(default_factory=dict, init=False, repr=False)
     _new_gdn_states: dict[int, Any] = field(default_factory=dict, init=False, repr=False)
 
@@ -216,6 +217,8 @@ class TPRAttentionContext:
 
     def set_new_kv(self, layer_number: int, key: Tensor, value: Tensor) -> None:
         _check_layer(layer_number)
+        if self.new_kv_observer is not None:
+            self.new_kv_observer((key, value))
         if not self.record_new_kv:
             return
         if layer_number in self._new_key_values:

@@ -85,6 +85,7 @@ class _Chunk:
     gdn_graph: dict = field(default_factory=dict)
     loss: Tensor | None = None
     metrics: list = field(default_factory=list)
+    offload: Any = None                               # DeferredOffload of a retained push forward
 
 
 @dataclass
@@ -117,16 +118,22 @@ class ForestExecutor:
     """Runs a :class:`ForestExecutionPlan` (PPO objective) level-wise in packed chunks."""
 
     def __init__(self, model: nn.Module, objective, *, mode: str = "retain", token_budget: int = 8192,
-                 loss_scale: float = 1.0, cp=None) -> None:
+                 loss_scale: float = 1.0, cp=None, offload=None) -> None:
         """``token_budget`` is the packed token count one rank forwards at a time; ``cp`` (a
         :class:`~bridge_b200.parallel.forest_cp.ForestCP`) partitions every chunk's segments over a
-        context-parallel group (chunks then hold ``token_budget * cp.size`` tokens)."""
+        context-parallel group (chunks then hold ``token_budget * cp.size`` tokens); ``offload`` (an
+        enabled :class:`~bridge_b200.tpr.activation_offload.OffloadConfig`) moves the tensors saved for
+        backward to pinned host memory -- for a leaf chunk during its forward+backward, for a retained
+        push chunk from its forward until its pop -- while prefix anchors and new K/V stay resident."""
         if mode not in ("retain", "recompute"):
             raise ValueError(f"mode must be 'retain' or 'recompute', got {mode!r}")
         self.model, self.objective, self.mode = model, objective, mode
         self.token_budget = int(token_budget)
         self.loss_scale = loss_scale
         self.cp = cp
+        self.offload = offload if (offload is not None and offload.enabled) else None
+        self._live: list[_Chunk] = []
+        self.offloaded_bytes = 0
         self.attn_layers = tuple(getattr(model, "attention_layer_numbers", ()))
         self.gdn_layers = tuple(getattr(model, "gdn_layer_numbers", ()))
         self.device = model_device(model)
@@ -250,7 +257,32 @@ class ForestExecutor:
             return tp_size(self.model.tp_group)
         return 1
 
-    def _forward(self, nodes: list[_Node], *, grad: bool, record: bool):
+    def _protected(self) -> list[Tensor]:
+        """Tensors offload must leave on the device: every live chunk's anchors."""
+        out: list[Tensor] = []
+        for ch in self._live:
+            for pair in list(ch.kv_anchor.values()) + list(ch.gdn_anchor.values()):
+                out.extend(pair)
+        return out
+
+    def _offload_scope(self):
+        import contextlib
+
+        if self.offload is None:
+            return contextlib.nullcontext(None)
+        from .activation_offload import offload_scope
+
+        import contextlib
+
+        @contextlib.contextmanager
+        def counted():
+            with offload_scope(self.model, self.offload, self._protected()) as off:
+                yield off
+            self.offloaded_bytes += off.offloaded_bytes
+
+        return counted()
+
+    def _forward(self, nodes: list[_Node], *, grad: bool, record: bool, observer=None):
         """Packed forward of ``nodes``.  A trailing pad segment (token 0, no prefix, no loss) is added
         when sequence parallelism needs the row count to divide over TP, and an idle CP rank (no
         segments in this chunk) forwards a pad segment alone so every rank makes the same collectives."""
@@ -275,7 +307,8 @@ class ForestExecutor:
         gdn0 = self._gdn_init(nodes, pad_seqs=1 if pad else 0) if nodes else {}
         ctx = TPRAttentionContext(prefix_length=0, suffix_length=sum(seq_lens), past_key_values=bank,
                                   layout=layout, initial_gdn_states=gdn0,
-                                  capture_gdn_final_state=record, record_new_kv=record)
+                                  capture_gdn_final_state=record, record_new_kv=record,
+                                  new_kv_observer=observer)
         max_pos = max([n.start + n.length for n in nodes] + [pad])
         with (torch.enable_grad() if grad else torch.no_grad()), use_tpr_attention_context(ctx):
             hidden = self.model(dev_ip[0], dev_ip[1], max_pos)
@@ -328,7 +361,15 @@ class ForestExecutor:
         for b, n in enumerate(order):
             n.chunk, n.row0, n.batch_index = ch, row, b
             row += n.length
-        ctx, hidden = self._forward(local, grad=grad, record=True)
+        if grad and self.offload is not None:
+            from .activation_offload import DeferredOffload
+
+            ch.offload = DeferredOffload(self.model, self.offload, self._protected())
+            with ch.offload.capture() as off:
+                ctx, hidden = self._forward(local, grad=grad, record=True, observer=off.protect)
+        else:
+            ctx, hidden = self._forward(local, grad=grad, record=True)
+        self._live.append(ch)
         stats["fwd"] += sum(n.length for n in local)
         kv, gdn = self._exchange(ctx, local, counts)
         for layer, (k, v) in kv.items():
@@ -349,7 +390,10 @@ class ForestExecutor:
         return ch
 
     def _visit_leaves(self, nodes: list[_Node], stats: dict, acc: dict) -> None:
-        nodes = self._place(nodes)[0]
+        with self._offload_scope():
+            self._visit_leaves_body(self._place(nodes)[0], stats, acc)
+
+    def _visit_leaves_body(self, nodes: list[_Node], stats: dict, acc: dict) -> None:
         ctx, hidden = self._forward(nodes, grad=True, record=False)
         stats["fwd"] += sum(n.length for n in nodes)
         stats["bwd"] += sum(n.length for n in nodes)
@@ -362,6 +406,23 @@ class ForestExecutor:
         (loss * self.loss_scale).backward()
 
     def _pop_chunk(self, ch: _Chunk, stats: dict, acc: dict) -> None:
+        import contextlib
+
+        if ch.offload is not None:
+            scope = ch.offload.backward()
+        elif self.mode == "recompute":
+            scope = self._offload_scope()
+        else:
+            scope = contextlib.nullcontext()
+        with scope:
+            self._pop_chunk_body(ch, stats, acc)
+        if ch.offload is not None:
+            self.offloaded_bytes += ch.offload.off.offloaded_bytes
+        ch.offload = None
+        if ch in self._live:
+            self._live.remove(ch)
+
+    def _pop_chunk_body(self, ch: _Chunk, stats: dict, acc: dict) -> None:
         if self.mode == "recompute":
             # Re-run the chunk with grad over the (still anchored) ancestors, then relay.
             ctx, hidden = self._forward(ch.local, grad=True, record=True)

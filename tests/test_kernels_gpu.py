@@ -404,3 +404,40 @@ def test_embedding_lookup_and_scatter_add(start, use_main):
         _close(w.main_grad - 0.5, g_ref, 1e-4, 1e-5, "main_grad")
     else:
         _close(w.grad, g_ref, 1e-2, 1e-2, "grad")
+
+
+def test_moe_route_sort_and_combine():
+    """Device routing vs torch: top-k ids (descending, ties to the lower id), renormalised weights, the
+    stable expert sort, counts; the gather-reduce combine and both backward kernels vs autograd."""
+    from bridge_b200.ops._ext import kernels
+
+    m = kernels()
+    T, E, k, H = 1000, 512, 10, 256
+    logits = torch.randn(T, E, device=DEV)
+    w, idx, counts, offsets, pos, order = m.moe_route(logits, k)
+    lr = logits.clone().requires_grad_()
+    p = torch.softmax(lr, -1)
+    wr, ir = torch.topk(p, k, -1)
+    wr = wr / wr.sum(-1, keepdim=True)
+    assert torch.equal(idx.long(), ir)
+    _close(w, wr, 1e-5, 1e-4, "w")
+    flat = ir.reshape(-1)
+    assert torch.equal(order.long(), torch.argsort(flat, stable=True))
+    assert torch.equal(pos.long()[order.long()], torch.arange(T * k, device=DEV))
+    assert torch.equal(counts.long(), torch.bincount(flat, minlength=E))
+    assert int(offsets[-1]) == T * k
+    ys = torch.randn(T * k, H, device=DEV).bfloat16()
+    y = m.moe_combine(ys, pos, w.reshape(-1).contiguous(), T)
+    ysr = ys.float().requires_grad_()
+    yr = (ysr[pos.long()].view(T, k, H) * wr.detach()[..., None]).sum(1)
+    _close(y, yr, 2e-2, 1e-2, "combine")
+    dy = torch.randn(T, H, device=DEV).bfloat16()
+    dys, dw = m.moe_combine_bwd(dy, ys, pos, w.reshape(-1).contiguous())
+    yr.backward(dy.float())
+    _close(dys, ysr.grad, 2e-2, 1e-2, "dys")
+    dwr = (dy.float()[:, None, :] * ys.float()[pos.long()].view(T, k, H)).sum(-1)
+    _close(dw.view(T, k), dwr, 5e-2, 1e-2, "dw")
+    g = torch.randn(T, k, device=DEV)
+    dl = m.moe_route_bwd(idx, w, g.contiguous(), E)
+    (wr * g).sum().backward()
+    _close(dl, lr.grad, 1e-5, 1e-4, "dlogits")

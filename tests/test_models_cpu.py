@@ -101,3 +101,26 @@ def test_activation_offload_scope_preserves_gradients():
     assert off.offloaded_bytes > 0
     for n, p in model.named_parameters():
         assert torch.allclose(p.grad, ref[n], atol=1e-6), n
+
+
+@pytest.mark.parametrize("mode", ["retain", "recompute"])
+def test_forest_activation_offload_preserves_gradients(mode, monkeypatch):
+    """EngineConfig.activation_offload reaches the forest executor: same loss and gradients, and the
+    saved activations of leaf and retained push chunks go through the offloader."""
+    from bridge_b200.engine import EngineConfig, TPREngine
+    from tests.helpers import nested_tree_batch
+
+    monkeypatch.setenv("TPR_OFFLOAD_MIN_BYTES", "4096")
+    cfg = get_config("tiny")
+    out, grads = {}, {}
+    for off in (False, True):
+        eng = TPREngine(cfg, EngineConfig(activation_offload=off, forest_mode=mode, token_budget=160), device="cpu",
+                        model=build_model(cfg, dtype=torch.float32, seed=0))
+        res = eng.forward_backward_batch(nested_tree_batch())
+        out[off] = res["loss"][0]
+        grads[off] = {n: p.main_grad.clone() for n, p in eng.model.named_parameters()}
+        if off:
+            assert res["metrics"]["tpr/offloaded_bytes"][0] > 0
+    assert out[True] == out[False]
+    for n in grads[False]:
+        assert torch.equal(grads[True][n], grads[False][n]), n
