@@ -218,6 +218,23 @@ class ForestCP:
         return outs
 
 
+_STACK_CP: dict = {}
+
+
+def gather_stack(x: Tensor, group) -> Tensor:
+    """``[n, *x.shape]``: every CP rank's ``x`` (differentiable; the backward returns this rank's slice of
+    the stacked gradient summed over ranks).  Moves over NVLink P2P on a single-node CUDA group (one
+    staging write, one barrier, peer loads), else ``all_gather`` / ``all_reduce``."""
+    cp = _STACK_CP.get(id(group))
+    if cp is None:
+        cp = _STACK_CP[id(group)] = ForestCP(group)
+    row = x.reshape(1, -1)
+    if (row.shape[1] * row.element_size()) % 16 and x.is_cuda:
+        row = torch.nn.functional.pad(row, (0, (-row.shape[1]) % (16 // row.element_size())))
+    out = cp.gather([row], [1] * cp.size)[0]
+    return out[:, :x.numel()].reshape(cp.size, *x.shape)
+
+
 def _kernels():
     from ..ops._ext import kernels
 

@@ -21,7 +21,11 @@ Two schedules are provided:
   rank.  The backward of each all-gather sums the gradients over ranks, so
   ``dh0`` and the map gradients reach their owners with no extra exchange.
   No token activations cross GPUs (the head-parallel schedule moves the whole
-  projection twice per layer); the price is a second delta-rule pass.
+  projection twice per layer); the price is a second delta-rule pass.  On a
+  single-node CUDA group the halos and maps (and their gradients) move by NVLink
+  P2P (:func:`~bridge_b200.parallel.forest_cp.gather_stack`: one staging write,
+  one barrier, peer loads; owner sums in the backward), elsewhere by
+  ``all_gather`` / ``all_reduce``.
 
 Parity: verl/models/mcore/tpr/parallel/gdn_state.py:13-104
 (gdn_cp_state_shapes, forward_gdn_cp_with_state); the sequence-sharded schedule is new.
@@ -240,6 +244,9 @@ def forward_gdn_cp_tpr(module, hidden_local: Tensor, ctx, backend):
 
 
 # ------------------------------------------------------------------ sequence-sharded schedule
+from .forest_cp import gather_stack  # noqa: E402  (conv halos and state maps: NVLink P2P on CUDA)
+
+
 class _AllGatherSum(torch.autograd.Function):
     """``[n, *x.shape]`` stack of every rank's ``x``; the backward sums the stacked gradient over ranks
     and returns this rank's slice (every rank may use every slice)."""
@@ -300,7 +307,7 @@ def gdn_sequence_sharded(module, proj: Tensor, pieces_by_rank: list[list[tuple[i
     # 1. conv halos: every piece's last W-1 pre-conv inputs
     pad_tail = qkv.new_zeros(W - 1, cc)
     tails = torch.stack([qkv[e - (W - 1):e] for s, e, _ in mine] + [pad_tail] * (P - len(mine)))
-    all_tails = _AllGatherSum.apply(tails, group)                       # [n, P, W-1, cc]
+    all_tails = gather_stack(tails, group)                       # [n, P, W-1, cc]
     h_conv0 = init.conv_state if init is not None else None
     h_rec0 = init.recurrent_state if init is not None else None
     prev = {}
@@ -316,7 +323,7 @@ def gdn_sequence_sharded(module, proj: Tensor, pieces_by_rank: list[list[tuple[i
     final_conv = _state_from_tail(all_tails[order[-1][1], order[-1][2]]) if order else None
     if not mine:                       # this rank holds only padding: it still takes part in both gathers
         maps = proj.new_zeros((P, hv, K, K + V), dtype=torch.float32)
-        all_maps = _AllGatherSum.apply(maps, group)
+        all_maps = gather_stack(maps, group)
         o_local = proj.new_zeros(proj.shape[0], vd)
         S = h_rec0.float() if h_rec0 is not None else proj.new_zeros((1, hv, K, V), dtype=torch.float32)
         for _, j, i in order:
@@ -344,7 +351,7 @@ def gdn_sequence_sharded(module, proj: Tensor, pieces_by_rank: list[list[tuple[i
     maps = torch.cat([m_end.float(), c_end.float()], dim=-1)           # [pieces, hv, K, K+V]
     if len(mine) < P:
         maps = torch.cat([maps, maps.new_zeros((P - len(mine),) + maps.shape[1:])])
-    all_maps = _AllGatherSum.apply(maps, group)                         # [n, P, hv, K, K+V]
+    all_maps = gather_stack(maps, group)                         # [n, P, hv, K, K+V]
     # 3. compose the pieces in global order
     S = h_rec0.float() if h_rec0 is not None else q.new_zeros((1, hv, K, V), dtype=torch.float32)
     start = {}
