@@ -288,6 +288,17 @@ void dp_adamw_allgather(torch::Tensor master, torch::Tensor m, torch::Tensor v, 
   BB_POST_LAUNCH();
 }
 
+// dst[0:nbytes) = *src_ptr (a peer's symmetric buffer, or any device address) by the copy engine on the
+// current stream: the NVLink transfer takes no SMs away from a concurrently running GEMM.
+void p2p_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes) {
+  TORCH_CHECK(dst.is_cuda() && dst.is_contiguous() && nbytes >= 0 &&
+                  nbytes <= (int64_t)(dst.numel() * dst.element_size()) && src_ptr != 0,
+              "p2p_copy: contiguous CUDA dst of at least nbytes and a non-null source");
+  if (nbytes == 0) return;
+  BB_CHECK_CUDA(cudaMemcpyAsync(dst.data_ptr(), reinterpret_cast<const void*>(src_ptr), (size_t)nbytes,
+                                cudaMemcpyDeviceToDevice, at::cuda::getCurrentCUDAStream()));
+}
+
 int64_t symm_error_code() {
   unsigned int v = 0;
   BB_CHECK_CUDA(cudaMemcpyFromSymbol(&v, g_symm_error, sizeof(v)));

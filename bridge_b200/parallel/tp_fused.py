@@ -18,11 +18,11 @@ Two implementations of the same pair of collectives (``TPR_TP_OVERLAP``):
 
 * ``kernel`` -- the single-launch fused tcgen05 kernels described above;
 * ``split`` (default) -- the CTA-pair tcgen05 GEMM (the fastest GEMM of this framework) on row blocks,
-  with the NVLink traffic on a side stream under it.  AG: the local rows' GEMM starts at once while
-  a P2P row-copy kernel pulls the peers' rows; the remote rows' GEMM follows.  RS: the GEMMs of the
-  peers' row blocks write into this rank's symmetric send slots first; after one barrier the side
-  stream sums the peers' slots for this rank's rows (P2P loads, FP32) while the local block's GEMM
-  runs; one add finishes.  Each call still uses one barrier; the side stream always rejoins the
+  with the NVLink traffic on a side stream under it, moved by the copy engines (``p2p_copy``: no SMs
+  taken from the GEMM).  AG: the local rows' GEMM starts at once while the peers' rows are pulled; the
+  remote rows' GEMM follows.  RS: the GEMMs of the peers' row blocks write into this rank's symmetric
+  send slots first; after one barrier the side stream pulls the peers' slots for this rank's rows
+  while the local block's GEMM runs; one add finishes.  Each call still uses one barrier; the side stream always rejoins the
   compute stream before the call returns, so the two-buffer argument above still holds.
 
 Parity: Megatron sequence-parallel ColumnParallelLinear / RowParallelLinear as used by the
@@ -131,7 +131,9 @@ class TPFusedComm:
         ev.record(main)
         with torch.cuda.stream(side):
             side.wait_event(ev)
-            kernels().p2p_gather_rows(gather, buf.ptrs, ranks, rows)   # all rows, own ones locally
+            m = kernels()
+            for j in range(n):      # copy engine: the NVLink pull takes no SMs from the GEMM below
+                m.p2p_copy(gather[j * ms:(j + 1) * ms], buf.ptrs[j], ms * k * 2)
         gemm(x_local, w, b_mn=b_mn, out=y[r * ms:(r + 1) * ms])          # local rows meanwhile
         main.wait_stream(side)
         for j in range(n):
@@ -155,18 +157,18 @@ class TPFusedComm:
             gemm(a[j * ms:(j + 1) * ms], w, b_mn=b_mn, out=slots[j])
         self.heap.barrier()                                   # every rank's blocks for every owner landed
         side, main = self._side(), torch.cuda.current_stream()
-        _, _, own_rows = self._rows_index(ms, a.device)
-        peers = [p + r * slot * 2 for j, p in enumerate(buf.ptrs) if j != r]
-        part = torch.empty((ms, nout), dtype=a.dtype, device=a.device)
+        parts = torch.empty((n - 1, ms, nout), dtype=a.dtype, device=a.device)
         ev = torch.cuda.Event()
         ev.record(main)
         with torch.cuda.stream(side):
             side.wait_event(ev)
-            kernels().p2p_reduce_rows(part, peers, own_rows, False, None)   # sum of the peers' partials
-        own = gemm(a[r * ms:(r + 1) * ms], w, b_mn=b_mn)                    # local block meanwhile
+            m = kernels()
+            for i, j in enumerate(q for q in range(n) if q != r):   # the peers' partials for my rows
+                m.p2p_copy(parts[i], buf.ptrs[j] + r * slot * 2, slot * 2)
+        own = gemm(a[r * ms:(r + 1) * ms], w, b_mn=b_mn)                  # local block meanwhile
         main.wait_stream(side)
-        part.record_stream(side)
-        return own.add_(part)
+        parts.record_stream(side)
+        return own.add_(parts[0]) if n == 2 else own.add_(parts.float().sum(0).to(own.dtype))
 
     def close(self) -> None:
         self.heap.close()

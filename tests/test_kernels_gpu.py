@@ -414,7 +414,7 @@ def test_moe_route_sort_and_combine():
     m = kernels()
     T, E, k, H = 1000, 512, 10, 256
     logits = torch.randn(T, E, device=DEV)
-    w, idx, counts, offsets, pos, order = m.moe_route(logits, k)
+    idx, w, counts, offsets, pos, order = m.moe_route(logits, k)
     lr = logits.clone().requires_grad_()
     p = torch.softmax(lr, -1)
     wr, ir = torch.topk(p, k, -1)

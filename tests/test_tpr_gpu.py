@@ -119,8 +119,8 @@ def test_forest_activation_offload_gpu(mode):
     dev = torch.device("cuda")
     batch = tree_batch(n_trees=2, prefix=1024, siblings=4, resp=512, seed=9)
     res, peaks, grads = {}, {}, {}
-    for off in (False, True):
-        eng = TPREngine(_cfg(), EngineConfig(forest_mode=mode, token_budget=4096, activation_offload=off),
+    for off in (False, "again", True):       # "again": a second run without offload (run-to-run noise)
+        eng = TPREngine(_cfg(), EngineConfig(forest_mode=mode, token_budget=4096, activation_offload=off is True),
                         device=dev, model=build_model(_cfg(), device=dev, seed=0))
         set_old_log_probs(eng.model, batch)
         torch.cuda.synchronize()
@@ -133,7 +133,10 @@ def test_forest_activation_offload_gpu(mode):
         del eng
     assert res[True]["metrics"]["tpr/offloaded_bytes"][0] > 0
     assert abs(res[True]["loss"][0] - res[False]["loss"][0]) <= 1e-5 * abs(res[False]["loss"][0]) + 1e-7
+    # the attention backward reduces prefix dK/dV with FP32 atomics, so two plain runs already differ by
+    # bf16 rounding flips; offload must stay within a small multiple of that run-to-run noise
     for n, g in grads[False].items():
         rel = float((grads[True][n] - g).norm() / (g.norm() + 1e-12))
-        assert rel < 1e-3, (n, rel)
+        noise = float((grads["again"][n] - g).norm() / (g.norm() + 1e-12))
+        assert rel < 4 * noise + 1e-4, (n, rel, noise)
     assert peaks[True] < peaks[False], peaks
