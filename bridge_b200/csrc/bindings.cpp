@@ -99,6 +99,8 @@ void dp_adamw_allgather(torch::Tensor master, torch::Tensor m, torch::Tensor v, 
 int64_t symm_error_code();
 void p2p_gather_rows(torch::Tensor out, std::vector<int64_t> peers, torch::Tensor src_rank, torch::Tensor src_row);
 void p2p_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes);
+void dp_bucket_signal(std::vector<int64_t> flags, int64_t rank, int64_t max_buckets, int64_t bucket, int64_t epoch);
+void dp_bucket_wait(int64_t mine, int64_t n, int64_t max_buckets, int64_t bucket, int64_t epoch, double timeout_s);
 void p2p_reduce_rows(torch::Tensor out, std::vector<int64_t> peers, torch::Tensor src_row, bool src_f32,
                      c10::optional<torch::Tensor> add);
 torch::Tensor tp_ag_gemm(torch::Tensor gather, torch::Tensor b, bool b_mn, std::vector<int64_t> peers, int64_t rank,
@@ -156,6 +158,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_adamw_allgather", &dp_adamw_allgather, "AdamW on the local shard + P2P-store parameter all-gather");
   m.def("symm_error_code", &symm_error_code);
   m.def("p2p_gather_rows", &p2p_gather_rows, "out[i] = peer[src_rank[i]][src_row[i]] (P2P loads)");
+  m.def("dp_bucket_signal", &dp_bucket_signal, "mark a gradient bucket final on every peer (release store)");
+  m.def("dp_bucket_wait", &dp_bucket_wait, "bounded wait until every peer marked the bucket final");
   m.def("p2p_copy", &p2p_copy, "copy-engine copy from a device address (e.g. a peer's symmetric buffer)");
   m.def("p2p_reduce_rows", &p2p_reduce_rows, "out[i] = sum_r peer[r][src_row[i]] (+add) (P2P loads)");
   m.def("symm_clear_error", &symm_clear_error);

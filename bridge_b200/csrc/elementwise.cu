@@ -608,13 +608,14 @@ __global__ void logprob_grad_kernel(__nv_bfloat16* __restrict__ logits, const in
 }
 
 // ----------------------------------------------------------------------------------------- PPO loss
+// Grid-stride over the tokens; each block writes its five partial sums (loss, clip, dual clip, -log ratio,
+// ratio) to part[block]; ppo_loss_finalize_kernel sums the blocks in a fixed order (deterministic).
 __global__ void ppo_loss_kernel(const float* __restrict__ x, const float* __restrict__ old,
-                                const float* __restrict__ adv, const float* __restrict__ wts, float* __restrict__ out,
-                                float* __restrict__ grad, float* __restrict__ stats, long n, float inv_denom,
-                                float lo, float hi, float cdual) {
+                                const float* __restrict__ adv, const float* __restrict__ wts, float* __restrict__ part,
+                                float* __restrict__ grad, long n, float inv_denom, float lo, float hi, float cdual) {
   __shared__ float scratch[32];
   float ls = 0.f, cf = 0.f, dcf = 0.f, kl = 0.f, rs = 0.f;
-  for (long i = threadIdx.x; i < n; i += blockDim.x) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const float a = adv[i];
     const float d = x[i] - old[i];
     const float dc = fminf(fmaxf(d, -20.f), 20.f);
@@ -650,13 +651,24 @@ __global__ void ppo_loss_kernel(const float* __restrict__ x, const float* __rest
   kl = bb::block_sum(kl, scratch);
   rs = bb::block_sum(rs, scratch);
   if (threadIdx.x == 0) {
-    out[0] = ls * inv_denom;
-    const float inv_n = 1.f / (float)(n > 0 ? n : 1);
-    stats[0] = cf * inv_n;
-    stats[1] = dcf * inv_n;
-    stats[2] = kl * inv_n;
-    stats[3] = rs * inv_n;
+    float* p = part + 5 * (long)blockIdx.x;
+    p[0] = ls;
+    p[1] = cf;
+    p[2] = dcf;
+    p[3] = kl;
+    p[4] = rs;
   }
+}
+
+__global__ void ppo_loss_finalize_kernel(const float* __restrict__ part, int blocks, long n, float inv_denom,
+                                         float* __restrict__ out, float* __restrict__ stats) {
+  if (threadIdx.x != 0) return;
+  float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int b = 0; b < blocks; ++b)
+    for (int j = 0; j < 5; ++j) acc[j] += part[5 * b + j];
+  out[0] = acc[0] * inv_denom;
+  const float inv_n = 1.f / (float)(n > 0 ? n : 1);
+  for (int j = 0; j < 4; ++j) stats[j] = acc[j + 1] * inv_n;
 }
 
 // ----------------------------------------------------------------------------------------- AdamW
@@ -1139,10 +1151,16 @@ std::vector<torch::Tensor> ppo_loss_fwd(torch::Tensor x, torch::Tensor old, torc
   auto out = torch::empty({}, x.options());
   auto grad = torch::empty_like(x);
   auto stats = torch::empty({4}, x.options());
-  ppo_loss_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+  const int blocks = (int)std::max<long>(1, std::min<long>((n + 1023) / 1024, (long)sm_count() * 2));
+  auto part = torch::empty({blocks, 5}, x.options());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  ppo_loss_kernel<<<blocks, 1024, 0, stream>>>(
       x.data_ptr<float>(), old.data_ptr<float>(), adv.data_ptr<float>(),
-      w.has_value() ? w->data_ptr<float>() : nullptr, out.data_ptr<float>(), grad.data_ptr<float>(),
-      stats.data_ptr<float>(), n, (float)(1.0 / denom), (float)lo, (float)hi, (float)c);
+      w.has_value() ? w->data_ptr<float>() : nullptr, part.data_ptr<float>(), grad.data_ptr<float>(), n,
+      (float)(1.0 / denom), (float)lo, (float)hi, (float)c);
+  BB_POST_LAUNCH();
+  ppo_loss_finalize_kernel<<<1, 32, 0, stream>>>(part.data_ptr<float>(), blocks, n, (float)(1.0 / denom),
+                                                 out.data_ptr<float>(), stats.data_ptr<float>());
   BB_POST_LAUNCH();
   return {out, grad, stats};
 }

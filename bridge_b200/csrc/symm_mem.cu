@@ -82,6 +82,35 @@ __global__ void symm_barrier_kernel(PeerPtrs pads, int rank, int n, uint64_t epo
   }
 }
 
+// Per-bucket readiness flags for the reduce-scatter overlapped with backward: flags live in a
+// symmetric buffer laid out [peer][bucket] (uint64 epochs).  `signal` (1 warp, after the bucket's
+// gradients on the compute stream) stores `epoch` into slot [rank][bucket] of every peer's buffer with
+// release semantics; `wait` (1 warp, on the reduce-scatter stream) spins with acquire loads until
+// every peer's slot of `bucket` reached `epoch`, bounded by `timeout_ns` (error word 0x200 + peer).
+__global__ void dp_bucket_signal_kernel(PeerPtrs flags, int rank, int n, int max_buckets, int bucket,
+                                        uint64_t epoch) {
+  const int j = threadIdx.x;
+  if (j >= n) return;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  st_release_sys(static_cast<uint64_t*>(flags.p[j]) + (size_t)rank * max_buckets + bucket, epoch);
+}
+
+__global__ void dp_bucket_wait_kernel(const uint64_t* __restrict__ mine, int n, int max_buckets, int bucket,
+                                      uint64_t epoch, uint64_t timeout_ns) {
+  const int j = threadIdx.x;
+  if (j >= n) return;
+  const uint64_t* slot = mine + (size_t)j * max_buckets + bucket;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys(slot) < epoch) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      atomicCAS(&g_symm_error, 0u, 0x200u + (unsigned)j);
+      return;
+    }
+    __nanosleep(256);
+  }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 __device__ __forceinline__ float block_sum_512(float v, float* red) {
   v = bb::warp_sum(v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
@@ -285,6 +314,23 @@ void dp_adamw_allgather(torch::Tensor master, torch::Tensor m, torch::Tensor v, 
   if (bf16_params) BB_AG(__nv_bfloat16);
   else BB_AG(float);
 #undef BB_AG
+  BB_POST_LAUNCH();
+}
+
+void dp_bucket_signal(std::vector<int64_t> flags, int64_t rank, int64_t max_buckets, int64_t bucket, int64_t epoch) {
+  TORCH_CHECK(bucket >= 0 && bucket < max_buckets && rank >= 0 && rank < (int64_t)flags.size(),
+              "dp_bucket_signal: bucket / rank out of range");
+  dp_bucket_signal_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      make_ptrs(flags), (int)rank, (int)flags.size(), (int)max_buckets, (int)bucket, (uint64_t)epoch);
+  BB_POST_LAUNCH();
+}
+
+void dp_bucket_wait(int64_t mine, int64_t n, int64_t max_buckets, int64_t bucket, int64_t epoch, double timeout_s) {
+  TORCH_CHECK(mine != 0 && mine % 16 == 0 && n >= 1 && n <= kMaxPeers && bucket >= 0 && bucket < max_buckets,
+              "dp_bucket_wait: bad flag buffer, peer count or bucket");
+  dp_bucket_wait_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint64_t*>(mine), (int)n, (int)max_buckets, (int)bucket, (uint64_t)epoch,
+      (uint64_t)(timeout_s * 1e9));
   BB_POST_LAUNCH();
 }
 

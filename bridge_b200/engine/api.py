@@ -236,6 +236,9 @@ def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss:
                 cp = engine._tpr_forest_cp = ForestCP(rt.group, comm=ec.cp_comm)
         fx = ForestExecutor(model, objective, mode=ec.forest_mode, token_budget=ec.token_budget,
                             loss_scale=float(rt.size), cp=cp, offload=offload_config(ec))
+        # the data-parallel reduction of each layer's gradients starts as soon as the step's last
+        # backward has finished that layer (sharded NVLink optimizer)
+        fx.before_final_backward = getattr(engine.optimizer, "arm_overlap", None)
         fx.profiler = profiler
         if prepared.nodes is None:
             prepared.nodes = fx.plan(forest)

@@ -85,7 +85,8 @@ class TPREngine:
             from .optim import ShardedNVLinkAdamW
 
             self.symm_heap = SymmetricHeap(grad_group, self.device)
-            self.optimizer = ShardedNVLinkAdamW(model, optim_config, self.symm_heap)
+            self.optimizer = ShardedNVLinkAdamW(model, optim_config, self.symm_heap,
+                                                tp_group=self.parallel.tp_group if self.parallel.tp > 1 else None)
             self.grad_reducer = DataParallelGradReducer(None)   # reduction happens inside optimizer.step()
         else:
             self.optimizer = MixedPrecisionAdamW(model, optim_config)
@@ -108,7 +109,7 @@ class TPREngine:
         """TP sum of replicated-but-partial gradients (qk-norm / GDN norm weights, norms under SP), then
         the data-parallel reduction."""
         tp = self.parallel.tp_group
-        if tp is not None and self.parallel.tp > 1:
+        if tp is not None and self.parallel.tp > 1 and not getattr(self.optimizer, "handles_tp_partial_grads", False):
             import torch.distributed as dist
 
             for p in self.model.parameters():

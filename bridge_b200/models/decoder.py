@@ -11,6 +11,8 @@ rows are never computed.
 
 from __future__ import annotations
 
+import functools
+
 import torch
 import torch.nn as nn
 from torch import Tensor
@@ -20,6 +22,10 @@ from ..parallel.tp import (VocabParallelEmbedding, copy_to_tp, gather_from_sp, r
                            tp_size)
 from .config import ModelConfig
 from .layers import DecoderLayer, RMSNorm, RotaryEmbedding
+
+
+def _layer_done_hook(callback, layer: int, grad):
+    callback(layer)
 
 
 class DecoderModel(nn.Module):
@@ -52,6 +58,9 @@ class DecoderModel(nn.Module):
                                                     dtype=torch.bfloat16) * cfg.init_std)
             self.lm_head.tp_split_dim = 0  # type: ignore[attr-defined]
         self.vocab_size = cfg.vocab_size
+        # Called with a layer index when the backward has finished that layer (its input gradient is
+        # computed); the sharded data-parallel optimizer uses it to start reducing the layer's bucket.
+        self.grad_ready_callback = None
 
     # ------------------------------------------------------------------ metadata
     @property
@@ -84,7 +93,10 @@ class DecoderModel(nn.Module):
         else:
             x = self.embed_tokens(input_ids)
         pending = None      # each block's MLP output is added inside the next block's first norm
-        for layer in self.layers:
+        cb = self.grad_ready_callback
+        for i, layer in enumerate(self.layers):
+            if cb is not None and x.requires_grad:
+                x.register_hook(functools.partial(_layer_done_hook, cb, i))
             x, pending = layer(x, rope, pending, True)
         x = self.norm(x) if pending is None else add_rmsnorm(x, pending, self.norm.weight, self.norm.eps)[1]
         if self.sequence_parallel:

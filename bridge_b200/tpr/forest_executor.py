@@ -134,6 +134,8 @@ class ForestExecutor:
         self.offload = offload if (offload is not None and offload.enabled) else None
         self._live: list[_Chunk] = []
         self.offloaded_bytes = 0
+        self.before_final_backward = None   # e.g. the sharded optimizer's arm_overlap
+        self._final = None                  # the chunk (or leaf group) whose backward is the step's last
         self.attn_layers = tuple(getattr(model, "attention_layer_numbers", ()))
         self.gdn_layers = tuple(getattr(model, "gdn_layer_numbers", ()))
         self.device = model_device(model)
@@ -391,9 +393,9 @@ class ForestExecutor:
 
     def _visit_leaves(self, nodes: list[_Node], stats: dict, acc: dict) -> None:
         with self._offload_scope():
-            self._visit_leaves_body(self._place(nodes)[0], stats, acc)
+            self._visit_leaves_body(self._place(nodes)[0], stats, acc, final_key=id(nodes))
 
-    def _visit_leaves_body(self, nodes: list[_Node], stats: dict, acc: dict) -> None:
+    def _visit_leaves_body(self, nodes: list[_Node], stats: dict, acc: dict, final_key=None) -> None:
         ctx, hidden = self._forward(nodes, grad=True, record=False)
         stats["fwd"] += sum(n.length for n in nodes)
         stats["bwd"] += sum(n.length for n in nodes)
@@ -403,6 +405,8 @@ class ForestExecutor:
         else:
             acc["metrics"].append(metrics)
         acc["loss"] = loss.detach() if acc["loss"] is None else acc["loss"] + loss.detach()
+        if self._final is final_key and self.before_final_backward is not None:
+            self.before_final_backward()
         (loss * self.loss_scale).backward()
 
     def _pop_chunk(self, ch: _Chunk, stats: dict, acc: dict) -> None:
@@ -455,6 +459,8 @@ class ForestExecutor:
                 grads += [ac.grad if ac.grad is not None else torch.zeros_like(ac),
                           ar.grad if ar.grad is not None else torch.zeros_like(ar)]
         if roots:
+            if self._final is ch and self.before_final_backward is not None:
+                self.before_final_backward()
             torch.autograd.backward(roots, grad_tensors=grads)
         stats["bwd"] += sum(n.length for n in ch.local)
         ch.kv_anchor.clear()
@@ -502,7 +508,12 @@ class ForestExecutor:
         # the same on every rank (TP and CP peers must form identical chunks).
         leaves.sort(key=lambda n: (n.depth == 0, n.parent.chunk.index if n.parent else 0,
                                    n.parent.row0 if n.parent else 0))
-        for grp in _chunked(leaves, budget):
+        leaf_groups = _chunked(leaves, budget)
+        if pushed and any(pushed.values()):
+            self._final = pushed[min(pushed)][0]       # the last pop: the first chunk of the top level
+        elif leaf_groups:
+            self._final = id(leaf_groups[-1])
+        for grp in leaf_groups:
             rec = self._prof_begin("visit_chunk", grp, grp[0].depth)
             self._visit_leaves(grp, stats, acc)
             self._prof_end(rec)

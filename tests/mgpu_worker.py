@@ -53,6 +53,22 @@ def dp_nvlink() -> None:
     cos = float(torch.nn.functional.cosine_similarity(da, db, dim=0))
     rel = float((da - db).norm() / da.norm())
     assert da.norm() > 0 and cos > 0.95 and rel < 0.3, (cos, rel)
+    # the sharded optimizer state comes back in parameter order (the same layout as the replicated one)
+    sa, sb = engines["nccl"].optimizer.state_dict(), engines["nvlink"].optimizer.state_dict()
+    assert sa["step"] == sb["step"] == 2
+    for x, y in zip(sa["arenas"], sb["arenas"]):
+        assert x["master"].shape == y["master"].shape
+        d = float((x["master"] - y["master"]).norm() / x["master"].norm())
+        assert d < 1e-2, d
+    # and loads back: a round trip leaves master / moments / parameters unchanged
+    before = {n: p.detach().clone() for n, p in engines["nvlink"].model.named_parameters()}
+    engines["nvlink"].optimizer.load_state_dict(sb)
+    again = engines["nvlink"].optimizer.state_dict()
+    for x, y in zip(sb["arenas"], again["arenas"]):
+        for key in ("master", "m", "v"):
+            assert torch.equal(x[key], y[key]), key
+    for n, p in engines["nvlink"].model.named_parameters():
+        assert torch.equal(p.detach(), before[n]), n
     engines["nvlink"].symm_heap.close()
     dist.barrier()
     if rank == 0:

@@ -68,3 +68,47 @@ def test_forest_digest_is_deterministic():
     b["input_ids"][0] = b["input_ids"][0].clone()
     b["input_ids"][0][-1] += 1
     assert d1 == d2 != digest_forest_plan(build_tree_execution_plans(keys, b))
+
+
+class _FakeBuffer:
+    def __init__(self, nbytes):
+        self.local = torch.zeros(nbytes, dtype=torch.uint8)
+        self.ptrs = [0]
+
+    def view(self, dtype, numel=None):
+        t = self.local.view(dtype)
+        return t if numel is None else t[:numel]
+
+
+class _FakeHeap:
+    def __init__(self, size, rank):
+        self.size, self.rank = size, rank
+
+    def alloc(self, nbytes):
+        return _FakeBuffer((int(nbytes) + 255) // 256 * 256)
+
+
+def test_sharded_arena_bucket_layout_round_trips():
+    """Bucket-interleaved shards of the NVLink optimizer: every bucket is padded to 8 x N and split N ways;
+    gathering all ranks' pieces and reordering gives the parameters back in order, and the inverse
+    recovers each rank's piece."""
+    from bridge_b200.engine.optim import _ShardedArena, bucket_groups
+    from bridge_b200.models import get_config
+    from bridge_b200.models.decoder import build_model
+
+    cfg = get_config("tiny", num_layers=3)
+    n = 3
+    pieces, ref = [], None
+    for r in range(n):
+        model = build_model(cfg, dtype=torch.float32, seed=0)
+        groups = bucket_groups(model)
+        assert [g[0] for g in groups] == ["embed", 0, 1, 2, "tail"]
+        flat = torch.cat([p.detach().reshape(-1).clone() for _, g in groups for p in g])
+        ref = flat if ref is None else ref
+        a = _ShardedArena(groups, torch.float32, _FakeHeap(n, r))
+        for _, off, padded, sub, lo in a.buckets:
+            assert padded % (8 * n) == 0 and sub * n == padded and off % (8 * n) == 0
+        assert a.master.numel() == a.shard == sum(b[3] for b in a.buckets)
+        pieces.append(a.master.clone())
+        assert torch.equal(a.from_param_order(flat, r), a.master)
+    assert torch.equal(a.to_param_order(pieces), ref)
