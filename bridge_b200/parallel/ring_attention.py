@@ -138,6 +138,17 @@ def _source_positions(shard: SequenceShard, src: int, offset: int, device):
     return g + offset, g < shard.global_length
 
 
+def _block_visible(cur_shard: SequenceShard, rank: int, p_cur: int, shard: SequenceShard, src: int,
+                   off: int) -> bool:
+    """Whether any local query sees any valid key of source ``src`` (the ring's SKIP test), decided from
+    the shard geometry on the host -- no device synchronisation per ring step."""
+    q_pos, _ = _source_positions(cur_shard, rank, p_cur, None)
+    k_pos, k_valid = _source_positions(shard, src, off, None)
+    if not bool(k_valid.any()):
+        return False
+    return int(k_pos[k_valid].min()) <= int(q_pos.max())
+
+
 class _RingTPRAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, meta, *prefix_flat):
@@ -154,7 +165,7 @@ class _RingTPRAttention(torch.autograd.Function):
             for step in range(n):
                 src = (rank - step) % n
                 k_pos, k_valid = _source_positions(shard, src, off, dev)
-                if bool(((k_pos[None, :] <= q_pos[:, None]) & k_valid[None, :]).any()):
+                if _block_visible(cur_shard, rank, P, shard, src, off):
                     o_b, lse_b = block_attention_forward(q, buf[0], buf[1], q_pos, k_pos, q_valid, k_valid, scale)
                     o_acc, lse_acc = merge_attention(o_acc, lse_acc, o_b, lse_b)
                 if step < n - 1:
@@ -184,7 +195,7 @@ class _RingTPRAttention(torch.autograd.Function):
             for step in range(n):
                 src = (rank - step) % n
                 k_pos, k_valid = _source_positions(shard, src, off, dev)
-                if bool(((k_pos[None, :] <= q_pos[:, None]) & k_valid[None, :]).any()):
+                if _block_visible(cur_shard, rank, P, shard, src, off):
                     gq, gk, gv = block_attention_backward(q, pkt[0], pkt[1], do, lse, delta, q_pos, k_pos, q_valid,
                                                           k_valid, scale)
                     dq += gq
