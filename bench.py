@@ -60,7 +60,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--siblings", type=int, default=8)
     p.add_argument("--resp", type=int, default=None)
     p.add_argument("--token-budget", type=int, default=int(os.environ.get("TPR_TOKEN_BUDGET", "0")) or None)
-    p.add_argument("--mode", default=os.environ.get("TPR_FOREST_MODE", "retain"))
+    p.add_argument("--mode", default=os.environ.get("TPR_FOREST_MODE"), help="default: the config's (#3: recompute)")
     p.add_argument("--tp", type=int, default=None, help="default: the config-#2 layout for --gpus")
     p.add_argument("--cp", type=int, default=None, help="default: the config-#2 layout for --gpus")
     p.add_argument("--no-sp", action="store_true", help="TP without sequence parallelism")
@@ -82,10 +82,12 @@ def parse() -> argparse.Namespace:
 
 # per-config defaults: model, tree shape, per-rank token budget
 CONFIG_DEFAULTS = {
-    2: dict(model="qwen3_4b", trees_per_gpu=8, prefix=512, resp=512, token_budget=16384),
-    3: dict(model="qwen3_4b", trees_per_gpu=2, prefix=0, resp=0, token_budget=32768),
-    4: dict(model="hybrid_gdn_2b", trees_per_gpu=8, prefix=512, resp=512, token_budget=16384),
-    5: dict(model="qwen3_next_24l", trees_per_gpu=4, prefix=1024, resp=1024, token_budget=16384),
+    2: dict(model="qwen3_4b", trees_per_gpu=8, prefix=512, resp=512, token_budget=16384, mode="retain"),
+    # sessions: whole turns of up to 24k tokens per segment, pushed segments recomputed at pop time (the
+    # reference's memory profile) so only one chunk's activations exist at a time (offloaded to host)
+    3: dict(model="qwen3_4b", trees_per_gpu=2, prefix=0, resp=0, token_budget=24576, mode="recompute"),
+    4: dict(model="hybrid_gdn_2b", trees_per_gpu=8, prefix=512, resp=512, token_budget=16384, mode="retain"),
+    5: dict(model="qwen3_next_24l", trees_per_gpu=4, prefix=1024, resp=1024, token_budget=16384, mode="retain"),
 }
 
 

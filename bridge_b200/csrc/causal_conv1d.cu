@@ -14,6 +14,8 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace {
@@ -134,6 +136,160 @@ __global__ void conv_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv
   }
 }
 
+// Backward, streaming form: two channels per thread (bf16x2 loads / stores, 128 bytes per warp per
+// row) and one pass over the chunk's rows that reads each x and dy row once.  Registers hold a
+// sliding window of the last W inputs (for the pre-activation and the weight gradient) and of the
+// last W pre-activation gradients da (for dx).  dx of row p needs da(p .. p + W - 1), so the pass
+// runs W - 1 rows past the chunk end; the first W - 1 da values of the sequence are kept for dh0.
+template <int W>
+__global__ void conv_bwd2_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                 const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ bias,
+                                 const __nv_bfloat16* __restrict__ h0, const __nv_bfloat16* __restrict__ dhT,
+                                 const int* __restrict__ cu, __nv_bfloat16* __restrict__ dx, float* __restrict__ dw,
+                                 float* __restrict__ db, float* __restrict__ dh0, int C, bool silu_act) {
+  const int c = 2 * (blockIdx.x * blockDim.x + threadIdx.x);   // channels c, c + 1
+  const int b = blockIdx.y;
+  const int q0 = cu[b], L = cu[b + 1] - q0;
+  const int t0 = blockIdx.z * CH;
+  if (c >= C || t0 >= L) return;
+  const int t1 = min(L, t0 + CH);
+  float wt[2][W];
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    wt[0][j] = __bfloat162float(w[(size_t)c * W + j]);
+    wt[1][j] = __bfloat162float(w[(size_t)(c + 1) * W + j]);
+  }
+  const float bv0 = bias ? __bfloat162float(bias[c]) : 0.f, bv1 = bias ? __bfloat162float(bias[c + 1]) : 0.f;
+  auto load2 = [&](const __nv_bfloat16* base, int row, float& a, float& b2) {
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(base + (size_t)(q0 + row) * C + c);
+    a = __low2float(v);
+    b2 = __high2float(v);
+  };
+  auto x_at = [&](int p, float& a, float& b2) {
+    if (p >= 0) {
+      load2(x, p, a, b2);
+    } else if (h0) {
+      a = __bfloat162float(h0[((size_t)b * C + c) * W + (W + p)]);
+      b2 = __bfloat162float(h0[((size_t)b * C + c + 1) * W + (W + p)]);
+    } else {
+      a = b2 = 0.f;
+    }
+  };
+  float xw[2][W];      // xw[.][W-1] = input of the current row t
+  float daw[2][W];     // daw[.][W-1] = da of the current row t
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    daw[0][j] = daw[1][j] = 0.f;
+    xw[0][j] = xw[1][j] = 0.f;
+  }
+#pragma unroll
+  for (int j = 1; j < W; ++j) x_at(t0 - W + j, xw[0][j], xw[1][j]);   // inputs t0-W+1 .. t0-1 (slots 1..W-1)
+  float gw[2][W], gb[2] = {0.f, 0.f}, head[2][W];
+#pragma unroll
+  for (int j = 0; j < W; ++j) gw[0][j] = gw[1][j] = head[0][j] = head[1][j] = 0.f;
+  const int t_end = min(L, t1 + W - 1);
+  for (int t = t0; t < t_end; ++t) {
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      xw[0][j] = xw[0][j + 1];
+      xw[1][j] = xw[1][j + 1];
+      daw[0][j] = daw[0][j + 1];
+      daw[1][j] = daw[1][j + 1];
+    }
+    load2(x, t, xw[0][W - 1], xw[1][W - 1]);
+    float g0, g1;
+    load2(dy, t, g0, g1);
+    float a0 = bv0, a1 = bv1;
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      a0 += wt[0][j] * xw[0][j];
+      a1 += wt[1][j] * xw[1][j];
+    }
+    if (silu_act) {
+      const float s0 = 1.f / (1.f + __expf(-a0)), s1 = 1.f / (1.f + __expf(-a1));
+      g0 *= s0 * (1.f + a0 * (1.f - s0));
+      g1 *= s1 * (1.f + a1 * (1.f - s1));
+    }
+    daw[0][W - 1] = g0;
+    daw[1][W - 1] = g1;
+    if (t < t1) {                                  // weight / bias gradients of this chunk's outputs
+      gb[0] += g0;
+      gb[1] += g1;
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        gw[0][j] += g0 * xw[0][j];
+        gw[1][j] += g1 * xw[1][j];
+      }
+      if (t < W - 1) {                             // first outputs of the sequence: they read h0
+        head[0][t] = g0;
+        head[1][t] = g1;
+      }
+    }
+    const int p = t - (W - 1);                     // dx row whose da window is now complete
+    if (p >= t0) {
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < W; ++j) {                 // output p + W - 1 - j reads input p through tap j
+        d0 += wt[0][j] * daw[0][W - 1 - j];
+        d1 += wt[1][j] * daw[1][W - 1 - j];
+      }
+      const int sl = p - L + W;                    // final-state slot holding input p
+      if (dhT && sl >= 1 && sl < W) {
+        d0 += __bfloat162float(dhT[((size_t)b * C + c) * W + sl]);
+        d1 += __bfloat162float(dhT[((size_t)b * C + c + 1) * W + sl]);
+      }
+      *reinterpret_cast<__nv_bfloat162*>(dx + (size_t)(q0 + p) * C + c) = __floats2bfloat162_rn(d0, d1);
+    }
+  }
+  // rows of the chunk whose da window reaches past the sequence end (p > L - W): finish them with da = 0
+  for (int p = t_end - (W - 1); p < t1; ++p) {   // the window shifts once per row, emitted from t0 on
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      daw[0][j] = daw[0][j + 1];
+      daw[1][j] = daw[1][j + 1];
+    }
+    daw[0][W - 1] = daw[1][W - 1] = 0.f;
+    if (p < t0) continue;
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      d0 += wt[0][j] * daw[0][W - 1 - j];
+      d1 += wt[1][j] * daw[1][W - 1 - j];
+    }
+    const int sl = p - L + W;
+    if (dhT && sl >= 1 && sl < W) {
+      d0 += __bfloat162float(dhT[((size_t)b * C + c) * W + sl]);
+      d1 += __bfloat162float(dhT[((size_t)b * C + c + 1) * W + sl]);
+    }
+    *reinterpret_cast<__nv_bfloat162*>(dx + (size_t)(q0 + p) * C + c) = __floats2bfloat162_rn(d0, d1);
+  }
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    atomicAdd(&dw[(size_t)c * W + j], gw[0][j]);
+    atomicAdd(&dw[(size_t)(c + 1) * W + j], gw[1][j]);
+  }
+  if (db) {
+    atomicAdd(&db[c], gb[0]);
+    atomicAdd(&db[c + 1], gb[1]);
+  }
+  if (blockIdx.z == 0 && dh0) {
+    // initial-state slot s (input position s - W) is read by outputs t = 0 .. s - 1 through tap s - 1 - t
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      float* hs = dh0 + ((size_t)b * C + c + q) * W;
+      hs[0] = 0.f;
+#pragma unroll
+      for (int sidx = 1; sidx < W; ++sidx) {
+        float g = 0.f;
+        for (int t = 0; t < min(L, sidx); ++t) g += wt[q][sidx - 1 - t] * head[q][t];
+        const int s2 = sidx - L;                   // a sequence shorter than W - 1: the final state reads it
+        if (dhT && s2 >= 1) g += __bfloat162float(dhT[((size_t)b * C + c + q) * W + s2]);
+        hs[sidx] = g;
+      }
+    }
+  }
+}
+
 }  // namespace
 
 std::vector<torch::Tensor> causal_conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
@@ -183,10 +339,12 @@ std::vector<torch::Tensor> causal_conv1d_bwd(torch::Tensor dy, torch::Tensor x, 
   if (bias.has_value()) biasb = bias->to(at::kBFloat16).contiguous();
   if (dhT.has_value()) dhTb = dhT->to(at::kBFloat16).contiguous();
   auto dyc = dy.contiguous();
-  dim3 grid((C + 127) / 128, B, (max_len + CH - 1) / CH);
+  const bool pair = (C % 2) == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) % 4) == 0 &&
+                    (reinterpret_cast<uintptr_t>(dyc.data_ptr()) % 4) == 0 && !std::getenv("BB_CONV_BWD_V1");
+  dim3 grid(pair ? (C / 2 + 127) / 128 : (C + 127) / 128, B, (max_len + CH - 1) / CH);
   auto stream = at::cuda::getCurrentCUDAStream();
 #define BB_CB(WW)                                                                                              \
-  conv_bwd_kernel<WW><<<grid, 128, 0, stream>>>(                                                               \
+  (pair ? conv_bwd2_kernel<WW> : conv_bwd_kernel<WW>)<<<grid, 128, 0, stream>>>(                                                               \
       (const __nv_bfloat16*)dyc.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)wb.data_ptr(), \
       bias.has_value() ? (const __nv_bfloat16*)biasb.data_ptr() : nullptr,                                     \
       h0.has_value() ? (const __nv_bfloat16*)h0b.data_ptr() : nullptr,                                         \

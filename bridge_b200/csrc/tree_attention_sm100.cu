@@ -44,21 +44,6 @@ struct alignas(64) AttnMaps {
   CUtensorMap q, k, v, pk, pv;
 };
 
-// 2^x for the softmax on the FMA pipe: x = n + f (n = floor(x), f in [0, 1)), 2^f from a cubic fitted
-// here by iteratively reweighted least squares in relative error (p(0) = 1, max relative error 8.7e-5
-// on [0, 1) -- far below the bf16 rounding of P), and 2^n added to the exponent bits.  x <= -127 gives
-// exactly 0 (so a masked -inf score vanishes).  The softmax loops evaluate every other exponential with
-// this instead of the MUFU ex2 unit, which is otherwise as busy as the tensor core on a 128 x 128 tile.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -127.f);
-  const float n = floorf(x);
-  const float f = x - n;
-  float p = fmaf(f, 0.07705727f, 0.22765567f);
-  p = fmaf(p, f, 0.69511441f);
-  p = fmaf(p, f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
-}
-
 __device__ __forceinline__ void load_tile128(unsigned char* dst, const CUtensorMap* map, uint64_t* bar, int col0,
                                              int row0) {
   sm100::tma_load_2d(dst, map, bar, col0, row0);
@@ -257,7 +242,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float p0 = exp2f(s[c * 8 + 2 * e] - msafe);
-          const float p1 = exp2_fma(s[c * 8 + 2 * e + 1] - msafe);
+          const float p1 = exp2f(s[c * 8 + 2 * e + 1] - msafe);
           rs += p0 + p1;
           __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
           pk[e] = *reinterpret_cast<uint32_t*>(&hv);
@@ -497,7 +482,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int qq = qbase + c * 32 + e;
           const bool vis = key_ok && (mode == 1 || key <= qq);  // invalid q rows carry lse=+inf -> p=0
           const float arg = __uint_as_float(rs[e]) * scale_log2 - lse_s[c * 32 + e];
-          const float pe = vis ? ((e & 1) ? exp2_fma(arg) : exp2f(arg)) : 0.f;
+          const float pe = vis ? exp2f(arg) : 0.f;
           p[e] = pe;
           ds[e] = pe * (__uint_as_float(rd[e]) - del_s[c * 32 + e]);
         }
@@ -742,7 +727,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int qq = qbase + c * 32 + e;
           const bool vis = key_ok && (mode == 1 || key <= qq);  // invalid q rows carry lse=+inf -> p=0
           const float arg = __uint_as_float(rs[e]) * scale_log2 - lse_s[bi * 64 + c * 32 + e];
-          const float pe = vis ? ((e & 1) ? exp2_fma(arg) : exp2f(arg)) : 0.f;
+          const float pe = vis ? exp2f(arg) : 0.f;
           p[e] = pe;
           ds[e] = pe * (__uint_as_float(rd[e]) - del_s[bi * 64 + c * 32 + e]);
         }
@@ -934,7 +919,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int e = 0; e < 32; ++e) {
           const bool vis = row_ok && (kbase + c * 32 + e) < klim;
           const float arg = __uint_as_float(rs[e]) * scale_log2 - lse_r;
-          const float pe = vis ? ((e & 1) ? exp2_fma(arg) : exp2f(arg)) : 0.f;
+          const float pe = vis ? exp2f(arg) : 0.f;
           ds[e] = pe * (__uint_as_float(rd[e]) - del_r);
         }
         store_row32_sw128(smem + SmemDQ::DS, row, c, ds);
@@ -1139,7 +1124,7 @@ __global__ void __launch_bounds__(DQ2_THREADS, 1)
         for (int e = 0; e < 32; ++e) {
           const bool vis = row_ok && (kbase + c * 32 + e) < klim;
           const float arg = __uint_as_float(rs[e]) * scale_log2 - lse_r;
-          const float pe = vis ? ((e & 1) ? exp2_fma(arg) : exp2f(arg)) : 0.f;
+          const float pe = vis ? exp2f(arg) : 0.f;
           ds[e] = pe * (__uint_as_float(rd[e]) - del_r);
         }
         store_row32_sw128(ds_tile, row, c, ds);

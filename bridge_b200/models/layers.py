@@ -128,7 +128,8 @@ class TPRGatedDeltaNet(nn.Module):
 
     tpr_state_kind = "gdn"
 
-    def __init__(self, cfg: ModelConfig, layer_number: int, *, tp_group=None, device=None) -> None:
+    def __init__(self, cfg: ModelConfig, layer_number: int, *, tp_group=None, sequence_parallel=False,
+                 device=None) -> None:
         super().__init__()
         n = tp_size(tp_group)
         if cfg.gdn_num_qk_heads % n or cfg.gdn_num_v_heads % n:
@@ -139,8 +140,11 @@ class TPRGatedDeltaNet(nn.Module):
         self.w = cfg.gdn_conv_kernel
         self.chunk = cfg.gdn_chunk_size
         kd, vd = cfg.gdn_num_qk_heads * self.dk, cfg.gdn_num_v_heads * self.dv
+        # under sequence parallelism the input projection all-gathers the token shard first (and the output
+        # projection reduce-scatters), so the conv and the delta rule always see whole sequences
         self.in_proj = ColumnParallelLinear(cfg.hidden_size, 2 * kd + 2 * vd + 2 * cfg.gdn_num_v_heads,
-                                            group=tp_group, std=cfg.init_std, device=device)
+                                            group=tp_group, sequence_parallel=sequence_parallel, std=cfg.init_std,
+                                            device=device)
         c_local = (2 * kd + vd) // n
         self.conv_weight = nn.Parameter(torch.randn(c_local, self.w, device=device, dtype=torch.bfloat16)
                                         * (1.0 / math.sqrt(self.w)))
@@ -149,7 +153,7 @@ class TPRGatedDeltaNet(nn.Module):
         self.norm_weight = nn.Parameter(torch.ones(self.dv, device=device, dtype=torch.bfloat16))
         if n > 1:  # shared across heads; each TP rank sees only its heads
             self.norm_weight.tp_partial_grad = True  # type: ignore[attr-defined]
-        self.out_proj = RowParallelLinear(vd, cfg.hidden_size, group=tp_group,
+        self.out_proj = RowParallelLinear(vd, cfg.hidden_size, group=tp_group, sequence_parallel=sequence_parallel,
                                           std=scaled_init_std(cfg.init_std, cfg.num_layers), device=device)
         self.eps = cfg.rms_eps
         self.scale = 1.0 / math.sqrt(self.dk)
@@ -170,7 +174,8 @@ class TPRGatedDeltaNet(nn.Module):
             from ..parallel.gdn_state import forward_gdn_cp_tpr
 
             return forward_gdn_cp_tpr(self, x, ctx, backend)          # CP-sharded tokens: head-parallel
-        proj = self.in_proj(x)
+        proj = self.in_proj(x)                 # all tokens of the forward (gathered under SP)
+        t = proj.shape[0]
         qkv, z, b, a = proj.split((2 * kd + vd, vd, self.hv, self.hv), dim=-1)
         if ctx is not None and ctx.layout is not None:
             cu = [0]
@@ -234,7 +239,8 @@ class DecoderLayer(nn.Module):
             self.self_attention = TPRSelfAttention(cfg, layer_number, tp_group=tp_group,
                                                    sequence_parallel=sequence_parallel, device=device)
         else:
-            self.self_attention = TPRGatedDeltaNet(cfg, layer_number, tp_group=tp_group, device=device)
+            self.self_attention = TPRGatedDeltaNet(cfg, layer_number, tp_group=tp_group,
+                                                   sequence_parallel=sequence_parallel, device=device)
         if cfg.is_moe:
             from .moe import MoELayer
 

@@ -86,6 +86,8 @@ class _ConvFn(torch.autograd.Function):
 
 def causal_conv1d(x: Tensor, weight: Tensor, bias: Tensor | None, cu_seqlens: list[int], cu_dev: Tensor | None,
                   initial_state: Tensor | None, *, activation: bool = True):
+    if cu_seqlens[-1] != x.shape[0]:
+        raise ValueError(f"causal_conv1d: the sequences cover {cu_seqlens[-1]} rows but x has {x.shape[0]}")
     if on_gpu(x):
         if cu_dev is None:
             cu_dev = torch.tensor(cu_seqlens, dtype=torch.int32, device=x.device)
@@ -219,6 +221,9 @@ def chunk_gated_delta_rule(q, k, v, g, beta, cu_seqlens: list[int], cu_dev: Tens
     (64, 64), (64, 128), (32, 64), (32, 32)).  The kernels always work in 64-token chunks: the
     chunking changes rounding only, not the result, so ``chunk_size`` applies to the PyTorch path.
     """
+    if cu_seqlens[-1] != q.shape[0] or k.shape[0] != q.shape[0] or v.shape[0] != q.shape[0]:
+        raise ValueError(f"chunk_gated_delta_rule: the sequences cover {cu_seqlens[-1]} rows but q/k/v have "
+                         f"{q.shape[0]}/{k.shape[0]}/{v.shape[0]}")
     if on_gpu(q):
         if (q.shape[-1], v.shape[-1]) not in _GDR_SHAPES or q.dtype != torch.bfloat16:
             raise NotImplementedError("gated delta rule kernel: bf16 with (key dim, value dim) in "

@@ -242,8 +242,28 @@ def bench_gdn(t: Timer, small: bool):
     _report("gated_delta_rule_bwd", {"T": T, "H": H, "K": K, "V": V}, ms, flops=3 * fl)
 
 
+def bench_moe(t: Timer, small: bool):
+    """Device MoE routing (top-k + stable expert sort), combine and its backward at the config #5 shape
+    (512 experts, top-10, hidden 2048; 16384 tokens per rank, 4096 with --small)."""
+    from bridge_b200.ops._ext import kernels
+
+    m = kernels()
+    T, E, k, H = (4096 if small else 16384), 512, 10, 2048
+    logits = torch.randn(T, E, device="cuda")
+    idx, w, counts, offsets, pos, order = m.moe_route(logits, k)
+    ms = t(lambda: m.moe_route(logits, k))
+    _report("moe_route", {"T": T, "E": E, "k": k}, ms, bytes_=T * E * 4 + T * k * 16)
+    ys = torch.randn(T * k, H, device="cuda", dtype=torch.bfloat16)
+    wf = w.reshape(-1).contiguous()
+    ms = t(lambda: m.moe_combine(ys, pos, wf, T))
+    _report("moe_combine", {"T": T, "k": k, "H": H}, ms, bytes_=(T * k + T) * H * 2)
+    dy = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    ms = t(lambda: m.moe_combine_bwd(dy, ys, pos, wf))
+    _report("moe_combine_bwd", {"T": T, "k": k, "H": H}, ms, bytes_=(2 * T * k + T) * H * 2)
+
+
 OPS = {"gemm": bench_gemm, "attention": bench_attention, "elementwise": bench_elementwise,
-       "logprob": bench_logprob, "ppo": bench_ppo, "gdn": bench_gdn}
+       "logprob": bench_logprob, "ppo": bench_ppo, "gdn": bench_gdn, "moe": bench_moe}
 
 
 def main(argv=None):

@@ -308,3 +308,13 @@ def test_forest_tp2_cp2_sequence_parallel_matches_flattened():
         assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
         worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
         assert worst[1] < 1e-4, worst
+
+
+def test_forest_tp2_cp2_sequence_parallel_hybrid_matches_flattened():
+    """BASELINE config #4's axes through the forest executor: the hybrid GDN model at TP2 (sequence
+    parallel: the GDN projections gather / scatter the token shard) x CP2 (GDN states gathered over CP)."""
+    res = run_ranks(4, _tpcp_worker, "ring", "tiny_hybrid", "head", "forest", True)
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst

@@ -18,8 +18,13 @@ def _close(a, b, atol, rtol, name=""):
 @pytest.mark.parametrize("W", [4, 3, 2])
 @pytest.mark.parametrize("with_h0,with_bias,with_dht", [(True, False, True), (False, True, False),
                                                         (True, True, False)])
-def test_causal_conv1d(W, with_h0, with_bias, with_dht):
+@pytest.mark.parametrize("bwd", ["stream2", "v1"])
+def test_causal_conv1d(W, with_h0, with_bias, with_dht, bwd, monkeypatch):
+    """Forward and both backward kernels (two-channel streaming default, one-channel v1)."""
     from bridge_b200.ops.gdn import causal_conv1d, causal_conv1d_reference
+
+    if bwd == "v1":
+        monkeypatch.setenv("BB_CONV_BWD_V1", "1")
 
     torch.manual_seed(W)
     lens = [100, 2, 64, 131, 1, 70]

@@ -119,8 +119,8 @@ def test_forest_activation_offload_gpu(mode):
     dev = torch.device("cuda")
     batch = tree_batch(n_trees=2, prefix=1024, siblings=4, resp=512, seed=9)
     res, peaks, grads = {}, {}, {}
-    for off in (False, "again", True):       # "again": a second run without offload (run-to-run noise)
-        eng = TPREngine(_cfg(), EngineConfig(forest_mode=mode, token_budget=4096, activation_offload=off is True),
+    for off in (False, True):
+        eng = TPREngine(_cfg(), EngineConfig(forest_mode=mode, token_budget=4096, activation_offload=off),
                         device=dev, model=build_model(_cfg(), device=dev, seed=0))
         set_old_log_probs(eng.model, batch)
         torch.cuda.synchronize()
@@ -133,10 +133,18 @@ def test_forest_activation_offload_gpu(mode):
         del eng
     assert res[True]["metrics"]["tpr/offloaded_bytes"][0] > 0
     assert abs(res[True]["loss"][0] - res[False]["loss"][0]) <= 1e-5 * abs(res[False]["loss"][0]) + 1e-7
-    # the attention backward reduces prefix dK/dV with FP32 atomics, so two plain runs already differ by
-    # bf16 rounding flips; offload must stay within a small multiple of that run-to-run noise
+    # the attention backward reduces prefix dK/dV with FP32 atomics (bf16 rounding flips between runs), so
+    # the offloaded run is held to the same oracle as the plain one: the flattened non-TPR computation
+    ref = build_model(_cfg(), device=dev, seed=0)
+    loss_ref, _ = flat_ppo_loss(ref, batch)
+    loss_ref.backward()
+    gr = {n: p.grad.float() for n, p in ref.named_parameters()}
+    for off in (False, True):
+        assert abs(res[off]["loss"][0] - float(loss_ref)) <= 2e-3 * abs(float(loss_ref)) + 1e-4
+        for n, g in grads[off].items():
+            rel = float((g - gr[n]).norm() / (gr[n].norm() + 1e-12))
+            assert rel < 3e-2 and _cos(g, gr[n]) > 0.999, (off, n, rel)
     for n, g in grads[False].items():
         rel = float((grads[True][n] - g).norm() / (g.norm() + 1e-12))
-        noise = float((grads["again"][n] - g).norm() / (g.norm() + 1e-12))
-        assert rel < 4 * noise + 1e-4, (n, rel, noise)
+        assert rel < 1e-2, (n, rel)
     assert peaks[True] < peaks[False], peaks
