@@ -123,14 +123,21 @@ class ActivationOffloader:
         if s.restored is not None:
             return
         if s.device.type == "cuda":
-            ctx = torch.cuda.stream(stream) if stream is not None else torch.cuda.stream(torch.cuda.current_stream())
-            with ctx:
-                cur = torch.cuda.current_stream()
-                cur.wait_event(s.d2h_done)
-                dev = torch.empty(s.shape, dtype=s.dtype, device=s.device)
+            # allocate from the compute stream's pool (the tensor is consumed there; a prefetch-stream pool
+            # would hold its own copies of freed blocks), fill it on the prefetch stream
+            main = torch.cuda.current_stream()
+            dev = torch.empty(s.shape, dtype=s.dtype, device=s.device)
+            copy_stream = stream if stream is not None else main
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(s.d2h_done)
+                if copy_stream is not main:
+                    # the block may have been freed by compute work still in flight: write after it
+                    copy_stream.wait_stream(main)
                 dev.view(-1).copy_(s.host, non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record()
+            if copy_stream is not main:
+                dev.record_stream(copy_stream)
             s.restored, s.h2d_done = dev, ev
         else:
             s.restored = s.host.view(s.shape).clone()

@@ -116,12 +116,17 @@ def test_forest_activation_offload_gpu(mode):
     from bridge_b200.engine import EngineConfig, TPREngine
     from bridge_b200.models.decoder import build_model
 
+    from bridge_b200.models import get_config
+
     dev = torch.device("cuda")
-    batch = tree_batch(n_trees=2, prefix=1024, siblings=4, resp=512, seed=9)
+    # deep and wide enough that the saved activations, not the weights or the LM head, set the peak
+    cfg = get_config("tiny", hidden_size=1024, num_heads=8, num_kv_heads=2, head_dim=128, intermediate_size=4096,
+                     num_layers=8)
+    batch = tree_batch(n_trees=2, prefix=2048, siblings=4, resp=1024, seed=9)
     res, peaks, grads = {}, {}, {}
     for off in (False, True):
-        eng = TPREngine(_cfg(), EngineConfig(forest_mode=mode, token_budget=4096, activation_offload=off),
-                        device=dev, model=build_model(_cfg(), device=dev, seed=0))
+        eng = TPREngine(cfg, EngineConfig(forest_mode=mode, token_budget=8192, activation_offload=off),
+                        device=dev, model=build_model(cfg, device=dev, seed=0))
         set_old_log_probs(eng.model, batch)
         torch.cuda.synchronize()
         torch.cuda.reset_peak_memory_stats()
@@ -135,7 +140,7 @@ def test_forest_activation_offload_gpu(mode):
     assert abs(res[True]["loss"][0] - res[False]["loss"][0]) <= 1e-5 * abs(res[False]["loss"][0]) + 1e-7
     # the attention backward reduces prefix dK/dV with FP32 atomics (bf16 rounding flips between runs), so
     # the offloaded run is held to the same oracle as the plain one: the flattened non-TPR computation
-    ref = build_model(_cfg(), device=dev, seed=0)
+    ref = build_model(cfg, device=dev, seed=0)
     loss_ref, _ = flat_ppo_loss(ref, batch)
     loss_ref.backward()
     gr = {n: p.grad.float() for n, p in ref.named_parameters()}
