@@ -32,10 +32,18 @@ def _env_min_bytes() -> int:
     return int(os.environ.get("TPR_OFFLOAD_MIN_BYTES", str(1 << 20)))
 
 
+def _env_inflight_bytes() -> int:
+    return int(os.environ.get("TPR_OFFLOAD_INFLIGHT_BYTES", str(16 << 30)))
+
+
 @dataclass(frozen=True)
 class OffloadConfig:
     enabled: bool = False
     min_bytes: int = field(default_factory=_env_min_bytes)     # smaller saved tensors stay on the device
+    # device bytes whose device->host copy may still be pending: above it the forward waits for the
+    # oldest copies (the host link is slower than the GPU produces activations, and a tensor's device
+    # memory is only released once its copy finished)
+    max_inflight_bytes: int = field(default_factory=_env_inflight_bytes)
     prefetch: bool = True
     force_restore_sync: bool = os.environ.get("TPR_OFFLOAD_B_FORCE_RESTORE_SYNC", "0") == "1"
 
@@ -89,6 +97,8 @@ class ActivationOffloader:
         self.d2h = torch.cuda.Stream() if self.cuda else None
         self.h2d = torch.cuda.Stream() if self.cuda else None
         self.offloaded_bytes = 0
+        self._inflight: list = []          # (d2h done event, bytes), oldest first
+        self._inflight_bytes = 0
 
     def protect(self, tensors) -> None:
         for t in tensors:
@@ -111,6 +121,12 @@ class ActivationOffloader:
                 t.record_stream(self.d2h)
                 done = torch.cuda.Event()
                 done.record()
+            self._inflight.append((done, nbytes))
+            self._inflight_bytes += nbytes
+            while self._inflight_bytes > self.cfg.max_inflight_bytes and len(self._inflight) > 1:
+                old_ev, old_n = self._inflight.pop(0)
+                old_ev.synchronize()
+                self._inflight_bytes -= old_n
         else:
             host.copy_(t.reshape(-1))
             done = None
