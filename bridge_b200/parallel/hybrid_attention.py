@@ -5,7 +5,10 @@ zigzag-sharded over the R ring ranks (padded to ``lcm(cp, 2R)``) and each
 ring rank's two chunks are cut into U contiguous pieces, one per Ulysses rank.
 Attention: seq->head all-to-all inside the Ulysses group (every member then
 holds its ring rank's whole zigzag shard for ``H/U`` heads), ring attention
-over the R ring ranks, head->seq all-to-all back.
+over the R ring ranks, head->seq all-to-all back.  On a single-node CUDA ring
+group the ring leg is the NVLink transport of the ring backend (P2P KV row
+gathers, the tcgen05 tree-attention kernel, P2P owner reduction of dK/dV);
+elsewhere the NCCL / gloo ring.
 
 Parity: verl/models/mcore/tpr/parallel/hybrid_attention.py:42-495
 (HybridCPTopology, rank layout, shard, A2A -> ring -> A2A).
@@ -93,8 +96,17 @@ def hybrid_cp_rectangular_attention(query: Tensor, key: Tensor, value: Tensor, *
                      sequence_to_head(b.value, ug))
         for b in prefix_blocks
     )
-    oh = ring_cp_attention(qh, kh, vh, prefix_blocks=ring_prefix, current_shard=_ring_view(current_shard, topology),
-                           cp_group=topology.ring_group, softmax_scale=softmax_scale)
+    ring_shard = _ring_view(current_shard, topology)
+    from .cp_p2p import cp_comm, p2p_cp_attention
+
+    comm = cp_comm(topology.ring_group, qh)
+    if comm is not None:        # CUDA, one node: P2P KV rows + tcgen05 tree attention + P2P owner reduction
+        scale = softmax_scale if softmax_scale is not None else qh.shape[-1] ** -0.5
+        oh = p2p_cp_attention(qh, kh, vh, prefix_blocks=ring_prefix, current_shard=ring_shard, comm=comm,
+                              softmax_scale=scale)
+    else:                       # NCCL / gloo ring (baseline and CPU path)
+        oh = ring_cp_attention(qh, kh, vh, prefix_blocks=ring_prefix, current_shard=ring_shard,
+                               cp_group=topology.ring_group, softmax_scale=softmax_scale)
     return head_to_sequence(oh, ug)
 
 
