@@ -38,6 +38,34 @@ using bf = __nv_bfloat16;
 __device__ __forceinline__ float b2f(bf x) { return __bfloat162float(x); }
 __device__ __forceinline__ bf f2b(float x) { return __float2bfloat16(x); }
 
+// Optional phase timing, off unless enabled from the host (gdr_phase_profile): after a block barrier,
+// thread 0 adds the SM cycles the block spent in each phase to a device table [kernel][phase].
+// Kernels: 0 prep, 1 scan, 2 bwd scan, 3 bwd chunk.
+__device__ int g_gdr_prof_on;
+__device__ unsigned long long g_gdr_prof[4][16];
+
+struct PhaseClock {
+  bool on = false;
+  long long t = 0;
+  __device__ __forceinline__ PhaseClock() {
+#if defined(__CUDA_ARCH__)
+    on = g_gdr_prof_on != 0;
+    if (on) t = clock64();
+#endif
+  }
+  __device__ __forceinline__ void mark(int kern, int phase) {
+#if defined(__CUDA_ARCH__)
+    if (!on) return;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const long long now = clock64();
+      atomicAdd(&g_gdr_prof[kern][phase], (unsigned long long)(now - t));
+      t = now;
+    }
+#endif
+  }
+};
+
 struct Chunk {
   int row0, n, b, c;
 };
@@ -180,6 +208,7 @@ __global__ void __launch_bounds__(NT) gdr_prep_kernel(const bf* __restrict__ k, 
   float* sB = sE + CS;
   const Chunk ch = load_chunk_desc(chunks, blockIdx.x);
   const int h = blockIdx.y;
+  PhaseClock pc;
   load_rows<KD>(sK, SM::LK, k, ch.row0, ch.n, H, h, KD, 0);
   for (int t = threadIdx.x; t < CS; t += NT) sB[t] = t < ch.n ? beta[(size_t)(ch.row0 + t) * H + h] : 0.f;
   chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);
@@ -193,13 +222,16 @@ __global__ void __launch_bounds__(NT) gdr_prep_kernel(const bf* __restrict__ k, 
     sVb[t * SM::LV + c] = t < ch.n ? f2b(sB[t] * b2f(v[((size_t)(ch.row0 + t) * H + h) * VD + c])) : f2b(0.f);
   }
   __syncthreads();
+  pc.mark(0, 0);
   build_T<KD>(sK, SM::LK, sG, sB, sA, sTf, sTb, ch.n);
+  pc.mark(0, 1);
   wm::block_gemm<false, false>(CS, KD, CS, sTb, 72, sKb, SM::LK, [&](int t, int c, float val) {
     if (t < ch.n) wk[((size_t)(ch.row0 + t) * H + h) * KD + c] = f2b(val);
   });
   wm::block_gemm<false, false>(CS, VD, CS, sTb, 72, sVb, SM::LV, [&](int t, int c, float val) {
     if (t < ch.n) wv[((size_t)(ch.row0 + t) * H + h) * VD + c] = f2b(val);
   });
+  pc.mark(0, 2);
 }
 
 template <int KD, int VB>
@@ -250,6 +282,7 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
   const int v0 = vb * VB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c_begin = seq_chunk0[b], c_end = seq_chunk0[b + 1];
+  PhaseClock pc;
 
   float st[ST::PER_WARP][2][4];
 #pragma unroll
@@ -287,6 +320,7 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
     load_rows<KD>(sWk, SM::LK, wk, ch.row0, ch.n, H, h, KD, 0);
     load_rows<VB>(sWv, SM::LV, wv, ch.row0, ch.n, H, h, VD, v0);
     chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);  // ends with __syncthreads
+    pc.mark(1, 0);
     // P = D o Q K^T (s <= t)
     wm::block_gemm<false, true>(CS, CS, KD, sQ, SM::LK, sK, SM::LK, [&](int t, int s, float val) {
       sP[t * 72 + s] = f2b((s <= t && t < ch.n) ? __expf(sG[t] - sG[s]) * val : 0.f);
@@ -299,6 +333,7 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
       if (t < ch.n) u[((size_t)(ch.row0 + t) * H + h) * VD + v0 + c] = f2b(uu);
     });
     __syncthreads();
+    pc.mark(1, 1);
     // O = scale (Gam o (Q S0) + P U)
     {
       const int tn = VB / 16, tiles = (CS / 16) * tn;
@@ -319,6 +354,7 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
           }
       }
     }
+    pc.mark(1, 2);
     // S1 = Gam_last S0 + K^T (E o U)
     const float gl = sGam[ch.n - 1];
 #pragma unroll
@@ -333,6 +369,7 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
         for (int e = 0; e < 4; ++e) st[i][j][e] = gl * st[i][j][e] + c[j][e];
     }
     __syncthreads();
+    pc.mark(1, 3);
   }
 #pragma unroll
   for (int i = 0; i < ST::PER_WARP; ++i) {
@@ -399,6 +436,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
   const int v0 = vb * VB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c_begin = seq_chunk0[b], c_end = seq_chunk0[b + 1];
+  PhaseClock pc;
 
   float ds[ST::PER_WARP][2][4];
 #pragma unroll
@@ -448,10 +486,12 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
       const int t = i / VB, c = i % VB;
       sGdO[t * SM::LV + c] = f2b(scale * sGam[t] * b2f(sdO[t * SM::LV + c]));
     }
+    pc.mark(2, 0);
     wm::block_gemm<false, true>(CS, CS, KD, sQ, SM::LK, sK, SM::LK, [&](int t, int s, float val) {
       sP[t * 72 + s] = f2b((s <= t && t < ch.n) ? __expf(sG[t] - sG[s]) * val : 0.f);
     });
     __syncthreads();
+    pc.mark(2, 1);
     // dU = scale P^T dO + E o (K dS1);  de_s = sum_j (K dS1)_sj U_sj
     {
       const int tn = VB / 16, tiles = (CS / 16) * tn;
@@ -477,19 +517,24 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
       }
     }
     __syncthreads();
+    pc.mark(2, 2);
     // state-dependent gradient pieces (summed over the V blocks with atomics)
     wm::block_gemm2<false, true>(CS, KD, VB, sdO, SM::LV, sS, sSl, SM::LV, [&](int t, int c, float val) {
       if (t < ch.n) atomicAdd(&dq[((size_t)(ch.row0 + t) * H + h) * KD + c], scale * sGam[t] * val);
     });
+    pc.mark(2, 3);
     wm::block_gemm2<false, true>(CS, KD, VB, sU, SM::LV, sdS, sdSl, SM::LV, [&](int t, int c, float val) {
       if (t < ch.n) atomicAdd(&dk[((size_t)(ch.row0 + t) * H + h) * KD + c], sE[t] * val);
     });
+    pc.mark(2, 4);
     wm::block_gemm2<false, true>(CS, KD, VB, snDU, SM::LV, sS, sSl, SM::LV, [&](int t, int c, float val) {
       if (t < ch.n) atomicAdd(&dwk[((size_t)(ch.row0 + t) * H + h) * KD + c], val);
     });
+    pc.mark(2, 5);
     wm::block_gemm2<false, false>(CS, VB, KD, sQ, SM::LK, sS, sSl, SM::LV, [&](int t, int c, float val) {
       if (t < ch.n) atomicAdd(&sdG[t], scale * sGam[t] * val * b2f(sdO[t * SM::LV + c]));
     });
+    pc.mark(2, 6);
     // dS0 = Gam_last dS1 + Q^T (scale Gam o dO) - Wk^T dU
     const float gl = sGam[ch.n - 1];
 #pragma unroll
@@ -506,6 +551,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
         for (int e = 0; e < 4; ++e) ds[i][j][e] = gl * ds[i][j][e] + c[j][e];
     }
     __syncthreads();
+    pc.mark(2, 7);
     if (threadIdx.x == 0) {
       float tot = 0.f, dsum = 0.f;
       for (int w = 0; w < NT / 32; ++w) dsum += sred[w];
@@ -516,6 +562,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
     for (int t = threadIdx.x; t < ch.n; t += NT)
       atomicAdd(&dG[(size_t)(ch.row0 + t) * H + h], sdG[t] - sde[t] * sE[t]);
     __syncthreads();
+    pc.mark(2, 8);
   }
   if (dh0) {
 #pragma unroll
@@ -584,6 +631,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
   float* sdb = sdG + CS;
   const Chunk ch = load_chunk_desc(chunks, blockIdx.x);
   const int h = blockIdx.y, n = ch.n, row0 = ch.row0;
+  PhaseClock pc;
   auto rk = [&](int t) { return ((size_t)(row0 + t) * H + h) * KD; };
   auto rv = [&](int t) { return ((size_t)(row0 + t) * H + h) * VD; };
 
@@ -608,12 +656,15 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
     sdU[t * SM::LV + c] = f2b(t < n ? du[rv(t) + c] : 0.f);
   }
   __syncthreads();
+  pc.mark(3, 0);
   build_T<KD>(sK, SM::LK, sG, sB, sA, sTf, sTb, n);          // sA = D o KK^T (strict), sTb = T
+  pc.mark(3, 1);
   // P (fp32, into sTf) and dP = scale dO U^T;  dG from P: rowsum(dP o P) - colsum(dP o P)
   wm::block_gemm<false, true>(CS, CS, KD, sQ, SM::LK, sK, SM::LK, [&](int t, int s, float val) {
     sTf[t * 65 + s] = (s <= t && t < n) ? __expf(sG[t] - sG[s]) * val : 0.f;
   });
   __syncthreads();
+  pc.mark(3, 2);
   wm::block_gemm<false, true>(CS, CS, VD, sdO, SM::LV, sU, SM::LV, [&](int t, int s, float val) {
     const bool ok = s <= t && t < n;
     const float dp = ok ? scale * val : 0.f;
@@ -625,6 +676,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
     }
   });
   __syncthreads();
+  pc.mark(3, 3);
   // dq += (dP o D) K ;  dk += (dP o D)^T Q
   wm::block_gemm<false, false>(CS, KD, CS, sX1, 72, sK, SM::LK, [&](int t, int c, float val) {
     if (t < n) dq[rk(t) + c] += val;
@@ -633,6 +685,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
     if (t < n) dk[rk(t) + c] += val;
   });
   __syncthreads();
+  pc.mark(3, 4);
   // dT = dU (beta V)^T + dWk (beta Gam K)^T   (into sX1)
   {
     const int tiles = (CS / 16) * (CS / 16);
@@ -652,6 +705,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
     }
   }
   __syncthreads();
+  pc.mark(3, 5);
   // dVb = T^T dU -> dv = beta dVb, dbeta += <dVb, V>;  dKb = T^T dWk -> dk += beta Gam dKb, dbeta, dG
   wm::block_gemm<true, false>(CS, VD, CS, sTb, 72, sdU, SM::LV, [&](int s, int c, float val) {
     if (s < n) {
@@ -667,11 +721,13 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
       atomicAdd(&sdG[s], sB[s] * sGam[s] * kv * val);
     }
   });
+  pc.mark(3, 6);
   // X2 = dT T^T
   wm::block_gemm<false, true>(CS, CS, CS, sX1, 72, sTb, 72, [&](int t, int s, float val) {
     sX2[t * 72 + s] = f2b(val);
   });
   __syncthreads();
+  pc.mark(3, 7);
   for (int i = threadIdx.x; i < CS * 72; i += NT) sX1[i] = f2b(0.f);
   __syncthreads();
   // dL = -T^T X2;  dA_ts = beta_t dL_ts (s < t) -> dbeta, dG, and M = dKK + dKK^T with dKK = dA o D
@@ -689,10 +745,12 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
     }
   });
   __syncthreads();
+  pc.mark(3, 8);
   wm::block_gemm<false, false>(CS, KD, CS, sX1, 72, sK, SM::LK, [&](int t, int c, float val) {
     if (t < n) dk[rk(t) + c] += val;
   });
   __syncthreads();
+  pc.mark(3, 9);
   if (threadIdx.x == 0) {
     float acc = 0.f;
     for (int t = n - 1; t >= 0; --t) {
@@ -701,6 +759,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
       dbeta[(size_t)(row0 + t) * H + h] = sdb[t];
     }
   }
+  pc.mark(3, 10);
 }
 
 template <typename Kern>
@@ -756,6 +815,28 @@ void launch_bwd(const torch::Tensor& dout, const float* dhT, const torch::Tensor
       dG.data_ptr<float>(), dg.data_ptr<float>(), db.data_ptr<float>(), H, scale);
   BB_POST_LAUNCH();
 }
+
+}  // namespace
+
+// Phase timing of the gated-delta-rule kernels (a profiling aid; see PhaseClock).  Enabling clears
+// the table; reading returns int64 [4, 16] summed SM cycles per (kernel, phase).
+void gdr_phase_profile(bool enable) {
+  const int on = enable ? 1 : 0;
+  unsigned long long zero[4][16] = {};
+  BB_CHECK_CUDA(cudaMemcpyToSymbol(g_gdr_prof, zero, sizeof(zero)));
+  BB_CHECK_CUDA(cudaMemcpyToSymbol(g_gdr_prof_on, &on, sizeof(on)));
+}
+
+torch::Tensor gdr_phase_read() {
+  unsigned long long tab[4][16];
+  BB_CHECK_CUDA(cudaMemcpyFromSymbol(tab, g_gdr_prof, sizeof(tab)));
+  auto out = torch::empty({4, 16}, torch::TensorOptions().dtype(torch::kInt64));
+  for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 16; ++j) out[i][j] = (int64_t)tab[i][j];
+  return out;
+}
+
+namespace {
 
 #define BB_GDR_DISPATCH(KD, VD, CALL)                                                  \
   if (K == KD && V == VD) {                                                           \

@@ -9,8 +9,10 @@ the backward math of the next.  The prefix-KV anchors of the segment (and the
 new K/V a Pop hands to autograd as roots) are never offloaded: they are read
 by every descendant and must stay resident.
 
-Pinned host buffers come from a size-bucketed pool so steady-state steps do
-no ``cudaHostAlloc``.
+Pinned host memory comes in large slabs shared by every scope: a scope packs
+its tensors first-fit into the slabs it holds and returns them all at its
+release, so chunks of any token count reuse the same host memory and
+steady-state steps do no ``cudaHostAlloc``.
 
 Parity: verl/models/mcore/tpr/activation_offload.py:61-328 (scope, limits,
 protected external storages, forced same-layer restore).  Built on
@@ -57,22 +59,64 @@ def validate_activation_offload(model: nn.Module, cp_size: int, cp_backend, cfg:
         raise NotImplementedError(f"activation offload requires CP=1 or the ring backend, got {name!r}")
 
 
-class _PinnedPool:
+def _env_slab_bytes() -> int:
+    return int(os.environ.get("TPR_OFFLOAD_SLAB_BYTES", str(1 << 30)))
+
+
+_ALIGN = 512
+
+
+class _PinnedSlabs:
+    """Free pinned host slabs (uint8).  Tensors of every shape and dtype are packed into them, so the
+    host memory held is the peak of bytes offloaded at once (plus the unused slab tails), not one buffer
+    per distinct tensor size: chunks differ in token count, and a pool keyed by exact size would pin a
+    fresh set of buffers for every chunk shape."""
+
     def __init__(self) -> None:
-        self.free: dict[tuple, list[Tensor]] = {}
+        self.free: list[Tensor] = []
 
-    def get(self, numel: int, dtype) -> Tensor:
-        key = (numel, dtype)
-        lst = self.free.get(key)
-        if lst:
-            return lst.pop()
-        return torch.empty(numel, dtype=dtype, pin_memory=torch.cuda.is_available())
+    def take(self, nbytes: int) -> Tensor:
+        fits = [s for s in self.free if s.numel() >= nbytes]
+        if fits:
+            slab = min(fits, key=lambda s: s.numel())
+            self.free.remove(slab)
+            return slab
+        unit = _env_slab_bytes()
+        size = max(unit, -(-nbytes // unit) * unit)
+        return torch.empty(size, dtype=torch.uint8, pin_memory=torch.cuda.is_available())
 
-    def put(self, t: Tensor) -> None:
-        self.free.setdefault((t.numel(), t.dtype), []).append(t)
+    def give(self, slab: Tensor) -> None:
+        self.free.append(slab)
+
+    def held_bytes(self) -> int:
+        return sum(s.numel() for s in self.free)
 
 
-_POOL = _PinnedPool()
+_SLABS = _PinnedSlabs()
+
+
+class _HostArena:
+    """The slabs one offload scope holds, filled first-fit."""
+
+    def __init__(self) -> None:
+        self.slabs: list[list] = []          # [slab, bytes used]
+
+    def alloc(self, numel: int, dtype) -> Tensor:
+        nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        need = -(-nbytes // _ALIGN) * _ALIGN
+        for entry in self.slabs:
+            slab, used = entry
+            if slab.numel() - used >= need:
+                entry[1] = used + need
+                return slab[used:used + nbytes].view(dtype)
+        slab = _SLABS.take(need)
+        self.slabs.append([slab, need])
+        return slab[:nbytes].view(dtype)
+
+    def release(self) -> None:
+        for slab, _ in self.slabs:
+            _SLABS.give(slab)
+        self.slabs.clear()
 
 
 class _Saved:
@@ -99,6 +143,7 @@ class ActivationOffloader:
         self.offloaded_bytes = 0
         self._inflight: list = []          # (d2h done event, bytes), oldest first
         self._inflight_bytes = 0
+        self.arena = _HostArena()
 
     def protect(self, tensors) -> None:
         for t in tensors:
@@ -111,7 +156,7 @@ class ActivationOffloader:
         if (nbytes < self.cfg.min_bytes or isinstance(t, nn.Parameter) or t.untyped_storage().data_ptr()
                 in self.protected or not t.is_contiguous()):
             return t
-        host = _POOL.get(t.numel(), t.dtype)
+        host = self.arena.alloc(t.numel(), t.dtype)
         if t.is_cuda:
             ev = torch.cuda.Event()
             ev.record()
@@ -178,18 +223,16 @@ class ActivationOffloader:
             self._restore(s, self.h2d)
 
     def release(self) -> None:
-        """Return the pinned buffers to the pool once no copy can still touch them: the D2H copies
-        have finished, and so has every H2D prefetch (one that was issued but never unpacked may
-        still be reading its host buffer)."""
+        """Return the pinned slabs once no copy can still touch them: the D2H copies have finished,
+        and so has every H2D prefetch (one that was issued but never unpacked may still be reading
+        its host buffer)."""
         if self.cuda:
             torch.cuda.current_stream().wait_stream(self.d2h)
             torch.cuda.current_stream().wait_stream(self.h2d)
             self.d2h.synchronize()
             self.h2d.synchronize()
-        for lst in self.by_layer.values():
-            for s in lst:
-                _POOL.put(s.host)
         self.by_layer.clear()
+        self.arena.release()
 
 
 class _LayerTracker:

@@ -240,6 +240,22 @@ def bench_gdn(t: Timer, small: bool):
     do = torch.randn_like(o)
     ms = t(lambda: m.gdr_bwd(do, None, q, k, v, g, beta, ck, wk, u, chunks, seq0, most, True, K ** -0.5))
     _report("gated_delta_rule_bwd", {"T": T, "H": H, "K": K, "V": V}, ms, flops=3 * fl)
+    # where the cycles of each kernel go: one timed-off fwd + bwd with the in-kernel phase clocks on
+    m.gdr_phase_profile(True)
+    m.gdr_fwd(q, k, v, g, beta, s0, chunks, seq0, most, K ** -0.5)
+    m.gdr_bwd(do, None, q, k, v, g, beta, ck, wk, u, chunks, seq0, most, True, K ** -0.5)
+    torch.cuda.synchronize()
+    tab = m.gdr_phase_read()
+    m.gdr_phase_profile(False)
+    names = {0: ("prep", ["load", "build_T", "Wk/Wv"]),
+             1: ("scan", ["ckpt+load", "P,U", "O", "S1"]),
+             2: ("bwd_scan", ["ckpt+load", "P", "dU", "dq", "dk", "dwk", "dG", "dS0", "dG tail"]),
+             3: ("bwd_chunk", ["load", "build_T", "P", "dP", "dq/dk", "dT", "dv/dk", "X2", "dL", "dk", "tail"])}
+    for kid, (kname, phases) in names.items():
+        row = [int(x) for x in tab[kid].tolist()]
+        tot = sum(row) or 1
+        print(json.dumps({"op": f"gdr_phases_{kname}", "block_cycles": tot,
+                          "share": {p: round(row[i] / tot, 3) for i, p in enumerate(phases)}}))
 
 
 def bench_moe(t: Timer, small: bool):

@@ -103,6 +103,31 @@ def test_activation_offload_scope_preserves_gradients():
         assert torch.allclose(p.grad, ref[n], atol=1e-6), n
 
 
+def test_offload_host_arena_reuses_slabs(monkeypatch):
+    """Saved tensors of every size and dtype share pinned slabs; scopes of different chunk shapes reuse
+    the slabs a released scope handed back instead of allocating new host memory."""
+    from bridge_b200.tpr import activation_offload as ao
+
+    monkeypatch.setenv("TPR_OFFLOAD_SLAB_BYTES", str(1 << 16))
+    monkeypatch.setattr(ao, "_SLABS", ao._PinnedSlabs())
+    for rows in (37, 53, 29, 61, 41):               # a different chunk shape per scope
+        arena = ao._HostArena()
+        got = []
+        for dtype, cols in ((torch.float32, 64), (torch.bfloat16, 96), (torch.int64, 8), (torch.float32, 1)):
+            src = torch.randn(rows, cols).to(dtype) if dtype != torch.int64 else torch.arange(rows * cols)
+            h = arena.alloc(src.numel(), src.dtype)
+            assert h.dtype == src.dtype and h.numel() == src.numel() and h.data_ptr() % 64 == 0
+            h.copy_(src.reshape(-1))
+            got.append((h, src))
+        big = arena.alloc(3 << 15, torch.float32)     # larger than one slab: a slab of its own
+        big.fill_(1.0)
+        for h, src in got:                             # no two tensors overlap
+            assert torch.equal(h.view(src.shape), src)
+        arena.release()
+    # two slabs at most were ever live at once, plus the big one
+    assert len(ao._SLABS.free) <= 3, [s.numel() for s in ao._SLABS.free]
+
+
 @pytest.mark.parametrize("mode", ["retain", "recompute"])
 def test_forest_activation_offload_preserves_gradients(mode, monkeypatch):
     """EngineConfig.activation_offload reaches the forest executor: same loss and gradients, and the

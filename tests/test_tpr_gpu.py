@@ -110,14 +110,20 @@ def test_hybrid_tpr_vs_flat_bf16(preset, head_dim):
 
 
 @pytest.mark.parametrize("mode", ["retain", "recompute"])
-def test_forest_activation_offload_gpu(mode):
+def test_forest_activation_offload_gpu(mode, monkeypatch):
     """Activation offload through the engine on the GPU: same loss and gradients (within bf16 / atomic
-    reordering), saved tensors really moved to pinned host memory, and a lower device peak."""
+    reordering), saved tensors really moved to pinned host memory, and a lower device peak.
+
+    The forward of this model produces activations faster than PCIe drains them, so the device bytes
+    whose host copy is still pending are capped well below the chunk's activations: without the cap a
+    chunk that is forwarded and back-propagated at once (every leaf chunk, and every chunk in recompute
+    mode) would hold all of them until the backward."""
     from bridge_b200.engine import EngineConfig, TPREngine
     from bridge_b200.models.decoder import build_model
 
     from bridge_b200.models import get_config
 
+    monkeypatch.setenv("TPR_OFFLOAD_INFLIGHT_BYTES", str(256 << 20))
     dev = torch.device("cuda")
     # deep and wide enough that the saved activations, not the weights or the LM head, set the peak
     cfg = get_config("tiny", hidden_size=1024, num_heads=8, num_kv_heads=2, head_dim=128, intermediate_size=4096,
