@@ -83,9 +83,10 @@ def parse() -> argparse.Namespace:
 # per-config defaults: model, tree shape, per-rank token budget
 CONFIG_DEFAULTS = {
     2: dict(model="qwen3_4b", trees_per_gpu=8, prefix=512, resp=512, token_budget=16384, mode="retain"),
-    # sessions: whole turns of up to 24k tokens per segment, pushed segments recomputed at pop time (the
-    # reference's memory profile) so only one chunk's activations exist at a time (offloaded to host)
-    3: dict(model="qwen3_4b", trees_per_gpu=2, prefix=0, resp=0, token_budget=24576, mode="recompute"),
+    # sessions: shared turns of up to 24k tokens (cut into budget-sized prefix pieces), pushed segments
+    # recomputed at pop time (the reference's memory profile) so only one chunk's activations exist at a
+    # time, offloaded to pinned host memory
+    3: dict(model="qwen3_4b", trees_per_gpu=2, prefix=0, resp=0, token_budget=16384, mode="recompute"),
     4: dict(model="hybrid_gdn_2b", trees_per_gpu=8, prefix=512, resp=512, token_budget=16384, mode="retain"),
     5: dict(model="qwen3_next_24l", trees_per_gpu=4, prefix=1024, resp=1024, token_budget=16384, mode="retain"),
 }

@@ -75,22 +75,32 @@ __device__ __forceinline__ Chunk load_chunk_desc(const int* chunks, int i) {
   return {d.x, d.y, d.z, d.w};
 }
 
-// rows [row0, row0+n) of a [T, H, W] bf16 tensor (head h, columns [c0, c0+w)) -> smem [64][ld]; zero rows >= n
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  const int bytes = valid ? 16 : 0;   // 0: nothing is read, the 16 destination bytes are zero-filled
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// rows [row0, row0+n) of a [T, H, W] bf16 tensor (head h, columns [c0, c0+w)) -> smem [64][ld]; zero rows >= n.
+// Asynchronous (cp.async): every load of a phase is in flight at once; chunk_decay, which every kernel
+// runs before reading the rows, waits for them.
 template <int W>
 __device__ __forceinline__ void load_rows(bf* dst, int ld, const bf* __restrict__ src, int row0, int n, int H, int h,
                                           int width, int c0) {
   constexpr int VEC = W / 8;
+#pragma unroll 4
   for (int i = threadIdx.x; i < CS * VEC; i += NT) {
     const int t = i / VEC, v = i % VEC;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (t < n) val = *reinterpret_cast<const uint4*>(src + ((size_t)(row0 + t) * H + h) * width + c0 + v * 8);
-    *reinterpret_cast<uint4*>(dst + t * ld + v * 8) = val;
+    const bf* g = src + ((size_t)(row0 + (t < n ? t : 0)) * H + h) * width + c0 + v * 8;
+    cp_async16(dst + t * ld + v * 8, g, t < n);
   }
 }
 
 // G = cumsum(g) over the chunk (rows >= n hold the last value), Gam = e^G, E = e^{G_last - G}.
 __device__ __forceinline__ void chunk_decay(const float* __restrict__ g, int row0, int n, int H, int h, float* sG,
                                             float* sGam, float* sE) {
+  cp_async_wait_all();  // this thread's load_rows copies (made visible by the barriers below)
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float a = lane < n ? g[(size_t)(row0 + lane) * H + h] : 0.f;
@@ -145,21 +155,24 @@ __device__ void build_T(const bf* sK, int ldk, const float* sG, const float* sB,
   __syncthreads();
   float* scratch = sTf + CS * 65;  // callers reserve 4 x 16 x 17 floats after sTf
   for (int d = 1; d < 4; ++d) {
-    const int blk = warp;              // block (i, j) = (j + d, j), j = warp
-    if (blk + d < 4) {
-      const int i = blk + d, j = blk;
-      float* X = scratch + warp * 16 * 17;
-      // X = sum_{k=j}^{i-1} L_ik T_kj  (16 x 16), each lane 8 elements
-      for (int e = lane; e < 256; e += 32) {
+    // the 4 - d blocks (i, j) = (j + d, j) of this level, each shared by wpb warps (all 8 busy)
+    const int nblk = 4 - d, wpb = (NT / 32) / nblk;
+    const int j = warp / wpb, part = warp % wpb;
+    const bool active = j < nblk;
+    const int i = j + d;
+    float* X = scratch + (active ? j : 0) * 16 * 17;
+    if (active) {
+      // X = diag(beta_i) sum_{k=j}^{i-1} A_ik T_kj  (16 x 16)
+      for (int e = part * 32 + lane; e < 256; e += wpb * 32) {
         const int r = e / 16, c = e % 16;
         float acc = 0.f;
-        for (int kb = j; kb < i; ++kb)
-          for (int m = 0; m < 16; ++m)
-            acc += sB[i * 16 + r] * sA[(i * 16 + r) * 65 + kb * 16 + m] * sTf[(kb * 16 + m) * 65 + j * 16 + c];
-        X[r * 17 + c] = acc;
+        for (int m = j * 16; m < i * 16; ++m) acc += sA[(i * 16 + r) * 65 + m] * sTf[m * 65 + j * 16 + c];
+        X[r * 17 + c] = sB[i * 16 + r] * acc;
       }
-      __syncwarp();
-      for (int e = lane; e < 256; e += 32) {
+    }
+    __syncthreads();
+    if (active) {
+      for (int e = part * 32 + lane; e < 256; e += wpb * 32) {
         const int r = e / 16, c = e % 16;
         float acc = 0.f;
         for (int m = 0; m <= r; ++m) acc += sTf[(i * 16 + r) * 65 + i * 16 + m] * X[m * 17 + c];
@@ -502,6 +515,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
         wm::warp_tile<false, false>(c1, sK, SM::LK, sdS, SM::LV, m0, n0, KD);
         wm::warp_tile<false, false>(c1, sK, SM::LK, sdSl, SM::LV, m0, n0, KD);
         wm::warp_tile<true, false>(c2, sP, 72, sdO, SM::LV, m0, n0, CS);
+        float racc[2] = {0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -511,9 +525,17 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
             snDU[r * SM::LV + c] = f2b(-d);
             if (r < ch.n) {
               du[((size_t)(ch.row0 + r) * H + h) * VD + v0 + c] = d;
-              atomicAdd(&sde[r], c1[j][e] * b2f(sU[r * SM::LV + c]));
+              racc[e >> 1] += c1[j][e] * b2f(sU[r * SM::LV + c]);
             }
           }
+        // per-row sums inside the tile first (four lanes share a row), one shared atomic per row
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float v = racc[hh];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          if ((lane & 3) == 0 && v != 0.f) atomicAdd(&sde[m0 + (lane >> 2) + 8 * hh], v);
+        }
       }
     }
     __syncthreads();
@@ -531,8 +553,9 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
       if (t < ch.n) atomicAdd(&dwk[((size_t)(ch.row0 + t) * H + h) * KD + c], val);
     });
     pc.mark(2, 5);
-    wm::block_gemm2<false, false>(CS, VB, KD, sQ, SM::LK, sS, sSl, SM::LV, [&](int t, int c, float val) {
-      if (t < ch.n) atomicAdd(&sdG[t], scale * sGam[t] * val * b2f(sdO[t * SM::LV + c]));
+    wm::block_gemm_red<false, false>(CS, VB, KD, sQ, SM::LK, sS, sSl, SM::LV, sdG, nullptr, nullptr,
+                                     [&](int t, int c, float val, float (&rc)[2], float (&)[1]) {
+      if (t < ch.n) rc[0] += scale * sGam[t] * val * b2f(sdO[t * SM::LV + c]);
     });
     pc.mark(2, 6);
     // dS0 = Gam_last dS1 + Q^T (scale Gam o dO) - Wk^T dU
@@ -599,6 +622,10 @@ struct BChunkSmem {
   static constexpr size_t TF = A + sizeof(float) * CS * 65;  // T (solve) + scratch, then P
   static constexpr size_t VEC = TF + sizeof(float) * (CS * 65 + 4 * 16 * 17);  // G Gam E B dG db
   static constexpr size_t TOTAL = VEC + sizeof(float) * 6 * CS;
+  // from the dq / dk phase on, U and dO are dead: their bytes hold the FP32 dk accumulator [64][KD + 4]
+  static constexpr int LDK = KD + 4;
+  static_assert(DO == U + sizeof(bf) * CS * LV && sizeof(float) * CS * LDK <= 2 * sizeof(bf) * CS * LV,
+                "dk accumulator must fit in the U + dO buffers");
 };
 
 template <int KD, int VD>
@@ -665,14 +692,15 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
   });
   __syncthreads();
   pc.mark(3, 2);
-  wm::block_gemm<false, true>(CS, CS, VD, sdO, SM::LV, sU, SM::LV, [&](int t, int s, float val) {
+  wm::block_gemm_red<false, true>(CS, CS, VD, sdO, SM::LV, sU, nullptr, SM::LV, sdG, nullptr, sdG,
+                                  [&](int t, int s, float val, float (&rc)[2], float (&cc)[1]) {
     const bool ok = s <= t && t < n;
     const float dp = ok ? scale * val : 0.f;
     sX1[t * 72 + s] = f2b(ok ? dp * __expf(sG[t] - sG[s]) : 0.f);
     if (ok && s != t) {
       const float pp = dp * sTf[t * 65 + s];
-      atomicAdd(&sdG[t], pp);
-      atomicAdd(&sdG[s], -pp);
+      rc[0] += pp;
+      cc[0] -= pp;
     }
   });
   __syncthreads();
@@ -681,10 +709,15 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
   wm::block_gemm<false, false>(CS, KD, CS, sX1, 72, sK, SM::LK, [&](int t, int c, float val) {
     if (t < n) dq[rk(t) + c] += val;
   });
+  // the in-chunk dk terms are summed in shared memory (dead U / dO bytes) and added to dk once at the end
+  float* sDK = reinterpret_cast<float*>(smem + SM::U);
   wm::block_gemm<true, false>(CS, KD, CS, sX1, 72, sQ, SM::LK, [&](int t, int c, float val) {
-    if (t < n) dk[rk(t) + c] += val;
+    sDK[t * SM::LDK + c] = val;
   });
   __syncthreads();
+  // raw V rows (for dbeta) into the now dead Q buffer when they fit, in flight during dT
+  constexpr bool kVInQ = VD <= SM::LK;
+  if (kVInQ) load_rows<VD>(sQ, SM::LK, v, row0, n, H, h, VD, 0);
   pc.mark(3, 4);
   // dT = dU (beta V)^T + dWk (beta Gam K)^T   (into sX1)
   {
@@ -704,21 +737,24 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
         }
     }
   }
+  cp_async_wait_all();
   __syncthreads();
   pc.mark(3, 5);
   // dVb = T^T dU -> dv = beta dVb, dbeta += <dVb, V>;  dKb = T^T dWk -> dk += beta Gam dKb, dbeta, dG
-  wm::block_gemm<true, false>(CS, VD, CS, sTb, 72, sdU, SM::LV, [&](int s, int c, float val) {
+  wm::block_gemm_red<true, false>(CS, VD, CS, sTb, 72, sdU, nullptr, SM::LV, sdb, nullptr, nullptr,
+                                  [&](int s, int c, float val, float (&rc)[2], float (&)[1]) {
     if (s < n) {
       dv[rv(s) + c] = f2b(sB[s] * val);
-      atomicAdd(&sdb[s], val * b2f(v[rv(s) + c]));
+      rc[0] += val * (kVInQ ? b2f(sQ[s * SM::LK + c]) : b2f(v[rv(s) + c]));
     }
   });
-  wm::block_gemm<true, false>(CS, KD, CS, sTb, 72, sdWk, SM::LK, [&](int s, int c, float val) {
+  wm::block_gemm_red<true, false>(CS, KD, CS, sTb, 72, sdWk, nullptr, SM::LK, sdb, sdG, nullptr,
+                                  [&](int s, int c, float val, float (&rc)[2], float (&)[1]) {
     if (s < n) {
       const float kv = b2f(sK[s * SM::LK + c]);
-      dk[rk(s) + c] += sB[s] * sGam[s] * val;
-      atomicAdd(&sdb[s], sGam[s] * kv * val);
-      atomicAdd(&sdG[s], sB[s] * sGam[s] * kv * val);
+      sDK[s * SM::LDK + c] += sB[s] * sGam[s] * val;
+      rc[0] += sGam[s] * kv * val;
+      rc[1] += sB[s] * sGam[s] * kv * val;
     }
   });
   pc.mark(3, 6);
@@ -731,14 +767,15 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
   for (int i = threadIdx.x; i < CS * 72; i += NT) sX1[i] = f2b(0.f);
   __syncthreads();
   // dL = -T^T X2;  dA_ts = beta_t dL_ts (s < t) -> dbeta, dG, and M = dKK + dKK^T with dKK = dA o D
-  wm::block_gemm<true, false>(CS, CS, CS, sTb, 72, sX2, 72, [&](int t, int s, float val) {
+  wm::block_gemm_red<true, false>(CS, CS, CS, sTb, 72, sX2, nullptr, 72, sdb, sdG, sdG,
+                                  [&](int t, int s, float val, float (&rc)[2], float (&cc)[1]) {
     if (s < t && t < n) {
       const float dl = -val;
       const float a = sA[t * 65 + s];
       const float da = sB[t] * dl;
-      atomicAdd(&sdb[t], dl * a);
-      atomicAdd(&sdG[t], da * a);
-      atomicAdd(&sdG[s], -da * a);
+      rc[0] += dl * a;
+      rc[1] += da * a;
+      cc[0] -= da * a;
       const bf m = f2b(da * __expf(sG[t] - sG[s]));
       sX1[t * 72 + s] = m;
       sX1[s * 72 + t] = m;
@@ -747,9 +784,23 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
   __syncthreads();
   pc.mark(3, 8);
   wm::block_gemm<false, false>(CS, KD, CS, sX1, 72, sK, SM::LK, [&](int t, int c, float val) {
-    if (t < n) dk[rk(t) + c] += val;
+    sDK[t * SM::LDK + c] += val;
   });
   __syncthreads();
+  // one coalesced read-modify-write of dk (the scan kernel already added the state terms)
+  for (int i = threadIdx.x; i < CS * (KD / 4); i += NT) {
+    const int t = i / (KD / 4), c4 = (i % (KD / 4)) * 4;
+    if (t < n) {
+      float4* dst = reinterpret_cast<float4*>(dk + rk(t) + c4);
+      float4 a = *dst;
+      const float* src = sDK + t * SM::LDK + c4;
+      a.x += src[0];
+      a.y += src[1];
+      a.z += src[2];
+      a.w += src[3];
+      *dst = a;
+    }
+  }
   pc.mark(3, 9);
   if (threadIdx.x == 0) {
     float acc = 0.f;

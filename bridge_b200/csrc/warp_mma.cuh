@@ -98,3 +98,61 @@ __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bflo
 }
 
 }  // namespace wm
+
+namespace wm {
+
+// As block_gemm (or block_gemm2 when Blo != nullptr), for epilogues that also sum per-row and per-column
+// contributions into shared-memory vectors: `epi(row, col, value, rc, cc)` adds to rc[0..1] (summed
+// into rdst0[row], rdst1[row]) and cc[0] (summed into cdst[col]).  The sums are reduced inside each
+// warp's 16 x 16 tile with shuffles first, so a tile issues 16 shared atomics per vector instead of one
+// per element (the per-element form serialises on the four lanes that share a row).  Null destinations
+// are skipped.
+template <bool A_T, bool B_KMAJ, typename Epi>
+__device__ __forceinline__ void block_gemm_red(int M, int N, int K, const __nv_bfloat16* A, int lda,
+                                               const __nv_bfloat16* B, const __nv_bfloat16* Blo, int ldb,
+                                               float* rdst0, float* rdst1, float* cdst, Epi epi) {
+  const int warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int tn = N / 16, tiles = (M / 16) * tn;
+  for (int t = warp; t < tiles; t += nwarp) {
+    const int m0 = (t / tn) * 16, n0 = (t % tn) * 16;
+    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    warp_tile<A_T, B_KMAJ>(c, A, lda, B, ldb, m0, n0, K);
+    if (Blo != nullptr) warp_tile<A_T, B_KMAJ>(c, A, lda, Blo, ldb, m0, n0, K);
+    float racc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};   // [row half][vector]
+    float cacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};   // [j][e & 1]
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float rc[2] = {0.f, 0.f}, cc[1] = {0.f};
+        epi(m0 + (lane >> 2) + 8 * (e >> 1), n0 + 8 * j + 2 * (lane & 3) + (e & 1), c[j][e], rc, cc);
+        racc[e >> 1][0] += rc[0];
+        racc[e >> 1][1] += rc[1];
+        cacc[j][e & 1] += cc[0];
+      }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float v = racc[hh][k];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        float* dst = k == 0 ? rdst0 : rdst1;
+        if (dst != nullptr && (lane & 3) == 0 && v != 0.f) atomicAdd(&dst[m0 + (lane >> 2) + 8 * hh], v);
+      }
+    if (cdst != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          float v = cacc[j][b];
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          v += __shfl_xor_sync(0xffffffffu, v, 16);
+          if (lane < 4 && v != 0.f) atomicAdd(&cdst[n0 + 8 * j + 2 * lane + b], v);
+        }
+    }
+  }
+}
+
+}  // namespace wm

@@ -198,13 +198,11 @@ def max_segment_tokens(forest) -> int:
 
 
 def forest_fits(engine, forest, rt) -> bool:
-    """Whether the batched forest executor runs this forest: always on one CP rank; under CP when every
-    segment fits whole into one rank's token budget (segment-granular placement).  Otherwise the
-    per-tree executor splits each segment over the CP group with the configured backend."""
-    ec = engine.engine_config
-    if ec.executor != "forest":
-        return False
-    return rt.group is None or max_segment_tokens(forest) <= ec.token_budget
+    """Whether the batched forest executor runs this forest (``executor="forest"``, the default).  It
+    runs any forest, on one rank or under CP: a segment longer than one rank's token budget becomes a
+    chain of budget-sized pieces (each the prefix of the next).  ``executor="segment"`` selects the
+    per-tree executor, which splits every segment over the CP group with the configured backend."""
+    return engine.engine_config.executor == "forest"
 
 
 def execute_prepared_tpr_batch(engine, prepared: PreparedTPRBatch, *, sync_loss: bool = True) -> dict:

@@ -214,6 +214,9 @@ class ActivationOffloader:
                 s.h2d_done.synchronize()
             s.restored.record_stream(torch.cuda.current_stream())
         out = s.restored
+        # the consumer owns the restored tensor now: keeping a reference here (``by_layer`` lives until
+        # release) would hold every restored activation on the device until the scope ends
+        s.restored, s.h2d_done = None, None
         return out
 
     def prefetch_layer(self, layer: int) -> None:

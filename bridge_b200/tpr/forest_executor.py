@@ -179,7 +179,57 @@ class ForestExecutor:
                 n = by_id[sid]
                 n.ref_rows, n.ref_targets, n.ref_samples, n.ref_flat = (tab.query_offsets, tab.targets,
                                                                         tab.sample_rows, tab.flat_index)
-        return nodes
+        return self._split_long(nodes)
+
+    def _split_long(self, nodes: list[_Node]) -> list[_Node]:
+        """Cut every segment longer than one rank's token budget into a chain of pieces of at most the
+        budget: each piece is the parent of the next and reaches the earlier pieces as prefix K/V (and
+        GDN state), exactly like a shared prefix.  No chunk then holds more than the budget, whatever the
+        turn lengths, and under CP every segment can be placed whole on one rank.  Loss rows stay with
+        the piece holding their query token."""
+        cap = self.token_budget
+        if all(n.length <= cap for n in nodes):
+            return nodes
+        out: list[_Node] = []
+        for n in nodes:
+            out.append(n)
+            if n.length <= cap:
+                continue
+            total = n.length
+            pieces = -(-total // cap)
+            step = -(-total // pieces)
+            tokens, children = n.tokens, n.children
+            rows, tg, sm, fl = n.ref_rows, n.ref_targets, n.ref_samples, n.ref_flat
+            prev = None
+            for i in range(pieces):
+                a, b = i * step, min(total, (i + 1) * step)
+                piece = n if i == 0 else _Node(n.tree, n.seg_id, tokens[a:b], n.start + a, 0, prev)
+                piece.tokens = tokens[a:b]
+                piece.children = [] if i < pieces - 1 else children
+                if prev is not None:
+                    prev.children = [piece]
+                    out.append(piece)
+                if rows is not None:
+                    keep = (rows >= a) & (rows < b)
+                    piece.ref_rows = rows[keep] - a
+                    piece.ref_targets, piece.ref_samples, piece.ref_flat = tg[keep], sm[keep], fl[keep]
+                    if piece.ref_rows.numel() == 0:
+                        piece.ref_rows = piece.ref_targets = piece.ref_samples = piece.ref_flat = None
+                prev = piece
+            for c in children:
+                c.parent = prev
+        # depths follow the (longer) chains
+        for n in out:
+            n.depth = 0
+        for n in out:
+            if n.parent is None:
+                stack = [n]
+                while stack:
+                    x = stack.pop()
+                    for c in x.children:
+                        c.depth = x.depth + 1
+                        stack.append(c)
+        return out
 
     # ------------------------------------------------------------------ one packed forward
     def _prefix_bank(self, nodes: list[_Node]):

@@ -291,6 +291,17 @@ def test_forest_cp2_hybrid_gdn_matches_flattened():
         assert worst[1] < 1e-4, worst
 
 
+@pytest.mark.parametrize("preset,layers", [("tiny", 2), ("tiny_hybrid", 4)])
+def test_forest_cp2_splits_long_segments_matches_flattened(preset, layers):
+    """A per-rank budget (48) below the prompt length (128): long segments become prefix chains whose
+    pieces are placed whole on CP ranks (K/V and GDN states of earlier pieces gathered like any prefix)."""
+    res = run_ranks(2, _forest_worker, preset, layers, 48, "recompute")
+    for r in res:
+        assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
+        worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 1e-4, worst
+
+
 def test_forest_cp3_idle_rank_matches_flattened():
     """More ranks than segments at some level: an idle rank forwards a pad segment and still joins every
     collective."""

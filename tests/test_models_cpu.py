@@ -98,9 +98,36 @@ def test_activation_offload_scope_preserves_gradients():
     model.zero_grad()
     with offload_scope(model, OffloadConfig(enabled=True, min_bytes=1)) as off:
         model(ids, pos).pow(2).mean().backward()
+        # restored tensors belong to the backward that consumed them, not to the offloader (only a
+        # prefetched tensor that no backward node read is still held, until the scope releases)
+        left = sum(s.restored.numel() * s.restored.element_size() for lst in off.by_layer.values() for s in lst
+                   if s.restored is not None)
+        assert left <= 0.02 * off.offloaded_bytes, (left, off.offloaded_bytes)
     assert off.offloaded_bytes > 0
     for n, p in model.named_parameters():
         assert torch.allclose(p.grad, ref[n], atol=1e-6), n
+
+
+@pytest.mark.parametrize("mode", ["retain", "recompute"])
+@pytest.mark.parametrize("preset", ["tiny", "tiny_hybrid"])
+def test_forest_splits_segments_longer_than_the_budget(mode, preset):
+    """A token budget shorter than the prompt (128 tokens) cuts long segments into prefix chains: same
+    loss and gradients as a budget that holds every segment whole."""
+    from bridge_b200.engine import EngineConfig, TPREngine
+    from tests.helpers import nested_tree_batch
+
+    cfg = get_config(preset)
+    batch = nested_tree_batch(prefix=128, mid=40, resp=24)
+    out, grads = {}, {}
+    for budget in (4096, 48):
+        eng = TPREngine(cfg, EngineConfig(forest_mode=mode, token_budget=budget), device="cpu",
+                        model=build_model(cfg, dtype=torch.float32, seed=0))
+        res = eng.forward_backward_batch(batch)
+        out[budget] = float(res["loss"][0])
+        grads[budget] = {n: p.main_grad.clone() for n, p in eng.model.named_parameters()}
+    assert abs(out[48] - out[4096]) <= 1e-5 * abs(out[4096]) + 1e-7, out
+    for n, g in grads[4096].items():
+        assert torch.allclose(grads[48][n], g, rtol=1e-4, atol=1e-6), n
 
 
 def test_offload_host_arena_reuses_slabs(monkeypatch):
