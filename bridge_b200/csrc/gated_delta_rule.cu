@@ -38,6 +38,26 @@ using bf = __nv_bfloat16;
 __device__ __forceinline__ float b2f(bf x) { return __bfloat162float(x); }
 __device__ __forceinline__ bf f2b(float x) { return __float2bfloat16(x); }
 
+// four consecutive bf16 (8-byte aligned) <-> float4
+__device__ __forceinline__ float4 ld_bf4(const bf* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void st_bf4(bf* p, float4 v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+__device__ __forceinline__ float4 scale4(float4 v, float s) { return make_float4(s * v.x, s * v.y, s * v.z, s * v.w); }
+// the bf16 rounding of each element, back in FP32
+__device__ __forceinline__ float4 ld_bf4_round(float4 v) {
+  return make_float4(b2f(f2b(v.x)), b2f(f2b(v.y)), b2f(f2b(v.z)), b2f(f2b(v.w)));
+}
+
 // Optional phase timing, off unless enabled from the host (gdr_phase_profile): after a block barrier,
 // thread 0 adds the SM cycles the block spent in each phase to a device table [kernel][phase].
 // Kernels: 0 prep, 1 scan, 2 bwd scan, 3 bwd chunk.
@@ -138,19 +158,20 @@ __device__ void build_T(const bf* sK, int ldk, const float* sG, const float* sB,
   for (int i = threadIdx.x; i < CS * 65; i += NT) sTf[i] = 0.f;
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp < 4) {  // diagonal block w: rows / cols [16w, 16w + 16)
-    const int o = warp * 16;
-    const int c = lane & 15;
-    if (lane < 16) sTf[(o + c) * 65 + o + c] = 1.f;
-    __syncwarp();
-    for (int r = 1; r < 16; ++r) {
-      if (lane < r) {
-        float acc = 0.f;
-        for (int s2 = c; s2 < r; ++s2) acc += sA[(o + r) * 65 + o + s2] * sTf[(o + s2) * 65 + o + c];
-        sTf[(o + r) * 65 + o + c] = -sB[o + r] * acc;
-      }
-      __syncwarp();
+  if (threadIdx.x < 64) {
+    // diagonal blocks: each of the 4 x 16 columns of the four unit-lower 16 x 16 inverses is an
+    // independent forward substitution, one thread per column with the column in registers
+    const int o = (threadIdx.x >> 4) * 16, c = threadIdx.x & 15;
+    float col[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float acc = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < r; ++s2) acc += sA[(o + r) * 65 + o + s2] * col[s2];   // col[s2] = 0 for s2 < c
+      col[r] = r < c ? 0.f : (r == c ? 1.f : -sB[o + r] * acc);
     }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) sTf[(o + r) * 65 + o + c] = col[r];
   }
   __syncthreads();
   float* scratch = sTf + CS * 65;  // callers reserve 4 x 16 x 17 floats after sTf
@@ -165,18 +186,31 @@ __device__ void build_T(const bf* sK, int ldk, const float* sG, const float* sB,
       // X = diag(beta_i) sum_{k=j}^{i-1} A_ik T_kj  (16 x 16)
       for (int e = part * 32 + lane; e < 256; e += wpb * 32) {
         const int r = e / 16, c = e % 16;
-        float acc = 0.f;
-        for (int m = j * 16; m < i * 16; ++m) acc += sA[(i * 16 + r) * 65 + m] * sTf[m * 65 + j * 16 + c];
-        X[r * 17 + c] = sB[i * 16 + r] * acc;
+        float acc0 = 0.f, acc1 = 0.f;
+        for (int kb = j; kb < i; ++kb) {
+          const float* a = sA + (i * 16 + r) * 65 + kb * 16;
+          const float* t = sTf + (kb * 16) * 65 + j * 16 + c;
+#pragma unroll
+          for (int m = 0; m < 16; m += 2) {
+            acc0 += a[m] * t[m * 65];
+            acc1 += a[m + 1] * t[(m + 1) * 65];
+          }
+        }
+        X[r * 17 + c] = sB[i * 16 + r] * (acc0 + acc1);
       }
     }
     __syncthreads();
     if (active) {
       for (int e = part * 32 + lane; e < 256; e += wpb * 32) {
         const int r = e / 16, c = e % 16;
-        float acc = 0.f;
-        for (int m = 0; m <= r; ++m) acc += sTf[(i * 16 + r) * 65 + i * 16 + m] * X[m * 17 + c];
-        sTf[(i * 16 + r) * 65 + j * 16 + c] = -acc;
+        const float* tr = sTf + (i * 16 + r) * 65 + i * 16;   // T_ii row r (zero above the diagonal)
+        float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; m += 2) {
+          acc0 += tr[m] * X[m * 17 + c];
+          acc1 += tr[m + 1] * X[(m + 1) * 17 + c];
+        }
+        sTf[(i * 16 + r) * 65 + j * 16 + c] = -(acc0 + acc1);
       }
     }
     __syncthreads();
@@ -226,13 +260,16 @@ __global__ void __launch_bounds__(NT) gdr_prep_kernel(const bf* __restrict__ k, 
   for (int t = threadIdx.x; t < CS; t += NT) sB[t] = t < ch.n ? beta[(size_t)(ch.row0 + t) * H + h] : 0.f;
   chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);
   // scaled operands: Kb = beta Gam K, Vb = beta V
-  for (int i = threadIdx.x; i < CS * KD; i += NT) {
-    const int t = i / KD, c = i % KD;
-    sKb[t * SM::LK + c] = f2b(sB[t] * sGam[t] * b2f(sK[t * SM::LK + c]));
+#pragma unroll 4
+  for (int i = threadIdx.x; i < CS * KD / 4; i += NT) {
+    const int t = i / (KD / 4), c = (i % (KD / 4)) * 4;
+    st_bf4(sKb + t * SM::LK + c, scale4(ld_bf4(sK + t * SM::LK + c), sB[t] * sGam[t]));
   }
-  for (int i = threadIdx.x; i < CS * VD; i += NT) {
-    const int t = i / VD, c = i % VD;
-    sVb[t * SM::LV + c] = t < ch.n ? f2b(sB[t] * b2f(v[((size_t)(ch.row0 + t) * H + h) * VD + c])) : f2b(0.f);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < CS * VD / 4; i += NT) {
+    const int t = i / (VD / 4), c = (i % (VD / 4)) * 4;
+    st_bf4(sVb + t * SM::LV + c, t < ch.n ? scale4(ld_bf4(v + ((size_t)(ch.row0 + t) * H + h) * VD + c), sB[t])
+                                          : make_float4(0.f, 0.f, 0.f, 0.f));
   }
   __syncthreads();
   pc.mark(0, 0);
@@ -321,11 +358,12 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < 4; e += 2) {
           const int r = (t / ST::TN) * 16 + (lane >> 2) + 8 * (e >> 1);
-          const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
-          ck[(size_t)r * VD + v0 + c] = st[i][j][e];
+          const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3);
+          *reinterpret_cast<float2*>(ck + (size_t)r * VD + v0 + c) = make_float2(st[i][j][e], st[i][j][e + 1]);
           wm::split_bf16(st[i][j][e], sS[r * SM::LV + c], sSl[r * SM::LV + c]);
+          wm::split_bf16(st[i][j][e + 1], sS[r * SM::LV + c + 1], sSl[r * SM::LV + c + 1]);
         }
     }
     load_rows<KD>(sQ, SM::LK, q, ch.row0, ch.n, H, h, KD, 0);
@@ -467,9 +505,13 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
   for (int ci = c_end - 1; ci >= c_begin; --ci) {
     const Chunk ch = load_chunk_desc(chunks, ci);
     const float* ck = ckpt + (((size_t)b * H + h) * nc_max + ch.c) * KD * VD;
-    for (int i = threadIdx.x; i < KD * VB; i += NT) {
-      const int r = i / VB, c = i % VB;
-      wm::split_bf16(ck[(size_t)r * VD + v0 + c], sS[r * SM::LV + c], sSl[r * SM::LV + c]);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < KD * VB / 4; i += NT) {
+      const int r = i / (VB / 4), c = (i % (VB / 4)) * 4;
+      const float4 x = *reinterpret_cast<const float4*>(ck + (size_t)r * VD + v0 + c);
+      const float4 hi = ld_bf4_round(x);
+      st_bf4(sS + r * SM::LV + c, hi);
+      st_bf4(sSl + r * SM::LV + c, make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w));
     }
     float dot = 0.f;  // <dS1, S0> partial
 #pragma unroll
@@ -479,11 +521,13 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < 4; e += 2) {
           const int r = (t / ST::TN) * 16 + (lane >> 2) + 8 * (e >> 1);
-          const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+          const int c = (t % ST::TN) * 16 + 8 * j + 2 * (lane & 3);
           wm::split_bf16(ds[i][j][e], sdS[r * SM::LV + c], sdSl[r * SM::LV + c]);
-          dot += ds[i][j][e] * ck[(size_t)r * VD + v0 + c];
+          wm::split_bf16(ds[i][j][e + 1], sdS[r * SM::LV + c + 1], sdSl[r * SM::LV + c + 1]);
+          const float2 s0 = *reinterpret_cast<const float2*>(ck + (size_t)r * VD + v0 + c);
+          dot += ds[i][j][e] * s0.x + ds[i][j][e + 1] * s0.y;
         }
     }
     dot = bb::warp_sum(dot);
@@ -541,16 +585,22 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
     __syncthreads();
     pc.mark(2, 2);
     // state-dependent gradient pieces (summed over the V blocks with atomics)
-    wm::block_gemm2<false, true>(CS, KD, VB, sdO, SM::LV, sS, sSl, SM::LV, [&](int t, int c, float val) {
-      if (t < ch.n) atomicAdd(&dq[((size_t)(ch.row0 + t) * H + h) * KD + c], scale * sGam[t] * val);
+    // (float2 atomics: the two V blocks of a head add into the same rows)
+    wm::block_gemm_pairs<false, true>(CS, KD, VB, sdO, SM::LV, sS, sSl, SM::LV, [&](int t, int c, float a, float b) {
+      if (t < ch.n) {
+        const float f = scale * sGam[t];
+        atomicAdd(reinterpret_cast<float2*>(&dq[((size_t)(ch.row0 + t) * H + h) * KD + c]), make_float2(f * a, f * b));
+      }
     });
     pc.mark(2, 3);
-    wm::block_gemm2<false, true>(CS, KD, VB, sU, SM::LV, sdS, sdSl, SM::LV, [&](int t, int c, float val) {
-      if (t < ch.n) atomicAdd(&dk[((size_t)(ch.row0 + t) * H + h) * KD + c], sE[t] * val);
+    wm::block_gemm_pairs<false, true>(CS, KD, VB, sU, SM::LV, sdS, sdSl, SM::LV, [&](int t, int c, float a, float b) {
+      if (t < ch.n)
+        atomicAdd(reinterpret_cast<float2*>(&dk[((size_t)(ch.row0 + t) * H + h) * KD + c]),
+                  make_float2(sE[t] * a, sE[t] * b));
     });
     pc.mark(2, 4);
-    wm::block_gemm2<false, true>(CS, KD, VB, snDU, SM::LV, sS, sSl, SM::LV, [&](int t, int c, float val) {
-      if (t < ch.n) atomicAdd(&dwk[((size_t)(ch.row0 + t) * H + h) * KD + c], val);
+    wm::block_gemm_pairs<false, true>(CS, KD, VB, snDU, SM::LV, sS, sSl, SM::LV, [&](int t, int c, float a, float b) {
+      if (t < ch.n) atomicAdd(reinterpret_cast<float2*>(&dwk[((size_t)(ch.row0 + t) * H + h) * KD + c]), make_float2(a, b));
     });
     pc.mark(2, 5);
     wm::block_gemm_red<false, false>(CS, VB, KD, sQ, SM::LK, sS, sSl, SM::LV, sdG, nullptr, nullptr,
@@ -672,15 +722,18 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
     sdb[t] = 0.f;
   }
   chunk_decay(g, row0, n, H, h, sG, sGam, sE);
-  for (int i = threadIdx.x; i < CS * KD; i += NT) {
-    const int t = i / KD, c = i % KD;
-    sKb[t * SM::LK + c] = f2b(sB[t] * sGam[t] * b2f(sK[t * SM::LK + c]));
-    sdWk[t * SM::LK + c] = f2b(t < n ? dwk[rk(t) + c] : 0.f);
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < CS * KD / 4; i += NT) {
+    const int t = i / (KD / 4), c = (i % (KD / 4)) * 4;
+    st_bf4(sKb + t * SM::LK + c, scale4(ld_bf4(sK + t * SM::LK + c), sB[t] * sGam[t]));
+    st_bf4(sdWk + t * SM::LK + c, t < n ? *reinterpret_cast<const float4*>(dwk + rk(t) + c) : z4);
   }
-  for (int i = threadIdx.x; i < CS * VD; i += NT) {
-    const int t = i / VD, c = i % VD;
-    sVb[t * SM::LV + c] = f2b(t < n ? sB[t] * b2f(v[rv(t) + c]) : 0.f);
-    sdU[t * SM::LV + c] = f2b(t < n ? du[rv(t) + c] : 0.f);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < CS * VD / 4; i += NT) {
+    const int t = i / (VD / 4), c = (i % (VD / 4)) * 4;
+    st_bf4(sVb + t * SM::LV + c, t < n ? scale4(ld_bf4(v + rv(t) + c), sB[t]) : z4);
+    st_bf4(sdU + t * SM::LV + c, t < n ? *reinterpret_cast<const float4*>(du + rv(t) + c) : z4);
   }
   __syncthreads();
   pc.mark(3, 0);

@@ -156,3 +156,27 @@ __device__ __forceinline__ void block_gemm_red(int M, int N, int K, const __nv_b
 }
 
 }  // namespace wm
+
+namespace wm {
+
+// As block_gemm / block_gemm2 (Blo != nullptr), with the epilogue called once per pair of adjacent
+// columns: `epi(row, col, value(col), value(col + 1))`, col even (vector stores / float2 atomics).
+template <bool A_T, bool B_KMAJ, typename Epi>
+__device__ __forceinline__ void block_gemm_pairs(int M, int N, int K, const __nv_bfloat16* A, int lda,
+                                                 const __nv_bfloat16* B, const __nv_bfloat16* Blo, int ldb, Epi epi) {
+  const int warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int tn = N / 16, tiles = (M / 16) * tn;
+  for (int t = warp; t < tiles; t += nwarp) {
+    const int m0 = (t / tn) * 16, n0 = (t % tn) * 16;
+    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    warp_tile<A_T, B_KMAJ>(c, A, lda, B, ldb, m0, n0, K);
+    if (Blo != nullptr) warp_tile<A_T, B_KMAJ>(c, A, lda, Blo, ldb, m0, n0, K);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2)
+        epi(m0 + (lane >> 2) + 8 * (e >> 1), n0 + 8 * j + 2 * (lane & 3), c[j][e], c[j][e + 1]);
+  }
+}
+
+}  // namespace wm
