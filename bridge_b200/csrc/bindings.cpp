@@ -81,6 +81,8 @@ std::vector<torch::Tensor> gdr_fwd(torch::Tensor q, torch::Tensor k, torch::Tens
                                    torch::Tensor beta, c10::optional<torch::Tensor> h0, torch::Tensor chunks,
                                    torch::Tensor seq0, int64_t max_chunks, double scale);
 void gdr_phase_profile(bool enable);
+void attn_phase_profile(bool enable);
+torch::Tensor attn_phase_read();
 torch::Tensor gdr_phase_read();
 std::vector<torch::Tensor> gdr_bwd(torch::Tensor dout, c10::optional<torch::Tensor> dhT, torch::Tensor q,
                                    torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
@@ -151,6 +153,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("causal_conv1d_bwd", &causal_conv1d_bwd);
   m.def("gdr_fwd", &gdr_fwd, "chunked gated delta rule forward (returns o, final state, chunk checkpoints)");
   m.def("gdr_bwd", &gdr_bwd, "chunked gated delta rule backward");
+  m.def("attn_phase_profile", &attn_phase_profile, "enable / disable (and clear) tcgen05 attention forward phase timing");
+  m.def("attn_phase_read", &attn_phase_read, "attention forward cycles {startup, loop, epilogue, tiles, ctas}");
   m.def("gdr_phase_profile", &gdr_phase_profile, "enable / disable (and clear) gated-delta-rule phase timing");
   m.def("gdr_phase_read", &gdr_phase_read, "summed SM cycles per (kernel, phase) of the gated delta rule");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle (symmetric peer memory)");

@@ -10,8 +10,11 @@
 //   warps 2-5   softmax (one thread per query row): tcgen05.ld S, mask, online softmax in the exp2
 //               domain with a lazily updated reference max (O is rescaled in TMEM only when the row max
 //               grows by more than 2^8), P -> smem (128-byte swizzle), epilogue O / l -> bf16, LSE.
+//               P is double-buffered, so the exponentials of tile j run while P_{j-1} V_{j-1} is on the
+//               tensor cores (only a rescale of O waits for that product); tiles whose every key is
+//               visible to every row skip the mask, and the softmax scale is folded into the exponent.
 //
-// TMEM: S0 | S1 | O = 384 of 512 columns.  Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + P 32 KB.
+// TMEM: S0 | S1 | O = 384 of 512 columns.  Shared memory: Q 32 KB + 2 x (K 32 KB + V 32 KB) + 2 x P 32 KB.
 // All waits are bounded (sm100_common.cuh).
 #include <torch/extension.h>
 #include <string>
@@ -35,10 +38,17 @@ struct Smem {
   static constexpr int Q = 0;
   static constexpr int K0 = Q + TILE_BYTES;
   static constexpr int V0 = K0 + 2 * TILE_BYTES;
-  static constexpr int P = V0 + 2 * TILE_BYTES;
-  static constexpr int BAR = P + TILE_BYTES;
+  static constexpr int P = V0 + 2 * TILE_BYTES;   // [2] P tiles
+  static constexpr int BAR = P + 2 * TILE_BYTES;
   static constexpr int TOTAL = BAR + 256;
 };
+static_assert(Smem::TOTAL + 1024 <= 232448, "forward shared memory above the 227 KB per-block limit");
+
+// Optional phase timing of the forward (a profiling aid, off unless attn_phase_profile(true)): the first
+// softmax thread of each CTA adds the SM cycles from kernel entry to the first S tile, of the tile loop
+// and of the epilogue, plus its tile count: g_attn_prof = {startup, loop, epilogue, tiles, ctas}.
+__device__ int g_attn_prof_on;
+__device__ unsigned long long g_attn_prof[8];
 
 struct alignas(64) AttnMaps {
   CUtensorMap q, k, v, pk, pv;
@@ -68,6 +78,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int q0 = cu[seq], n = cu[seq + 1] - q0;
   const int m0 = blockIdx.x * BQ;
   if (m0 >= n) return;  // before any TMEM/barrier work
+  const bool prof = threadIdx.x == 64 && g_attn_prof_on != 0;
+  long long t_entry = prof ? clock64() : 0, t_first = 0;
   const int po = poff[seq], pl = plen[seq];
   const int n_pre = (pl + BKV - 1) / BKV;
   const int n_self_keys = min(n, m0 + BQ);
@@ -82,9 +94,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* kv_empty = bars + 3;  // [2]
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* p_full = bars + 9;    // [2] P_j written (softmax -> MMA)
+  uint64_t* p_free = bars + 11;   // [2] P_j V_j done: P buffer reusable, O holds tiles <= j
+  uint64_t* o_done = bars + 13;   // the last P V done (epilogue)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -94,8 +107,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       sm100::mbar_init(&kv_empty[i], 1);
       sm100::mbar_init(&s_full[i], 1);
       sm100::mbar_init(&s_free[i], 128);
+      sm100::mbar_init(&p_full[i], 128);
+      sm100::mbar_init(&p_free[i], 1);
     }
-    sm100::mbar_init(p_full, 128);
     sm100::mbar_init(o_done, 1);
     sm100::fence_mbar_init();
   }
@@ -130,14 +144,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t p_base = sm100::smem_addr(smem + Smem::P);
       bool ok = sm100::mbar_wait(bar_q, 0, err, 12);
       auto issue_pv = [&](int j) -> bool {
-        if (!sm100::mbar_wait(p_full, j & 1, err, 13)) return false;
+        if (!sm100::mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, 13)) return false;
         sm100::tc_fence_after();
         const uint32_t v_base = sm100::smem_addr(smem + Smem::V0 + (j & 1) * TILE_BYTES);
+        const uint32_t pj = p_base + (j & 1) * TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          sm100::umma_bf16(TM_O, kmajor_desc(p_base, kk), vmajor_desc(v_base, kk), IDESC_O, (j > 0 || kk > 0));
-        sm100::umma_commit(o_done);
+          sm100::umma_bf16(TM_O, kmajor_desc(pj, kk), vmajor_desc(v_base, kk), IDESC_O, (j > 0 || kk > 0));
+        sm100::umma_commit(&p_free[j & 1]);
         sm100::umma_commit(&kv_empty[j & 1]);
+        if (j == ntiles - 1) sm100::umma_commit(o_done);
         return true;
       };
       for (int j = 0; j < ntiles && ok; ++j) {
@@ -180,30 +196,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ok = false;
         break;
       }
+      if (prof && j == 0) t_first = clock64();
       sm100::tc_fence_after();
-      float s[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t r[32];
-        sm100::tmem_ld32(TM_S0 + st * BKV + lane_off + c * 32, r);
-        sm100::tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[e]);
-      }
+      // the four 32-column loads in flight together, one wait
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      const uint32_t ts = TM_S0 + st * BKV + lane_off;
+      sm100::tmem_ld32(ts, r0);
+      sm100::tmem_ld32(ts + 32, r1);
+      sm100::tmem_ld32(ts + 64, r2);
+      sm100::tmem_ld32(ts + 96, r3);
+      sm100::tmem_ld_wait();
+      sm100::tmem_regs_ready(r0);
+      sm100::tmem_regs_ready(r1);
+      sm100::tmem_regs_ready(r2);
+      sm100::tmem_regs_ready(r3);
       sm100::tc_fence_before();
       sm100::mbar_arrive(&s_free[st]);  // S buffer may be overwritten by S_{j+2}
-      // mask + scale
+      float s[BKV];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        s[e] = __uint_as_float(r0[e]);
+        s[32 + e] = __uint_as_float(r1[e]);
+        s[64 + e] = __uint_as_float(r2[e]);
+        s[96 + e] = __uint_as_float(r3[e]);
+      }
+      // keys [kb, klim) are visible to this row; a tile wholly inside every row's range skips the mask
       const bool pre = j < n_pre;
       const int kb = pre ? j * BKV : (j - n_pre) * BKV;
-      const int klim = pre ? pl : min(n, qi + 1);  // keys [kb, klim) visible to this row
+      const int klim = pre ? pl : min(n, qi + 1);
       float mx = -INFINITY;
+      if (__all_sync(0xffffffffu, row_ok && kb + BKV <= klim)) {
 #pragma unroll
-      for (int e = 0; e < BKV; ++e) {
-        const bool vis = row_ok && (kb + e) < klim;
-        const float x = vis ? s[e] * scale_log2 : -INFINITY;
-        s[e] = x;
-        mx = fmaxf(mx, x);
+        for (int e = 0; e < BKV; ++e) mx = fmaxf(mx, s[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < BKV; ++e) {
+          const float x = (row_ok && (kb + e) < klim) ? s[e] : -INFINITY;
+          s[e] = x;
+          mx = fmaxf(mx, x);
+        }
       }
+      mx *= scale_log2;   // scale > 0: the max of the scaled scores
       // lazily updated reference max
       float alpha = 1.f;
       if (mx > m_ref + RESCALE_THRESHOLD || (m_ref == -INFINITY && mx > -INFINITY)) {
@@ -211,53 +244,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - m_new);
         m_ref = m_new;
       }
-      // P_{j-1} V_{j-1} must be done before O is rescaled or P is overwritten
-      if (j > 0) {
-        const bool g2 = sm100::mbar_wait(o_done, (j - 1) & 1, err, 17);
-        if (!__all_sync(0xffffffffu, g2)) {
+      // P buffer j & 1 was read by P_{j-2} V_{j-2}
+      if (j >= 2) {
+        const bool g1 = sm100::mbar_wait(&p_free[st], ((j >> 1) - 1) & 1, err, 19);
+        if (!__all_sync(0xffffffffu, g1)) {
           ok = false;
           break;
-        }
-        sm100::tc_fence_after();
-        const bool need = __any_sync(0xffffffffu, alpha != 1.f);
-        if (need) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            sm100::tmem_ld32(TM_O + lane_off + c * 32, r);
-            sm100::tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            sm100::tmem_st32(TM_O + lane_off + c * 32, r);
-          }
-          sm100::tmem_st_wait();
         }
       }
       float rs = 0.f;
       const float msafe = (m_ref == -INFINITY) ? 0.f : m_ref;
+      unsigned char* sPj = sP + st * TILE_BYTES;
       // P -> smem, 128-byte swizzle: 16-byte chunk index XOR (row & 7) within each 64-key block
 #pragma unroll
       for (int c = 0; c < BKV / 8; ++c) {
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = exp2f(s[c * 8 + 2 * e] - msafe);
-          const float p1 = exp2f(s[c * 8 + 2 * e + 1] - msafe);
+          const float p0 = exp2f(fmaf(s[c * 8 + 2 * e], scale_log2, -msafe));
+          const float p1 = exp2f(fmaf(s[c * 8 + 2 * e + 1], scale_log2, -msafe));
           rs += p0 + p1;
           __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
           pk[e] = *reinterpret_cast<uint32_t*>(&hv);
         }
         const int blk = c >> 3, chunk = c & 7;
-        unsigned char* dst = sP + blk * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
+        unsigned char* dst = sPj + blk * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l = l * alpha + rs;
+      // a new reference max: O (tiles < j) is rescaled once P_{j-1} V_{j-1} has landed, before P_j V_j
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        const int jp = j - 1;
+        const bool g2 = sm100::mbar_wait(&p_free[jp & 1], (jp >> 1) & 1, err, 17);
+        if (!__all_sync(0xffffffffu, g2)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(TM_O + lane_off + c * 32, r);
+          sm100::tmem_ld_wait();
+          sm100::tmem_regs_ready(r);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          sm100::tmem_st32(TM_O + lane_off + c * 32, r);
+        }
+        sm100::tmem_st_wait();
+      }
       sm100::fence_proxy_async_smem();
       sm100::tc_fence_before();
-      sm100::mbar_arrive(p_full);
+      sm100::mbar_arrive(&p_full[st]);
     }
     // epilogue
-    const bool g3 = ok && sm100::mbar_wait(o_done, (ntiles - 1) & 1, err, 18);
+    const long long t_loop = prof ? clock64() : 0;
+    const bool g3 = ok && sm100::mbar_wait(o_done, 0, err, 18);
     if (__all_sync(0xffffffffu, g3)) {
       sm100::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -281,6 +323,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (row_ok) lse[(size_t)h * T + q0 + qi] = l > 0.f ? (m_ref + log2f(l)) * 0.6931471805599453f : -INFINITY;
+    }
+    if (prof) {
+      const long long t_end = clock64();
+      atomicAdd(&g_attn_prof[0], (unsigned long long)(t_first - t_entry));
+      atomicAdd(&g_attn_prof[1], (unsigned long long)(t_loop - t_first));
+      atomicAdd(&g_attn_prof[2], (unsigned long long)(t_end - t_loop));
+      atomicAdd(&g_attn_prof[3], (unsigned long long)ntiles);
+      atomicAdd(&g_attn_prof[4], 1ull);
     }
   }
   sm100::tc_fence_before();
@@ -715,21 +765,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t tm_s = tmem + bi * 128, tm_dp = tmem + bi * 128 + 64;
       unsigned char* pt = smem + SmemDKDV2::PT0 + bi * PT_BYTES;
       unsigned char* dst = smem + SmemDKDV2::DS0 + bi * PT_BYTES;
-#pragma unroll 1
+      // S^T and dP^T of the 64 queries in flight together, one wait
+      uint32_t rs0[32], rd0[32], rs1[32], rd1[32];
+      sm100::tmem_ld32(tm_s + lane_off, rs0);
+      sm100::tmem_ld32(tm_dp + lane_off, rd0);
+      sm100::tmem_ld32(tm_s + lane_off + 32, rs1);
+      sm100::tmem_ld32(tm_dp + lane_off + 32, rd1);
+      sm100::tmem_ld_wait();
+      sm100::tmem_regs_ready(rs0);
+      sm100::tmem_regs_ready(rd0);
+      sm100::tmem_regs_ready(rs1);
+      sm100::tmem_regs_ready(rd1);
+      // prefix keys, and own keys below every query of the step, need no causal test (invalid query
+      // rows carry lse = +inf, so their p is 0 either way)
+      const bool all_vis = mode == 1 || kb + BKV - 1 <= qbase;
+      const float* lse_b = lse_s + bi * 64;
+      const float* del_b = del_s + bi * 64;
+#pragma unroll
       for (int c = 0; c < BQ2 / 32; ++c) {
-        uint32_t rs[32], rd[32];
-        sm100::tmem_ld32(tm_s + lane_off + c * 32, rs);
-        sm100::tmem_ld32(tm_dp + lane_off + c * 32, rd);
-        sm100::tmem_ld_wait();
         float p[32], ds[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const int qq = qbase + c * 32 + e;
-          const bool vis = key_ok && (mode == 1 || key <= qq);  // invalid q rows carry lse=+inf -> p=0
-          const float arg = __uint_as_float(rs[e]) * scale_log2 - lse_s[bi * 64 + c * 32 + e];
-          const float pe = vis ? exp2f(arg) : 0.f;
+          const float sv = __uint_as_float(c == 0 ? rs0[e] : rs1[e]);
+          const float dpv = __uint_as_float(c == 0 ? rd0[e] : rd1[e]);
+          const bool vis = key_ok && (all_vis || key <= qbase + c * 32 + e);
+          const float pe = vis ? exp2f(fmaf(sv, scale_log2, -lse_b[c * 32 + e])) : 0.f;
           p[e] = pe;
-          ds[e] = pe * (__uint_as_float(rd[e]) - del_s[bi * 64 + c * 32 + e]);
+          ds[e] = pe * (dpv - del_b[c * 32 + e]);
         }
         store_row32_sw128(pt, row, c, p);
         store_row32_sw128(dst, row, c, ds);
@@ -1119,12 +1181,15 @@ __global__ void __launch_bounds__(DQ2_THREADS, 1)
         sm100::tmem_ld32(tmem + b * 64 + lane_off + c * 32, rs);
         sm100::tmem_ld32(tmem + 128 + b * 64 + lane_off + c * 32, rd);
         sm100::tmem_ld_wait();
+        sm100::tmem_regs_ready(rs);
+        sm100::tmem_regs_ready(rd);
         float ds[32];
+        // keys of this half wholly visible to every row of the warp: no per-key test
+        const bool all_vis = __all_sync(0xffffffffu, row_ok && kbase + c * 32 + 32 <= klim);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const bool vis = row_ok && (kbase + c * 32 + e) < klim;
-          const float arg = __uint_as_float(rs[e]) * scale_log2 - lse_r;
-          const float pe = vis ? exp2f(arg) : 0.f;
+          const bool vis = all_vis || (row_ok && (kbase + c * 32 + e) < klim);
+          const float pe = vis ? exp2f(fmaf(__uint_as_float(rs[e]), scale_log2, -lse_r)) : 0.f;
           ds[e] = pe * (__uint_as_float(rd[e]) - del_r);
         }
         store_row32_sw128(ds_tile, row, c, ds);
@@ -1275,6 +1340,21 @@ std::vector<torch::Tensor> tree_attn_fwd_sm100(torch::Tensor q, torch::Tensor k,
 }
 
 int64_t attn_error_code() { return attn_error_word().item<int>(); }
+
+void attn_phase_profile(bool enable) {
+  const int on = enable ? 1 : 0;
+  unsigned long long zero[8] = {};
+  BB_CHECK_CUDA(cudaMemcpyToSymbol(g_attn_prof, zero, sizeof(zero)));
+  BB_CHECK_CUDA(cudaMemcpyToSymbol(g_attn_prof_on, &on, sizeof(on)));
+}
+
+torch::Tensor attn_phase_read() {
+  unsigned long long tab[8];
+  BB_CHECK_CUDA(cudaMemcpyFromSymbol(tab, g_attn_prof, sizeof(tab)));
+  auto out = torch::empty({8}, torch::TensorOptions().dtype(torch::kInt64));
+  for (int i = 0; i < 8; ++i) out[i] = (int64_t)tab[i];
+  return out;
+}
 
 std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                                torch::Tensor pk, torch::Tensor pv, torch::Tensor o, torch::Tensor lse,

@@ -123,6 +123,17 @@ def bench_attention(t: Timer, small: bool):
     do = torch.randn_like(o)
     ms = t(lambda: m.tree_attn_bwd_sm100(do, q, k, v, pk, pv, o, lse, *args))
     _report("attn_bwd_tcgen05", shape, ms, flops=2.5 * fl)
+    # forward CTA time split: entry -> first S tile, tile loop, epilogue (one untimed launch)
+    m.attn_phase_profile(True)
+    m.tree_attn_fwd_sm100(q, k, v, pk, pv, *args)
+    torch.cuda.synchronize()
+    st, loop, epi, tiles, ctas = [int(x) for x in m.attn_phase_read().tolist()[:5]]
+    m.attn_phase_profile(False)
+    tot = max(st + loop + epi, 1)
+    print(json.dumps({"op": "attn_fwd_phases", "ctas": ctas, "tiles": tiles,
+                      "cycles_per_cta": round(tot / max(ctas, 1)), "loop_cycles_per_tile": round(loop / max(tiles, 1)),
+                      "share": {"startup": round(st / tot, 3), "loop": round(loop / tot, 3),
+                                "epilogue": round(epi / tot, 3)}}))
 
 
 def bench_elementwise(t: Timer, small: bool):
