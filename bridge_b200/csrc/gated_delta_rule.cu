@@ -151,13 +151,14 @@ __device__ __forceinline__ void chunk_decay(const float* __restrict__ g, int row
 // inverts one unit-lower diagonal block by warp-synchronous substitution, then the off-diagonal
 // blocks follow level by level, T_ij = -T_ii sum_{j<=k<i} L_ik T_kj (L_ik = diag(beta) A block).
 template <int KD>
-__device__ void build_T(const bf* sK, int ldk, const float* sG, const float* sB, float* sA, float* sTf, bf* sTb, int n) {
+__device__ void build_T(const bf* sK, int ldk, const float* sG, const float* sB, float* sA, float* sTf, bf* sTb, int n,
+                        PhaseClock& pc, int kid) {
   wm::block_gemm<false, true>(CS, CS, KD, sK, ldk, sK, ldk, [&](int t, int s, float v) {
     sA[t * 65 + s] = (s < t && t < n) ? __expf(sG[t] - sG[s]) * v : 0.f;
   });
   for (int i = threadIdx.x; i < CS * 65; i += NT) sTf[i] = 0.f;
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pc.mark(kid, 12);
   if (threadIdx.x < 64) {
     // diagonal blocks: each of the 4 x 16 columns of the four unit-lower 16 x 16 inverses is an
     // independent forward substitution, one thread per column with the column in registers
@@ -174,52 +175,68 @@ __device__ void build_T(const bf* sK, int ldk, const float* sG, const float* sB,
     for (int r = 0; r < 16; ++r) sTf[(o + r) * 65 + o + c] = col[r];
   }
   __syncthreads();
+  pc.mark(kid, 13);
   float* scratch = sTf + CS * 65;  // callers reserve 4 x 16 x 17 floats after sTf
   for (int d = 1; d < 4; ++d) {
-    // the 4 - d blocks (i, j) = (j + d, j) of this level, each shared by wpb warps (all 8 busy)
-    const int nblk = 4 - d, wpb = (NT / 32) / nblk;
-    const int j = warp / wpb, part = warp % wpb;
+    // the 4 - d blocks (i, j) = (j + d, j) of this level; one thread per 2 x 2 output tile (64 per
+    // block), so every loaded A / T value serves two products
+    const int nblk = 4 - d;
+    const int j = threadIdx.x >> 6, tile = threadIdx.x & 63;
     const bool active = j < nblk;
     const int i = j + d;
+    const int r0 = (tile >> 3) * 2, c0 = (tile & 7) * 2;
     float* X = scratch + (active ? j : 0) * 16 * 17;
     if (active) {
       // X = diag(beta_i) sum_{k=j}^{i-1} A_ik T_kj  (16 x 16)
-      for (int e = part * 32 + lane; e < 256; e += wpb * 32) {
-        const int r = e / 16, c = e % 16;
-        float acc0 = 0.f, acc1 = 0.f;
-        for (int kb = j; kb < i; ++kb) {
-          const float* a = sA + (i * 16 + r) * 65 + kb * 16;
-          const float* t = sTf + (kb * 16) * 65 + j * 16 + c;
-#pragma unroll
-          for (int m = 0; m < 16; m += 2) {
-            acc0 += a[m] * t[m * 65];
-            acc1 += a[m + 1] * t[(m + 1) * 65];
-          }
-        }
-        X[r * 17 + c] = sB[i * 16 + r] * (acc0 + acc1);
+      float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+      const float* ar0 = sA + (i * 16 + r0) * 65;
+      const float* ar1 = ar0 + 65;
+      const float* tc = sTf + j * 16 + c0;
+#pragma unroll 4
+      for (int m = j * 16; m < i * 16; ++m) {
+        const float x0 = ar0[m], x1 = ar1[m];
+        const float t0 = tc[m * 65], t1 = tc[m * 65 + 1];
+        a00 += x0 * t0;
+        a01 += x0 * t1;
+        a10 += x1 * t0;
+        a11 += x1 * t1;
       }
+      const float b0 = sB[i * 16 + r0], b1 = sB[i * 16 + r0 + 1];
+      X[r0 * 17 + c0] = b0 * a00;
+      X[r0 * 17 + c0 + 1] = b0 * a01;
+      X[(r0 + 1) * 17 + c0] = b1 * a10;
+      X[(r0 + 1) * 17 + c0 + 1] = b1 * a11;
     }
     __syncthreads();
     if (active) {
-      for (int e = part * 32 + lane; e < 256; e += wpb * 32) {
-        const int r = e / 16, c = e % 16;
-        const float* tr = sTf + (i * 16 + r) * 65 + i * 16;   // T_ii row r (zero above the diagonal)
-        float acc0 = 0.f, acc1 = 0.f;
+      // T_ij = -T_ii X  (T_ii is zero above its diagonal)
+      float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+      const float* tr0 = sTf + (i * 16 + r0) * 65 + i * 16;
+      const float* tr1 = tr0 + 65;
 #pragma unroll
-        for (int m = 0; m < 16; m += 2) {
-          acc0 += tr[m] * X[m * 17 + c];
-          acc1 += tr[m + 1] * X[(m + 1) * 17 + c];
-        }
-        sTf[(i * 16 + r) * 65 + j * 16 + c] = -(acc0 + acc1);
+      for (int m = 0; m < 16; ++m) {
+        const float x0 = tr0[m], x1 = tr1[m];
+        const float t0 = X[m * 17 + c0], t1 = X[m * 17 + c0 + 1];
+        a00 += x0 * t0;
+        a01 += x0 * t1;
+        a10 += x1 * t0;
+        a11 += x1 * t1;
       }
+      float* o0 = sTf + (i * 16 + r0) * 65 + j * 16 + c0;
+      o0[0] = -a00;
+      o0[1] = -a01;
+      o0[65] = -a10;
+      o0[66] = -a11;
     }
     __syncthreads();
   }
+  pc.mark(kid, 14);
   for (int i = threadIdx.x; i < CS * CS; i += NT) {
     const int r = i / CS, c = i % CS;
     sTb[r * 72 + c] = f2b(r < n ? sTf[r * 65 + c] : 0.f);
   }
   __syncthreads();
+  pc.mark(kid, 15);
 }
 
 // ------------------------------------------------------------------------------------------------ forward
@@ -273,13 +290,16 @@ __global__ void __launch_bounds__(NT) gdr_prep_kernel(const bf* __restrict__ k, 
   }
   __syncthreads();
   pc.mark(0, 0);
-  build_T<KD>(sK, SM::LK, sG, sB, sA, sTf, sTb, ch.n);
+  build_T<KD>(sK, SM::LK, sG, sB, sA, sTf, sTb, ch.n, pc, 0);
   pc.mark(0, 1);
-  wm::block_gemm<false, false>(CS, KD, CS, sTb, 72, sKb, SM::LK, [&](int t, int c, float val) {
-    if (t < ch.n) wk[((size_t)(ch.row0 + t) * H + h) * KD + c] = f2b(val);
+  // (bf16 pairs: one 4-byte store per two columns)
+  wm::block_gemm_pairs<false, false>(CS, KD, CS, sTb, 72, sKb, nullptr, SM::LK, [&](int t, int c, float a, float b) {
+    if (t < ch.n)
+      *reinterpret_cast<__nv_bfloat162*>(wk + ((size_t)(ch.row0 + t) * H + h) * KD + c) = __floats2bfloat162_rn(a, b);
   });
-  wm::block_gemm<false, false>(CS, VD, CS, sTb, 72, sVb, SM::LV, [&](int t, int c, float val) {
-    if (t < ch.n) wv[((size_t)(ch.row0 + t) * H + h) * VD + c] = f2b(val);
+  wm::block_gemm_pairs<false, false>(CS, VD, CS, sTb, 72, sVb, nullptr, SM::LV, [&](int t, int c, float a, float b) {
+    if (t < ch.n)
+      *reinterpret_cast<__nv_bfloat162*>(wv + ((size_t)(ch.row0 + t) * H + h) * VD + c) = __floats2bfloat162_rn(a, b);
   });
   pc.mark(0, 2);
 }
@@ -377,11 +397,14 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
       sP[t * 72 + s] = f2b((s <= t && t < ch.n) ? __expf(sG[t] - sG[s]) * val : 0.f);
     });
     // U = Wv - Wk S0
-    wm::block_gemm2<false, false>(CS, VB, KD, sWk, SM::LK, sS, sSl, SM::LV, [&](int t, int c, float val) {
-      const float uu = t < ch.n ? b2f(sWv[t * SM::LV + c]) - val : 0.f;
-      sU[t * SM::LV + c] = f2b(uu);
-      sEU[t * SM::LV + c] = f2b(sE[t] * uu);
-      if (t < ch.n) u[((size_t)(ch.row0 + t) * H + h) * VD + v0 + c] = f2b(uu);
+    wm::block_gemm_pairs<false, false>(CS, VB, KD, sWk, SM::LK, sS, sSl, SM::LV, [&](int t, int c, float a, float b) {
+      const bool ok = t < ch.n;
+      const float2 wv2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sWv + t * SM::LV + c));
+      const float u0 = ok ? wv2.x - a : 0.f, u1 = ok ? wv2.y - b : 0.f;
+      const __nv_bfloat162 uh = __floats2bfloat162_rn(u0, u1);
+      *reinterpret_cast<__nv_bfloat162*>(sU + t * SM::LV + c) = uh;
+      *reinterpret_cast<__nv_bfloat162*>(sEU + t * SM::LV + c) = __floats2bfloat162_rn(sE[t] * u0, sE[t] * u1);
+      if (ok) *reinterpret_cast<__nv_bfloat162*>(u + ((size_t)(ch.row0 + t) * H + h) * VD + v0 + c) = uh;
     });
     __syncthreads();
     pc.mark(1, 1);
@@ -398,10 +421,12 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
 #pragma unroll
         for (int j = 0; j < 2; ++j)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int r = m0 + (lane >> 2) + 8 * (e >> 1), c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+          for (int e = 0; e < 4; e += 2) {
+            const int r = m0 + (lane >> 2) + 8 * (e >> 1), c = n0 + 8 * j + 2 * (lane & 3);
             if (r < ch.n)
-              o[((size_t)(ch.row0 + r) * H + h) * VD + v0 + c] = f2b(scale * (sGam[r] * c1[j][e] + c2[j][e]));
+              *reinterpret_cast<__nv_bfloat162*>(o + ((size_t)(ch.row0 + r) * H + h) * VD + v0 + c) =
+                  __floats2bfloat162_rn(scale * (sGam[r] * c1[j][e] + c2[j][e]),
+                                        scale * (sGam[r] * c1[j][e + 1] + c2[j][e + 1]));
           }
       }
     }
@@ -563,13 +588,16 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
 #pragma unroll
         for (int j = 0; j < 2; ++j)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int r = m0 + (lane >> 2) + 8 * (e >> 1), c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
-            const float d = r < ch.n ? scale * c2[j][e] + sE[r] * c1[j][e] : 0.f;
-            snDU[r * SM::LV + c] = f2b(-d);
-            if (r < ch.n) {
-              du[((size_t)(ch.row0 + r) * H + h) * VD + v0 + c] = d;
-              racc[e >> 1] += c1[j][e] * b2f(sU[r * SM::LV + c]);
+          for (int e = 0; e < 4; e += 2) {
+            const int r = m0 + (lane >> 2) + 8 * (e >> 1), c = n0 + 8 * j + 2 * (lane & 3);
+            const bool ok = r < ch.n;
+            const float d0 = ok ? scale * c2[j][e] + sE[r] * c1[j][e] : 0.f;
+            const float d1 = ok ? scale * c2[j][e + 1] + sE[r] * c1[j][e + 1] : 0.f;
+            *reinterpret_cast<__nv_bfloat162*>(snDU + r * SM::LV + c) = __floats2bfloat162_rn(-d0, -d1);
+            if (ok) {
+              *reinterpret_cast<float2*>(du + ((size_t)(ch.row0 + r) * H + h) * VD + v0 + c) = make_float2(d0, d1);
+              const float2 uu = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sU + r * SM::LV + c));
+              racc[e >> 1] += c1[j][e] * uu.x + c1[j][e + 1] * uu.y;
             }
           }
         // per-row sums inside the tile first (four lanes share a row), one shared atomic per row
@@ -737,7 +765,7 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
   }
   __syncthreads();
   pc.mark(3, 0);
-  build_T<KD>(sK, SM::LK, sG, sB, sA, sTf, sTb, n);          // sA = D o KK^T (strict), sTb = T
+  build_T<KD>(sK, SM::LK, sG, sB, sA, sTf, sTb, n, pc, 3);   // sA = D o KK^T (strict), sTb = T
   pc.mark(3, 1);
   // P (fp32, into sTf) and dP = scale dO U^T;  dG from P: rowsum(dP o P) - colsum(dP o P)
   wm::block_gemm<false, true>(CS, CS, KD, sQ, SM::LK, sK, SM::LK, [&](int t, int s, float val) {
@@ -759,8 +787,9 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
   __syncthreads();
   pc.mark(3, 3);
   // dq += (dP o D) K ;  dk += (dP o D)^T Q
-  wm::block_gemm<false, false>(CS, KD, CS, sX1, 72, sK, SM::LK, [&](int t, int c, float val) {
-    if (t < n) dq[rk(t) + c] += val;
+  // (float2 atomics whose result is unused: the add is posted, the warp does not wait for the old value)
+  wm::block_gemm_pairs<false, false>(CS, KD, CS, sX1, 72, sK, nullptr, SM::LK, [&](int t, int c, float a, float b) {
+    if (t < n) atomicAdd(reinterpret_cast<float2*>(dq + rk(t) + c), make_float2(a, b));
   });
   // the in-chunk dk terms are summed in shared memory (dead U / dO bytes) and added to dk once at the end
   float* sDK = reinterpret_cast<float*>(smem + SM::U);
@@ -840,18 +869,12 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
     sDK[t * SM::LDK + c] += val;
   });
   __syncthreads();
-  // one coalesced read-modify-write of dk (the scan kernel already added the state terms)
+  // one coalesced pass of posted float4 adds into dk (the scan kernel already added the state terms)
   for (int i = threadIdx.x; i < CS * (KD / 4); i += NT) {
     const int t = i / (KD / 4), c4 = (i % (KD / 4)) * 4;
     if (t < n) {
-      float4* dst = reinterpret_cast<float4*>(dk + rk(t) + c4);
-      float4 a = *dst;
       const float* src = sDK + t * SM::LDK + c4;
-      a.x += src[0];
-      a.y += src[1];
-      a.z += src[2];
-      a.w += src[3];
-      *dst = a;
+      atomicAdd(reinterpret_cast<float4*>(dk + rk(t) + c4), make_float4(src[0], src[1], src[2], src[3]));
     }
   }
   pc.mark(3, 9);

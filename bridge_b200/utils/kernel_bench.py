@@ -258,6 +258,7 @@ def bench_gdn(t: Timer, small: bool):
     torch.cuda.synchronize()
     tab = m.gdr_phase_read()
     m.gdr_phase_profile(False)
+    sub = {12: "T:KK^T", 13: "T:diag", 14: "T:levels", 15: "T:bf16"}   # inside build_T (prep, bwd chunk)
     names = {0: ("prep", ["load", "build_T", "Wk/Wv"]),
              1: ("scan", ["ckpt+load", "P,U", "O", "S1"]),
              2: ("bwd_scan", ["ckpt+load", "P", "dU", "dq", "dk", "dwk", "dG", "dS0", "dG tail"]),
@@ -265,8 +266,9 @@ def bench_gdn(t: Timer, small: bool):
     for kid, (kname, phases) in names.items():
         row = [int(x) for x in tab[kid].tolist()]
         tot = sum(row) or 1
-        print(json.dumps({"op": f"gdr_phases_{kname}", "block_cycles": tot,
-                          "share": {p: round(row[i] / tot, 3) for i, p in enumerate(phases)}}))
+        share = {p: round(row[i] / tot, 3) for i, p in enumerate(phases)}
+        share.update({v: round(row[k] / tot, 3) for k, v in sub.items() if row[k]})
+        print(json.dumps({"op": f"gdr_phases_{kname}", "block_cycles": tot, "share": share}))
 
 
 def bench_moe(t: Timer, small: bool):
