@@ -55,6 +55,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", default="bridge", choices=["bridge", "reference"])
     p.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5], help="BASELINE config number")
     p.add_argument("--model", default=None, help="default: the config's model")
+    p.add_argument("--num-layers", type=int, default=None,
+                   help="truncate the model (a functional check on fewer GPUs; not the named config)")
     p.add_argument("--trees-per-gpu", type=int, default=None, help="default: the config's (8, #3: 2 sessions)")
     p.add_argument("--prefix", type=int, default=None)
     p.add_argument("--siblings", type=int, default=8)
@@ -290,7 +292,7 @@ def main() -> None:
     dev = torch.device("cuda", torch.cuda.current_device())
     if world > 1:
         collective_probe(device=dev)
-    cfg = get_config(args.model)
+    cfg = get_config(args.model) if args.num_layers is None else get_config(args.model, num_layers=args.num_layers)
     tp, cp, ep = layout(args)
     sp = tp > 1 and not args.no_sp
     ec = EngineConfig(tensor_model_parallel_size=tp, context_parallel_size=cp, expert_model_parallel_size=ep,
@@ -371,7 +373,7 @@ def main() -> None:
         value = ppo_tokens_global / (ms / 1e3)
         par = parallelism_name(tp, cp, dp, ep)
         named = (args.config, args.model, par, world, n_trees, args.prefix, args.siblings, args.resp) == \
-            (2, "qwen3_4b", "tp2cp4", 8, 64, 512, 8, 512)
+            (2, "qwen3_4b", "tp2cp4", 8, 64, 512, 8, 512) and args.num_layers is None
         line = {
             "metric": METRIC,
             "value": value,
@@ -387,7 +389,8 @@ def main() -> None:
             "dtype": "bf16",
             "data": "synthetic (uniform token ids from seed, advantages N(0,1), random-init weights)",
             "config": {
-                "baseline_config": args.config, "model": args.model,
+                "baseline_config": args.config, "model": args.model, "num_layers": cfg.num_layers,
+                "truncated": args.num_layers is not None,
                 "global_batch": n_trees * (16 if args.config == 3 else args.siblings),
                 "seq_len": "6 turns of 2k-6k, <= 48k" if args.config == 3 else args.prefix + args.resp,
                 "parallelism": par, "sequence_parallel": sp, "activation_offload": ec.activation_offload,

@@ -132,4 +132,9 @@ def get_config(name: str, **overrides) -> ModelConfig:
         base = PRESETS[name]
     except KeyError as exc:
         raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}") from exc
+    if "num_layers" in overrides and "layer_types" not in overrides and base.layer_types is not None:
+        n = overrides["num_layers"]
+        if n > len(base.layer_types):
+            raise ValueError(f"{name} defines {len(base.layer_types)} layer types; cannot build {n} layers")
+        overrides["layer_types"] = base.layer_types[:n]   # a truncated hybrid keeps its layer pattern
     return replace(base, **overrides) if overrides else base
