@@ -101,6 +101,9 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
 // rows [row0, row0+n) of a [T, H, W] bf16 tensor (head h, columns [c0, c0+w)) -> smem [64][ld]; zero rows >= n.
 // Asynchronous (cp.async): every load of a phase is in flight at once; chunk_decay, which every kernel
@@ -118,9 +121,10 @@ __device__ __forceinline__ void load_rows(bf* dst, int ld, const bf* __restrict_
 }
 
 // G = cumsum(g) over the chunk (rows >= n hold the last value), Gam = e^G, E = e^{G_last - G}.
+template <bool WAIT_LOADS = true>
 __device__ __forceinline__ void chunk_decay(const float* __restrict__ g, int row0, int n, int H, int h, float* sG,
                                             float* sGam, float* sE) {
-  cp_async_wait_all();  // this thread's load_rows copies (made visible by the barriers below)
+  if (WAIT_LOADS) cp_async_wait_all();  // this thread's load_rows copies (made visible by the barriers below)
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float a = lane < n ? g[(size_t)(row0 + lane) * H + h] : 0.f;
@@ -275,6 +279,15 @@ __global__ void __launch_bounds__(NT) gdr_prep_kernel(const bf* __restrict__ k, 
   PhaseClock pc;
   load_rows<KD>(sK, SM::LK, k, ch.row0, ch.n, H, h, KD, 0);
   for (int t = threadIdx.x; t < CS; t += NT) sB[t] = t < ch.n ? beta[(size_t)(ch.row0 + t) * H + h] : 0.f;
+  // raw V rows into registers while the K rows are in flight
+  constexpr int VPT = CS * VD / 4 / NT;
+  float4 vreg[VPT];
+#pragma unroll
+  for (int a = 0; a < VPT; ++a) {
+    const int i = threadIdx.x + a * NT;
+    const int t = i / (VD / 4), c = (i % (VD / 4)) * 4;
+    vreg[a] = t < ch.n ? ld_bf4(v + ((size_t)(ch.row0 + t) * H + h) * VD + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);
   // scaled operands: Kb = beta Gam K, Vb = beta V
 #pragma unroll 4
@@ -282,11 +295,11 @@ __global__ void __launch_bounds__(NT) gdr_prep_kernel(const bf* __restrict__ k, 
     const int t = i / (KD / 4), c = (i % (KD / 4)) * 4;
     st_bf4(sKb + t * SM::LK + c, scale4(ld_bf4(sK + t * SM::LK + c), sB[t] * sGam[t]));
   }
-#pragma unroll 4
-  for (int i = threadIdx.x; i < CS * VD / 4; i += NT) {
+#pragma unroll
+  for (int a = 0; a < VPT; ++a) {
+    const int i = threadIdx.x + a * NT;
     const int t = i / (VD / 4), c = (i % (VD / 4)) * 4;
-    st_bf4(sVb + t * SM::LV + c, t < ch.n ? scale4(ld_bf4(v + ((size_t)(ch.row0 + t) * H + h) * VD + c), sB[t])
-                                          : make_float4(0.f, 0.f, 0.f, 0.f));
+    st_bf4(sVb + t * SM::LV + c, scale4(vreg[a], sB[t]));
   }
   __syncthreads();
   pc.mark(0, 0);
@@ -307,16 +320,19 @@ __global__ void __launch_bounds__(NT) gdr_prep_kernel(const bf* __restrict__ k, 
 template <int KD, int VB>
 struct ScanSmem {
   static constexpr int LK = KD + 8, LV = VB + 8;
+  // the row inputs of a chunk (Q, K, Wk, Wv), double-buffered: buffer b at ROWS * b
   static constexpr size_t Q = 0;
   static constexpr size_t K = Q + sizeof(bf) * CS * LK;
   static constexpr size_t WK = K + sizeof(bf) * CS * LK;
-  static constexpr size_t S = WK + sizeof(bf) * CS * LK;       // state, bf16 hi then lo
+  static constexpr size_t WV = WK + sizeof(bf) * CS * LK;
+  static constexpr size_t ROWS = WV + sizeof(bf) * CS * LV;
+  static constexpr size_t S = 2 * ROWS;                        // state, bf16 hi then lo
   static constexpr size_t U = S + 2 * sizeof(bf) * KD * LV;
   static constexpr size_t EU = U + sizeof(bf) * CS * LV;
-  static constexpr size_t WV = EU + sizeof(bf) * CS * LV;
-  static constexpr size_t P = WV + sizeof(bf) * CS * LV;
+  static constexpr size_t P = EU + sizeof(bf) * CS * LV;
   static constexpr size_t VEC = P + sizeof(bf) * CS * 72;
   static constexpr size_t TOTAL = VEC + sizeof(float) * 3 * CS;
+  static_assert(TOTAL <= 232448, "scan shared memory above the per-block limit");
 };
 
 // state tiles (16 x 16) of a [KD, VB] matrix owned by warp w: t = w, w + 8, ...
@@ -336,14 +352,10 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
   using SM = ScanSmem<KD, VB>;
   using ST = StateTiles<KD, VB>;
   extern __shared__ __align__(16) unsigned char smem[];
-  bf* sQ = reinterpret_cast<bf*>(smem + SM::Q);
-  bf* sK = reinterpret_cast<bf*>(smem + SM::K);
-  bf* sWk = reinterpret_cast<bf*>(smem + SM::WK);
   bf* sS = reinterpret_cast<bf*>(smem + SM::S);
   bf* sSl = sS + KD * SM::LV;
   bf* sU = reinterpret_cast<bf*>(smem + SM::U);
   bf* sEU = reinterpret_cast<bf*>(smem + SM::EU);
-  bf* sWv = reinterpret_cast<bf*>(smem + SM::WV);
   bf* sP = reinterpret_cast<bf*>(smem + SM::P);
   float* sG = reinterpret_cast<float*>(smem + SM::VEC);
   float* sGam = sG + CS;
@@ -367,8 +379,24 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
         st[i][j][e] = (t < ST::TILES && h0) ? h0[(((size_t)b * H + h) * KD + r) * VD + v0 + c] : 0.f;
       }
   }
+  // the next chunk's rows are fetched (cp.async) while this chunk computes
+  auto fetch = [&](int cj, int buf) {
+    const Chunk cn = load_chunk_desc(chunks, cj);
+    unsigned char* base = smem + buf * SM::ROWS;
+    load_rows<KD>(reinterpret_cast<bf*>(base + SM::Q), SM::LK, q, cn.row0, cn.n, H, h, KD, 0);
+    load_rows<KD>(reinterpret_cast<bf*>(base + SM::K), SM::LK, k, cn.row0, cn.n, H, h, KD, 0);
+    load_rows<KD>(reinterpret_cast<bf*>(base + SM::WK), SM::LK, wk, cn.row0, cn.n, H, h, KD, 0);
+    load_rows<VB>(reinterpret_cast<bf*>(base + SM::WV), SM::LV, wv, cn.row0, cn.n, H, h, VD, v0);
+    cp_async_commit();
+  };
+  if (c_begin < c_end) fetch(c_begin, 0);
   for (int ci = c_begin; ci < c_end; ++ci) {
     const Chunk ch = load_chunk_desc(chunks, ci);
+    const int buf = (ci - c_begin) & 1;
+    bf* sQ = reinterpret_cast<bf*>(smem + buf * SM::ROWS + SM::Q);
+    bf* sK = reinterpret_cast<bf*>(smem + buf * SM::ROWS + SM::K);
+    bf* sWk = reinterpret_cast<bf*>(smem + buf * SM::ROWS + SM::WK);
+    bf* sWv = reinterpret_cast<bf*>(smem + buf * SM::ROWS + SM::WV);
     float* ck = ckpt + (((size_t)b * H + h) * nc_max + ch.c) * KD * VD;
     // checkpoint S0 (FP32) and its bf16 copy for the tensor cores
 #pragma unroll
@@ -386,11 +414,14 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
           wm::split_bf16(st[i][j][e + 1], sS[r * SM::LV + c + 1], sSl[r * SM::LV + c + 1]);
         }
     }
-    load_rows<KD>(sQ, SM::LK, q, ch.row0, ch.n, H, h, KD, 0);
-    load_rows<KD>(sK, SM::LK, k, ch.row0, ch.n, H, h, KD, 0);
-    load_rows<KD>(sWk, SM::LK, wk, ch.row0, ch.n, H, h, KD, 0);
-    load_rows<VB>(sWv, SM::LV, wv, ch.row0, ch.n, H, h, VD, v0);
-    chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);  // ends with __syncthreads
+    // buffer buf ^ 1 was last read by the previous chunk, which ended with a block barrier
+    if (ci + 1 < c_end) {
+      fetch(ci + 1, buf ^ 1);
+      cp_async_wait_group<1>();   // this chunk's rows have landed; the next chunk's may still be in flight
+    } else {
+      cp_async_wait_group<0>();
+    }
+    chunk_decay<false>(g, ch.row0, ch.n, H, h, sG, sGam, sE);  // ends with __syncthreads
     pc.mark(1, 0);
     // P = D o Q K^T (s <= t)
     wm::block_gemm<false, true>(CS, CS, KD, sQ, SM::LK, sK, SM::LK, [&](int t, int s, float val) {
@@ -749,19 +780,34 @@ __global__ void __launch_bounds__(NT) gdr_bwd_chunk_kernel(
     sdG[t] = t < n ? dG_in[(size_t)(row0 + t) * H + h] : 0.f;
     sdb[t] = 0.f;
   }
-  chunk_decay(g, row0, n, H, h, sG, sGam, sE);
+  // the FP32 dWk / dU rows and the raw V rows are read while the cp.async rows are in flight (V is
+  // held in registers until beta is visible)
   const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
   for (int i = threadIdx.x; i < CS * KD / 4; i += NT) {
     const int t = i / (KD / 4), c = (i % (KD / 4)) * 4;
-    st_bf4(sKb + t * SM::LK + c, scale4(ld_bf4(sK + t * SM::LK + c), sB[t] * sGam[t]));
     st_bf4(sdWk + t * SM::LK + c, t < n ? *reinterpret_cast<const float4*>(dwk + rk(t) + c) : z4);
   }
-#pragma unroll 4
-  for (int i = threadIdx.x; i < CS * VD / 4; i += NT) {
+  constexpr int VPT = CS * VD / 4 / NT;   // V float4 groups per thread
+  float4 vreg[VPT];
+#pragma unroll
+  for (int a = 0; a < VPT; ++a) {
+    const int i = threadIdx.x + a * NT;
     const int t = i / (VD / 4), c = (i % (VD / 4)) * 4;
-    st_bf4(sVb + t * SM::LV + c, t < n ? scale4(ld_bf4(v + rv(t) + c), sB[t]) : z4);
     st_bf4(sdU + t * SM::LV + c, t < n ? *reinterpret_cast<const float4*>(du + rv(t) + c) : z4);
+    vreg[a] = t < n ? ld_bf4(v + rv(t) + c) : z4;
+  }
+  chunk_decay(g, row0, n, H, h, sG, sGam, sE);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < CS * KD / 4; i += NT) {
+    const int t = i / (KD / 4), c = (i % (KD / 4)) * 4;
+    st_bf4(sKb + t * SM::LK + c, scale4(ld_bf4(sK + t * SM::LK + c), sB[t] * sGam[t]));
+  }
+#pragma unroll
+  for (int a = 0; a < VPT; ++a) {
+    const int i = threadIdx.x + a * NT;
+    const int t = i / (VD / 4), c = (i % (VD / 4)) * 4;
+    st_bf4(sVb + t * SM::LV + c, scale4(vreg[a], sB[t]));
   }
   __syncthreads();
   pc.mark(3, 0);
