@@ -497,10 +497,12 @@ __global__ void __launch_bounds__(NT) gdr_scan_kernel(
 template <int KD, int VB>
 struct BScanSmem {
   static constexpr int LK = KD + 8, LV = VB + 8;
+  // Q, K, Wk rows of a chunk, double-buffered: buffer b at ROWS * b
   static constexpr size_t Q = 0;
   static constexpr size_t K = Q + sizeof(bf) * CS * LK;
   static constexpr size_t WK = K + sizeof(bf) * CS * LK;
-  static constexpr size_t S = WK + sizeof(bf) * CS * LK;
+  static constexpr size_t ROWS = WK + sizeof(bf) * CS * LK;
+  static constexpr size_t S = 2 * ROWS;
   static constexpr size_t DS = S + 2 * sizeof(bf) * KD * LV;   // S0 and dS1, each bf16 hi then lo
   static constexpr size_t U = DS + 2 * sizeof(bf) * KD * LV;
   static constexpr size_t DO = U + sizeof(bf) * CS * LV;
@@ -509,6 +511,7 @@ struct BScanSmem {
   static constexpr size_t P = NDU + sizeof(bf) * CS * LV;
   static constexpr size_t VEC = P + sizeof(bf) * CS * 72;   // G Gam E dG de red
   static constexpr size_t TOTAL = VEC + sizeof(float) * (5 * CS + 32);
+  static_assert(TOTAL <= 232448, "backward scan shared memory above the per-block limit");
 };
 
 template <int KD, int VD, int VB>
@@ -521,9 +524,6 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
   using SM = BScanSmem<KD, VB>;
   using ST = StateTiles<KD, VB>;
   extern __shared__ __align__(16) unsigned char smem[];
-  bf* sQ = reinterpret_cast<bf*>(smem + SM::Q);
-  bf* sK = reinterpret_cast<bf*>(smem + SM::K);
-  bf* sWk = reinterpret_cast<bf*>(smem + SM::WK);
   bf* sS = reinterpret_cast<bf*>(smem + SM::S);
   bf* sSl = sS + KD * SM::LV;
   bf* sdS = reinterpret_cast<bf*>(smem + SM::DS);
@@ -558,17 +558,51 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
         ds[i][j][e] = (t < ST::TILES && dhT) ? dhT[(((size_t)b * H + h) * KD + r) * VD + v0 + c] : 0.f;
       }
   }
+  // Chunks run in reverse; the previous chunk's Q / K / Wk rows (cp.async, other buffer) and its FP32
+  // state checkpoint (registers) are fetched while this chunk computes.
+  constexpr int CPT = KD * VB / 4 / NT;   // checkpoint float4 groups per thread
+  auto ck_of = [&](int cj) {
+    return ckpt + (((size_t)b * H + h) * nc_max + load_chunk_desc(chunks, cj).c) * KD * VD;
+  };
+  auto fetch_rows = [&](int cj, int buf) {
+    const Chunk cn = load_chunk_desc(chunks, cj);
+    unsigned char* base = smem + buf * SM::ROWS;
+    load_rows<KD>(reinterpret_cast<bf*>(base + SM::Q), SM::LK, q, cn.row0, cn.n, H, h, KD, 0);
+    load_rows<KD>(reinterpret_cast<bf*>(base + SM::K), SM::LK, k, cn.row0, cn.n, H, h, KD, 0);
+    load_rows<KD>(reinterpret_cast<bf*>(base + SM::WK), SM::LK, wk, cn.row0, cn.n, H, h, KD, 0);
+    cp_async_commit();
+  };
+  float4 ckreg[CPT];
+  auto fetch_ck = [&](int cj) {
+    const float* src = ck_of(cj);
+#pragma unroll
+    for (int a = 0; a < CPT; ++a) {
+      const int i = threadIdx.x + a * NT;
+      const int r = i / (VB / 4), c = (i % (VB / 4)) * 4;
+      ckreg[a] = *reinterpret_cast<const float4*>(src + (size_t)r * VD + v0 + c);
+    }
+  };
+  if (c_begin < c_end) {
+    fetch_rows(c_end - 1, 0);
+    fetch_ck(c_end - 1);
+  }
   for (int ci = c_end - 1; ci >= c_begin; --ci) {
     const Chunk ch = load_chunk_desc(chunks, ci);
+    const int buf = (c_end - 1 - ci) & 1;
+    bf* sQ = reinterpret_cast<bf*>(smem + buf * SM::ROWS + SM::Q);
+    bf* sK = reinterpret_cast<bf*>(smem + buf * SM::ROWS + SM::K);
+    bf* sWk = reinterpret_cast<bf*>(smem + buf * SM::ROWS + SM::WK);
     const float* ck = ckpt + (((size_t)b * H + h) * nc_max + ch.c) * KD * VD;
-#pragma unroll 4
-    for (int i = threadIdx.x; i < KD * VB / 4; i += NT) {
+#pragma unroll
+    for (int a = 0; a < CPT; ++a) {
+      const int i = threadIdx.x + a * NT;
       const int r = i / (VB / 4), c = (i % (VB / 4)) * 4;
-      const float4 x = *reinterpret_cast<const float4*>(ck + (size_t)r * VD + v0 + c);
+      const float4 x = ckreg[a];
       const float4 hi = ld_bf4_round(x);
       st_bf4(sS + r * SM::LV + c, hi);
       st_bf4(sSl + r * SM::LV + c, make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w));
     }
+    if (ci > c_begin) fetch_ck(ci - 1);
     float dot = 0.f;  // <dS1, S0> partial
 #pragma unroll
     for (int i = 0; i < ST::PER_WARP; ++i) {
@@ -588,13 +622,18 @@ __global__ void __launch_bounds__(NT) gdr_bwd_scan_kernel(
     }
     dot = bb::warp_sum(dot);
     if (lane == 0) sred[warp] = dot;
-    load_rows<KD>(sQ, SM::LK, q, ch.row0, ch.n, H, h, KD, 0);
-    load_rows<KD>(sK, SM::LK, k, ch.row0, ch.n, H, h, KD, 0);
-    load_rows<KD>(sWk, SM::LK, wk, ch.row0, ch.n, H, h, KD, 0);
     load_rows<VB>(sU, SM::LV, u, ch.row0, ch.n, H, h, VD, v0);
     load_rows<VB>(sdO, SM::LV, dout, ch.row0, ch.n, H, h, VD, v0);
+    cp_async_commit();
+    // buffer buf ^ 1 was last read by the chunk before, which ended with a block barrier
+    if (ci > c_begin) {
+      fetch_rows(ci - 1, buf ^ 1);
+      cp_async_wait_group<1>();   // this chunk's rows (and U / dO) have landed
+    } else {
+      cp_async_wait_group<0>();
+    }
     for (int t = threadIdx.x; t < CS; t += NT) sdG[t] = sde[t] = 0.f;
-    chunk_decay(g, ch.row0, ch.n, H, h, sG, sGam, sE);  // syncs
+    chunk_decay<false>(g, ch.row0, ch.n, H, h, sG, sGam, sE);  // syncs
     for (int i = threadIdx.x; i < CS * VB; i += NT) {
       const int t = i / VB, c = i % VB;
       sGdO[t * SM::LV + c] = f2b(scale * sGam[t] * b2f(sdO[t * SM::LV + c]));
