@@ -1226,23 +1226,44 @@ __global__ void __launch_bounds__(DQ2_THREADS, 1)
   }
 }
 
+// delta[h, t] = <dO[t, h, :], O[t, h, :]>: each half-warp reduces one 128-wide row (16 lanes x 16 bytes);
+// a warp takes two pairs of rows per step (loop bounds uniform across the warp for the shuffles)
 __global__ void delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
                              float* __restrict__ delta, int T, int Hq) {
-  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, sub = lane & 15, half = lane >> 4;
   const long total = (long)T * Hq;
-  for (long it = (long)blockIdx.x * warps + (threadIdx.x >> 5); it < total; it += (long)gridDim.x * warps) {
-    const int t = (int)(it / Hq), h = (int)(it % Hq);
-    const bb::bf16x8* a = reinterpret_cast<const bb::bf16x8*>(dout + ((size_t)t * Hq + h) * D);
-    const bb::bf16x8* o = reinterpret_cast<const bb::bf16x8*>(out + ((size_t)t * Hq + h) * D);
-    float fa[8], fo[8];
-    bb::unpack8(a[lane & 15], fa);
-    bb::unpack8(o[lane & 15], fo);
-    float s = 0.f;
-    if (lane < 16)
+  const long nwarps = (long)gridDim.x * (blockDim.x >> 5);
+  const long w = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (long base = 2 * w; base < total; base += 4 * nwarps) {
+    const long r0 = base + half, r1 = base + 2 * nwarps + half;
+    const bool v0 = r0 < total, v1 = r1 < total;
+    bb::bf16x8 a0{}, o0{}, a1{}, o1{};
+    if (v0) {
+      a0 = reinterpret_cast<const bb::bf16x8*>(dout + r0 * D)[sub];
+      o0 = reinterpret_cast<const bb::bf16x8*>(out + r0 * D)[sub];
+    }
+    if (v1) {
+      a1 = reinterpret_cast<const bb::bf16x8*>(dout + r1 * D)[sub];
+      o1 = reinterpret_cast<const bb::bf16x8*>(out + r1 * D)[sub];
+    }
+    float fa[8], fo[8], s0 = 0.f, s1 = 0.f;
+    bb::unpack8(a0, fa);
+    bb::unpack8(o0, fo);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s += fa[e] * fo[e];
-    s = bb::warp_sum(s);
-    if (lane == 0) delta[(size_t)h * T + t] = s;
+    for (int e = 0; e < 8; ++e) s0 += fa[e] * fo[e];
+    bb::unpack8(a1, fa);
+    bb::unpack8(o1, fo);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s1 += fa[e] * fo[e];
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+    }
+    if (sub == 0) {
+      if (v0) delta[(size_t)(r0 % Hq) * T + r0 / Hq] = s0;
+      if (v1) delta[(size_t)(r1 % Hq) * T + r1 / Hq] = s1;
+    }
   }
 }
 
@@ -1376,7 +1397,7 @@ std::vector<torch::Tensor> tree_attn_bwd_sm100(torch::Tensor dout, torch::Tensor
   auto stream = at::cuda::getCurrentCUDAStream();
   auto delta = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
   {
-    const int blocks = (int)std::min<long>(((long)T * Hq + 7) / 8, 148l * 16);
+    const int blocks = (int)std::max<long>(1, std::min<long>(((long)T * Hq + 31) / 32, 148l * 16));
     delta_kernel<<<blocks, 256, 0, stream>>>((const __nv_bfloat16*)dout.data_ptr(), (const __nv_bfloat16*)o.data_ptr(),
                                              delta.data_ptr<float>(), T, Hq);
     BB_POST_LAUNCH();
