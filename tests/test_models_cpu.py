@@ -176,3 +176,15 @@ def test_forest_activation_offload_preserves_gradients(mode, monkeypatch):
     assert out[True] == out[False]
     for n in grads[False]:
         assert torch.equal(grads[True][n], grads[False][n]), n
+
+
+def test_truncated_hybrid_config_keeps_layer_pattern():
+    """``get_config(name, num_layers=n)`` on a hybrid preset keeps the first n entries of its layer pattern
+    (bench.py --num-layers relies on it) and refuses more layers than the pattern defines."""
+    full = get_config("qwen3_next_24l")
+    cut = get_config("qwen3_next_24l", num_layers=8)
+    assert cut.num_layers == 8 and cut.layer_types == full.layer_types[:8]
+    assert cut.num_experts == full.num_experts and cut.attention_layer_numbers == (4, 8)
+    with pytest.raises(ValueError):
+        get_config("tiny_hybrid", num_layers=5)
+
