@@ -165,20 +165,25 @@ class ForestExecutor:
             if cols is not None:
                 from .tree_plan_builder import ObjectiveRefs
 
+                # one ref table per tree (grouped by segment), sliced per segment
                 order_ = np.argsort(cols[:, 0], kind="stable")
                 sorted_cols = cols[order_]
+                tab = self.objective.ref_table(ObjectiveRefs(sorted_cols))
                 sids, starts = np.unique(sorted_cols[:, 0], return_index=True)
                 bounds = list(starts[1:]) + [len(sorted_cols)]
-                refs = {int(sid): ObjectiveRefs(sorted_cols[a:b]) for sid, a, b in zip(sids, starts, bounds)}
+                for sid, a, b in zip(sids.tolist(), starts.tolist(), bounds):
+                    n = by_id[sid]
+                    n.ref_rows, n.ref_targets = tab.query_offsets[a:b], tab.targets[a:b]
+                    n.ref_samples, n.ref_flat = tab.sample_rows[a:b], tab.flat_index[a:b]
             else:
                 refs = defaultdict(list)
                 for r in tree.objective_refs:
                     refs[r.segment_id].append(r)
-            for sid, lst in refs.items():
-                tab = self.objective.ref_table(lst)
-                n = by_id[sid]
-                n.ref_rows, n.ref_targets, n.ref_samples, n.ref_flat = (tab.query_offsets, tab.targets,
-                                                                        tab.sample_rows, tab.flat_index)
+                for sid, lst in refs.items():
+                    tab = self.objective.ref_table(lst)
+                    n = by_id[sid]
+                    n.ref_rows, n.ref_targets, n.ref_samples, n.ref_flat = (tab.query_offsets, tab.targets,
+                                                                            tab.sample_rows, tab.flat_index)
         return self._split_long(nodes)
 
     def _split_long(self, nodes: list[_Node]) -> list[_Node]:

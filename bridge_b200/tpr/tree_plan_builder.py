@@ -178,30 +178,34 @@ def _tree_segment_plan(tree: TrajectoryTree, inputs) -> SegmentPlan:
     return SegmentPlan(specs, root_id=tree.root_id, topology_only=True)
 
 
-def _row_chains(tree: TrajectoryTree) -> dict[int, np.ndarray]:
-    """Member row -> node ids from the root down to the node where the row ends."""
-    chains: dict[int, np.ndarray] = {}
+def _row_chains(tree: TrajectoryTree) -> dict[int, tuple[np.ndarray, np.ndarray]]:
+    """Member row -> (node ids from the root down to the node where the row ends, their [start, end)
+    token spans); rows ending at the same node share both arrays."""
+    chains: dict[int, tuple[np.ndarray, np.ndarray]] = {}
     for node in tree.nodes.values():
         if not node.terminal_rows:
             continue
         up = [node.node_id]
         while tree.get(up[-1]).parent_id is not None:
             up.append(tree.get(up[-1]).parent_id)
-        chain = np.asarray(up[::-1], dtype=np.int64)
+        ids = up[::-1]
+        chain = np.asarray(ids, dtype=np.int64)
+        spans = np.asarray([(tree.get(n).segment.start, tree.get(n).segment.end) for n in ids],
+                           dtype=np.int64).reshape(-1, 2)
         for row in node.terminal_rows:
             if row in chains:
                 raise ValueError(f"tree {tree.key}: row {row} ends at two different nodes")
-            chains[row] = chain
+            chains[row] = (chain, spans)
     if set(chains) != set(tree.member_rows):
         raise ValueError(f"tree {tree.key}: rows {sorted(set(tree.member_rows) - set(chains))} end at no node")
     return chains
 
 
-def _row_refs(tree: TrajectoryTree, chain: np.ndarray, row: int, tokens, n_resp: int, off: np.ndarray) -> np.ndarray:
+def _row_refs(tree: TrajectoryTree, chain_spans: tuple[np.ndarray, np.ndarray], row: int, tokens, n_resp: int,
+              off: np.ndarray) -> np.ndarray:
     """Ref columns of one row: the token at response offset ``off`` (absolute position ``t``) is
     predicted by query ``t - 1``, owned by the first node of the chain whose span contains it."""
-    spans = np.asarray([(tree.get(int(n)).segment.start, tree.get(int(n)).segment.end) for n in chain],
-                       dtype=np.int64).reshape(-1, 2)
+    chain, spans = chain_spans
     t = tokens.numel() - n_resp + off
     q = t - 1
     k = np.searchsorted(spans[:, 1], q, side="right")
@@ -211,8 +215,14 @@ def _row_refs(tree: TrajectoryTree, chain: np.ndarray, row: int, tokens, n_resp:
     kk = np.minimum(k, len(chain) - 1)
     if not bool((spans[kk, 0] <= q).all()):
         raise ValueError(f"row {row}: a query position falls between node spans")
-    targets = tokens.detach().cpu().numpy().astype(np.int64)[t]
-    return np.stack([chain[k], q - spans[k, 0], targets, np.full_like(off, row), off], axis=1)
+    targets = tokens.detach().cpu().numpy()[t].astype(np.int64, copy=False)
+    out = np.empty((off.size, 5), dtype=np.int64)
+    out[:, 0] = chain[k]
+    out[:, 1] = q - spans[k, 0]
+    out[:, 2] = targets
+    out[:, 3] = row
+    out[:, 4] = off
+    return out
 
 
 def build_tree_execution_plans(
