@@ -226,9 +226,18 @@ def ring_cp_attention(query: Tensor, key: Tensor, value: Tensor, *, prefix_block
 
 def ordinary_ring_cp_attention(query: Tensor, key: Tensor, value: Tensor, *, cp_group, global_length: int,
                                softmax_scale: float | None = None) -> Tensor:
-    """Whole-sequence causal ring attention (no external prefix) over zigzag shards."""
+    """Whole-sequence causal ring attention (no external prefix) over zigzag shards: the NVLink P2P
+    path (row gathers + tcgen05 tree attention + owner reduction of dK/dV) on a single-node CUDA group,
+    the NCCL / gloo ring otherwise."""
+    from .cp_p2p import cp_comm, p2p_cp_attention
+
     shard = make_ring_sequence_shard(global_length, cp_rank=dist.get_rank(cp_group),
                                      cp_size=dist.get_world_size(cp_group))
+    comm = cp_comm(cp_group, query)
+    if comm is not None:
+        scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(query.shape[-1])
+        return p2p_cp_attention(query, key, value, prefix_blocks=(), current_shard=shard, comm=comm,
+                                softmax_scale=scale)
     return ring_cp_attention(query, key, value, prefix_blocks=(), current_shard=shard, cp_group=cp_group,
                              softmax_scale=softmax_scale)
 

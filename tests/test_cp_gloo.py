@@ -329,3 +329,46 @@ def test_forest_tp2_cp2_sequence_parallel_hybrid_matches_flattened():
         assert abs(r["loss"] - r["loss_ref"]) < 1e-5 * max(1.0, abs(r["loss_ref"])), r
         worst = max(r["grad_rel"].items(), key=lambda kv: kv[1])
         assert worst[1] < 1e-4, worst
+
+
+def _ordinary_ring_worker(rank, world, length):
+    """Whole-sequence causal ring attention on zigzag shards vs full FP32 causal attention."""
+    import torch
+    import torch.distributed as dist
+
+    from bridge_b200.parallel.ring_attention import ordinary_ring_cp_attention
+    from bridge_b200.tpr.shard import make_ring_sequence_shard
+
+    g = torch.Generator().manual_seed(5)
+    hq, hkv, d = 4, 2, 16
+    q = torch.randn(length, hq, d, generator=g)
+    k = torch.randn(length, hkv, d, generator=g)
+    v = torch.randn(length, hkv, d, generator=g)
+    do = torch.randn(length, hq, d, generator=g)
+    # reference: causal attention over the whole sequence (GQA)
+    qr, kr, vr = (t.clone().requires_grad_(True) for t in (q, k, v))
+    s = torch.einsum("qhd,khd->hqk", qr, kr.repeat_interleave(hq // hkv, 1)) * d ** -0.5
+    mask = torch.ones(length, length, dtype=torch.bool).tril()
+    p = torch.softmax(s.masked_fill(~mask, float("-inf")), -1)
+    o_ref = torch.einsum("hqk,khd->qhd", p, vr.repeat_interleave(hq // hkv, 1))
+    (o_ref * do).sum().backward()
+    shard = make_ring_sequence_shard(length, cp_rank=rank, cp_size=world)
+    # physical rows of this rank (padding rows past the sequence end carry zeros and no loss)
+    idx = torch.cat([torch.arange(a, b) for a, b in shard.physical_global_ranges])
+    valid = idx < length
+    pick = lambda t: torch.where(valid[:, None, None], t[idx.clamp(max=length - 1)], torch.zeros(()))  # noqa: E731
+    ql, kl, vl = (pick(t).clone().requires_grad_(True) for t in (q, k, v))
+    o = ordinary_ring_cp_attention(ql, kl, vl, cp_group=dist.group.WORLD, global_length=length)
+    (o * pick(do)).sum().backward()
+    sel = valid
+    err = lambda a, b: float((a[sel] - b[idx[sel]]).abs().max())  # noqa: E731
+    return {"o": err(o.detach(), o_ref.detach()), "dq": err(ql.grad, qr.grad),
+            # dK/dV of each key arrive at its owner rank after the ring; compare the owned rows
+            "dk": err(kl.grad, kr.grad), "dv": err(vl.grad, vr.grad)}
+
+
+@pytest.mark.parametrize("length", [40, 37])
+def test_ordinary_ring_matches_full_causal_attention(length):
+    """The whole-sequence ring entry (no external prefix), padded and unpadded zigzag shards."""
+    for r in run_ranks(2, _ordinary_ring_worker, length):
+        assert max(r.values()) < 1e-4, r
